@@ -1,0 +1,376 @@
+"""Committed tokens/s of the speculative draft -> verify -> accept -> commit step.
+
+Default workload (N=1 and per rank at N>1, weak scaling): the GPT-2-small-shaped
+pair in bf16 (target d768/12L/12H/ff3072, draft d384/4L/6H/ff1536, vocab
+32000, random-init weights, seed 0), 256 concurrent requests with prompts of
+U[128,1024] synthetic tokens, k=5, block 16, greedy.  A step is one
+``batched_speculative_step`` over the 256 active rows.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl pse|reference]
+
+Rank 0 prints one JSON line.  ``value`` times K steps replayed from the
+captured CUDA graph with everything resident in HBM (CUDA events, max over
+ranks); ``e2e`` times K further steps through the public Python API
+(request ids in, accepted tokens out, one host<->device round trip per step).
+``roofline`` is the verify-attention kernel (the step's largest HBM stream)
+timed live on the same cache state; ``cpu_baseline`` is the reference's CPU
+path (the oracle port, fp32) on a bounded sample.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for p in (ROOT, os.path.join(ROOT, "paged-speculative-engine_b200")):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+
+def _peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}",
+                 "--query-gpu=clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+                 "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_power_cap",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 7:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = float(parts[1])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[3:7]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def build_pair(workload, dtype, device, seed=0):
+    import pse
+    from pse.model import LlamaConfig, ModelConfig, TinyGPT, TinyLlama
+    pr = workload.pair
+    torch.manual_seed(seed)
+    if pr.kind == "gpt":
+        d = TinyGPT(ModelConfig(vocab_size=pr.vocab, **pr.draft))
+        t = TinyGPT(ModelConfig(vocab_size=pr.vocab, **pr.target))
+    else:
+        d = TinyLlama(LlamaConfig(vocab_size=pr.vocab, **pr.draft))
+        t = TinyLlama(LlamaConfig(vocab_size=pr.vocab, **pr.target))
+    return d.eval(), t.eval()
+
+
+def cache_for(model, workload, n_rows, dtype, device, extra_tokens):
+    import pse
+    cfg = model.cfg
+    kv = getattr(cfg, "n_kv_heads", cfg.n_heads)
+    hd = cfg.d_model // cfg.n_heads
+    bs = workload.block_size
+    per_row = workload.prompt_hi + workload.max_new_tokens + extra_tokens
+    nb = n_rows * ((per_row + bs - 1) // bs) + 8
+    return pse.PagedKVCache(cfg.n_layers, kv, hd, bs, nb, dtype=dtype, device=device, max_requests=n_rows,
+                            max_blocks_per_request=(per_row + bs - 1) // bs)
+
+
+def run_pse(args, rank, world, device):
+    import pse
+    import pse._native as N
+    from pse import workload as wl
+    from pse.speculative import runner_for
+
+    w = wl.WORKLOADS[args.workload]
+    dtype = torch.bfloat16 if w.dtype == "bfloat16" else torch.float32
+    B = args.rows or w.max_batch_size
+    d, t = build_pair(w, dtype, device)
+    dc = cache_for(d, w, B, dtype, device, w.k + 2)
+    tc = cache_for(t, w, B, dtype, device, w.k + 2)
+    prompts = wl.prompts(w, seed=rank, n=B)
+    rids = [f"g{rank}r{i}" for i in range(B)]
+    dn, tn = {}, {}
+    t0 = time.perf_counter()
+    for r, p in zip(rids, prompts):
+        dn[r], tn[r] = pse.prefill_request(d, t, dc, tc, r, p)
+    torch.cuda.synchronize()
+    prefill_s = time.perf_counter() - t0
+    k, T = w.k, w.temperature
+
+    def api_step():
+        res = pse.batched_speculative_step(d, t, rids, dc, tc, dn, tn, k, T)
+        for r in rids:
+            dn[r] = res.draft_next_logits[r]
+            tn[r] = res.target_next_logits[r]
+        return sum(len(v) for v in res.accepted_tokens.values())
+
+    before = sum(N.launches.values())
+    api_step()  # first step of this batch size runs eagerly: count its kernels
+    kernels_per_step = sum(N.launches.values()) - before
+    for _ in range(max(args.warmup, 3) - 1):
+        api_step()
+    runner = runner_for(d, t, dc, tc, k)
+    graph = [g for key, g in runner.graphs.items() if key[0] == B][0]
+    b = runner.bufs[B]
+    nacc_hist = torch.zeros(args.steps, B, dtype=torch.int32, device=device)
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+
+    # ---- device-resident timed region: K graph replays ----
+    launches_before = sum(N.launches.values())
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(device.index or 0) as clk:
+        e0.record()
+        for s in range(args.steps):
+            graph.replay()
+            nacc_hist[s].copy_(b.n_acc)
+        e1.record()
+        barrier()
+    ms = e0.elapsed_time(e1)
+    committed = int(nacc_hist.sum().item()) + args.steps * B
+    # host mirrors of the lengths after the replays
+    for c in (dc, tc):
+        c._resync_lengths()
+    # ---- e2e through the public API ----
+    barrier()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record()
+    e2e_tokens = sum(api_step() for _ in range(args.steps))
+    f1.record()
+    barrier()
+    e2e_ms = f0.elapsed_time(f1)
+
+    # ---- verify-attention kernel, timed live on the current target state ----
+    dm = runner.dm_t
+    hd, hq, hk = dm.head_dim, dm.q_heads, dm.kv_heads
+    lens = tc._blocks.seq_len[b.slots_t.long()]
+    base = (lens - k).clamp(min=0).to(torch.int32)
+    ctx = (base + k).to(torch.int64)
+    max_ctx = int(ctx.max().item())
+    q = torch.randn(B * k, hq * hd, dtype=dtype, device=device)
+    out = torch.empty_like(q)
+    wsb = N.size_call("pse_paged_attention_workspace", B, k, hq, hk, hd, max_ctx)
+    ws = torch.empty(max(wsb, 1), dtype=torch.uint8, device=device)
+    st = N.stream_ptr()
+    reps = 20
+
+    def attn_all_layers():
+        for li in range(dm.n_layers):
+            N.call("pse_paged_attention", tc.state, tc.layer(li), q.data_ptr(), q.stride(0), out.data_ptr(),
+                   out.stride(0), b.slots_t.data_ptr(), base.data_ptr(), B, k, hq, 1.0 / math.sqrt(hd), max_ctx,
+                   ws.data_ptr(), ws.numel(), st)
+
+    attn_all_layers()
+    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a0.record()
+    for _ in range(reps):
+        attn_all_layers()
+    a1.record()
+    torch.cuda.synchronize()
+    attn_ms = a0.elapsed_time(a1) / (reps * dm.n_layers)
+    esize = torch.finfo(dtype).bits // 8
+    attn_bytes = int(ctx.sum().item()) * hk * hd * 2 * esize + 2 * q.numel() * esize + B * 4 * tc.max_blocks
+
+    stats = torch.tensor([committed, ms, e2e_tokens, e2e_ms], dtype=torch.float64, device=device)
+    if world > 1:
+        tot = stats.clone()
+        torch.distributed.all_reduce(tot, op=torch.distributed.ReduceOp.SUM)
+        mx = stats.clone()
+        torch.distributed.all_reduce(mx, op=torch.distributed.ReduceOp.MAX)
+        committed, e2e_tokens = int(tot[0].item()), int(tot[2].item())
+        ms, e2e_ms = float(mx[1].item()), float(mx[3].item())
+    launches = sum(N.launches.values()) - launches_before
+    return dict(committed=committed, ms=ms, e2e_tokens=e2e_tokens, e2e_ms=e2e_ms, attn_ms=attn_ms,
+                attn_bytes=attn_bytes, prefill_s=prefill_s, clocks=clk.summary(), B=B, k=k,
+                kernels_per_step=kernels_per_step, launches_counted=launches, dtype=str(dtype),
+                h2d=2 * B * 4, d2h=(B * (k + 1) + B + 2) * 4)
+
+
+def cpu_reference(args, sample_rows, sample_steps, threads):
+    """The reference's CPU path (the oracle port of engine/*.py, fp32) on a
+    bounded sample of the same workload: prefill is untimed, then
+    ``sample_steps`` batched speculative steps over ``sample_rows`` rows."""
+    from oracle.model import LlamaConfig, ModelConfig, TinyGPT, TinyLlama
+    from oracle.paged_cache import PagedKVCache
+    from oracle.speculative import batched_speculative_step, prefill_request
+    from pse import workload as wl
+
+    torch.set_num_threads(threads)
+    w = wl.WORKLOADS[args.workload]
+    pr = w.pair
+    torch.manual_seed(0)
+    if pr.kind == "gpt":
+        d = TinyGPT(ModelConfig(vocab_size=pr.vocab, **pr.draft)).eval()
+        t = TinyGPT(ModelConfig(vocab_size=pr.vocab, **pr.target)).eval()
+    else:
+        d = TinyLlama(LlamaConfig(vocab_size=pr.vocab, **pr.draft)).eval()
+        t = TinyLlama(LlamaConfig(vocab_size=pr.vocab, **pr.target)).eval()
+
+    def mk(m):
+        c = m.cfg
+        kv = getattr(c, "n_kv_heads", c.n_heads)
+        per = w.prompt_hi + w.max_new_tokens + w.k + 2
+        return PagedKVCache(c.n_layers, kv, c.d_model // c.n_heads, w.block_size,
+                            sample_rows * ((per + w.block_size - 1) // w.block_size) + 8)
+
+    dc, tc = mk(d), mk(t)
+    prompts = wl.prompts(w, seed=0, n=sample_rows)
+    rids = [f"c{i}" for i in range(sample_rows)]
+    dn, tn = {}, {}
+    for r, p in zip(rids, prompts):
+        dn[r], tn[r] = prefill_request(d, t, dc, tc, r, p)
+    tok = 0
+    t0 = time.perf_counter()
+    for _ in range(sample_steps):
+        res = batched_speculative_step(d, t, rids, dc, tc, dn, tn, w.k, w.temperature)
+        tok += sum(len(v) for v in res.accepted_tokens.values())
+        dn, tn = res.draft_next_logits, res.target_next_logits
+    dt = time.perf_counter() - t0
+    return dict(value=tok / dt, tokens=tok, seconds=dt, cores=threads,
+                sample=f"{sample_rows} of {w.max_batch_size} rows x {sample_steps} steps of the {w.name} "
+                       f"workload (prompts from the same seed), fp32 oracle port, prefill untimed")
+
+
+def config_block(args, w, B, world):
+    return {"workload": f"{w.name}: {w.n_requests if args.rows is None else B} rows/GPU, prompts "
+                        f"U[{w.prompt_lo},{w.prompt_hi}], k={w.k}, block {w.block_size}, "
+                        f"{'greedy' if w.temperature == 0 else 'T=%g' % w.temperature}",
+            "rows_per_gpu": B, "k": w.k, "block_size": w.block_size,
+            "target": w.pair.target, "draft": w.pair.draft, "vocab": w.pair.vocab,
+            "parallelism": f"request shards x{world}",
+            "l2": "KV working set per step (GBs) >> 126 MB L2; no flush needed"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="pse", choices=["pse", "reference"])
+    ap.add_argument("--workload", default="gpt2-small")
+    ap.add_argument("--rows", type=int, default=None)
+    ap.add_argument("--cpu-rows", type=int, default=4)
+    ap.add_argument("--cpu-steps", type=int, default=2)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+
+    from pse import workload as wl
+    w = wl.WORKLOADS[args.workload]
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    metric = "committed tokens/s"
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        threads = os.cpu_count() or 1
+        r = cpu_reference(args, args.cpu_rows, args.cpu_steps, threads)
+        line = {"impl": "reference", "metric": metric, "value": r["value"], "unit": "tokens/s", "n_gpus": args.gpus,
+                "steps": args.cpu_steps, "warmup": 0, "ms_per_step": 1000 * r["seconds"] / args.cpu_steps,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic prompts, random-init weights",
+                "config": config_block(args, w, args.cpu_rows, 1),
+                "cpu_baseline": {"value": r["value"], "unit": "tokens/s", "cores": r["cores"], "kind": "port",
+                                 "sample": r["sample"]},
+                "e2e": {"value": r["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
+
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+    device = torch.device("cuda", local if world > 1 else torch.cuda.current_device())
+    torch.cuda.set_device(device)
+    import pse._build
+    pse._build.build()
+    r = run_pse(args, rank, world, device)
+    peak, peak_kind = _peaks()
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_reference(args, args.cpu_rows, args.cpu_steps, os.cpu_count() or 1)
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+    if rank != 0:
+        return
+    value = r["committed"] / (r["ms"] / 1000.0)
+    achieved = r["attn_bytes"] / (r["attn_ms"] / 1000.0) / 1e9
+    line = {
+        "metric": metric, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": max(args.warmup, 3), "ms_per_step": r["ms"] / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16" if "bfloat16" in r["dtype"] else "f32",
+        "data": "synthetic prompts (seeded), random-init weights (seed 0)",
+        "config": config_block(args, w, r["B"], world),
+        "e2e": {"value": r["e2e_tokens"] / (r["e2e_ms"] / 1000.0), "unit": "tokens/s",
+                "h2d_bytes_per_step": r["h2d"], "d2h_bytes_per_step": r["d2h"]},
+        "roofline": {"kernel": "pse_paged_attention (target verify, width k, all layers)", "bound": "hbm",
+                     "achieved": achieved, "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
+                     "frac": achieved / peak, "traffic": None, "avg_launch_us": r["attn_ms"] * 1000},
+        "cpu_baseline": None if cpu is None else {"value": cpu["value"], "unit": "tokens/s", "cores": cpu["cores"],
+                                                  "kind": "port", "sample": cpu["sample"]},
+        "clocks": r["clocks"],
+        "gpu_launches": r["kernels_per_step"] * args.steps,
+        "prefill_s": r["prefill_s"],
+    }
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

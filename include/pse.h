@@ -1,0 +1,223 @@
+/*
+ * pse.h -- C ABI of libpse.so, the sm_100a kernels of the speculative
+ * draft -> verify -> accept/reject -> commit path.
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream
+ * (as void*), launches asynchronously on that stream, allocates nothing and
+ * never synchronises.  Return value: 0 on success, a cudaError_t value from
+ * the launch, or one of the PSE_EINVAL... codes below for bad arguments
+ * (checked on the host before anything is launched).
+ *
+ * Cache-state errors found on the device (pool exhausted, truncate beyond
+ * length, double free) are latched in the state's `status` word instead of
+ * trapping; while it is non-zero every state-mutating kernel is a no-op.  The
+ * host reads the word at a step boundary and raises the reference's
+ * exception (MemoryError / ValueError).
+ *
+ * Each declaration names the reference interface it replaces
+ * (vedantjain09/paged-speculative-engine, engine/...:line).
+ */
+#ifndef PSE_H_
+#define PSE_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- return codes (host-side argument checks) ---- */
+#define PSE_OK 0
+#define PSE_EINVAL 10001       /* bad size / pointer / unsupported combination */
+#define PSE_EWORKSPACE 10002   /* workspace smaller than the query function said */
+
+/* ---- device status latch bits ---- */
+#define PSE_STATUS_OOM 1              /* pool exhausted (reference: MemoryError) */
+#define PSE_STATUS_TABLE_OVERFLOW 2   /* block table too narrow for the row */
+#define PSE_STATUS_TRUNCATE_LONG 4    /* truncate beyond length (ValueError) */
+#define PSE_STATUS_DOUBLE_FREE 8      /* block freed twice (ValueError) */
+#define PSE_STATUS_BAD_BLOCK 16       /* block id out of range */
+
+/* ---- element types ---- */
+#define PSE_F32 0
+#define PSE_BF16 1
+
+/* Device bookkeeping of one paged cache (one model).  All arrays on device. */
+typedef struct {
+  int32_t *block_table; /* [num_slots, max_blocks] physical block ids, -1 unused */
+  int32_t *seq_len;     /* [num_slots] tokens held by the row                   */
+  int32_t *nblocks;     /* [num_slots] blocks held by the row                   */
+  int32_t *free_stack;  /* [num_blocks] LIFO stack, valid entries [0, *free_top) */
+  int32_t *free_top;    /* [1]                                                  */
+  uint8_t *block_free;  /* [num_blocks] 1 while the block is on the stack       */
+  int32_t *status;      /* [1] error latch (PSE_STATUS_* bits)                  */
+  int32_t num_blocks;
+  int32_t block_size;
+  int32_t max_blocks;
+  int32_t num_slots;
+} pse_block_state;
+
+/* One layer's K and V pools: [num_blocks, kv_heads, block_size, head_dim]. */
+typedef struct {
+  void *k_pool;
+  void *v_pool;
+  int32_t kv_heads;
+  int32_t head_dim;
+  int32_t dtype; /* PSE_F32 or PSE_BF16 */
+} pse_kv_layer;
+
+/* ------------------------------------------------------------------------ */
+/* Block pool / free list                                                   */
+/* ------------------------------------------------------------------------ */
+
+/* BlockAllocator.__init__ (engine/paged_cache.py:37-39) and PagedKVCache's
+ * empty tables (engine/paged_cache.py:89-90): stack = [0..n-1], all tables -1,
+ * lengths 0, status 0. */
+int pse_block_init(pse_block_state st, void *stream);
+
+/* BlockAllocator.allocate (engine/paged_cache.py:45-48): pops the stack top
+ * into *out_id, or writes -1 and latches PSE_STATUS_OOM. */
+int pse_block_alloc_one(pse_block_state st, int32_t *out_id, void *stream);
+
+/* BlockAllocator.free (engine/paged_cache.py:50-56): pushes `block_id`
+ * (device scalar); latches PSE_STATUS_DOUBLE_FREE / BAD_BLOCK instead. */
+int pse_block_free_one(pse_block_state st, const int32_t *block_id, void *stream);
+
+/* The allocation half of PagedKVCache.append (engine/paged_cache.py:116-130)
+ * for `rows` rows of one batched forward (engine/batched_forward.py:67-70):
+ * every row grows by `width` tokens, missing blocks are popped in row order
+ * (exclusive prefix sum over rows), base_len[i] receives the row's length
+ * before the call and seq_len advances.  On exhaustion the state is the
+ * reference's after its MemoryError (earlier rows complete, the failing row
+ * keeps its partial blocks, later rows untouched) and OOM is latched. */
+int pse_kv_reserve(pse_block_state st, const int32_t *slots, int32_t rows, int32_t width,
+                   int32_t *base_len, void *stream);
+
+/* PagedKVCache.truncate (engine/paged_cache.py:140-154) for many rows in call
+ * order, as the commit loop of engine/speculative.py:162-164 runs it.  New
+ * length of row i = new_len[i] if new_len != NULL, else base_len[i] +
+ * accepted[i].  Trailing blocks are pushed from the table end. */
+int pse_kv_truncate(pse_block_state st, const int32_t *slots, int32_t rows, const int32_t *new_len,
+                    const int32_t *base_len, const int32_t *accepted, void *stream);
+
+/* PagedKVCache.free_request (engine/paged_cache.py:156-160) for many rows in
+ * call order: each row's blocks are pushed in forward table order. */
+int pse_kv_release(pse_block_state st, const int32_t *slots, int32_t rows, void *stream);
+
+/* ------------------------------------------------------------------------ */
+/* KV append and paged attention                                            */
+/* ------------------------------------------------------------------------ */
+
+/* The copy half of PagedKVCache.append (engine/paged_cache.py:131-136): token
+ * w of row i, head h, element d is read from k_src/v_src + (i*width + w) *
+ * tok_stride + h * head_stride + d and written at position base_len[i] + w of
+ * the row.  Sources have the pool's dtype.  Blocks must have been reserved. */
+int pse_kv_append(pse_block_state st, pse_kv_layer kv, const void *k_src, const void *v_src,
+                  int64_t tok_stride, int64_t head_stride, const int32_t *slots,
+                  const int32_t *base_len, int32_t rows, int32_t width, void *stream);
+
+/* PagedKVCache.gather (engine/paged_cache.py:162-198) for one layer: padded
+ * [rows, kv_heads, max_len, head_dim] K and V, zeros past each row's length. */
+int pse_kv_gather(pse_block_state st, pse_kv_layer kv, const int32_t *slots, int32_t rows,
+                  int32_t max_len, void *k_out, void *v_out, void *stream);
+
+/* Attention of engine/model.py:99-116 over the paged state, replacing the
+ * gather + masked matmul of engine/batched_forward.py:37-65.  Query w of row
+ * i (head h at q + (i*width + w) * q_tok_stride + h*head_dim) sits at position
+ * base_len[i] + w and attends to positions 0..base_len[i]+w of the row, whose
+ * K/V are already in the pool.  Grouped heads: query head h reads KV head
+ * h / (q_heads / kv_heads).  `max_ctx` bounds base_len[i] + width over rows
+ * (it sizes the split-KV grid; rows may be shorter).  Output has the pool's
+ * dtype.  workspace: float scratch of pse_paged_attention_workspace() bytes. */
+int pse_paged_attention(pse_block_state st, pse_kv_layer kv, const void *q, int64_t q_tok_stride,
+                        void *out, int64_t out_tok_stride, const int32_t *slots, const int32_t *base_len,
+                        int32_t rows, int32_t width, int32_t q_heads, float scale, int32_t max_ctx,
+                        void *workspace, size_t workspace_bytes, void *stream);
+
+size_t pse_paged_attention_workspace(int32_t rows, int32_t width, int32_t q_heads, int32_t kv_heads,
+                                     int32_t head_dim, int32_t max_ctx);
+
+/* ------------------------------------------------------------------------ */
+/* Sampling, accept/resample                                                */
+/* ------------------------------------------------------------------------ */
+
+/* Uniform source of the explicit-uniform mode (replaces the torch.Generator
+ * draws of engine/sampling.py:16-18 and engine/speculative.py:136):
+ * out[i*n + j] = Philox4x32-10 uniform keyed (seed, req_key[i], step[i], j). */
+int pse_philox_uniforms(uint64_t seed, const uint32_t *req_key, const int32_t *step, int32_t rows,
+                        int32_t n, double *out, void *stream);
+
+/* One draft-round draw per row (engine/speculative.py:99-108 with
+ * engine/sampling.py:10-23): logits row of row i = logits + (index ? index[i] :
+ * i) * row_stride.  T <= 0: argmax (first maximum).  T > 0: inverse CDF of
+ * softmax(l / T) at uniform u[i*u_stride + u_col].  The token goes to
+ * out[i*out_stride] and, if out2 != NULL, to out2[i*out2_stride]. */
+int pse_sample_tokens(const float *logits, int64_t row_stride, const int32_t *index, int32_t rows,
+                      int32_t vocab, float temperature, const double *u, int64_t u_stride,
+                      int32_t u_col, int32_t *out, int64_t out_stride, int32_t *out2,
+                      int64_t out2_stride, void *stream);
+
+/* Fused accept / reject / residual / bonus of engine/speculative.py:119-157
+ * (and _residual_sample, :43-50), one CTA per row.  Target position 0 is
+ * target0 + (t0_index ? t0_index[i] : i) * t0_stride; positions 1..k are
+ * verify + i*v_row + (j-1)*v_pos.  Draft position 0 is draft0 + (d0_index ?
+ * d0_index[i] : i) * d0_stride; positions 1..k-1 are draft_rest + i*dr_row +
+ * (j-1)*dr_pos (draft logits are unused when T <= 0).  drafts[i*k + j] are
+ * the drafted ids, u[i*u_stride + k + j] the accept uniforms and u[i*u_stride
+ * + 2k] the residual / bonus uniform.  Writes tokens[i*(k+1) + 0..n] (the
+ * accepted drafts then the corrected / bonus token), n_accepted[i] and
+ * final_token[i] (= tokens[i*(k+1) + n_accepted[i]]). */
+int pse_spec_accept(const float *target0, int64_t t0_stride, const int32_t *t0_index,
+                    const float *verify, int64_t v_row, int64_t v_pos,
+                    const float *draft0, int64_t d0_stride, const int32_t *d0_index,
+                    const float *draft_rest, int64_t dr_row, int64_t dr_pos,
+                    const int32_t *drafts, const double *u, int64_t u_stride, int32_t rows,
+                    int32_t k, int32_t vocab, float temperature, int32_t *tokens,
+                    int32_t *n_accepted, int32_t *final_token, void *stream);
+
+/* ------------------------------------------------------------------------ */
+/* Model pieces (TinyGPT engine/model.py:121-206; Llama-style variant)       */
+/* ------------------------------------------------------------------------ */
+
+/* x[i*width + w, :] = tok_emb[ids[i*width + w]] + pos_emb[base_len[i] + w]
+ * (engine/model.py:174-181); pos_emb may be NULL (rotary models).  x is fp32,
+ * the tables have `emb_dtype`, `vocab` rows of tok_emb and `n_pos` rows of
+ * pos_emb (out-of-range ids / positions contribute zeros). */
+int pse_embed(const int32_t *ids, const int32_t *base_len, int32_t rows, int32_t width,
+              const void *tok_emb, const void *pos_emb, int32_t d, int32_t emb_dtype, int32_t vocab,
+              int32_t n_pos, float *x, void *stream);
+
+/* LayerNorm (engine/model.py:124-126, eps 1e-5, biased variance) or RMSNorm
+ * (rms != 0, beta ignored) of fp32 rows into out (out_dtype). */
+int pse_norm(const float *x, int64_t ldx, const void *gamma, const void *beta, int32_t param_dtype,
+             int32_t n_rows, int32_t d, float eps, int32_t rms, void *out, int64_t ldo,
+             int32_t out_dtype, void *stream);
+
+/* Elementwise epilogues on [n_rows, n] row-major data:
+ * op 0: y = gelu(y + bias)            (engine/model.py:127-129, exact erf GELU)
+ * op 1: x(fp32) += y + bias           (residual add, engine/model.py:140-141)
+ * op 2: y2[:, :n] = silu(y[:, :n]) * y[:, n:2n]   (SwiGLU)
+ * bias may be NULL. y has `dtype`. */
+int pse_epilogue(int32_t op, void *y, int64_t ldy, const void *bias, float *x, int64_t ldx, void *y2,
+                 int64_t ldy2, int32_t n_rows, int32_t n, int32_t dtype, void *stream);
+
+/* Rotate-half RoPE in place on the q and k heads of a fused qkv buffer
+ * (q heads at column 0, k heads after them), position base_len[i] + w. */
+int pse_rope(void *qkv, int64_t ld, int32_t rows, int32_t width, int32_t q_heads, int32_t kv_heads,
+             int32_t head_dim, const int32_t *base_len, float theta, int32_t dtype, void *stream);
+
+/* Scatter rows: dst[index[i] * ld_dst + :n] = src[i * ld_src + :n] (fp32),
+ * for index[i] in [0, n_dst_rows). */
+int pse_scatter_rows(const float *src, int64_t ld_src, const int32_t *index, int32_t rows, int32_t n,
+                     float *dst, int64_t ld_dst, int32_t n_dst_rows, void *stream);
+
+/* Number of kernels the library registers (load check) and a version tag. */
+int pse_version(void);
+int pse_warmup(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PSE_H_ */

@@ -1,0 +1,207 @@
+// Per-token model pieces around the projections: embedding, LayerNorm /
+// RMSNorm, bias + GELU / residual / SwiGLU epilogues, RoPE and a row scatter.
+// TinyGPT semantics follow engine/model.py:121-206.
+
+#include "common.cuh"
+
+namespace pse {
+namespace {
+
+// x[t] = tok_emb[ids[t]] + pos_emb[base_len[t / width] + t % width]
+// Ids outside [0, vocab) and positions outside [0, n_pos) read nothing (the
+// host rejects them before launch; the device only stays in bounds).
+__global__ void embed_kernel(const int32_t* ids, const int32_t* base_len, int width, const void* tok_emb,
+                             const void* pos_emb, int d, int dtype, float* x, int vocab, int n_pos) {
+  const int t = blockIdx.x;
+  const int i = t / width, w = t % width;
+  const int64_t tok = ids[t];
+  const int64_t pos = base_len ? (int64_t)base_len[i] + w : 0;
+  const bool tok_ok = tok >= 0 && tok < vocab;
+  const bool pos_ok = pos_emb != nullptr && pos >= 0 && pos < n_pos;
+  for (int c = threadIdx.x; c < d; c += blockDim.x) {
+    float v = tok_ok ? load_as_f32(tok_emb, tok * d + c, dtype) : 0.f;
+    if (pos_ok) v += load_as_f32(pos_emb, pos * d + c, dtype);
+    x[(int64_t)t * d + c] = v;
+  }
+}
+
+template <int THREADS>
+__device__ __forceinline__ float block_sum_f(float v, float* sh) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  v = warp_sum(v);
+  if (lane == 0) sh[warp] = v;
+  __syncthreads();
+  float t = 0.f;
+#pragma unroll
+  for (int w = 0; w < THREADS / 32; ++w) t += sh[w];
+  __syncthreads();
+  return t;
+}
+
+template <int THREADS>
+__global__ void __launch_bounds__(THREADS) norm_kernel(const float* x, int64_t ldx, const void* gamma,
+                                                       const void* beta, int pdtype, int d, float eps, int rms,
+                                                       void* out, int64_t ldo, int odtype) {
+  __shared__ float sh[THREADS / 32];
+  const float* row = x + (int64_t)blockIdx.x * ldx;
+  float mean = 0.f;
+  if (!rms) {
+    float s = 0.f;
+    for (int c = threadIdx.x; c < d; c += THREADS) s += row[c];
+    mean = block_sum_f<THREADS>(s, sh) / d;
+  }
+  float s2 = 0.f;
+  for (int c = threadIdx.x; c < d; c += THREADS) {
+    const float z = row[c] - mean;
+    s2 += z * z;
+  }
+  const float var = block_sum_f<THREADS>(s2, sh) / d;
+  const float inv = rsqrtf(var + eps);
+  for (int c = threadIdx.x; c < d; c += THREADS) {
+    float y = (row[c] - mean) * inv * load_as_f32(gamma, c, pdtype);
+    if (!rms && beta) y += load_as_f32(beta, c, pdtype);
+    store_from_f32(out, (int64_t)blockIdx.x * ldo + c, y, odtype);
+  }
+}
+
+__device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.f + erff(x * 0.70710678118654752440f)); }
+
+__device__ __forceinline__ float silu(float x) { return x / (1.f + expf(-x)); }
+
+__global__ void epilogue_kernel(int op, void* y, int64_t ldy, const void* bias, float* x, int64_t ldx, void* y2,
+                                int64_t ldy2, int n_rows, int n, int dtype) {
+  const int64_t total = (int64_t)n_rows * n;
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = e / n;
+    const int c = (int)(e % n);
+    if (op == 0) {
+      float v = load_as_f32(y, r * ldy + c, dtype);
+      if (bias) v += load_as_f32(bias, c, dtype);
+      store_from_f32(y, r * ldy + c, gelu_erf(v), dtype);
+    } else if (op == 1) {
+      float v = load_as_f32(y, r * ldy + c, dtype);
+      if (bias) v += load_as_f32(bias, c, dtype);
+      x[r * ldx + c] += v;
+    } else {
+      const float g = load_as_f32(y, r * ldy + c, dtype);
+      const float u = load_as_f32(y, r * ldy + n + c, dtype);
+      store_from_f32(y2, r * ldy2 + c, silu(g) * u, dtype);
+    }
+  }
+}
+
+// Rotate-half RoPE on the q heads and k heads of a fused qkv row.
+__global__ void rope_kernel(void* qkv, int64_t ld, int width, int q_heads, int kv_heads, int hd,
+                            const int32_t* base_len, float theta, int dtype, int64_t total) {
+  const int half = hd / 2;
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+    const int p = (int)(e % half);
+    int64_t r = e / half;
+    const int h = (int)(r % (q_heads + kv_heads));
+    const int64_t t = r / (q_heads + kv_heads);
+    const int64_t pos = (int64_t)base_len[t / width] + t % width;
+    const double inv_freq = pow((double)theta, -2.0 * p / hd);
+    double sn, cs;
+    sincos((double)pos * inv_freq, &sn, &cs);
+    const float c = (float)cs, s = (float)sn;
+    const int64_t off = t * ld + (int64_t)h * hd;
+    const float x1 = load_as_f32(qkv, off + p, dtype), x2 = load_as_f32(qkv, off + p + half, dtype);
+    store_from_f32(qkv, off + p, x1 * c - x2 * s, dtype);
+    store_from_f32(qkv, off + p + half, x2 * c + x1 * s, dtype);
+  }
+}
+
+__global__ void scatter_rows_kernel(const float* src, int64_t ld_src, const int32_t* index, int rows, int n,
+                                    float* dst, int64_t ld_dst, int n_dst_rows) {
+  const int64_t total = (int64_t)rows * n;
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t i = e / n;
+    const int c = (int)(e % n);
+    const int r = index[i];
+    if (r >= 0 && r < n_dst_rows) dst[(int64_t)r * ld_dst + c] = src[i * ld_src + c];
+  }
+}
+
+inline int grid_for(int64_t work, int threads) {
+  int64_t g = (work + threads - 1) / threads;
+  if (g > (int64_t)kNumSMs * 32) g = (int64_t)kNumSMs * 32;
+  return g < 1 ? 1 : (int)g;
+}
+
+}  // namespace
+}  // namespace pse
+
+using namespace pse;
+
+extern "C" int pse_embed(const int32_t* ids, const int32_t* base_len, int32_t rows, int32_t width,
+                         const void* tok_emb, const void* pos_emb, int32_t d, int32_t emb_dtype, int32_t vocab,
+                         int32_t n_pos, float* x, void* stream) {
+  if (rows < 0 || width < 0 || d <= 0 || vocab <= 0) return PSE_EINVAL;
+  if (rows == 0 || width == 0) return PSE_OK;
+  if (!ids || !tok_emb || !x || (pos_emb && !base_len)) return PSE_EINVAL;
+  embed_kernel<<<rows * width, 128, 0, (cudaStream_t)stream>>>(ids, base_len, width, tok_emb, pos_emb, d, emb_dtype, x,
+                                                               vocab, n_pos);
+  PSE_LAUNCH_CHECK();
+  return PSE_OK;
+}
+
+extern "C" int pse_norm(const float* x, int64_t ldx, const void* gamma, const void* beta, int32_t param_dtype,
+                        int32_t n_rows, int32_t d, float eps, int32_t rms, void* out, int64_t ldo, int32_t out_dtype,
+                        void* stream) {
+  if (n_rows < 0 || d <= 0) return PSE_EINVAL;
+  if (n_rows == 0) return PSE_OK;
+  if (!x || !gamma || !out) return PSE_EINVAL;
+  if (d <= 256)
+    norm_kernel<64><<<n_rows, 64, 0, (cudaStream_t)stream>>>(x, ldx, gamma, beta, param_dtype, d, eps, rms, out, ldo,
+                                                              out_dtype);
+  else
+    norm_kernel<256><<<n_rows, 256, 0, (cudaStream_t)stream>>>(x, ldx, gamma, beta, param_dtype, d, eps, rms, out,
+                                                                ldo, out_dtype);
+  PSE_LAUNCH_CHECK();
+  return PSE_OK;
+}
+
+extern "C" int pse_epilogue(int32_t op, void* y, int64_t ldy, const void* bias, float* x, int64_t ldx, void* y2,
+                            int64_t ldy2, int32_t n_rows, int32_t n, int32_t dtype, void* stream) {
+  if (n_rows < 0 || n < 0 || op < 0 || op > 2) return PSE_EINVAL;
+  if (n_rows == 0 || n == 0) return PSE_OK;
+  if (!y || (op == 1 && !x) || (op == 2 && !y2)) return PSE_EINVAL;
+  epilogue_kernel<<<grid_for((int64_t)n_rows * n, 256), 256, 0, (cudaStream_t)stream>>>(op, y, ldy, bias, x, ldx, y2,
+                                                                                         ldy2, n_rows, n, dtype);
+  PSE_LAUNCH_CHECK();
+  return PSE_OK;
+}
+
+extern "C" int pse_rope(void* qkv, int64_t ld, int32_t rows, int32_t width, int32_t q_heads, int32_t kv_heads,
+                        int32_t head_dim, const int32_t* base_len, float theta, int32_t dtype, void* stream) {
+  if (rows < 0 || width < 0 || head_dim <= 0 || head_dim % 2) return PSE_EINVAL;
+  if (rows == 0 || width == 0) return PSE_OK;
+  if (!qkv || !base_len) return PSE_EINVAL;
+  const int64_t total = (int64_t)rows * width * (q_heads + kv_heads) * (head_dim / 2);
+  rope_kernel<<<grid_for(total, 256), 256, 0, (cudaStream_t)stream>>>(qkv, ld, width, q_heads, kv_heads, head_dim,
+                                                                      base_len, theta, dtype, total);
+  PSE_LAUNCH_CHECK();
+  return PSE_OK;
+}
+
+extern "C" int pse_scatter_rows(const float* src, int64_t ld_src, const int32_t* index, int32_t rows, int32_t n,
+                                float* dst, int64_t ld_dst, int32_t n_dst_rows, void* stream) {
+  if (rows < 0 || n < 0) return PSE_EINVAL;
+  if (rows == 0 || n == 0) return PSE_OK;
+  if (!src || !index || !dst) return PSE_EINVAL;
+  scatter_rows_kernel<<<grid_for((int64_t)rows * n, 256), 256, 0, (cudaStream_t)stream>>>(src, ld_src, index, rows, n,
+                                                                                          dst, ld_dst, n_dst_rows);
+  PSE_LAUNCH_CHECK();
+  return PSE_OK;
+}
+
+extern "C" int pse_version(void) { return 1; }
+
+extern "C" int pse_warmup(void) {
+  // Force the module's kernels to load now (lazy loading would otherwise do
+  // it at the first launch, which may sit inside a stream capture).
+  cudaFuncAttributes attr;
+  cudaError_t e = cudaFuncGetAttributes(&attr, embed_kernel);
+  if (e != cudaSuccess) return (int)e;
+  return PSE_OK;
+}

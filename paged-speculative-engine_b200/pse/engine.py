@@ -1,0 +1,162 @@
+"""The paged forward and the device-resident speculative step.
+
+One forward of width W over B rows (engine/batched_forward.py:27-72 and
+engine/model.py:158-206, re-planned for the device):
+
+    reserve blocks for W tokens per row (pse_kv_reserve, rows in call order)
+    x = tok_emb[ids] + pos_emb[len + w]                       (pse_embed)
+    per layer:
+        h = norm1(x)                                          (pse_norm)
+        qkv = h Wqkv^T + b                                    (GEMM)
+        [rope on q, k]                                        (pse_rope, Llama layout)
+        K, V -> their blocks                                  (pse_kv_append)
+        a = paged attention of q over the row's blocks        (pse_paged_attention)
+        x += a Wo^T + bo                                      (GEMM + pse_epilogue)
+        h = norm2(x); u = act(h W1^T + b1); x += u W2^T + b2  (GEMM + pse_epilogue)
+    logits = norm_f(x) Wlm^T                                  (GEMM, fp32 out)
+
+The residual stream is fp32; GEMM operands, K/V and attention run in the
+cache dtype (fp32 or bf16).  No step synchronises the host.
+
+The speculative step (engine/speculative.py:77-177) runs k width-1 draft
+forwards with a sampling kernel between them, one width-k verify forward,
+the fused accept kernel, the batched truncate of both caches and the two
+width-1 bonus forwards -- all on the device, optionally replayed from a CUDA
+graph -- and returns with one device->host copy of the accepted tokens.
+"""
+from __future__ import annotations
+
+import math
+import weakref
+
+import torch
+
+from . import _native as N
+from .device_model import DeviceModel
+
+
+class Scratch:
+    """Activation buffers of one model, grown on demand (never inside a capture)."""
+
+    def __init__(self, dm: DeviceModel):
+        self.dm = dm
+        self.cap = 0
+        self.generation = 0  # bumped on every reallocation (captured graphs hold the old pointers)
+        self.ws = torch.empty(0, dtype=torch.uint8, device=dm.device)
+        self.base_len = torch.empty(0, dtype=torch.int32, device=dm.device)
+
+    def ensure(self, tokens: int) -> None:
+        if tokens <= self.cap:
+            return
+        cap = max(tokens, 2 * self.cap, 16)
+        dm, dev, dt = self.dm, self.dm.device, self.dm.dtype
+        self.x = torch.empty(cap, dm.d_model, dtype=torch.float32, device=dev)
+        self.h = torch.empty(cap, dm.d_model, dtype=dt, device=dev)
+        self.qkv = torch.empty(cap, dm.qkv_width, dtype=dt, device=dev)
+        self.attn = torch.empty(cap, dm.q_heads * dm.head_dim, dtype=dt, device=dev)
+        self.tmp = torch.empty(cap, dm.d_model, dtype=dt, device=dev)
+        up = 2 * dm.d_ff if dm.kind == "llama" else dm.d_ff
+        self.up = torch.empty(cap, up, dtype=dt, device=dev)
+        self.act = torch.empty(cap, dm.d_ff, dtype=dt, device=dev) if dm.kind == "llama" else self.up
+        self.cap = cap
+        self.generation += 1
+
+    def ensure_ws(self, nbytes: int) -> None:
+        if nbytes > self.ws.numel():
+            self.ws = torch.empty(max(nbytes, 2 * self.ws.numel()), dtype=torch.uint8, device=self.dm.device)
+            self.generation += 1
+
+
+_scratch: "weakref.WeakKeyDictionary[DeviceModel, Scratch]" = weakref.WeakKeyDictionary()
+
+
+def scratch_for(dm: DeviceModel) -> Scratch:
+    s = _scratch.get(dm)
+    if s is None:
+        s = Scratch(dm)
+        _scratch[dm] = s
+    return s
+
+
+def _mm(a: torch.Tensor, w: torch.Tensor, out: torch.Tensor, bias: torch.Tensor | None = None) -> None:
+    """out = a @ w^T (+ bias), cuBLAS via torch, no TF32."""
+    if bias is not None:
+        torch.addmm(bias, a, w.t(), out=out)
+    else:
+        torch.mm(a, w.t(), out=out)
+
+
+def lm_head(dm: DeviceModel, h: torch.Tensor, out: torch.Tensor) -> None:
+    """fp32 logits from the final normed hidden rows."""
+    if dm.dtype == torch.float32:
+        torch.mm(h, dm.lm_w.t(), out=out)
+    else:
+        out.copy_(torch.mm(h, dm.lm_w.t(), out_dtype=torch.float32))
+
+
+def forward(dm: DeviceModel, cache, slots: torch.Tensor, ids: torch.Tensor, rows: int, width: int,
+            base_len: torch.Tensor, max_ctx: int, logits_out: torch.Tensor | None, last_only: bool = False,
+            scratch: Scratch | None = None) -> None:
+    """One paged forward.  ``slots`` int32 [rows]; ``ids`` int32 [rows*width];
+    ``base_len`` int32 [rows] receives the rows' lengths before the call;
+    ``max_ctx`` >= every row's length after it.  ``logits_out`` fp32
+    [rows*width, V] (or [rows, V] with ``last_only``) or None."""
+    T = rows * width
+    sc = scratch or scratch_for(dm)
+    sc.ensure(T)
+    st = N.stream_ptr()
+    state = cache.state
+    dt = N.dtype_code(dm.dtype)
+    d, hd = dm.d_model, dm.head_dim
+    nq, nk = dm.q_heads * hd, dm.kv_heads * hd
+    N.call("pse_kv_reserve", state, slots.data_ptr(), rows, width, base_len.data_ptr(), st)
+    x, h, qkv, attn, tmp, up, act = (sc.x[:T], sc.h[:T], sc.qkv[:T], sc.attn[:T], sc.tmp[:T], sc.up[:T],
+                                      sc.act[:T])
+    N.call("pse_embed", ids.data_ptr(), base_len.data_ptr(), rows, width, dm.tok_emb.data_ptr(),
+           None if dm.pos_emb is None else dm.pos_emb.data_ptr(), d, dt, dm.vocab,
+           0 if dm.pos_emb is None else dm.pos_emb.shape[0], x.data_ptr(), st)
+    ws_bytes = N.size_call("pse_paged_attention_workspace", rows, width, dm.q_heads, dm.kv_heads, hd, max_ctx)
+    sc.ensure_ws(ws_bytes)
+    scale = 1.0 / math.sqrt(hd)
+    rms = 1 if dm.kind == "llama" else 0
+    for li, L in enumerate(dm.layers):
+        N.call("pse_norm", x.data_ptr(), d, L.norm1_w.data_ptr(), N.ptr(L.norm1_b), dt, T, d, dm.eps, rms,
+               h.data_ptr(), d, dt, st)
+        _mm(h, L.qkv_w, qkv, L.qkv_b)
+        if dm.kind == "llama":
+            N.call("pse_rope", qkv.data_ptr(), qkv.stride(0), rows, width, dm.q_heads, dm.kv_heads, hd,
+                   base_len.data_ptr(), dm.rope_theta, dt, st)
+        kvl = cache.layer(li)
+        N.call("pse_kv_append", state, kvl, qkv.data_ptr() + nq * qkv.element_size(),
+               qkv.data_ptr() + (nq + nk) * qkv.element_size(), qkv.stride(0), hd, slots.data_ptr(),
+               base_len.data_ptr(), rows, width, st)
+        N.call("pse_paged_attention", state, kvl, qkv.data_ptr(), qkv.stride(0), attn.data_ptr(), attn.stride(0),
+               slots.data_ptr(), base_len.data_ptr(), rows, width, dm.q_heads, scale, max_ctx,
+               sc.ws.data_ptr(), sc.ws.numel(), st)
+        _mm(attn, L.out_w, tmp)
+        N.call("pse_epilogue", 1, tmp.data_ptr(), d, N.ptr(L.out_b), x.data_ptr(), d, None, 0, T, d, dt, st)
+        N.call("pse_norm", x.data_ptr(), d, L.norm2_w.data_ptr(), N.ptr(L.norm2_b), dt, T, d, dm.eps, rms,
+               h.data_ptr(), d, dt, st)
+        _mm(h, L.up_w, up)
+        if dm.kind == "llama":
+            N.call("pse_epilogue", 2, up.data_ptr(), up.stride(0), None, None, 0, act.data_ptr(), act.stride(0),
+                   T, dm.d_ff, dt, st)
+        else:
+            N.call("pse_epilogue", 0, up.data_ptr(), up.stride(0), N.ptr(L.up_b), None, 0, None, 0, T, dm.d_ff,
+                   dt, st)
+        _mm(act, L.down_w, tmp)
+        N.call("pse_epilogue", 1, tmp.data_ptr(), d, N.ptr(L.down_b), x.data_ptr(), d, None, 0, T, d, dt, st)
+    if logits_out is None:
+        return
+    if last_only:
+        xs = x.view(rows, width, d)[:, width - 1]
+        n_out = rows
+        ldx = width * d
+    else:
+        xs = x
+        n_out = T
+        ldx = d
+    hf = h[:n_out]
+    N.call("pse_norm", xs.data_ptr(), ldx, dm.normf_w.data_ptr(), N.ptr(dm.normf_b), dt, n_out, d, dm.eps, rms,
+           hf.data_ptr(), d, dt, st)
+    lm_head(dm, hf, logits_out)

@@ -1,0 +1,321 @@
+"""Batched speculative step on the device, behind the reference's API
+(engine/speculative.py:35-177).
+
+Everything between the call and its single device->host copy runs on the
+GPU: k width-1 draft forwards with a sampling kernel between rounds
+(speculative.py:92-113), one width-k verify forward (:115-117), the fused
+accept / reject / residual / bonus kernel (:119-157), the batched truncate of
+both caches (:159-164) and the two width-1 bonus forwards (:166-177).  From the
+second step with a given batch size on, the whole program is replayed from a
+CUDA graph.
+
+Sampling at T > 0 uses explicit uniforms ([B, 2k+1] per step: u[j] draws draft
+j, u[k+j] tests position j, u[2k] is the residual / bonus draw), taken from
+``uniforms`` if given, else from ``generator`` (torch.rand on the host), else
+from the device Philox stream keyed by (seed, request id, request step).
+
+``draft_next_logits`` / ``target_next_logits`` in the result are views of
+per-request device buffers that the next step of the same request overwrites;
+passing them back unchanged (as the scheduler does) costs no copy.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import _native as N
+from .device_model import device_model
+from .engine import Scratch, forward
+
+DEFAULT_SEED = 0x5EED5EED
+USE_GRAPHS = True  # replay steps from CUDA graphs (from the second step of a batch size on)
+
+
+@dataclass
+class BatchStepResult:
+    """engine/speculative.py:35-40."""
+    accepted_tokens: dict
+    num_draft_accepted: dict
+    draft_next_logits: dict
+    target_next_logits: dict
+
+
+def _fnv1a(s: str) -> int:
+    h = 0x811C9DC5
+    for b in s.encode("utf-8"):
+        h = ((h ^ b) * 0x01000193) & 0xFFFFFFFF
+    return h
+
+
+def next_logits_buffer(cache, vocab: int) -> torch.Tensor:
+    """Per-slot fp32 [num_slots, vocab] buffer holding each request's next-token
+    logits (prefill and bonus outputs land here)."""
+    buf = getattr(cache, "_next_logits", None)
+    slots = cache.state.num_slots
+    if buf is None or buf.shape[0] < slots or buf.shape[1] != vocab:
+        new = torch.zeros(slots, vocab, dtype=torch.float32, device=cache.device)
+        if buf is not None and buf.shape[1] == vocab:
+            new[: buf.shape[0]] = buf
+        cache._next_logits = new
+    return cache._next_logits
+
+
+def _check_ids(ids, vocab: int) -> None:
+    if len(ids) and (min(ids) < 0 or max(ids) >= vocab):
+        raise IndexError(f"token id out of range for vocabulary of {vocab}")
+
+
+def _check_positions(dm, cache, request_ids, extra: int) -> int:
+    longest = max((cache.length(r) for r in request_ids), default=0) + extra
+    if dm.pos_emb is not None and longest > dm.max_seq_len:
+        raise IndexError(f"position {longest - 1} beyond max_seq_len {dm.max_seq_len}")
+    return longest
+
+
+@torch.no_grad()
+def prefill_request(draft_model, target_model, draft_cache, target_cache, request_id, prompt_ids):
+    """engine/speculative.py:53-73: seed both caches with the prompt and
+    return the two next-token logits rows (device views)."""
+    draft_cache.create_request(request_id)
+    target_cache.create_request(request_id)
+    prompt_ids = list(prompt_ids)
+    P = len(prompt_ids)
+    outs = []
+    for model, cache in ((draft_model, draft_cache), (target_model, target_cache)):
+        dm = device_model(model, cache.dtype, cache.device)
+        _check_ids(prompt_ids, dm.vocab)
+        _check_positions(dm, cache, [request_id], P)
+        cache.ensure_capacity([request_id], P)
+        buf = next_logits_buffer(cache, dm.vocab)
+        slot = cache.slot(request_id)
+        ids = torch.tensor(prompt_ids, dtype=torch.int32).to(cache.device, non_blocking=True)
+        slots = torch.tensor([slot], dtype=torch.int32).to(cache.device, non_blocking=True)
+        base = torch.empty(1, dtype=torch.int32, device=cache.device)
+        forward(dm, cache, slots, ids, 1, P, base, P, buf[slot:slot + 1], last_only=True)
+        cache.note_append([request_id], P)
+        outs.append(buf[slot])
+    draft_cache.check_status("prefill")
+    target_cache.check_status("prefill")
+    return outs[0], outs[1]
+
+
+class _StepBuffers:
+    def __init__(self, B: int, k: int, V: int, device):
+        i32 = dict(dtype=torch.int32, device=device)
+        self.B = B
+        self.slots_d = torch.empty(B, **i32)
+        self.slots_t = torch.empty(B, **i32)
+        self.base = torch.empty(k + 3, B, **i32)
+        self.round_ids = torch.empty(B, **i32)
+        self.drafts = torch.empty(B, k, **i32)
+        self.dlog = torch.empty(k, B, V, dtype=torch.float32, device=device)
+        self.vlog = torch.empty(B * k, V, dtype=torch.float32, device=device)
+        self.blog = torch.empty(B, V, dtype=torch.float32, device=device)
+        self.tokens = torch.empty(B, k + 1, **i32)
+        self.n_acc = torch.empty(B, **i32)
+        self.final = torch.empty(B, **i32)
+        self.u = torch.zeros(B, 2 * k + 1, dtype=torch.float64, device=device)
+        self.req_key = torch.empty(B, **i32)
+        self.steps = torch.empty(B, **i32)
+        n_pack = B * (k + 1) + B + 2
+        self.pack = torch.empty(n_pack, **i32)
+        self.host_pack = torch.empty(n_pack, dtype=torch.int32, pin_memory=True)
+        self.host_in = torch.empty(4 * B, dtype=torch.int32, pin_memory=True)
+
+
+class StepRunner:
+    """The device program of one speculative step for a (draft, target, caches, k)."""
+
+    def __init__(self, dm_d, dm_t, dcache, tcache, k: int):
+        if dm_d.vocab != dm_t.vocab:
+            raise ValueError("draft and target vocabularies differ")
+        self.dm_d, self.dm_t, self.dcache, self.tcache, self.k = dm_d, dm_t, dcache, tcache, k
+        self.V = dm_t.vocab
+        self.device = tcache.device
+        self.bufs: dict[int, _StepBuffers] = {}
+        self.graphs: dict = {}
+        self.warm: set = set()
+        self.request_steps: dict[str, int] = {}
+        self.seed = DEFAULT_SEED
+        self.use_graphs = USE_GRAPHS
+        self.sc_d = Scratch(dm_d)
+        self.sc_t = Scratch(dm_t)
+
+    # ---------------------------------------------------------------- device program
+    def _ctx_bound(self, cache, dm) -> int:
+        bound = cache.max_blocks * cache.block_size
+        if dm.pos_emb is not None:
+            bound = min(bound, dm.max_seq_len)
+        return bound
+
+    def _program(self, b: _StepBuffers, T: float, philox: bool, max_ctx_d: int, max_ctx_t: int) -> None:
+        k, V, B = self.k, self.V, b.B
+        st = N.stream_ptr()
+        dnext = next_logits_buffer(self.dcache, V)
+        tnext = next_logits_buffer(self.tcache, V)
+        nu = 2 * k + 1
+        if T > 0 and philox:
+            N.call("pse_philox_uniforms", self.seed, b.req_key.data_ptr(), b.steps.data_ptr(), B, nu,
+                   b.u.data_ptr(), st)
+        for j in range(k):
+            if j == 0:
+                src, idx = dnext, b.slots_d.data_ptr()
+            else:
+                src, idx = b.dlog[j - 1], None
+            N.call("pse_sample_tokens", src.data_ptr(), V, idx, B, V, float(T), b.u.data_ptr(), nu, j,
+                   b.drafts.data_ptr() + 4 * j, k, b.round_ids.data_ptr(), 1, st)
+            forward(self.dm_d, self.dcache, b.slots_d, b.round_ids, B, 1, b.base[j], max_ctx_d, b.dlog[j],
+                    scratch=self.sc_d)
+        forward(self.dm_t, self.tcache, b.slots_t, b.drafts.view(-1), B, k, b.base[k], max_ctx_t, b.vlog,
+                scratch=self.sc_t)
+        N.call("pse_spec_accept", tnext.data_ptr(), V, b.slots_t.data_ptr(), b.vlog.data_ptr(), k * V, V,
+               dnext.data_ptr(), V, b.slots_d.data_ptr(), b.dlog.data_ptr(), V, B * V,
+               b.drafts.data_ptr(), b.u.data_ptr(), nu, B, k, V, float(T), b.tokens.data_ptr(),
+               b.n_acc.data_ptr(), b.final.data_ptr(), st)
+        N.call("pse_kv_truncate", self.dcache.state, b.slots_d.data_ptr(), B, None, b.base[0].data_ptr(),
+               b.n_acc.data_ptr(), st)
+        N.call("pse_kv_truncate", self.tcache.state, b.slots_t.data_ptr(), B, None, b.base[k].data_ptr(),
+               b.n_acc.data_ptr(), st)
+        forward(self.dm_d, self.dcache, b.slots_d, b.final, B, 1, b.base[k + 1], max_ctx_d, b.blog,
+                scratch=self.sc_d)
+        N.call("pse_scatter_rows", b.blog.data_ptr(), V, b.slots_d.data_ptr(), B, V, dnext.data_ptr(), V,
+               dnext.shape[0], st)
+        forward(self.dm_t, self.tcache, b.slots_t, b.final, B, 1, b.base[k + 2], max_ctx_t, b.blog,
+                scratch=self.sc_t)
+        N.call("pse_scatter_rows", b.blog.data_ptr(), V, b.slots_t.data_ptr(), B, V, tnext.data_ptr(), V,
+               tnext.shape[0], st)
+        nt = B * (k + 1)
+        b.pack[:nt].copy_(b.tokens.view(-1))
+        b.pack[nt:nt + B].copy_(b.n_acc)
+        b.pack[nt + B:nt + B + 1].copy_(self.dcache.status_tensor())
+        b.pack[nt + B + 1:nt + B + 2].copy_(self.tcache.status_tensor())
+
+    # ---------------------------------------------------------------- host side
+    def step(self, request_ids, draft_next_logits, target_next_logits, temperature, generator=None,
+             uniforms=None, use_graph=None) -> BatchStepResult:
+        k, V = self.k, self.V
+        B = len(request_ids)
+        if B == 0:
+            return BatchStepResult({}, {}, {}, {})
+        if len(set(request_ids)) != B:
+            raise ValueError("request_ids must be unique")
+        dc, tc = self.dcache, self.tcache
+        _check_positions(self.dm_d, dc, request_ids, k + 1)
+        _check_positions(self.dm_t, tc, request_ids, k + 1)
+        dc.ensure_capacity(request_ids, k + 1)
+        tc.ensure_capacity(request_ids, k + 1)
+        b = self.bufs.get(B)
+        if b is None:
+            b = self.bufs[B] = _StepBuffers(B, k, V, self.device)
+        dnext = next_logits_buffer(dc, V)
+        tnext = next_logits_buffer(tc, V)
+        sd = [dc.slot(r) for r in request_ids]
+        stt = [tc.slot(r) for r in request_ids]
+        for r, s in zip(request_ids, sd):
+            t = draft_next_logits[r]
+            if t.data_ptr() != dnext[s].data_ptr():
+                dnext[s].copy_(t.reshape(-1), non_blocking=True)
+        for r, s in zip(request_ids, stt):
+            t = target_next_logits[r]
+            if t.data_ptr() != tnext[s].data_ptr():
+                tnext[s].copy_(t.reshape(-1), non_blocking=True)
+        T = float(temperature)
+        philox = False
+        hin = b.host_in
+        hin[:B] = torch.tensor(sd, dtype=torch.int32)
+        hin[B:2 * B] = torch.tensor(stt, dtype=torch.int32)
+        if T > 0:
+            if uniforms is not None:
+                u = torch.as_tensor(np.asarray(uniforms, dtype=np.float64) if not torch.is_tensor(uniforms)
+                                    else uniforms, dtype=torch.float64)
+                b.u.copy_(u.reshape(B, 2 * k + 1), non_blocking=True)
+            elif generator is not None:
+                b.u.copy_(torch.rand(B, 2 * k + 1, generator=generator, dtype=torch.float64), non_blocking=True)
+            else:
+                philox = True
+                keys = np.array([_fnv1a(r) for r in request_ids], dtype=np.uint32).view(np.int32)
+                hin[2 * B:3 * B] = torch.from_numpy(keys)
+                hin[3 * B:4 * B] = torch.tensor([self.request_steps.get(r, 0) for r in request_ids],
+                                                dtype=torch.int32)
+        b.slots_d.copy_(hin[:B], non_blocking=True)
+        b.slots_t.copy_(hin[B:2 * B], non_blocking=True)
+        if philox:
+            b.req_key.copy_(hin[2 * B:3 * B], non_blocking=True)
+            b.steps.copy_(hin[3 * B:4 * B], non_blocking=True)
+
+        graphs = self.use_graphs if use_graph is None else use_graph
+        mcd, mct = self._ctx_bound(dc, self.dm_d), self._ctx_bound(tc, self.dm_t)
+        if graphs:
+            # size every buffer the program touches before the graph key is taken
+            self.sc_d.ensure(B)
+            self.sc_t.ensure(B * k)
+            dmd, dmt = self.dm_d, self.dm_t
+            self.sc_d.ensure_ws(N.size_call("pse_paged_attention_workspace", B, 1, dmd.q_heads, dmd.kv_heads,
+                                            dmd.head_dim, mcd))
+            self.sc_t.ensure_ws(max(
+                N.size_call("pse_paged_attention_workspace", B, k, dmt.q_heads, dmt.kv_heads, dmt.head_dim, mct),
+                N.size_call("pse_paged_attention_workspace", B, 1, dmt.q_heads, dmt.kv_heads, dmt.head_dim, mct)))
+        key = (B, T, philox, dc.generation, tc.generation, self.sc_d.generation, self.sc_t.generation)
+        if graphs and key in self.graphs:
+            self.graphs[key].replay()
+        elif graphs and key in self.warm:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                self._program(b, T, philox, mcd, mct)
+            self.graphs[key] = g
+            g.replay()
+        else:
+            if graphs:
+                # eager steps use the same context bound so the captured
+                # program's buffers (split-KV workspace) are already sized
+                self._program(b, T, philox, mcd, mct)
+                self.warm.add(key)
+            else:
+                ld = max(dc.length(r) for r in request_ids) + k + 1
+                lt = max(tc.length(r) for r in request_ids) + k + 1
+                self._program(b, T, philox, ld, lt)
+        hp = b.host_pack
+        hp.copy_(b.pack, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        nt = B * (k + 1)
+        status_d, status_t = int(hp[nt + B]), int(hp[nt + B + 1])
+        if status_d or status_t:
+            for c, s in ((dc, status_d), (tc, status_t)):
+                if s:
+                    c.check_status("speculative step")
+        toks = hp[:nt].view(B, k + 1).tolist()
+        nacc = hp[nt:nt + B].tolist()
+        accepted, n_acc, dn, tn = {}, {}, {}, {}
+        for i, r in enumerate(request_ids):
+            n = nacc[i]
+            accepted[r] = toks[i][: n + 1]
+            n_acc[r] = n
+            dn[r] = dnext[sd[i]]
+            tn[r] = tnext[stt[i]]
+            self.request_steps[r] = self.request_steps.get(r, 0) + 1
+        dc.note_lengths(request_ids, [dc.length(r) + n_acc[r] + 1 for r in request_ids])
+        tc.note_lengths(request_ids, [tc.length(r) + n_acc[r] + 1 for r in request_ids])
+        return BatchStepResult(accepted, n_acc, dn, tn)
+
+
+def runner_for(draft_model, target_model, draft_cache, target_cache, k: int) -> StepRunner:
+    dm_d = device_model(draft_model, draft_cache.dtype, draft_cache.device)
+    dm_t = device_model(target_model, target_cache.dtype, target_cache.device)
+    runners = target_cache.__dict__.setdefault("_runners", {})
+    key = (id(draft_cache), id(dm_d), id(dm_t), k)
+    r = runners.get(key)
+    if r is None or r.dm_d is not dm_d or r.dm_t is not dm_t or r.dcache is not draft_cache:
+        r = runners[key] = StepRunner(dm_d, dm_t, draft_cache, target_cache, k)
+    return r
+
+
+@torch.no_grad()
+def batched_speculative_step(draft_model, target_model, request_ids, draft_cache, target_cache,
+                             draft_next_logits, target_next_logits, k, temperature, generator=None, *,
+                             uniforms=None, use_graph=None) -> BatchStepResult:
+    """engine/speculative.py:76-177 on the device."""
+    runner = runner_for(draft_model, target_model, draft_cache, target_cache, k)
+    return runner.step(list(request_ids), draft_next_logits, target_next_logits, temperature, generator,
+                       uniforms, use_graph)

@@ -1,0 +1,324 @@
+"""Kernel parity against the CPU oracle through the C ABI (libpse.so).
+
+Integer work (free list, block tables, Philox, token choices) must match bit
+for bit; floating-point outputs within the north-star tolerances (1e-4 abs in
+fp32, 2e-2 abs in bf16).  GPU only."""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import alloc as OA
+from oracle.accept import accept_row
+from oracle.attention import paged_attention as oracle_attention
+from oracle.philox import request_key, step_uniforms
+from oracle.sampling import inverse_cdf, sample_with_uniform, weights
+
+pytestmark = pytest.mark.gpu
+
+F32_TOL = 1e-4
+BF16_TOL = 2e-2
+
+
+def _N():
+    from pse import _native as N
+    N.load()
+    return N
+
+
+def _cache(**kw):
+    from pse import PagedKVCache
+    return PagedKVCache(**kw)
+
+
+# ---------------------------------------------------------------- free list / tables
+def _device_snapshot(cache):
+    b = cache._blocks
+    top = int(b.free_top.item())
+    return (b.block_table.cpu().numpy(), b.nblocks.cpu().numpy(), b.seq_len.cpu().numpy(),
+            b.free_stack[:top].cpu().numpy(), int(b.status.item()))
+
+
+@pytest.mark.parametrize("seed", range(6))
+def test_batched_reserve_truncate_release_bit_exact(seed):
+    N = _N()
+    rng = np.random.default_rng(seed)
+    nb, bs, slots_n, width = int(rng.integers(8, 200)), int(rng.integers(1, 17)), 12, 64
+    c = _cache(n_layers=1, n_heads=1, head_dim=2, block_size=bs, num_blocks=nb, max_requests=slots_n,
+               max_blocks_per_request=width)
+    ref = OA.BlockState(nb, bs, slots_n, width)
+    live: list[int] = []
+    st = N.stream_ptr()
+    for _ in range(60):
+        op = rng.choice(["reserve", "truncate", "release"], p=[0.5, 0.35, 0.15])
+        if op == "reserve" or not live:
+            free = [s for s in range(slots_n) if s not in live]
+            pick = list(rng.choice(free, size=min(len(free), int(rng.integers(1, 5))), replace=False)) if free else []
+            rows = [int(x) for x in pick] + ([int(x) for x in rng.choice(live, size=min(len(live), 3),
+                                                                         replace=False)] if live else [])
+            rng.shuffle(rows)
+            w = int(rng.integers(1, 12))
+            if any((ref.seq_len[s] + w + bs - 1) // bs > width for s in rows):
+                continue
+            ref.status = 0
+            base_ref = ref.reserve(rows, w)
+            slots = torch.tensor(rows, dtype=torch.int32, device="cuda")
+            base = torch.empty(len(rows), dtype=torch.int32, device="cuda")
+            N.call("pse_kv_reserve", c.state, slots.data_ptr(), len(rows), w, base.data_ptr(), st)
+            assert base.cpu().tolist() == base_ref.tolist()
+            for s in rows:
+                if s not in live:
+                    live.append(s)
+        elif op == "truncate":
+            rows = [int(x) for x in rng.choice(live, size=min(len(live), int(rng.integers(1, 5))), replace=False)]
+            new = [int(rng.integers(0, ref.seq_len[s] + 1)) for s in rows]
+            ref.truncate(rows, new)
+            slots = torch.tensor(rows, dtype=torch.int32, device="cuda")
+            nl = torch.tensor(new, dtype=torch.int32, device="cuda")
+            N.call("pse_kv_truncate", c.state, slots.data_ptr(), len(rows), nl.data_ptr(), None, None, st)
+        else:
+            rows = [int(x) for x in rng.choice(live, size=min(len(live), 2), replace=False)]
+            ref.release(rows)
+            slots = torch.tensor(rows, dtype=torch.int32, device="cuda")
+            N.call("pse_kv_release", c.state, slots.data_ptr(), len(rows), st)
+            live = [s for s in live if s not in rows]
+        table, nbk, lens, stack, status = _device_snapshot(c)
+        assert status == ref.status
+        if status:
+            c._blocks.status.zero_()
+            ref.status = 0
+        assert stack.tolist() == ref.free_list()
+        assert nbk.tolist() == ref.nblocks.tolist()
+        assert lens.tolist() == ref.seq_len.tolist()
+        for s in range(slots_n):
+            assert table[s, : nbk[s]].tolist() == ref.row_table(s)
+
+
+def test_truncate_from_step_form_and_error_latch():
+    N = _N()
+    c = _cache(n_layers=1, n_heads=1, head_dim=2, block_size=4, num_blocks=16, max_requests=4)
+    st = N.stream_ptr()
+    slots = torch.tensor([0, 1, 2], dtype=torch.int32, device="cuda")
+    base = torch.empty(3, dtype=torch.int32, device="cuda")
+    N.call("pse_kv_reserve", c.state, slots.data_ptr(), 3, 9, base.data_ptr(), st)
+    acc = torch.tensor([0, 5, 9], dtype=torch.int32, device="cuda")
+    base0 = torch.zeros(3, dtype=torch.int32, device="cuda")
+    N.call("pse_kv_truncate", c.state, slots.data_ptr(), 3, None, base0.data_ptr(), acc.data_ptr(), st)
+    assert c._blocks.seq_len[:3].tolist() == [0, 5, 9]
+    assert c._blocks.nblocks[:3].tolist() == [0, 2, 3]
+    # truncate beyond length latches the error; later mutations are no-ops until cleared
+    bad = torch.tensor([7], dtype=torch.int32, device="cuda")
+    N.call("pse_kv_truncate", c.state, slots[1:2].data_ptr(), 1, bad.data_ptr(), None, None, st)
+    assert int(c._blocks.status.item()) & N.STATUS_TRUNCATE_LONG
+    before = c._blocks.free_top.item()
+    N.call("pse_kv_release", c.state, slots.data_ptr(), 3, st)
+    assert c._blocks.free_top.item() == before
+    c._blocks.status.zero_()
+
+
+def test_reserve_exhaustion_matches_reference_partial_state():
+    N = _N()
+    c = _cache(n_layers=1, n_heads=1, head_dim=2, block_size=2, num_blocks=5, max_requests=4,
+               max_blocks_per_request=8)
+    ref = OA.BlockState(5, 2, 4, 8)
+    st = N.stream_ptr()
+    rows = [2, 0, 3]
+    base = torch.empty(3, dtype=torch.int32, device="cuda")
+    slots = torch.tensor(rows, dtype=torch.int32, device="cuda")
+    N.call("pse_kv_reserve", c.state, slots.data_ptr(), 3, 4, base.data_ptr(), st)
+    ref.reserve(rows, 4)
+    table, nbk, lens, stack, status = _device_snapshot(c)
+    assert status == ref.status == OA.OOM
+    assert nbk.tolist() == ref.nblocks.tolist() and lens.tolist() == ref.seq_len.tolist()
+    assert stack.tolist() == ref.free_list()
+    c._blocks.status.zero_()
+
+
+# ---------------------------------------------------------------- append / gather
+def test_append_then_gather_roundtrip_bf16_and_f32():
+    for dtype in (torch.float32, torch.bfloat16):
+        c = _cache(n_layers=2, n_heads=3, head_dim=64, block_size=16, num_blocks=64, dtype=dtype)
+        rng = torch.Generator().manual_seed(3)
+        truth = {}
+        for r, n in (("a", 5), ("b", 40), ("a", 17), ("c", 1), ("b", 3)):
+            if r not in truth:
+                c.create_request(r)
+                truth[r] = [[], []]
+            k = [torch.randn(3, n, 64, generator=rng).to(dtype) for _ in range(2)]
+            v = [torch.randn(3, n, 64, generator=rng).to(dtype) for _ in range(2)]
+            c.append(r, k, v)
+            truth[r][0].append(k)
+            truth[r][1].append(v)
+        ko, vo, mask, lens = c.gather(["a", "b", "c"])
+        for i, r in enumerate(["a", "b", "c"]):
+            for layer in range(2):
+                kk = torch.cat([t[layer] for t in truth[r][0]], dim=1)
+                vv = torch.cat([t[layer] for t in truth[r][1]], dim=1)
+                n = kk.shape[1]
+                assert torch.equal(ko[layer][i, :, :n].cpu(), kk)
+                assert torch.equal(vo[layer][i, :, :n].cpu(), vv)
+                assert not ko[layer][i, :, n:].any()
+
+
+# ---------------------------------------------------------------- paged attention
+ATTN_CASES = [
+    # rows, width, q_heads, kv_heads, head_dim, block_size, max_len, dtype
+    (3, 1, 2, 2, 4, 4, 30, torch.float32),
+    (4, 3, 2, 2, 6, 3, 25, torch.float32),
+    (5, 5, 4, 4, 32, 16, 200, torch.float32),
+    (2, 9, 2, 2, 8, 1, 40, torch.float32),
+    (6, 1, 12, 12, 64, 16, 700, torch.bfloat16),
+    (6, 6, 12, 12, 64, 16, 700, torch.bfloat16),
+    (3, 8, 32, 8, 128, 16, 900, torch.bfloat16),
+    (2, 4, 32, 8, 64, 32, 3000, torch.bfloat16),   # long context: split-KV path
+    (1, 1, 4, 4, 128, 16, 9000, torch.float32),    # single row, many splits
+    (1, 37, 2, 2, 16, 4, 60, torch.float32),       # prefill-like width, several query tiles
+]
+
+
+@pytest.mark.parametrize("case", ATTN_CASES)
+def test_paged_attention_matches_oracle(case):
+    N = _N()
+    rows, width, hq, hk, hd, bs, max_len, dtype = case
+    rng = np.random.default_rng(ATTN_CASES.index(case))
+    base = rng.integers(0, max_len, size=rows)
+    need = [(int(b) + width + bs - 1) // bs for b in base]
+    nb = sum(need) + 5
+    c = _cache(n_layers=1, n_heads=hk, head_dim=hd, block_size=bs, num_blocks=nb, dtype=dtype,
+               max_requests=rows, max_blocks_per_request=max(need))
+    perm = rng.permutation(nb)
+    tables, o = [], 0
+    for i, n in enumerate(need):
+        tables.append(perm[o:o + n].tolist())
+        o += n
+        c._blocks.block_table[i, :n] = torch.tensor(tables[-1], dtype=torch.int32)
+        c._blocks.nblocks[i] = n
+        c._blocks.seq_len[i] = int(base[i]) + width
+    g = torch.Generator().manual_seed(7)
+    kp = torch.randn(nb, hk, bs, hd, generator=g)
+    vp = torch.randn(nb, hk, bs, hd, generator=g)
+    c.k_pool[0].copy_(kp.to(dtype))
+    c.v_pool[0].copy_(vp.to(dtype))
+    q = torch.randn(rows * width, hq * hd, generator=g).to(dtype)
+    qd = q.cuda()
+    out = torch.empty_like(qd)
+    slots = torch.arange(rows, dtype=torch.int32, device="cuda")
+    base_d = torch.tensor(base, dtype=torch.int32, device="cuda")
+    max_ctx = int(base.max()) + width
+    ws_bytes = N.size_call("pse_paged_attention_workspace", rows, width, hq, hk, hd, max_ctx)
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device="cuda")
+    N.call("pse_paged_attention", c.state, c.layer(0), qd.data_ptr(), hq * hd, out.data_ptr(), hq * hd,
+           slots.data_ptr(), base_d.data_ptr(), rows, width, hq, 1.0 / math.sqrt(hd), max_ctx,
+           ws.data_ptr(), ws.numel(), N.stream_ptr())
+    want = oracle_attention(q.float().view(rows, width, hq, hd).numpy(), kp.to(dtype).float().numpy(),
+                            vp.to(dtype).float().numpy(), tables, base)
+    got = out.float().cpu().view(rows, width, hq, hd).numpy()
+    tol = F32_TOL if dtype == torch.float32 else BF16_TOL
+    assert np.abs(got - want).max() < tol
+
+
+# ---------------------------------------------------------------- Philox, sampling, accept
+def test_philox_uniforms_bit_exact():
+    N = _N()
+    keys = [request_key(f"r{i}") for i in range(37)]
+    steps = list(range(5, 42))
+    want = step_uniforms(0xDEADBEEF12345, keys, steps, 11)
+    kd = torch.from_numpy(np.array(keys, dtype=np.uint32).view(np.int32)).cuda()
+    sd = torch.tensor(steps, dtype=torch.int32, device="cuda")
+    out = torch.empty(37, 11, dtype=torch.float64, device="cuda")
+    N.call("pse_philox_uniforms", 0xDEADBEEF12345, kd.data_ptr(), sd.data_ptr(), 37, 11, out.data_ptr(),
+           N.stream_ptr())
+    assert np.array_equal(out.cpu().numpy(), want)
+
+
+@pytest.mark.parametrize("vocab,temp", [(257, 0.0), (257, 1.0), (32000, 0.7), (128256, 1.0)])
+def test_sample_tokens_matches_oracle(vocab, temp):
+    N = _N()
+    rows = 48
+    g = torch.Generator().manual_seed(vocab)
+    logits = torch.randn(rows, vocab, generator=g) * 3
+    logits[0, 5] = logits[0, 9] = logits[0].max() + 1  # greedy tie -> lowest index
+    u = torch.rand(rows, 3, generator=g, dtype=torch.float64)
+    out = torch.empty(rows, dtype=torch.int32, device="cuda")
+    ld, ud = logits.cuda(), u.cuda()
+    N.call("pse_sample_tokens", ld.data_ptr(), vocab, None, rows, vocab, temp, ud.data_ptr(), 3, 1,
+           out.data_ptr(), 1, None, 0, N.stream_ptr())
+    got = out.cpu().tolist()
+    want = [sample_with_uniform(logits[i].numpy(), temp, float(u[i, 1])) for i in range(rows)]
+    assert got == want
+    if temp == 0:
+        assert got[0] == 5
+
+
+def _accept_inputs(rows, k, vocab, temp, seed, agree):
+    g = torch.Generator().manual_seed(seed)
+    tgt = torch.randn(rows, k + 1, vocab, generator=g) * 3
+    drf = tgt[:, :k] + torch.randn(rows, k, vocab, generator=g) * (3 * (1 - agree))
+    u = torch.rand(rows, 2 * k + 1, generator=g, dtype=torch.float64)
+    drafts = np.zeros((rows, k), dtype=np.int64)
+    for i in range(rows):
+        for j in range(k):
+            if temp > 0:
+                drafts[i, j] = sample_with_uniform(drf[i, j].numpy(), temp, float(u[i, j]))
+            else:
+                drafts[i, j] = int(torch.argmax(tgt[i, j])) if (i + j) % 3 else int(torch.argmax(drf[i, j]))
+    return tgt, drf, u, drafts
+
+
+def _run_accept(N, tgt, drf, u, drafts, temp):
+    rows, kp1, vocab = tgt.shape
+    k = kp1 - 1
+    t0 = tgt[:, 0].contiguous().cuda()
+    ver = tgt[:, 1:].contiguous().cuda()
+    d0 = drf[:, 0].contiguous().cuda()
+    dr = drf[:, 1:].transpose(0, 1).contiguous().cuda() if k > 1 else d0  # [k-1, rows, V]
+    dd = torch.from_numpy(drafts.astype(np.int32)).cuda()
+    ud = u.cuda()
+    toks = torch.empty(rows, k + 1, dtype=torch.int32, device="cuda")
+    nacc = torch.empty(rows, dtype=torch.int32, device="cuda")
+    fin = torch.empty(rows, dtype=torch.int32, device="cuda")
+    N.call("pse_spec_accept", t0.data_ptr(), vocab, None, ver.data_ptr(), k * vocab, vocab,
+           d0.data_ptr(), vocab, None, dr.data_ptr(), vocab, rows * vocab, dd.data_ptr(), ud.data_ptr(),
+           2 * k + 1, rows, k, vocab, temp, toks.data_ptr(), nacc.data_ptr(), fin.data_ptr(), N.stream_ptr())
+    return toks.cpu().numpy(), nacc.cpu().numpy(), fin.cpu().numpy()
+
+
+@pytest.mark.parametrize("k,vocab,temp,agree", [
+    (1, 64, 0.0, 0.0), (4, 256, 0.0, 0.0), (8, 1000, 0.0, 0.0),
+    (3, 64, 1.0, 0.9), (5, 1000, 1.0, 0.97), (8, 4096, 0.8, 0.99), (2, 32000, 1.0, 0.0),
+])
+def test_accept_resample_matches_oracle(k, vocab, temp, agree):
+    N = _N()
+    rows = 64
+    tgt, drf, u, drafts = _accept_inputs(rows, k, vocab, temp, seed=k * 1000 + vocab, agree=agree)
+    toks, nacc, fin = _run_accept(N, tgt, drf, u, drafts, temp)
+    seen = set()
+    for i in range(rows):
+        want, n = accept_row(tgt[i].numpy(), drf[i].numpy(), drafts[i], u[i].numpy(), k, temp)
+        assert nacc[i] == n, (i, nacc[i], n)
+        assert toks[i, : n + 1].tolist() == want and fin[i] == want[-1]
+        seen.add(n)
+    if temp > 0 and agree > 0.9:
+        assert len(seen) > 1  # both accept and reject paths exercised
+
+
+def test_accept_all_accepted_uses_bonus_position():
+    N = _N()
+    rows, k, vocab = 8, 3, 50
+    tgt, _, u, _ = _accept_inputs(rows, k, vocab, 0.0, seed=1, agree=0)
+    drafts = np.stack([[int(torch.argmax(tgt[i, j])) for j in range(k)] for i in range(rows)])
+    toks, nacc, fin = _run_accept(N, tgt, tgt[:, :k].clone(), u, drafts, 0.0)
+    assert (nacc == k).all()
+    for i in range(rows):
+        assert fin[i] == int(torch.argmax(tgt[i, k]))
+    # T = 1 with identical draft and target: ratio is 1, every draft accepted
+    drafts = np.stack([[sample_with_uniform(tgt[i, j].numpy(), 1.0, float(u[i, j])) for j in range(k)]
+                       for i in range(rows)])
+    toks, nacc, fin = _run_accept(N, tgt, tgt[:, :k].clone(), u, drafts, 1.0)
+    assert (nacc == k).all()
+    for i in range(rows):
+        w, z = weights(tgt[i, k].numpy(), 1.0)
+        assert fin[i] == inverse_cdf(w, float(z), float(u[i, 2 * k]))

@@ -1,0 +1,42 @@
+"""The C-ABI library builds for sm_100a, loads without a GPU, and exports
+every entry point include/pse.h declares.  No kernel is launched.  CPU only."""
+from __future__ import annotations
+
+import os
+import re
+import subprocess
+
+import pytest
+
+from conftest import ROOT
+
+
+def _declared():
+    with open(os.path.join(ROOT, "include", "pse.h")) as f:
+        text = f.read()
+    return sorted(set(re.findall(r"^(?:int|size_t)\s+(pse_\w+)\s*\(", text, flags=re.M)))
+
+
+def test_library_builds_and_exports_every_declared_symbol():
+    from pse import _build, _native
+    lib_path = _build.build()
+    assert os.path.exists(lib_path)
+    lib = _native.load(require_cuda=False)
+    declared = _declared()
+    assert len(declared) >= 20
+    for name in declared:
+        assert hasattr(lib, name), name
+    nm = subprocess.run(["nm", "-D", "--defined-only", lib_path], capture_output=True, text=True, check=True).stdout
+    exported = set(re.findall(r"\bT\s+(pse_\w+)", nm))
+    assert set(declared) <= exported
+    # the ctypes prototype table covers the header exactly
+    assert set(_native.exported_symbols()) == set(declared)
+
+
+def test_engine_refuses_to_run_without_cuda():
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    import pse
+    with pytest.raises(RuntimeError):
+        pse.PagedKVCache(1, 1, 2, 4, 8)
