@@ -29,7 +29,7 @@ class DeviceLayer:
     down_b: torch.Tensor | None
 
 
-@dataclass
+@dataclass(eq=False)
 class DeviceModel:
     kind: str                   # "gpt" | "llama"
     vocab: int

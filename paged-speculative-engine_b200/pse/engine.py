@@ -27,7 +27,6 @@ graph -- and returns with one device->host copy of the accepted tokens.
 from __future__ import annotations
 
 import math
-import weakref
 
 import torch
 
@@ -67,14 +66,11 @@ class Scratch:
             self.generation += 1
 
 
-_scratch: "weakref.WeakKeyDictionary[DeviceModel, Scratch]" = weakref.WeakKeyDictionary()
-
-
 def scratch_for(dm: DeviceModel) -> Scratch:
-    s = _scratch.get(dm)
+    """The shared scratch of a device model (prefill and plain forwards)."""
+    s = dm.__dict__.get("_scratch")
     if s is None:
-        s = Scratch(dm)
-        _scratch[dm] = s
+        s = dm.__dict__["_scratch"] = Scratch(dm)
     return s
 
 
