@@ -38,6 +38,7 @@ extern "C" {
 #define PSE_STATUS_TRUNCATE_LONG 4    /* truncate beyond length (ValueError) */
 #define PSE_STATUS_DOUBLE_FREE 8      /* block freed twice (ValueError) */
 #define PSE_STATUS_BAD_BLOCK 16       /* block id out of range */
+#define PSE_STATUS_TIMEOUT 32         /* a bounded in-kernel wait expired */
 
 /* ---- element types ---- */
 #define PSE_F32 0
@@ -137,6 +138,12 @@ int pse_paged_attention(pse_block_state st, pse_kv_layer kv, const void *q, int6
 
 size_t pse_paged_attention_workspace(int32_t rows, int32_t width, int32_t q_heads, int32_t kv_heads,
                                      int32_t head_dim, int32_t max_ctx);
+
+/* bf16 pools with head_dim 64/128 and block_size 16/32/64 run the TMA +
+ * tensor-core kernel; every other shape runs the generic CUDA-core kernel.
+ * on != 0 forces the generic kernel for every shape (parity tests compare the
+ * two); no counterpart in the reference. */
+int pse_attention_force_generic(int32_t on);
 
 /* ------------------------------------------------------------------------ */
 /* Sampling, accept/resample                                                */

@@ -327,13 +327,15 @@ struct Plan {
   int rmax, maxd, n_qtiles, n_splits, split_tokens;
 };
 
+// The KV split count depends only on the call's shape (not on which kernel
+// runs it), so the workspace query and both kernels agree.
 Plan make_plan(int rows, int width, int q_heads, int kv_heads, int head_dim, int max_ctx) {
   Plan p;
   const int n_qrows = (q_heads / kv_heads) * width;
   p.rmax = n_qrows <= 1 ? 1 : n_qrows <= 2 ? 2 : n_qrows <= 4 ? 4 : 8;
   p.maxd = head_dim <= 32 ? 1 : head_dim <= 64 ? 2 : head_dim <= 128 ? 4 : 8;
   p.n_qtiles = ceil_div(n_qrows, p.rmax);
-  const long base_ctas = (long)rows * kv_heads * p.n_qtiles;
+  const long base_ctas = (long)rows * kv_heads * ceil_div(n_qrows, 16);
   const int target = 4 * kNumSMs;
   int splits = base_ctas >= target ? 1 : (int)((target + base_ctas - 1) / base_ctas);
   const int max_useful = ceil_div(max_ctx > 0 ? max_ctx : 1, 256);
@@ -397,9 +399,25 @@ int launch_d(const AttnArgs& a, const Plan& p, cudaStream_t s) {
 }
 
 }  // namespace
+
+bool tc_eligible(const pse_block_state& st, const pse_kv_layer& kv, int q_heads, int width);
+int tc_attention(const pse_block_state& st, const pse_kv_layer& kv, const void* q, int64_t q_tok_stride, void* out,
+                 int64_t out_tok_stride, const int32_t* slots, const int32_t* base_len, int rows, int width,
+                 int q_heads, float scale, int split_tokens, int n_splits, void* ws, cudaStream_t s);
+
 }  // namespace pse
 
 using namespace pse;
+
+namespace {
+bool g_force_generic = false;
+}
+
+/* Test hook: route every call to the generic kernel (1) or let the shape pick (0). */
+extern "C" int pse_attention_force_generic(int32_t on) {
+  g_force_generic = on != 0;
+  return PSE_OK;
+}
 
 extern "C" size_t pse_paged_attention_workspace(int32_t rows, int32_t width, int32_t q_heads, int32_t kv_heads,
                                                 int32_t head_dim, int32_t max_ctx) {
@@ -449,6 +467,18 @@ extern "C" int pse_paged_attention(pse_block_state st, pse_kv_layer kv, const vo
   a.n_qtiles = p.n_qtiles;
   a.ws = reinterpret_cast<float*>(workspace);
   cudaStream_t s = (cudaStream_t)stream;
+  if (tc_eligible(st, kv, q_heads, width) && !g_force_generic) {
+    int rc = tc_attention(st, kv, q, q_tok_stride, out, out_tok_stride, slots, base_len, rows, width, q_heads, scale,
+                          p.split_tokens, p.n_splits, workspace, s);
+    if (rc) return rc;
+    if (p.n_splits > 1) {
+      const int64_t items = (int64_t)rows * width * q_heads;
+      const int wpb = 8;
+      combine_kernel<__nv_bfloat16><<<(unsigned)((items + wpb - 1) / wpb), wpb * 32, 0, s>>>(a);
+      PSE_LAUNCH_CHECK();
+    }
+    return PSE_OK;
+  }
   if (kv.dtype == PSE_BF16) return launch_d<__nv_bfloat16>(a, p, s);
   if (kv.dtype == PSE_F32) return launch_d<float>(a, p, s);
   return PSE_EINVAL;

@@ -1,0 +1,504 @@
+// Paged attention for bf16 pools on sm_100a: TMA page loads + tensor-core math.
+//
+// Same contract as the generic kernel in attention.cu (engine/model.py:99-116
+// over the paged layout of engine/paged_cache.py:83-88), specialised for the
+// shapes that carry the bandwidth: bf16 K/V, head_dim 64 or 128, block_size
+// 16 / 32 / 64, up to 32 query rows (GQA group x width) per tile.
+//
+// CTA = 1 producer warp + 4 consumer warps, one (row, KV head, query tile,
+// KV split).  The producer walks the row's block table and, for every page of
+// a 64-token tile, issues 2-D TMA loads (cp.async.bulk.tensor, 128-byte
+// swizzle) of the page's K and V boxes [block_size x 64 columns] into a
+// 4-stage shared-memory ring, completing on an mbarrier with the transaction
+// byte count.  Pages past the row's end are requested at an out-of-range row,
+// so the TMA unit fills them with zeros and the byte count never changes.
+// Consumers run S = Q K^T and O += P V with mma.sync m16n8k16 (bf16 in, fp32
+// accumulate), fragments fetched with ldmatrix from the swizzled tiles (the
+// swizzle makes every ldmatrix conflict-free), an exp2-domain online softmax
+// per row, and release the stage through an "empty" mbarrier.  Warps split
+// the tile's tokens (and, with 32 query rows, the two 16-row m-tiles); their
+// partial (max, sum, O) are merged through shared memory at the end.
+//
+// Every mbarrier wait is bounded; on expiry the kernel latches
+// PSE_STATUS_TIMEOUT in the cache status word and stops issuing work.
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+#include <unordered_map>
+
+#include "common.cuh"
+
+namespace pse {
+namespace tc {
+
+constexpr int kConsumers = 4;
+constexpr int kThreads = (kConsumers + 1) * 32;
+constexpr int kTile = 64;     // tokens per pipeline stage
+constexpr uint32_t kSpinLimit = 1u << 22;
+
+// Ring depth: 4 x 16 KB stages for head_dim 64 (3 CTAs per SM), 3 x 32 KB for
+// head_dim 128 (2 CTAs per SM); either keeps >= 96 KB of K/V in flight per SM.
+__host__ __device__ constexpr int stages_for(int hd) { return hd == 64 ? 4 : 3; }
+
+struct Args {
+  const int32_t* block_table;
+  const int32_t* nblocks;
+  int max_blocks, block_size, num_blocks, num_slots;
+  int kv_heads, head_dim;
+  const __nv_bfloat16* q;
+  int64_t q_tok_stride;
+  __nv_bfloat16* out;
+  int64_t out_tok_stride;
+  const int32_t* slots;
+  const int32_t* base_len;
+  int rows, width, q_heads;
+  float scale_log2;
+  int split_tokens, n_splits, n_qtiles;
+  float* ws;
+  int32_t* status;
+  int oob_row;  // first row index past the pool's 2-D view (zero-fill requests)
+};
+
+__device__ __forceinline__ uint32_t su32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(bar)), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(su32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait for the phase of parity `parity` to complete.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (i >= 32) __nanosleep(32);
+  }
+  return false;
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+      ::"r"(su32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(su32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void mma16816(float* c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                         uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// Byte offset of element (row r, column d) inside a [rows x HD] bf16 tile
+// stored as HD/64 column halves of [rows x 128 B] with the 128-byte swizzle
+// (16-byte chunk c of row r stored at chunk c ^ (r % 8)).
+template <int HD>
+__device__ __forceinline__ uint32_t sw_off(int rows, int r, int d) {
+  return (uint32_t)(((d >> 6) * rows + r) * 128 + ((((d & 63) >> 3) ^ (r & 7)) << 4) + (d & 7) * 2);
+}
+
+// Page-major tile: tokens t = page * bs + row; each page holds HD/64 boxes.
+template <int HD>
+__device__ __forceinline__ uint32_t kv_off(int bs, int t, int d) {
+  const int page = t / bs, r = t % bs;
+  return (uint32_t)(((page * (HD / 64) + (d >> 6)) * bs + r) * 128 + ((((d & 63) >> 3) ^ (r & 7)) << 4) +
+                    (d & 7) * 2);
+}
+
+template <int HD, int MT>
+__global__ void __launch_bounds__(kThreads) attn_tc_kernel(const __grid_constant__ CUtensorMap tmk,
+                                                          const __grid_constant__ CUtensorMap tmv, Args a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  constexpr int kStages = stages_for(HD);
+  constexpr int kTileBytes = kTile * HD * 2;          // one of K or V for a stage
+  constexpr int kQRows = 16 * MT;
+  uint8_t* stage_k = smem;                            // [kStages][kTileBytes]
+  uint8_t* stage_v = smem + kStages * kTileBytes;     // [kStages][kTileBytes]
+  uint8_t* q_s = smem + 2 * kStages * kTileBytes;     // [kQRows x HD] swizzled
+  uint64_t* full = reinterpret_cast<uint64_t*>(q_s + kQRows * HD * 2);
+  uint64_t* empty = full + kStages;
+  int* abort_flag = reinterpret_cast<int*>(empty + kStages);
+  int* issued = abort_flag + 1;
+
+  const int group = a.q_heads / a.kv_heads;
+  const int n_qrows = group * a.width;
+  int bid = blockIdx.x;
+  const int qtile = bid % a.n_qtiles;
+  bid /= a.n_qtiles;
+  const int hk = bid % a.kv_heads;
+  const int i = bid / a.kv_heads;
+  const int split = blockIdx.y;
+  const int slot = a.slots[i];
+  const int base = a.base_len[i];
+  const int r0 = qtile * kQRows;
+  const int nr = min(kQRows, n_qrows - r0);
+  if (nr <= 0 || slot < 0 || slot >= a.num_slots || base < 0) return;
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int bs = a.block_size;
+  const int w_last = (r0 + nr - 1) / group;
+  const int kmax = base + w_last + 1;
+  const int k_lo = split * a.split_tokens;
+  const int k_hi = min(k_lo + a.split_tokens, kmax);
+  const int n_tiles = k_hi > k_lo ? (k_hi - k_lo + kTile - 1) / kTile : 0;
+
+  if (tid == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumers);
+    }
+    *abort_flag = 0;
+    *issued = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  // Query tile -> shared memory (bf16, swizzled), zero rows past nr.
+  for (int e = tid; e < kQRows * (HD / 2); e += kThreads) {
+    const int r = e / (HD / 2), d = (e % (HD / 2)) * 2;
+    uint32_t v = 0;
+    if (r < nr) {
+      const int rr = r0 + r, w = rr / group, g = rr % group;
+      v = *reinterpret_cast<const uint32_t*>(a.q + ((int64_t)i * a.width + w) * a.q_tok_stride +
+                                             (int64_t)(hk * group + g) * HD + d);
+    }
+    *reinterpret_cast<uint32_t*>(q_s + sw_off<HD>(kQRows, r, d)) = v;
+  }
+  __syncthreads();
+
+  if (warp == kConsumers) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      const int32_t* table = a.block_table + (int64_t)slot * a.max_blocks;
+      const int row_nb = a.nblocks[slot];
+      for (int t = 0; t < n_tiles; ++t) {
+        const int s = t % kStages;
+        if (!mbar_wait(&empty[s], ((t / kStages) & 1) ^ 1)) {
+          atomicOr(a.status, PSE_STATUS_TIMEOUT);
+          atomicExch(abort_flag, 1);
+          break;
+        }
+        *issued = t + 1;
+        mbar_expect_tx(&full[s], 2 * kTileBytes);
+        for (int p = 0; p < kTile / bs; ++p) {
+          const int tok0 = k_lo + t * kTile + p * bs;
+          const int pi = tok0 / bs;
+          int blk = -1;
+          if (tok0 < k_hi && pi < row_nb) blk = table[pi];
+          const int y = (blk >= 0 && blk < a.num_blocks) ? (blk * a.kv_heads + hk) * bs : a.oob_row;
+#pragma unroll
+          for (int c = 0; c < HD / 64; ++c) {
+            const int off = ((p * (HD / 64) + c) * bs) * 128;
+            tma_load_2d(stage_k + s * kTileBytes + off, &tmk, c * 64, y, &full[s]);
+            tma_load_2d(stage_v + s * kTileBytes + off, &tmv, c * 64, y, &full[s]);
+          }
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ consumers
+    const int mt = warp % MT;                  // this warp's 16-row m-tile
+    const int tok_base = (warp / MT) * (16 * MT);  // this warp's token slice within a tile
+    const int gid = lane >> 2, tid4 = lane & 3;
+    int qpos0 = -1, qpos1 = -1;
+    {
+      const int ra = mt * 16 + gid, rb = ra + 8;
+      if (ra < nr) qpos0 = base + (r0 + ra) / group;
+      if (rb < nr) qpos1 = base + (r0 + rb) / group;
+    }
+    float o[HD / 8][4];
+#pragma unroll
+    for (int n = 0; n < HD / 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+    const uint32_t qbase = su32(q_s);
+    // ldmatrix lane -> (row, col) helpers
+    const int lm = lane >> 3, lj = lane & 7;
+
+    for (int t = 0; t < n_tiles; ++t) {
+      const int s = t % kStages;
+      if (!mbar_wait(&full[s], (t / kStages) & 1)) {
+        atomicOr(a.status, PSE_STATUS_TIMEOUT);
+        atomicExch(abort_flag, 1);
+        break;
+      }
+      if (*reinterpret_cast<volatile int*>(abort_flag)) break;
+      const uint32_t kb = su32(stage_k + s * kTileBytes), vb = su32(stage_v + s * kTileBytes);
+#pragma unroll
+      for (int sub = 0; sub < MT; ++sub) {
+        const int t0 = tok_base + sub * 16;         // first token of this 16-token slice (tile-local)
+        const int tok_abs = k_lo + t * kTile + t0;  // its absolute position
+        float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
+          ldsm_x4(qbase + sw_off<HD>(16 * MT, mt * 16 + (lm & 1) * 8 + lj, kk * 16 + (lm >> 1) * 8), a0, a1, a2, a3);
+          ldsm_x4(kb + kv_off<HD>(bs, t0 + (lm >> 1) * 8 + lj, kk * 16 + (lm & 1) * 8), b0, b1, b2, b3);
+          mma16816(sc[0], a0, a1, a2, a3, b0, b1);
+          mma16816(sc[1], a0, a1, a2, a3, b2, b3);
+        }
+        // mask + online softmax (exp2 domain)
+        float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+        for (int n = 0; n < 2; ++n) {
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            const int tok = tok_abs + n * 8 + 2 * tid4 + c;
+            const bool live = tok < k_hi;
+            sc[n][c] = (live && tok <= qpos0) ? sc[n][c] * a.scale_log2 : -INFINITY;
+            sc[n][2 + c] = (live && tok <= qpos1) ? sc[n][2 + c] * a.scale_log2 : -INFINITY;
+            mx0 = fmaxf(mx0, sc[n][c]);
+            mx1 = fmaxf(mx1, sc[n][2 + c]);
+          }
+        }
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+        const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+        const float ms0 = mn0 == -INFINITY ? 0.f : mn0, ms1 = mn1 == -INFINITY ? 0.f : mn1;
+        const float c0 = exp2f(m0 - ms0), c1 = exp2f(m1 - ms1);
+        m0 = mn0;
+        m1 = mn1;
+        float p[2][4];
+#pragma unroll
+        for (int n = 0; n < 2; ++n) {
+          p[n][0] = exp2f(sc[n][0] - ms0);
+          p[n][1] = exp2f(sc[n][1] - ms0);
+          p[n][2] = exp2f(sc[n][2] - ms1);
+          p[n][3] = exp2f(sc[n][3] - ms1);
+        }
+        l0 = l0 * c0 + p[0][0] + p[0][1] + p[1][0] + p[1][1];
+        l1 = l1 * c1 + p[0][2] + p[0][3] + p[1][2] + p[1][3];
+#pragma unroll
+        for (int n = 0; n < HD / 8; ++n) {
+          o[n][0] *= c0;
+          o[n][1] *= c0;
+          o[n][2] *= c1;
+          o[n][3] *= c1;
+        }
+        const uint32_t pa0 = pack_bf16(p[0][0], p[0][1]), pa1 = pack_bf16(p[0][2], p[0][3]);
+        const uint32_t pa2 = pack_bf16(p[1][0], p[1][1]), pa3 = pack_bf16(p[1][2], p[1][3]);
+#pragma unroll
+        for (int n2 = 0; n2 < HD / 16; ++n2) {
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4_t(vb + kv_off<HD>(bs, t0 + (lm & 1) * 8 + lj, n2 * 16 + (lm >> 1) * 8), b0, b1, b2, b3);
+          mma16816(o[2 * n2], pa0, pa1, pa2, pa3, b0, b1);
+          mma16816(o[2 * n2 + 1], pa0, pa1, pa2, pa3, b2, b3);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+    // quad-reduce the row sums
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+    // park this warp's partial state for the merge (stage area is free now)
+    __syncwarp();
+    asm volatile("bar.sync 1, %0;" ::"r"(kConsumers * 32));
+    float* mw = reinterpret_cast<float*>(stage_k);           // [kConsumers][16]
+    float* lw = mw + kConsumers * 16;                         // [kConsumers][16]
+    float* ow = lw + kConsumers * 16;                         // [kConsumers][16][HD]
+    if (tid4 == 0) {
+      mw[warp * 16 + gid] = m0;
+      mw[warp * 16 + gid + 8] = m1;
+      lw[warp * 16 + gid] = l0;
+      lw[warp * 16 + gid + 8] = l1;
+    }
+#pragma unroll
+    for (int n = 0; n < HD / 8; ++n) {
+      const int d = n * 8 + 2 * tid4;
+      ow[(warp * 16 + gid) * HD + d] = o[n][0];
+      ow[(warp * 16 + gid) * HD + d + 1] = o[n][1];
+      ow[(warp * 16 + gid + 8) * HD + d] = o[n][2];
+      ow[(warp * 16 + gid + 8) * HD + d + 1] = o[n][3];
+    }
+    asm volatile("bar.sync 1, %0;" ::"r"(kConsumers * 32));
+    // combine: warps w with w % MT == mt cover m-tile mt
+    for (int e = tid; e < nr * HD; e += kConsumers * 32) {
+      const int r = e / HD, d = e % HD;
+      const int mtr = r / 16, rl = r % 16;
+      float M = -INFINITY;
+      for (int w2 = mtr; w2 < kConsumers; w2 += MT) M = fmaxf(M, mw[w2 * 16 + rl]);
+      float L = 0.f, acc = 0.f;
+      for (int w2 = mtr; w2 < kConsumers; w2 += MT) {
+        const float f = M == -INFINITY ? 0.f : exp2f(mw[w2 * 16 + rl] - M);
+        L += lw[w2 * 16 + rl] * f;
+        acc += ow[(w2 * 16 + rl) * HD + d] * f;
+      }
+      const int rr = r0 + r, w = rr / group, g = rr % group, h = hk * group + g;
+      const int64_t tokrow = (int64_t)i * a.width + w;
+      if (a.n_splits == 1) {
+        a.out[tokrow * a.out_tok_stride + (int64_t)h * HD + d] = __float2bfloat16_rn(L > 0.f ? acc / L : 0.f);
+      } else {
+        float* ws = a.ws + (((int64_t)split * a.rows * a.width + tokrow) * a.q_heads + h) * (HD + 2);
+        ws[d] = acc;
+        if (d == 0) {
+          ws[HD] = M == -INFINITY ? -INFINITY : M * 0.69314718055994531f;  // natural-log units
+          ws[HD + 1] = L;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  // Error path only: before the CTA's shared memory is released, wait (bounded)
+  // for the copies of the last tiles the producer issued.
+  if (tid == kConsumers * 32 && *reinterpret_cast<volatile int*>(abort_flag)) {
+    const int n = *issued;
+    for (int t = n > kStages ? n - kStages : 0; t < n; ++t) mbar_wait(&full[t % kStages], (t / kStages) & 1);
+  }
+}
+
+// ---------------------------------------------------------------- host side
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::mutex g_mu;
+std::unordered_map<uint64_t, CUtensorMap>* g_maps = nullptr;
+
+int encoder() {
+  if (g_encode) return 0;
+  cudaDriverEntryPointQueryResult q;
+  void* fn = nullptr;
+  cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+  if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn) return e != cudaSuccess ? (int)e : PSE_EINVAL;
+  g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  return 0;
+}
+
+// 2-D view of one layer's pool: rows = num_blocks * kv_heads * block_size,
+// columns = head_dim; box = [block_size rows x 64 columns], 128-byte swizzle.
+int tensor_map(const void* pool, int num_blocks, int kv_heads, int bs, int hd, CUtensorMap* out) {
+  const uint64_t key = reinterpret_cast<uint64_t>(pool) ^ ((uint64_t)num_blocks << 40) ^ ((uint64_t)bs << 32) ^
+                       ((uint64_t)hd << 24) ^ ((uint64_t)kv_heads << 48);
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!g_maps) g_maps = new std::unordered_map<uint64_t, CUtensorMap>();
+  auto it = g_maps->find(key);
+  if (it != g_maps->end()) {
+    *out = it->second;
+    return 0;
+  }
+  int rc = encoder();
+  if (rc) return rc;
+  CUtensorMap m;
+  const cuuint64_t dims[2] = {(cuuint64_t)hd, (cuuint64_t)num_blocks * kv_heads * bs};
+  const cuuint64_t strides[1] = {(cuuint64_t)hd * 2};
+  const cuuint32_t box[2] = {64, (cuuint32_t)bs};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(pool), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return PSE_EINVAL;
+  (*g_maps)[key] = m;
+  *out = m;
+  return 0;
+}
+
+template <int HD>
+constexpr size_t smem_bytes(int mt) {
+  return 1024 + 2 * stages_for(HD) * (size_t)kTile * HD * 2 + (size_t)16 * mt * HD * 2 + 2 * stages_for(HD) * 8 + 16;
+}
+
+template <int HD, int MT>
+int launch(const CUtensorMap& mk, const CUtensorMap& mv, const Args& a, cudaStream_t s) {
+  auto kern = attn_tc_kernel<HD, MT>;
+  constexpr size_t smem = smem_bytes<HD>(MT);
+  static_assert(smem <= 227 * 1024, "shared memory budget");
+  static const cudaError_t opt = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (opt != cudaSuccess) return (int)opt;
+  dim3 grid((unsigned)(a.rows * a.kv_heads * a.n_qtiles), (unsigned)a.n_splits);
+  kern<<<grid, kThreads, smem, s>>>(mk, mv, a);
+  PSE_LAUNCH_CHECK();
+  return PSE_OK;
+}
+
+}  // namespace tc
+
+bool tc_eligible(const pse_block_state& st, const pse_kv_layer& kv, int q_heads, int width) {
+  if (kv.dtype != PSE_BF16) return false;
+  if (kv.head_dim != 64 && kv.head_dim != 128) return false;
+  if (st.block_size != 16 && st.block_size != 32 && st.block_size != 64) return false;
+  if ((reinterpret_cast<uintptr_t>(kv.k_pool) | reinterpret_cast<uintptr_t>(kv.v_pool)) & 15) return false;
+  const long long rows = (long long)st.num_blocks * kv.kv_heads * st.block_size;
+  if (rows + st.block_size >= (1ll << 31)) return false;
+  (void)q_heads;
+  (void)width;
+  return true;
+}
+
+int tc_attention(const pse_block_state& st, const pse_kv_layer& kv, const void* q, int64_t q_tok_stride, void* out,
+                 int64_t out_tok_stride, const int32_t* slots, const int32_t* base_len, int rows, int width,
+                 int q_heads, float scale, int split_tokens, int n_splits, void* ws, cudaStream_t s) {
+  const int n_qrows = (q_heads / kv.kv_heads) * width;
+  const int MT = n_qrows <= 16 ? 1 : 2;
+  tc::Args a;
+  a.block_table = st.block_table;
+  a.nblocks = st.nblocks;
+  a.max_blocks = st.max_blocks;
+  a.block_size = st.block_size;
+  a.num_blocks = st.num_blocks;
+  a.num_slots = st.num_slots;
+  a.kv_heads = kv.kv_heads;
+  a.head_dim = kv.head_dim;
+  a.q = reinterpret_cast<const __nv_bfloat16*>(q);
+  a.q_tok_stride = q_tok_stride;
+  a.out = reinterpret_cast<__nv_bfloat16*>(out);
+  a.out_tok_stride = out_tok_stride;
+  a.slots = slots;
+  a.base_len = base_len;
+  a.rows = rows;
+  a.width = width;
+  a.q_heads = q_heads;
+  a.scale_log2 = scale * 1.4426950408889634f;
+  a.split_tokens = split_tokens;
+  a.n_splits = n_splits;
+  a.n_qtiles = ceil_div(n_qrows, 16 * MT);
+  a.ws = reinterpret_cast<float*>(ws);
+  a.status = st.status;
+  a.oob_row = st.num_blocks * kv.kv_heads * st.block_size;
+  CUtensorMap mk, mv;
+  int rc = tc::tensor_map(kv.k_pool, st.num_blocks, kv.kv_heads, st.block_size, kv.head_dim, &mk);
+  if (rc) return rc;
+  rc = tc::tensor_map(kv.v_pool, st.num_blocks, kv.kv_heads, st.block_size, kv.head_dim, &mv);
+  if (rc) return rc;
+  if (kv.head_dim == 64) return MT == 1 ? tc::launch<64, 1>(mk, mv, a, s) : tc::launch<64, 2>(mk, mv, a, s);
+  return MT == 1 ? tc::launch<128, 1>(mk, mv, a, s) : tc::launch<128, 2>(mk, mv, a, s);
+}
+
+}  // namespace pse

@@ -23,6 +23,7 @@ STATUS_TABLE_OVERFLOW = 2
 STATUS_TRUNCATE_LONG = 4
 STATUS_DOUBLE_FREE = 8
 STATUS_BAD_BLOCK = 16
+STATUS_TIMEOUT = 32
 
 c_p = ctypes.c_void_p
 c_i32 = ctypes.c_int32
@@ -65,6 +66,7 @@ _PROTOS = {
     "pse_epilogue": ([c_i32, c_p, c_i64, c_p, c_p, c_i64, c_p, c_i64, c_i32, c_i32, c_i32, c_p], 1),
     "pse_rope": ([c_p, c_i64, c_i32, c_i32, c_i32, c_i32, c_i32, c_p, c_f32, c_i32, c_p], 1),
     "pse_scatter_rows": ([c_p, c_i64, c_p, c_i32, c_i32, c_p, c_i64, c_i32, c_p], 1),
+    "pse_attention_force_generic": ([c_i32], 0),
 }
 _SIZE_PROTOS = {
     "pse_paged_attention_workspace": [c_i32, c_i32, c_i32, c_i32, c_i32, c_i32],

@@ -78,6 +78,8 @@ def _raise_for_status(bits: int, where: str) -> None:
         raise RuntimeError(f"block table too narrow during {where}")
     if bits & N.STATUS_BAD_BLOCK:
         raise RuntimeError(f"corrupt block id during {where}")
+    if bits & N.STATUS_TIMEOUT:
+        raise RuntimeError(f"a bounded device wait expired during {where}")
 
 
 class BlockAllocator:

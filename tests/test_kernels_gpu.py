@@ -176,13 +176,21 @@ ATTN_CASES = [
     (2, 4, 32, 8, 64, 32, 3000, torch.bfloat16),   # long context: split-KV path
     (1, 1, 4, 4, 128, 16, 9000, torch.float32),    # single row, many splits
     (1, 37, 2, 2, 16, 4, 60, torch.float32),       # prefill-like width, several query tiles
+    (1, 40, 4, 4, 64, 16, 50, torch.bfloat16),     # prefill-like width on the tensor-core path
+    (4, 1, 6, 6, 64, 64, 500, torch.bfloat16),     # block 64
+    (2, 5, 12, 12, 64, 32, 2100, torch.bfloat16),  # block 32, splits
+    (5, 6, 16, 4, 128, 16, 300, torch.bfloat16),   # GQA 4 x width 6 = 24 rows (two m-tiles, one padded)
+    (2, 1, 8, 8, 128, 16, 20000, torch.bfloat16),  # very long context, many splits
 ]
 
 
+@pytest.mark.parametrize("generic", [False, True])
 @pytest.mark.parametrize("case", ATTN_CASES)
-def test_paged_attention_matches_oracle(case):
+def test_paged_attention_matches_oracle(case, generic):
     N = _N()
     rows, width, hq, hk, hd, bs, max_len, dtype = case
+    if generic and dtype == torch.float32:
+        pytest.skip("fp32 pools always run the generic kernel")
     rng = np.random.default_rng(ATTN_CASES.index(case))
     base = rng.integers(0, max_len, size=rows)
     need = [(int(b) + width + bs - 1) // bs for b in base]
@@ -210,9 +218,15 @@ def test_paged_attention_matches_oracle(case):
     max_ctx = int(base.max()) + width
     ws_bytes = N.size_call("pse_paged_attention_workspace", rows, width, hq, hk, hd, max_ctx)
     ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device="cuda")
-    N.call("pse_paged_attention", c.state, c.layer(0), qd.data_ptr(), hq * hd, out.data_ptr(), hq * hd,
-           slots.data_ptr(), base_d.data_ptr(), rows, width, hq, 1.0 / math.sqrt(hd), max_ctx,
-           ws.data_ptr(), ws.numel(), N.stream_ptr())
+    N.call("pse_attention_force_generic", 1 if generic else 0)
+    try:
+        N.call("pse_paged_attention", c.state, c.layer(0), qd.data_ptr(), hq * hd, out.data_ptr(), hq * hd,
+               slots.data_ptr(), base_d.data_ptr(), rows, width, hq, 1.0 / math.sqrt(hd), max_ctx,
+               ws.data_ptr(), ws.numel(), N.stream_ptr())
+        torch.cuda.synchronize()
+    finally:
+        N.call("pse_attention_force_generic", 0)
+    assert int(c._blocks.status.item()) == 0
     want = oracle_attention(q.float().view(rows, width, hq, hd).numpy(), kp.to(dtype).float().numpy(),
                             vp.to(dtype).float().numpy(), tables, base)
     got = out.float().cpu().view(rows, width, hq, hd).numpy()
