@@ -161,6 +161,13 @@ def run_pse(args, rank, world, device):
     for _ in range(max(args.warmup, 3) - 1):
         api_step()
     runner = runner_for(d, t, dc, tc, k)
+    if args.profile_step:
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_push("pse_step")
+        pse.batched_speculative_step(d, t, rids, dc, tc, dn, tn, k, T, use_graph=False)
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
+        return None
     graph = [g for key, g in runner.graphs.items() if key[0] == B][0]
     b = runner.bufs[B]
     nacc_hist = torch.zeros(args.steps, B, dtype=torch.int32, device=device)
@@ -307,6 +314,8 @@ def main():
     ap.add_argument("--cpu-rows", type=int, default=4)
     ap.add_argument("--cpu-steps", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-step", action="store_true",
+                    help="after warm-up run one eager step inside the NVTX range 'pse_step' and exit (for ncu)")
     args = ap.parse_args()
 
     from pse import workload as wl
@@ -341,6 +350,8 @@ def main():
     import pse._build
     pse._build.build()
     r = run_pse(args, rank, world, device)
+    if r is None:
+        return
     peak, peak_kind = _peaks()
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
