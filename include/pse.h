@@ -31,6 +31,7 @@ extern "C" {
 #define PSE_OK 0
 #define PSE_EINVAL 10001       /* bad size / pointer / unsupported combination */
 #define PSE_EWORKSPACE 10002   /* workspace smaller than the query function said */
+#define PSE_ESCRATCH 10003     /* scratch need exceeds PSE_NOALLOC_SCRATCH_BYTES */
 
 /* ---- device status latch bits ---- */
 #define PSE_STATUS_OOM 1              /* pool exhausted (reference: MemoryError) */
@@ -138,6 +139,26 @@ int pse_paged_attention(pse_block_state st, pse_kv_layer kv, const void *q, int6
 
 size_t pse_paged_attention_workspace(int32_t rows, int32_t width, int32_t q_heads, int32_t kv_heads,
                                      int32_t head_dim, int32_t max_ctx);
+
+/* pse_paged_attention without a workspace argument, for hosts that cannot
+ * allocate device memory where they call this library (a runtime in another
+ * language that binds only this C ABI and has no CUDA allocator, or a process
+ * whose device memory belongs to another allocator that must not be bypassed).
+ * It allocates nothing: the split-KV scratch is a fixed array of
+ * PSE_NOALLOC_SCRATCH_BYTES compiled into the library, resident on every GPU
+ * that loads it until the process exits.  Calls whose scratch need
+ * (pse_paged_attention_workspace) exceeds that return PSE_ESCRATCH without
+ * launching.  The first call on each device looks up the array's device
+ * address (cudaGetSymbolAddress) with that device current; make that first
+ * call before any stream capture.  All calls share the array and it keeps the
+ * last call's contents (nothing in it needs to start at zero): calls that
+ * overlap on the GPU race, so issue them on one stream or otherwise ordered.
+ * No counterpart in the reference. */
+#define PSE_NOALLOC_SCRATCH_BYTES (8u << 20)
+int pse_paged_attention_noalloc(pse_block_state st, pse_kv_layer kv, const void *q, int64_t q_tok_stride,
+                                void *out, int64_t out_tok_stride, const int32_t *slots,
+                                const int32_t *base_len, int32_t rows, int32_t width, int32_t q_heads,
+                                float scale, int32_t max_ctx, void *stream);
 
 /* bf16 pools with head_dim 64/128 and block_size 16/32/64 run the TMA +
  * tensor-core kernel; every other shape runs the generic CUDA-core kernel.

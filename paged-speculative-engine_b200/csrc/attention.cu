@@ -14,6 +14,7 @@
 // base_len[i] + w and sees keys 0..base_len[i]+w.
 
 #include <cfloat>
+#include <mutex>
 
 #include "common.cuh"
 
@@ -470,6 +471,109 @@ extern "C" int pse_paged_attention(pse_block_state st, pse_kv_layer kv, const vo
   if (tc_eligible(st, kv, q_heads, width) && !g_force_generic) {
     int rc = tc_attention(st, kv, q, q_tok_stride, out, out_tok_stride, slots, base_len, rows, width, q_heads, scale,
                           p.split_tokens, p.n_splits, workspace, s);
+    if (rc) return rc;
+    if (p.n_splits > 1) {
+      const int64_t items = (int64_t)rows * width * q_heads;
+      const int wpb = 8;
+      combine_kernel<__nv_bfloat16><<<(unsigned)((items + wpb - 1) / wpb), wpb * 32, 0, s>>>(a);
+      PSE_LAUNCH_CHECK();
+    }
+    return PSE_OK;
+  }
+  if (kv.dtype == PSE_BF16) return launch_d<__nv_bfloat16>(a, p, s);
+  if (kv.dtype == PSE_F32) return launch_d<float>(a, p, s);
+  return PSE_EINVAL;
+}
+
+// ---------------------------------------------------------------------------
+// Attention without a caller-provided workspace.
+//
+// Some hosts of this library cannot allocate device memory where they call
+// it: a serving runtime in another language that binds only this C ABI and
+// has no CUDA allocator of its own, or a process whose device memory belongs
+// entirely to another allocator (a framework's caching allocator, a fixed
+// pre-reserved pool) that must not be bypassed with cudaMalloc.  For them,
+// pse_paged_attention_noalloc takes the split-KV scratch from the fixed array
+// below, which is part of the library image: every GPU that loads the library
+// holds these PSE_NOALLOC_SCRATCH_BYTES until the process exits.
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr size_t kNoallocScratchBytes = PSE_NOALLOC_SCRATCH_BYTES;
+static __device__ __align__(256) float g_noalloc_scratch[kNoallocScratchBytes / sizeof(float)];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kMaxDevices] = {};
+
+// Device address of g_noalloc_scratch on the current device.  In host code the
+// array's name is only a host-side stand-in, so the address is looked up once
+// per device (with that device current) and cached.
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return (int)e;
+  if (dev < 0 || dev >= kMaxDevices) return PSE_EINVAL;
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return (int)e;
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return PSE_OK;
+}
+
+}  // namespace
+
+extern "C" int pse_paged_attention_noalloc(pse_block_state st, pse_kv_layer kv, const void* q, int64_t q_tok_stride,
+                                           void* out, int64_t out_tok_stride, const int32_t* slots,
+                                           const int32_t* base_len, int32_t rows, int32_t width, int32_t q_heads,
+                                           float scale, int32_t max_ctx, void* stream) {
+  void* scratch = nullptr;
+  int rc = noalloc_scratch(&scratch);  // first call on a device: symbol lookup
+  if (rc) return rc;
+  if (rows < 0 || width < 0) return PSE_EINVAL;
+  if (rows == 0 || width == 0) return PSE_OK;
+  if (!q || !out || !slots || !base_len || !kv.k_pool || !kv.v_pool || !st.block_table || !st.nblocks)
+    return PSE_EINVAL;
+  if (kv.kv_heads <= 0 || q_heads <= 0 || q_heads % kv.kv_heads != 0) return PSE_EINVAL;
+  if (kv.head_dim <= 0 || kv.head_dim > 256 || max_ctx <= 0 || st.block_size <= 0) return PSE_EINVAL;
+  const size_t need = pse_paged_attention_workspace(rows, width, q_heads, kv.kv_heads, kv.head_dim, max_ctx);
+  if (need > kNoallocScratchBytes) return PSE_ESCRATCH;
+  Plan p = make_plan(rows, width, q_heads, kv.kv_heads, kv.head_dim, max_ctx);
+  AttnArgs a;
+  a.block_table = st.block_table;
+  a.nblocks = st.nblocks;
+  a.max_blocks = st.max_blocks;
+  a.block_size = st.block_size;
+  a.num_blocks = st.num_blocks;
+  a.num_slots = st.num_slots;
+  a.k_pool = kv.k_pool;
+  a.v_pool = kv.v_pool;
+  a.kv_heads = kv.kv_heads;
+  a.head_dim = kv.head_dim;
+  a.q = q;
+  a.q_tok_stride = q_tok_stride;
+  a.out = out;
+  a.out_tok_stride = out_tok_stride;
+  a.slots = slots;
+  a.base_len = base_len;
+  a.rows = rows;
+  a.width = width;
+  a.q_heads = q_heads;
+  a.scale = scale;
+  a.split_tokens = p.split_tokens;
+  a.n_splits = p.n_splits;
+  a.n_qtiles = p.n_qtiles;
+  // Every (split, row, head) slot of the scratch is written before the combine
+  // reads it, so stale contents from an earlier call never leak in.
+  a.ws = reinterpret_cast<float*>(scratch);
+  cudaStream_t s = (cudaStream_t)stream;
+  if (tc_eligible(st, kv, q_heads, width)) {
+    rc = tc_attention(st, kv, q, q_tok_stride, out, out_tok_stride, slots, base_len, rows, width, q_heads, scale,
+                      p.split_tokens, p.n_splits, scratch, s);
     if (rc) return rc;
     if (p.n_splits > 1) {
       const int64_t items = (int64_t)rows * width * q_heads;

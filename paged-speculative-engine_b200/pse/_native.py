@@ -24,6 +24,8 @@ STATUS_TRUNCATE_LONG = 4
 STATUS_DOUBLE_FREE = 8
 STATUS_BAD_BLOCK = 16
 STATUS_TIMEOUT = 32
+PSE_ESCRATCH = 10003
+NOALLOC_SCRATCH_BYTES = 8 << 20
 
 c_p = ctypes.c_void_p
 c_i32 = ctypes.c_int32
@@ -67,6 +69,8 @@ _PROTOS = {
     "pse_rope": ([c_p, c_i64, c_i32, c_i32, c_i32, c_i32, c_i32, c_p, c_f32, c_i32, c_p], 1),
     "pse_scatter_rows": ([c_p, c_i64, c_p, c_i32, c_i32, c_p, c_i64, c_i32, c_p], 1),
     "pse_attention_force_generic": ([c_i32], 0),
+    "pse_paged_attention_noalloc": ([BlockState, KVLayer, c_p, c_i64, c_p, c_i64, c_p, c_p, c_i32, c_i32, c_i32,
+                                     c_f32, c_i32, c_p], 1),
 }
 _SIZE_PROTOS = {
     "pse_paged_attention_workspace": [c_i32, c_i32, c_i32, c_i32, c_i32, c_i32],
