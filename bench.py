@@ -293,6 +293,77 @@ def cpu_reference(args, sample_rows, sample_steps, threads):
                        f"workload (prompts from the same seed), fp32 oracle port, prefill untimed")
 
 
+ATTN_SHAPES = {
+    # name: rows, width, q_heads, kv_heads, head_dim, block, ctx_lo, ctx_hi (ctx includes the width queries)
+    "gpt2-verify": (256, 5, 12, 12, 64, 16, 133, 1029),
+    "gpt2-draft": (256, 1, 6, 6, 64, 16, 129, 1025),
+    "verify-5a": (1024, 8, 32, 8, 128, 16, 512, 32768),
+}
+
+
+def micro_attention(args, device):
+    """Verify-attention kernel microbenchmark: one layer's pools, block tables a
+    random permutation of a shared pool, Q/K/V ~ N(0,1), bf16.  Bytes are the
+    algorithmic K/V bytes (sum of contexts x kv_heads x head_dim x 2 x 2 B) plus
+    Q and O; each timed launch reads a pool far larger than L2."""
+    import pse
+    import pse._native as N
+    rows, width, hq, hk, hd, bs, lo, hi = ATTN_SHAPES[args.attn_shape]
+    if args.rows:
+        rows = args.rows
+    rng = np.random.default_rng(0)
+    ctx = rng.integers(lo, hi + 1, size=rows)
+    need = (ctx + bs - 1) // bs
+    nb = int(need.sum())
+    c = pse.PagedKVCache(1, hk, hd, bs, nb, dtype=torch.bfloat16, device=device, max_requests=rows,
+                         max_blocks_per_request=int(need.max()))
+    perm = torch.from_numpy(rng.permutation(nb).astype(np.int32))
+    table = torch.full((rows, int(need.max())), -1, dtype=torch.int32)
+    o = 0
+    for i, n in enumerate(need):
+        table[i, :n] = perm[o:o + n]
+        o += n
+    c._blocks.block_table.copy_(table)
+    c._blocks.nblocks.copy_(torch.from_numpy(need.astype(np.int32)))
+    g = torch.Generator(device=device).manual_seed(1)
+    c.k_pool.normal_(generator=g)
+    c.v_pool.normal_(generator=g)
+    q = torch.randn(rows * width, hq * hd, device=device, generator=g).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    slots = torch.arange(rows, dtype=torch.int32, device=device)
+    base = torch.from_numpy((ctx - width).astype(np.int32)).to(device)
+    max_ctx = int(ctx.max())
+    wsb = N.size_call("pse_paged_attention_workspace", rows, width, hq, hk, hd, max_ctx)
+    ws = torch.empty(wsb, dtype=torch.uint8, device=device)
+    st = N.stream_ptr()
+
+    def launch():
+        N.call("pse_paged_attention", c.state, c.layer(0), q.data_ptr(), q.stride(0), out.data_ptr(), out.stride(0),
+               slots.data_ptr(), base.data_ptr(), rows, width, hq, 1.0 / math.sqrt(hd), max_ctx, ws.data_ptr(),
+               ws.numel(), st)
+
+    for _ in range(max(args.warmup, 3)):
+        launch()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(device.index or 0) as clk:
+        e0.record()
+        for _ in range(args.steps):
+            launch()
+        e1.record()
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    kv_bytes = int(ctx.sum()) * hk * hd * 2 * 2
+    alg = kv_bytes + 2 * q.numel() * 2 + rows * 4 * int(need.max())
+    peak, kind = _peaks()
+    gbs = alg / (ms / 1000) / 1e9
+    print(json.dumps({"metric": "paged attention HBM GB/s", "shape": args.attn_shape, "value": gbs, "unit": "GB/s",
+                      "frac_of_peak": gbs / peak, "peak": peak, "peak_kind": kind, "us_per_launch": ms * 1000,
+                      "algorithmic_bytes": alg, "rows": rows, "width": width, "q_heads": hq, "kv_heads": hk,
+                      "head_dim": hd, "block_size": bs, "ctx_mean": float(ctx.mean()),
+                      "pool_bytes": 2 * c.k_pool.numel() * 2, "clocks": clk.summary()}), flush=True)
+
+
 def config_block(args, w, B, world):
     return {"workload": f"{w.name}: {w.n_requests if args.rows is None else B} rows/GPU, prompts "
                         f"U[{w.prompt_lo},{w.prompt_hi}], k={w.k}, block {w.block_size}, "
@@ -314,6 +385,8 @@ def main():
     ap.add_argument("--cpu-rows", type=int, default=4)
     ap.add_argument("--cpu-steps", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--micro", choices=["attn"], default=None, help="kernel microbenchmark instead of the step")
+    ap.add_argument("--attn-shape", default="gpt2-verify", choices=sorted(ATTN_SHAPES))
     ap.add_argument("--profile-step", action="store_true",
                     help="after warm-up run one eager step inside the NVTX range 'pse_step' and exit (for ncu)")
     args = ap.parse_args()
@@ -349,6 +422,9 @@ def main():
     torch.cuda.set_device(device)
     import pse._build
     pse._build.build()
+    if args.micro == "attn":
+        micro_attention(args, device)
+        return
     r = run_pse(args, rank, world, device)
     if r is None:
         return

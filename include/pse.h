@@ -131,7 +131,8 @@ int pse_kv_gather(pse_block_state st, pse_kv_layer kv, const int32_t *slots, int
  * K/V are already in the pool.  Grouped heads: query head h reads KV head
  * h / (q_heads / kv_heads).  `max_ctx` bounds base_len[i] + width over rows
  * (it sizes the split-KV grid; rows may be shorter).  Output has the pool's
- * dtype.  workspace: float scratch of pse_paged_attention_workspace() bytes. */
+ * dtype.  workspace: pse_paged_attention_workspace() bytes (at least 256: a
+ * work counter the call zeroes on the stream, then split-KV partials). */
 int pse_paged_attention(pse_block_state st, pse_kv_layer kv, const void *q, int64_t q_tok_stride,
                         void *out, int64_t out_tok_stride, const int32_t *slots, const int32_t *base_len,
                         int32_t rows, int32_t width, int32_t q_heads, float scale, int32_t max_ctx,

@@ -404,7 +404,7 @@ int launch_d(const AttnArgs& a, const Plan& p, cudaStream_t s) {
 bool tc_eligible(const pse_block_state& st, const pse_kv_layer& kv, int q_heads, int width);
 int tc_attention(const pse_block_state& st, const pse_kv_layer& kv, const void* q, int64_t q_tok_stride, void* out,
                  int64_t out_tok_stride, const int32_t* slots, const int32_t* base_len, int rows, int width,
-                 int q_heads, float scale, int split_tokens, int n_splits, void* ws, cudaStream_t s);
+                 int q_heads, float scale, int split_tokens, int n_splits, void* ws, int* counter, cudaStream_t s);
 
 }  // namespace pse
 
@@ -420,12 +420,17 @@ extern "C" int pse_attention_force_generic(int32_t on) {
   return PSE_OK;
 }
 
+// Workspace layout: a 256-byte header (the persistent kernel's work counter,
+// zeroed by every call) followed by the split-KV partials
+// [n_splits][rows*width][q_heads][head_dim + 2] floats when the call splits.
+constexpr size_t kWsHeader = 256;
+
 extern "C" size_t pse_paged_attention_workspace(int32_t rows, int32_t width, int32_t q_heads, int32_t kv_heads,
                                                 int32_t head_dim, int32_t max_ctx) {
-  if (rows <= 0 || width <= 0 || q_heads <= 0 || kv_heads <= 0 || head_dim <= 0) return 0;
+  if (rows <= 0 || width <= 0 || q_heads <= 0 || kv_heads <= 0 || head_dim <= 0) return kWsHeader;
   Plan p = make_plan(rows, width, q_heads, kv_heads, head_dim, max_ctx);
-  if (p.n_splits <= 1) return 0;
-  return (size_t)p.n_splits * rows * width * q_heads * (head_dim + 2) * sizeof(float);
+  if (p.n_splits <= 1) return kWsHeader;
+  return kWsHeader + (size_t)p.n_splits * rows * width * q_heads * (head_dim + 2) * sizeof(float);
 }
 
 extern "C" int pse_paged_attention(pse_block_state st, pse_kv_layer kv, const void* q, int64_t q_tok_stride, void* out,
@@ -439,7 +444,7 @@ extern "C" int pse_paged_attention(pse_block_state st, pse_kv_layer kv, const vo
   if (kv.kv_heads <= 0 || q_heads <= 0 || q_heads % kv.kv_heads != 0) return PSE_EINVAL;
   if (kv.head_dim <= 0 || kv.head_dim > 256 || max_ctx <= 0 || st.block_size <= 0) return PSE_EINVAL;
   Plan p = make_plan(rows, width, q_heads, kv.kv_heads, kv.head_dim, max_ctx);
-  if (p.n_splits > 1 &&
+  if (!workspace ||
       workspace_bytes < pse_paged_attention_workspace(rows, width, q_heads, kv.kv_heads, kv.head_dim, max_ctx))
     return PSE_EWORKSPACE;
   AttnArgs a;
@@ -466,11 +471,11 @@ extern "C" int pse_paged_attention(pse_block_state st, pse_kv_layer kv, const vo
   a.split_tokens = p.split_tokens;
   a.n_splits = p.n_splits;
   a.n_qtiles = p.n_qtiles;
-  a.ws = reinterpret_cast<float*>(workspace);
+  a.ws = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(workspace) + kWsHeader);
   cudaStream_t s = (cudaStream_t)stream;
   if (tc_eligible(st, kv, q_heads, width) && !g_force_generic) {
     int rc = tc_attention(st, kv, q, q_tok_stride, out, out_tok_stride, slots, base_len, rows, width, q_heads, scale,
-                          p.split_tokens, p.n_splits, workspace, s);
+                          p.split_tokens, p.n_splits, a.ws, reinterpret_cast<int*>(workspace), s);
     if (rc) return rc;
     if (p.n_splits > 1) {
       const int64_t items = (int64_t)rows * width * q_heads;
@@ -567,13 +572,14 @@ extern "C" int pse_paged_attention_noalloc(pse_block_state st, pse_kv_layer kv, 
   a.split_tokens = p.split_tokens;
   a.n_splits = p.n_splits;
   a.n_qtiles = p.n_qtiles;
-  // Every (split, row, head) slot of the scratch is written before the combine
+  // The work counter at the start of the array is zeroed on the stream by every
+  // call; every (split, row, head) slot after it is written before the combine
   // reads it, so stale contents from an earlier call never leak in.
-  a.ws = reinterpret_cast<float*>(scratch);
+  a.ws = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(scratch) + kWsHeader);
   cudaStream_t s = (cudaStream_t)stream;
   if (tc_eligible(st, kv, q_heads, width)) {
     rc = tc_attention(st, kv, q, q_tok_stride, out, out_tok_stride, slots, base_len, rows, width, q_heads, scale,
-                      p.split_tokens, p.n_splits, scratch, s);
+                      p.split_tokens, p.n_splits, a.ws, reinterpret_cast<int*>(scratch), s);
     if (rc) return rc;
     if (p.n_splits > 1) {
       const int64_t items = (int64_t)rows * width * q_heads;

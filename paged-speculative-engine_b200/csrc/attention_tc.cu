@@ -38,9 +38,10 @@ constexpr int kThreads = (kConsumers + 1) * 32;
 constexpr int kTile = 64;     // tokens per pipeline stage
 constexpr uint32_t kSpinLimit = 1u << 22;
 
-// Ring depth: 4 x 16 KB stages for head_dim 64 (3 CTAs per SM), 3 x 32 KB for
-// head_dim 128 (2 CTAs per SM); either keeps >= 96 KB of K/V in flight per SM.
-__host__ __device__ constexpr int stages_for(int hd) { return hd == 64 ? 4 : 3; }
+// Ring depth: 3 x 16 KB stages for head_dim 64 (3 CTAs per SM), 2 x 32 KB for
+// head_dim 128 (2 CTAs per SM); either keeps >= 128 KB of K/V in flight per SM,
+// and the persistent CTAs never let the ring drain between work items.
+__host__ __device__ constexpr int stages_for(int hd) { return hd == 64 ? 3 : 2; }
 
 struct Args {
   const int32_t* block_table;
@@ -59,6 +60,8 @@ struct Args {
   float* ws;
   int32_t* status;
   int oob_row;  // first row index past the pool's 2-D view (zero-fill requests)
+  int n_items;  // rows * kv_heads * n_qtiles * n_splits
+  int* counter; // work counter (zeroed before the launch)
 };
 
 __device__ __forceinline__ uint32_t su32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -143,43 +146,60 @@ __device__ __forceinline__ uint32_t kv_off(int bs, int t, int d) {
                     (d & 7) * 2);
 }
 
+// One work item = (row, KV head, query tile, KV split).
+struct Item {
+  int i, hk, split, slot, base, r0, nr, k_lo, k_hi, n_tiles;
+};
+
+template <int QROWS>
+__device__ __forceinline__ Item decode_item(const Args& a, int e) {
+  Item it;
+  const int group = a.q_heads / a.kv_heads;
+  const int qtile = e % a.n_qtiles;
+  e /= a.n_qtiles;
+  it.hk = e % a.kv_heads;
+  e /= a.kv_heads;
+  it.i = e % a.rows;
+  it.split = e / a.rows;
+  it.slot = a.slots[it.i];
+  it.base = a.base_len[it.i];
+  it.r0 = qtile * QROWS;
+  it.nr = min(QROWS, group * a.width - it.r0);
+  const int w_last = (it.r0 + it.nr - 1) / group;
+  it.k_lo = it.split * a.split_tokens;
+  it.k_hi = min(it.k_lo + a.split_tokens, it.base + w_last + 1);
+  const bool ok = it.nr > 0 && it.slot >= 0 && it.slot < a.num_slots && it.base >= 0;
+  it.n_tiles = (ok && it.k_hi > it.k_lo) ? (it.k_hi - it.k_lo + kTile - 1) / kTile : 0;
+  return it;
+}
+
+constexpr int kFirst = 1, kLast = 2, kEmpty = 4, kEnd = 8;
+
 template <int HD, int MT>
 __global__ void __launch_bounds__(kThreads) attn_tc_kernel(const __grid_constant__ CUtensorMap tmk,
                                                           const __grid_constant__ CUtensorMap tmv, Args a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   constexpr int kStages = stages_for(HD);
-  constexpr int kTileBytes = kTile * HD * 2;          // one of K or V for a stage
+  constexpr int kTileBytes = kTile * HD * 2;  // one of K or V for a stage
   constexpr int kQRows = 16 * MT;
-  uint8_t* stage_k = smem;                            // [kStages][kTileBytes]
-  uint8_t* stage_v = smem + kStages * kTileBytes;     // [kStages][kTileBytes]
-  uint8_t* q_s = smem + 2 * kStages * kTileBytes;     // [kQRows x HD] swizzled
-  uint64_t* full = reinterpret_cast<uint64_t*>(q_s + kQRows * HD * 2);
+  uint8_t* stage_k = smem;                          // [kStages][kTileBytes]
+  uint8_t* stage_v = smem + kStages * kTileBytes;   // [kStages][kTileBytes]
+  uint8_t* q_s = smem + 2 * kStages * kTileBytes;   // [kQRows x HD] swizzled
+  float* mw = reinterpret_cast<float*>(q_s + kQRows * HD * 2);  // [kConsumers][16]
+  float* lw = mw + kConsumers * 16;                               // [kConsumers][16]
+  float* ow = lw + kConsumers * 16;                               // [kConsumers][16][HD]
+  uint64_t* full = reinterpret_cast<uint64_t*>(ow + kConsumers * 16 * HD);
   uint64_t* empty = full + kStages;
-  int* abort_flag = reinterpret_cast<int*>(empty + kStages);
+  int* desc_item = reinterpret_cast<int*>(empty + kStages);
+  int* desc_tile = desc_item + kStages;
+  int* desc_flags = desc_tile + kStages;
+  int* abort_flag = desc_flags + kStages;
   int* issued = abort_flag + 1;
-
-  const int group = a.q_heads / a.kv_heads;
-  const int n_qrows = group * a.width;
-  int bid = blockIdx.x;
-  const int qtile = bid % a.n_qtiles;
-  bid /= a.n_qtiles;
-  const int hk = bid % a.kv_heads;
-  const int i = bid / a.kv_heads;
-  const int split = blockIdx.y;
-  const int slot = a.slots[i];
-  const int base = a.base_len[i];
-  const int r0 = qtile * kQRows;
-  const int nr = min(kQRows, n_qrows - r0);
-  if (nr <= 0 || slot < 0 || slot >= a.num_slots || base < 0) return;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int bs = a.block_size;
-  const int w_last = (r0 + nr - 1) / group;
-  const int kmax = base + w_last + 1;
-  const int k_lo = split * a.split_tokens;
-  const int k_hi = min(k_lo + a.split_tokens, kmax);
-  const int n_tiles = k_hi > k_lo ? (k_hi - k_lo + kTile - 1) / kTile : 0;
+  const int group = a.q_heads / a.kv_heads;
 
   if (tid == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -190,190 +210,267 @@ __global__ void __launch_bounds__(kThreads) attn_tc_kernel(const __grid_constant
     *issued = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  // Query tile -> shared memory (bf16, swizzled), zero rows past nr.
-  for (int e = tid; e < kQRows * (HD / 2); e += kThreads) {
-    const int r = e / (HD / 2), d = (e % (HD / 2)) * 2;
-    uint32_t v = 0;
-    if (r < nr) {
-      const int rr = r0 + r, w = rr / group, g = rr % group;
-      v = *reinterpret_cast<const uint32_t*>(a.q + ((int64_t)i * a.width + w) * a.q_tok_stride +
-                                             (int64_t)(hk * group + g) * HD + d);
-    }
-    *reinterpret_cast<uint32_t*>(q_s + sw_off<HD>(kQRows, r, d)) = v;
-  }
   __syncthreads();
 
   if (warp == kConsumers) {
     // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      const int32_t* table = a.block_table + (int64_t)slot * a.max_blocks;
-      const int row_nb = a.nblocks[slot];
-      for (int t = 0; t < n_tiles; ++t) {
-        const int s = t % kStages;
-        if (!mbar_wait(&empty[s], ((t / kStages) & 1) ^ 1)) {
-          atomicOr(a.status, PSE_STATUS_TIMEOUT);
-          atomicExch(abort_flag, 1);
-          break;
-        }
-        *issued = t + 1;
-        mbar_expect_tx(&full[s], 2 * kTileBytes);
-        for (int p = 0; p < kTile / bs; ++p) {
-          const int tok0 = k_lo + t * kTile + p * bs;
-          const int pi = tok0 / bs;
-          int blk = -1;
-          if (tok0 < k_hi && pi < row_nb) blk = table[pi];
-          const int y = (blk >= 0 && blk < a.num_blocks) ? (blk * a.kv_heads + hk) * bs : a.oob_row;
-#pragma unroll
-          for (int c = 0; c < HD / 64; ++c) {
-            const int off = ((p * (HD / 64) + c) * bs) * 128;
-            tma_load_2d(stage_k + s * kTileBytes + off, &tmk, c * 64, y, &full[s]);
-            tma_load_2d(stage_v + s * kTileBytes + off, &tmv, c * 64, y, &full[s]);
+    // The whole warp walks the work items; lane 0 owns the barriers and issues
+    // the TMA copies.  Block-table entries are read 32 pages per coalesced warp
+    // load, one chunk ahead, so no copy waits on a dependent table read.
+    const unsigned FULL = 0xffffffffu;
+    const int ppt = kTile / bs;  // pages per tile (1, 2 or 4)
+    int t = 0;
+    bool run = true;
+    while (run) {
+      int e = 0;
+      if (lane == 0) e = atomicAdd(a.counter, 1);
+      e = __shfl_sync(FULL, e, 0);
+      if (e >= a.n_items) {
+        if (lane == 0) {
+          const int s = t % kStages;
+          if (mbar_wait(&empty[s], ((t / kStages) & 1) ^ 1)) {
+            desc_flags[s] = kEnd;
+            mbar_arrive(&full[s]);
+          } else {
+            atomicOr(a.status, PSE_STATUS_TIMEOUT);
+            atomicExch(abort_flag, 1);
           }
         }
+        break;
+      }
+      const Item it = decode_item<kQRows>(a, e);
+      if (it.n_tiles == 0) {
+        int stop = 0;
+        if (lane == 0) {
+          const int s = t % kStages;
+          if (mbar_wait(&empty[s], ((t / kStages) & 1) ^ 1)) {
+            desc_item[s] = e;
+            desc_tile[s] = 0;
+            desc_flags[s] = kFirst | kLast | kEmpty;
+            mbar_arrive(&full[s]);
+          } else {
+            atomicOr(a.status, PSE_STATUS_TIMEOUT);
+            atomicExch(abort_flag, 1);
+            stop = 1;
+          }
+        }
+        if (__shfl_sync(FULL, stop, 0)) break;
+        ++t;
+        continue;
+      }
+      const int32_t* table = a.block_table + (int64_t)it.slot * a.max_blocks;
+      const int row_nb = a.nblocks[it.slot];
+      const int page0 = it.k_lo / bs;
+      const int n_pages = it.n_tiles * ppt;
+      auto page_block = [&](int j) -> int {  // j: page index relative to page0
+        const int pi = page0 + j;
+        if (j >= n_pages || pi >= row_nb || pi * bs >= it.k_hi) return -1;
+        const int blk = table[pi];
+        return (blk >= 0 && blk < a.num_blocks) ? blk : -1;
+      };
+      int cur = page_block(lane);
+      for (int c0 = 0; c0 < n_pages && run; c0 += 32) {
+        const int nxt = page_block(c0 + 32 + lane);  // next chunk, in flight while this one is issued
+        const int tiles_here = min(32 / ppt, it.n_tiles - c0 / ppt);
+        for (int tl = 0; tl < tiles_here; ++tl) {
+          const int tt = c0 / ppt + tl;
+          int blks[4];
+#pragma unroll
+          for (int p = 0; p < 4; ++p) blks[p] = __shfl_sync(FULL, cur, (tl * ppt + p) & 31);
+          int stop = 0;
+          if (lane == 0) {
+            const int s = t % kStages;
+            if (!mbar_wait(&empty[s], ((t / kStages) & 1) ^ 1)) {
+              atomicOr(a.status, PSE_STATUS_TIMEOUT);
+              atomicExch(abort_flag, 1);
+              stop = 1;
+            } else {
+              desc_item[s] = e;
+              desc_tile[s] = tt;
+              desc_flags[s] = (tt == 0 ? kFirst : 0) | (tt == it.n_tiles - 1 ? kLast : 0);
+              *issued = t + 1;
+              mbar_expect_tx(&full[s], 2 * kTileBytes);
+#pragma unroll
+              for (int p = 0; p < 4; ++p) {
+                if (p < ppt) {
+                  const int y = blks[p] >= 0 ? (blks[p] * a.kv_heads + it.hk) * bs : a.oob_row;
+#pragma unroll
+                  for (int c = 0; c < HD / 64; ++c) {
+                    const int off = ((p * (HD / 64) + c) * bs) * 128;
+                    tma_load_2d(stage_k + s * kTileBytes + off, &tmk, c * 64, y, &full[s]);
+                    tma_load_2d(stage_v + s * kTileBytes + off, &tmv, c * 64, y, &full[s]);
+                  }
+                }
+              }
+            }
+          }
+          if (__shfl_sync(FULL, stop, 0)) {
+            run = false;
+            break;
+          }
+          ++t;
+        }
+        cur = nxt;
       }
     }
   } else {
     // ------------------------------------------------------------ consumers
-    const int mt = warp % MT;                  // this warp's 16-row m-tile
-    const int tok_base = (warp / MT) * (16 * MT);  // this warp's token slice within a tile
+    const int mt = warp % MT;                       // this warp's 16-row m-tile
+    const int tok_base = (warp / MT) * (16 * MT);   // this warp's token slice of a tile
     const int gid = lane >> 2, tid4 = lane & 3;
-    int qpos0 = -1, qpos1 = -1;
-    {
-      const int ra = mt * 16 + gid, rb = ra + 8;
-      if (ra < nr) qpos0 = base + (r0 + ra) / group;
-      if (rb < nr) qpos1 = base + (r0 + rb) / group;
-    }
-    float o[HD / 8][4];
-#pragma unroll
-    for (int n = 0; n < HD / 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
-    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
-    const uint32_t qbase = su32(q_s);
-    // ldmatrix lane -> (row, col) helpers
     const int lm = lane >> 3, lj = lane & 7;
-
-    for (int t = 0; t < n_tiles; ++t) {
+    const uint32_t qbase = su32(q_s);
+    float o[HD / 8][4];
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+    int qpos0 = -1, qpos1 = -1;
+    Item it{};
+    for (int t = 0;; ++t) {
       const int s = t % kStages;
       if (!mbar_wait(&full[s], (t / kStages) & 1)) {
         atomicOr(a.status, PSE_STATUS_TIMEOUT);
         atomicExch(abort_flag, 1);
         break;
       }
-      if (*reinterpret_cast<volatile int*>(abort_flag)) break;
-      const uint32_t kb = su32(stage_k + s * kTileBytes), vb = su32(stage_v + s * kTileBytes);
-#pragma unroll
-      for (int sub = 0; sub < MT; ++sub) {
-        const int t0 = tok_base + sub * 16;         // first token of this 16-token slice (tile-local)
-        const int tok_abs = k_lo + t * kTile + t0;  // its absolute position
-        float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-#pragma unroll
-        for (int kk = 0; kk < HD / 16; ++kk) {
-          uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
-          ldsm_x4(qbase + sw_off<HD>(16 * MT, mt * 16 + (lm & 1) * 8 + lj, kk * 16 + (lm >> 1) * 8), a0, a1, a2, a3);
-          ldsm_x4(kb + kv_off<HD>(bs, t0 + (lm >> 1) * 8 + lj, kk * 16 + (lm & 1) * 8), b0, b1, b2, b3);
-          mma16816(sc[0], a0, a1, a2, a3, b0, b1);
-          mma16816(sc[1], a0, a1, a2, a3, b2, b3);
-        }
-        // mask + online softmax (exp2 domain)
-        float mx0 = -INFINITY, mx1 = -INFINITY;
-#pragma unroll
-        for (int n = 0; n < 2; ++n) {
-#pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            const int tok = tok_abs + n * 8 + 2 * tid4 + c;
-            const bool live = tok < k_hi;
-            sc[n][c] = (live && tok <= qpos0) ? sc[n][c] * a.scale_log2 : -INFINITY;
-            sc[n][2 + c] = (live && tok <= qpos1) ? sc[n][2 + c] * a.scale_log2 : -INFINITY;
-            mx0 = fmaxf(mx0, sc[n][c]);
-            mx1 = fmaxf(mx1, sc[n][2 + c]);
+      const int flags = desc_flags[s];
+      if (flags & kEnd) break;
+      if (flags & kFirst) {
+        it = decode_item<kQRows>(a, desc_item[s]);
+        // every consumer warp is done with the previous item (its Q and merge area)
+        asm volatile("bar.sync 1, %0;" ::"r"(kConsumers * 32));
+        if (!(flags & kEmpty)) {
+          for (int e = tid; e < kQRows * (HD / 2); e += kConsumers * 32) {
+            const int r = e / (HD / 2), d = (e % (HD / 2)) * 2;
+            uint32_t v = 0;
+            if (r < it.nr) {
+              const int rr = it.r0 + r, w = rr / group, g = rr % group;
+              v = *reinterpret_cast<const uint32_t*>(a.q + ((int64_t)it.i * a.width + w) * a.q_tok_stride +
+                                                     (int64_t)(it.hk * group + g) * HD + d);
+            }
+            *reinterpret_cast<uint32_t*>(q_s + sw_off<HD>(kQRows, r, d)) = v;
           }
         }
-        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
-        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
-        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
-        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-        const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
-        const float ms0 = mn0 == -INFINITY ? 0.f : mn0, ms1 = mn1 == -INFINITY ? 0.f : mn1;
-        const float c0 = exp2f(m0 - ms0), c1 = exp2f(m1 - ms1);
-        m0 = mn0;
-        m1 = mn1;
-        float p[2][4];
+        asm volatile("bar.sync 1, %0;" ::"r"(kConsumers * 32));
 #pragma unroll
-        for (int n = 0; n < 2; ++n) {
-          p[n][0] = exp2f(sc[n][0] - ms0);
-          p[n][1] = exp2f(sc[n][1] - ms0);
-          p[n][2] = exp2f(sc[n][2] - ms1);
-          p[n][3] = exp2f(sc[n][3] - ms1);
-        }
-        l0 = l0 * c0 + p[0][0] + p[0][1] + p[1][0] + p[1][1];
-        l1 = l1 * c1 + p[0][2] + p[0][3] + p[1][2] + p[1][3];
+        for (int n = 0; n < HD / 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+        m0 = m1 = -INFINITY;
+        l0 = l1 = 0.f;
+        const int ra = mt * 16 + gid, rb = ra + 8;
+        qpos0 = ra < it.nr ? it.base + (it.r0 + ra) / group : -1;
+        qpos1 = rb < it.nr ? it.base + (it.r0 + rb) / group : -1;
+      }
+      if (!(flags & kEmpty)) {
+        const int tt = desc_tile[s];
+        const uint32_t kb = su32(stage_k + s * kTileBytes), vb = su32(stage_v + s * kTileBytes);
 #pragma unroll
-        for (int n = 0; n < HD / 8; ++n) {
-          o[n][0] *= c0;
-          o[n][1] *= c0;
-          o[n][2] *= c1;
-          o[n][3] *= c1;
-        }
-        const uint32_t pa0 = pack_bf16(p[0][0], p[0][1]), pa1 = pack_bf16(p[0][2], p[0][3]);
-        const uint32_t pa2 = pack_bf16(p[1][0], p[1][1]), pa3 = pack_bf16(p[1][2], p[1][3]);
+        for (int sub = 0; sub < MT; ++sub) {
+          const int t0 = tok_base + sub * 16;
+          const int tok_abs = it.k_lo + tt * kTile + t0;
+          float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
-        for (int n2 = 0; n2 < HD / 16; ++n2) {
-          uint32_t b0, b1, b2, b3;
-          ldsm_x4_t(vb + kv_off<HD>(bs, t0 + (lm & 1) * 8 + lj, n2 * 16 + (lm >> 1) * 8), b0, b1, b2, b3);
-          mma16816(o[2 * n2], pa0, pa1, pa2, pa3, b0, b1);
-          mma16816(o[2 * n2 + 1], pa0, pa1, pa2, pa3, b2, b3);
+          for (int kk = 0; kk < HD / 16; ++kk) {
+            uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
+            ldsm_x4(qbase + sw_off<HD>(kQRows, mt * 16 + (lm & 1) * 8 + lj, kk * 16 + (lm >> 1) * 8), a0, a1, a2,
+                    a3);
+            ldsm_x4(kb + kv_off<HD>(bs, t0 + (lm >> 1) * 8 + lj, kk * 16 + (lm & 1) * 8), b0, b1, b2, b3);
+            mma16816(sc[0], a0, a1, a2, a3, b0, b1);
+            mma16816(sc[1], a0, a1, a2, a3, b2, b3);
+          }
+          float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+          for (int n = 0; n < 2; ++n) {
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+              const int tok = tok_abs + n * 8 + 2 * tid4 + c;
+              const bool live = tok < it.k_hi;
+              sc[n][c] = (live && tok <= qpos0) ? sc[n][c] * a.scale_log2 : -INFINITY;
+              sc[n][2 + c] = (live && tok <= qpos1) ? sc[n][2 + c] * a.scale_log2 : -INFINITY;
+              mx0 = fmaxf(mx0, sc[n][c]);
+              mx1 = fmaxf(mx1, sc[n][2 + c]);
+            }
+          }
+          mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+          mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+          mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+          mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+          const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+          const float ms0 = mn0 == -INFINITY ? 0.f : mn0, ms1 = mn1 == -INFINITY ? 0.f : mn1;
+          const float c0 = exp2f(m0 - ms0), c1 = exp2f(m1 - ms1);
+          m0 = mn0;
+          m1 = mn1;
+          float p[2][4];
+#pragma unroll
+          for (int n = 0; n < 2; ++n) {
+            p[n][0] = exp2f(sc[n][0] - ms0);
+            p[n][1] = exp2f(sc[n][1] - ms0);
+            p[n][2] = exp2f(sc[n][2] - ms1);
+            p[n][3] = exp2f(sc[n][3] - ms1);
+          }
+          l0 = l0 * c0 + p[0][0] + p[0][1] + p[1][0] + p[1][1];
+          l1 = l1 * c1 + p[0][2] + p[0][3] + p[1][2] + p[1][3];
+#pragma unroll
+          for (int n = 0; n < HD / 8; ++n) {
+            o[n][0] *= c0;
+            o[n][1] *= c0;
+            o[n][2] *= c1;
+            o[n][3] *= c1;
+          }
+          const uint32_t pa0 = pack_bf16(p[0][0], p[0][1]), pa1 = pack_bf16(p[0][2], p[0][3]);
+          const uint32_t pa2 = pack_bf16(p[1][0], p[1][1]), pa3 = pack_bf16(p[1][2], p[1][3]);
+#pragma unroll
+          for (int n2 = 0; n2 < HD / 16; ++n2) {
+            uint32_t b0, b1, b2, b3;
+            ldsm_x4_t(vb + kv_off<HD>(bs, t0 + (lm & 1) * 8 + lj, n2 * 16 + (lm >> 1) * 8), b0, b1, b2, b3);
+            mma16816(o[2 * n2], pa0, pa1, pa2, pa3, b0, b1);
+            mma16816(o[2 * n2 + 1], pa0, pa1, pa2, pa3, b2, b3);
+          }
         }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
-    }
-    // quad-reduce the row sums
-    l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
-    l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
-    l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
-    l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
-    // park this warp's partial state for the merge (stage area is free now)
-    __syncwarp();
-    asm volatile("bar.sync 1, %0;" ::"r"(kConsumers * 32));
-    float* mw = reinterpret_cast<float*>(stage_k);           // [kConsumers][16]
-    float* lw = mw + kConsumers * 16;                         // [kConsumers][16]
-    float* ow = lw + kConsumers * 16;                         // [kConsumers][16][HD]
-    if (tid4 == 0) {
-      mw[warp * 16 + gid] = m0;
-      mw[warp * 16 + gid + 8] = m1;
-      lw[warp * 16 + gid] = l0;
-      lw[warp * 16 + gid + 8] = l1;
-    }
+      if (flags & kLast) {
+        // merge the warps' partial (max, sum, O) of this item and write it out
+        float L0 = l0 + __shfl_xor_sync(0xffffffffu, l0, 1);
+        L0 += __shfl_xor_sync(0xffffffffu, L0, 2);
+        float L1 = l1 + __shfl_xor_sync(0xffffffffu, l1, 1);
+        L1 += __shfl_xor_sync(0xffffffffu, L1, 2);
+        if (tid4 == 0) {
+          mw[warp * 16 + gid] = m0;
+          mw[warp * 16 + gid + 8] = m1;
+          lw[warp * 16 + gid] = L0;
+          lw[warp * 16 + gid + 8] = L1;
+        }
 #pragma unroll
-    for (int n = 0; n < HD / 8; ++n) {
-      const int d = n * 8 + 2 * tid4;
-      ow[(warp * 16 + gid) * HD + d] = o[n][0];
-      ow[(warp * 16 + gid) * HD + d + 1] = o[n][1];
-      ow[(warp * 16 + gid + 8) * HD + d] = o[n][2];
-      ow[(warp * 16 + gid + 8) * HD + d + 1] = o[n][3];
-    }
-    asm volatile("bar.sync 1, %0;" ::"r"(kConsumers * 32));
-    // combine: warps w with w % MT == mt cover m-tile mt
-    for (int e = tid; e < nr * HD; e += kConsumers * 32) {
-      const int r = e / HD, d = e % HD;
-      const int mtr = r / 16, rl = r % 16;
-      float M = -INFINITY;
-      for (int w2 = mtr; w2 < kConsumers; w2 += MT) M = fmaxf(M, mw[w2 * 16 + rl]);
-      float L = 0.f, acc = 0.f;
-      for (int w2 = mtr; w2 < kConsumers; w2 += MT) {
-        const float f = M == -INFINITY ? 0.f : exp2f(mw[w2 * 16 + rl] - M);
-        L += lw[w2 * 16 + rl] * f;
-        acc += ow[(w2 * 16 + rl) * HD + d] * f;
-      }
-      const int rr = r0 + r, w = rr / group, g = rr % group, h = hk * group + g;
-      const int64_t tokrow = (int64_t)i * a.width + w;
-      if (a.n_splits == 1) {
-        a.out[tokrow * a.out_tok_stride + (int64_t)h * HD + d] = __float2bfloat16_rn(L > 0.f ? acc / L : 0.f);
-      } else {
-        float* ws = a.ws + (((int64_t)split * a.rows * a.width + tokrow) * a.q_heads + h) * (HD + 2);
-        ws[d] = acc;
-        if (d == 0) {
-          ws[HD] = M == -INFINITY ? -INFINITY : M * 0.69314718055994531f;  // natural-log units
-          ws[HD + 1] = L;
+        for (int n = 0; n < HD / 8; ++n) {
+          const int d = n * 8 + 2 * tid4;
+          ow[(warp * 16 + gid) * HD + d] = o[n][0];
+          ow[(warp * 16 + gid) * HD + d + 1] = o[n][1];
+          ow[(warp * 16 + gid + 8) * HD + d] = o[n][2];
+          ow[(warp * 16 + gid + 8) * HD + d + 1] = o[n][3];
+        }
+        asm volatile("bar.sync 1, %0;" ::"r"(kConsumers * 32));
+        for (int e = tid; e < it.nr * HD; e += kConsumers * 32) {
+          const int r = e / HD, d = e % HD;
+          const int mtr = r / 16, rl = r % 16;
+          float M = -INFINITY;
+          for (int w2 = mtr; w2 < kConsumers; w2 += MT) M = fmaxf(M, mw[w2 * 16 + rl]);
+          float L = 0.f, acc = 0.f;
+          for (int w2 = mtr; w2 < kConsumers; w2 += MT) {
+            const float f = M == -INFINITY ? 0.f : exp2f(mw[w2 * 16 + rl] - M);
+            L += lw[w2 * 16 + rl] * f;
+            acc += ow[(w2 * 16 + rl) * HD + d] * f;
+          }
+          const int rr = it.r0 + r, w = rr / group, g = rr % group, h = it.hk * group + g;
+          const int64_t tokrow = (int64_t)it.i * a.width + w;
+          if (a.n_splits == 1) {
+            a.out[tokrow * a.out_tok_stride + (int64_t)h * HD + d] = __float2bfloat16_rn(L > 0.f ? acc / L : 0.f);
+          } else {
+            float* ws = a.ws + (((int64_t)it.split * a.rows * a.width + tokrow) * a.q_heads + h) * (HD + 2);
+            ws[d] = acc;
+            if (d == 0) {
+              ws[HD] = M == -INFINITY ? -INFINITY : M * 0.69314718055994531f;  // natural-log units
+              ws[HD + 1] = L;
+            }
+          }
         }
       }
     }
@@ -432,9 +529,13 @@ int tensor_map(const void* pool, int num_blocks, int kv_heads, int bs, int hd, C
 
 template <int HD>
 constexpr size_t smem_bytes(int mt) {
-  return 1024 + 2 * stages_for(HD) * (size_t)kTile * HD * 2 + (size_t)16 * mt * HD * 2 + 2 * stages_for(HD) * 8 + 16;
+  return 1024 + 2 * stages_for(HD) * (size_t)kTile * HD * 2 + (size_t)16 * mt * HD * 2 +
+         (size_t)(2 * kConsumers * 16 + kConsumers * 16 * HD) * 4 + 2 * stages_for(HD) * 8 + 3 * stages_for(HD) * 4 +
+         16;
 }
 
+// Persistent launch: as many CTAs as fit on the GPU at once (never more than
+// work items); each pulls items from the work counter until it runs dry.
 template <int HD, int MT>
 int launch(const CUtensorMap& mk, const CUtensorMap& mv, const Args& a, cudaStream_t s) {
   auto kern = attn_tc_kernel<HD, MT>;
@@ -442,7 +543,19 @@ int launch(const CUtensorMap& mk, const CUtensorMap& mv, const Args& a, cudaStre
   static_assert(smem <= 227 * 1024, "shared memory budget");
   static const cudaError_t opt = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (opt != cudaSuccess) return (int)opt;
-  dim3 grid((unsigned)(a.rows * a.kv_heads * a.n_qtiles), (unsigned)a.n_splits);
+  static int per_sm = 0;
+  if (per_sm == 0) {
+    int n = 0;
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kThreads, smem);
+    if (e != cudaSuccess) return (int)e;
+    per_sm = n > 0 ? n : 1;
+  }
+  int sms = kNumSMs;
+  int dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int grid = a.n_items < per_sm * sms ? a.n_items : per_sm * sms;
+  cudaError_t e = cudaMemsetAsync(a.counter, 0, sizeof(int), s);
+  if (e != cudaSuccess) return (int)e;
   kern<<<grid, kThreads, smem, s>>>(mk, mv, a);
   PSE_LAUNCH_CHECK();
   return PSE_OK;
@@ -464,7 +577,7 @@ bool tc_eligible(const pse_block_state& st, const pse_kv_layer& kv, int q_heads,
 
 int tc_attention(const pse_block_state& st, const pse_kv_layer& kv, const void* q, int64_t q_tok_stride, void* out,
                  int64_t out_tok_stride, const int32_t* slots, const int32_t* base_len, int rows, int width,
-                 int q_heads, float scale, int split_tokens, int n_splits, void* ws, cudaStream_t s) {
+                 int q_heads, float scale, int split_tokens, int n_splits, void* ws, int* counter, cudaStream_t s) {
   const int n_qrows = (q_heads / kv.kv_heads) * width;
   const int MT = n_qrows <= 16 ? 1 : 2;
   tc::Args a;
@@ -492,6 +605,9 @@ int tc_attention(const pse_block_state& st, const pse_kv_layer& kv, const void* 
   a.ws = reinterpret_cast<float*>(ws);
   a.status = st.status;
   a.oob_row = st.num_blocks * kv.kv_heads * st.block_size;
+  a.n_items = rows * kv.kv_heads * a.n_qtiles * n_splits;
+  a.counter = counter;
+  if (!counter) return PSE_EINVAL;
   CUtensorMap mk, mv;
   int rc = tc::tensor_map(kv.k_pool, st.num_blocks, kv.kv_heads, st.block_size, kv.head_dim, &mk);
   if (rc) return rc;
