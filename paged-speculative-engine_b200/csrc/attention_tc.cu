@@ -176,7 +176,7 @@ __device__ __forceinline__ Item decode_item(const Args& a, int e) {
 constexpr int kFirst = 1, kLast = 2, kEmpty = 4, kEnd = 8;
 
 template <int HD, int MT>
-__global__ void __launch_bounds__(kThreads) attn_tc_kernel(const __grid_constant__ CUtensorMap tmk,
+__global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2) attn_tc_kernel(const __grid_constant__ CUtensorMap tmk,
                                                           const __grid_constant__ CUtensorMap tmv, Args a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -216,61 +216,73 @@ __global__ void __launch_bounds__(kThreads) attn_tc_kernel(const __grid_constant
     // ------------------------------------------------------------ producer
     // The whole warp walks the work items; lane 0 owns the barriers and issues
     // the TMA copies.  Block-table entries are read 32 pages per coalesced warp
-    // load, one chunk ahead, so no copy waits on a dependent table read.
+    // load, one chunk ahead, and the next work item is claimed, decoded and its
+    // first table chunk fetched while the current item's last chunk is being
+    // issued, so no copy ever waits on a dependent global read.
     const unsigned FULL = 0xffffffffu;
     const int ppt = kTile / bs;  // pages per tile (1, 2 or 4)
-    int t = 0;
-    bool run = true;
-    while (run) {
+    auto claim = [&]() -> int {
       int e = 0;
       if (lane == 0) e = atomicAdd(a.counter, 1);
-      e = __shfl_sync(FULL, e, 0);
-      if (e >= a.n_items) {
-        if (lane == 0) {
-          const int s = t % kStages;
-          if (mbar_wait(&empty[s], ((t / kStages) & 1) ^ 1)) {
-            desc_flags[s] = kEnd;
-            mbar_arrive(&full[s]);
-          } else {
-            atomicOr(a.status, PSE_STATUS_TIMEOUT);
-            atomicExch(abort_flag, 1);
-          }
-        }
-        break;
-      }
-      const Item it = decode_item<kQRows>(a, e);
+      return __shfl_sync(FULL, e, 0);
+    };
+    auto page_block = [&](const Item& it, int j) -> int {  // j: page index within the item
+      if (j >= it.n_tiles * ppt) return -1;
+      const int pi = it.k_lo / bs + j;
+      if (pi >= a.nblocks[it.slot] || pi * bs >= it.k_hi) return -1;
+      const int blk = a.block_table[(int64_t)it.slot * a.max_blocks + pi];
+      return (blk >= 0 && blk < a.num_blocks) ? blk : -1;
+    };
+    // lane 0: acquire stage s for tile t (bounded); returns false on timeout
+    auto acquire = [&](int tt_global) -> bool {
+      if (mbar_wait(&empty[tt_global % kStages], ((tt_global / kStages) & 1) ^ 1)) return true;
+      atomicOr(a.status, PSE_STATUS_TIMEOUT);
+      atomicExch(abort_flag, 1);
+      return false;
+    };
+    int t = 0;
+    int e = claim();
+    Item it{};
+    int cur = -1;
+    if (e < a.n_items) {
+      it = decode_item<kQRows>(a, e);
+      cur = page_block(it, lane);
+    }
+    bool run = true;
+    while (run && e < a.n_items) {
+      const int e_next = claim();
+      Item it_next{};
+      int cur_next = -1;
+      bool next_ready = false;
       if (it.n_tiles == 0) {
         int stop = 0;
         if (lane == 0) {
-          const int s = t % kStages;
-          if (mbar_wait(&empty[s], ((t / kStages) & 1) ^ 1)) {
+          if (acquire(t)) {
+            const int s = t % kStages;
             desc_item[s] = e;
             desc_tile[s] = 0;
             desc_flags[s] = kFirst | kLast | kEmpty;
             mbar_arrive(&full[s]);
           } else {
-            atomicOr(a.status, PSE_STATUS_TIMEOUT);
-            atomicExch(abort_flag, 1);
             stop = 1;
           }
         }
         if (__shfl_sync(FULL, stop, 0)) break;
         ++t;
-        continue;
       }
-      const int32_t* table = a.block_table + (int64_t)it.slot * a.max_blocks;
-      const int row_nb = a.nblocks[it.slot];
-      const int page0 = it.k_lo / bs;
       const int n_pages = it.n_tiles * ppt;
-      auto page_block = [&](int j) -> int {  // j: page index relative to page0
-        const int pi = page0 + j;
-        if (j >= n_pages || pi >= row_nb || pi * bs >= it.k_hi) return -1;
-        const int blk = table[pi];
-        return (blk >= 0 && blk < a.num_blocks) ? blk : -1;
-      };
-      int cur = page_block(lane);
-      for (int c0 = 0; c0 < n_pages && run; c0 += 32) {
-        const int nxt = page_block(c0 + 32 + lane);  // next chunk, in flight while this one is issued
+      for (int c0 = 0; c0 < n_pages; c0 += 32) {
+        int nxt;
+        if (c0 + 32 < n_pages) {
+          nxt = page_block(it, c0 + 32 + lane);
+        } else {
+          if (e_next < a.n_items) {
+            it_next = decode_item<kQRows>(a, e_next);
+            cur_next = page_block(it_next, lane);
+          }
+          next_ready = true;
+          nxt = -1;
+        }
         const int tiles_here = min(32 / ppt, it.n_tiles - c0 / ppt);
         for (int tl = 0; tl < tiles_here; ++tl) {
           const int tt = c0 / ppt + tl;
@@ -279,12 +291,10 @@ __global__ void __launch_bounds__(kThreads) attn_tc_kernel(const __grid_constant
           for (int p = 0; p < 4; ++p) blks[p] = __shfl_sync(FULL, cur, (tl * ppt + p) & 31);
           int stop = 0;
           if (lane == 0) {
-            const int s = t % kStages;
-            if (!mbar_wait(&empty[s], ((t / kStages) & 1) ^ 1)) {
-              atomicOr(a.status, PSE_STATUS_TIMEOUT);
-              atomicExch(abort_flag, 1);
+            if (!acquire(t)) {
               stop = 1;
             } else {
+              const int s = t % kStages;
               desc_item[s] = e;
               desc_tile[s] = tt;
               desc_flags[s] = (tt == 0 ? kFirst : 0) | (tt == it.n_tiles - 1 ? kLast : 0);
@@ -310,7 +320,22 @@ __global__ void __launch_bounds__(kThreads) attn_tc_kernel(const __grid_constant
           }
           ++t;
         }
+        if (!run) break;
         cur = nxt;
+      }
+      if (!run) break;
+      if (!next_ready && e_next < a.n_items) {
+        it_next = decode_item<kQRows>(a, e_next);
+        cur_next = page_block(it_next, lane);
+      }
+      e = e_next;
+      it = it_next;
+      cur = cur_next;
+    }
+    if (run && lane == 0) {
+      if (acquire(t)) {
+        desc_flags[t % kStages] = kEnd;
+        mbar_arrive(&full[t % kStages]);
       }
     }
   } else {
@@ -319,10 +344,22 @@ __global__ void __launch_bounds__(kThreads) attn_tc_kernel(const __grid_constant
     const int tok_base = (warp / MT) * (16 * MT);   // this warp's token slice of a tile
     const int gid = lane >> 2, tid4 = lane & 3;
     const int lm = lane >> 3, lj = lane & 7;
-    const uint32_t qbase = su32(q_s);
+    // ldmatrix source offsets are fixed for the whole kernel (block size and
+    // the warp's token slice never change): compute them once.
+    uint32_t q_off[HD / 16], k_off[MT][HD / 16], v_off[MT][HD / 16];
+#pragma unroll
+    for (int kk = 0; kk < HD / 16; ++kk) {
+      q_off[kk] = su32(q_s) + sw_off<HD>(kQRows, mt * 16 + (lm & 1) * 8 + lj, kk * 16 + (lm >> 1) * 8);
+#pragma unroll
+      for (int sub = 0; sub < MT; ++sub) {
+        const int t0 = tok_base + sub * 16;
+        k_off[sub][kk] = kv_off<HD>(bs, t0 + (lm >> 1) * 8 + lj, kk * 16 + (lm & 1) * 8);
+        v_off[sub][kk] = kv_off<HD>(bs, t0 + (lm & 1) * 8 + lj, kk * 16 + (lm >> 1) * 8);
+      }
+    }
     float o[HD / 8][4];
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
-    int qpos0 = -1, qpos1 = -1;
+    int qpos0 = -1, qpos1 = -1, qpos_min = -1;
     Item it{};
     for (int t = 0;; ++t) {
       const int s = t % kStages;
@@ -357,35 +394,50 @@ __global__ void __launch_bounds__(kThreads) attn_tc_kernel(const __grid_constant
         const int ra = mt * 16 + gid, rb = ra + 8;
         qpos0 = ra < it.nr ? it.base + (it.r0 + ra) / group : -1;
         qpos1 = rb < it.nr ? it.base + (it.r0 + rb) / group : -1;
+        // smallest causal limit over this m-tile's valid rows: tokens at or
+        // below it are visible to every row of the tile
+        const int nr_mt = min(16, it.nr - mt * 16);
+        qpos_min = nr_mt > 0 ? it.base + (it.r0 + mt * 16) / group : -1;
       }
       if (!(flags & kEmpty)) {
         const int tt = desc_tile[s];
         const uint32_t kb = su32(stage_k + s * kTileBytes), vb = su32(stage_v + s * kTileBytes);
 #pragma unroll
         for (int sub = 0; sub < MT; ++sub) {
-          const int t0 = tok_base + sub * 16;
-          const int tok_abs = it.k_lo + tt * kTile + t0;
+          const int tok_abs = it.k_lo + tt * kTile + tok_base + sub * 16;
           float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
           for (int kk = 0; kk < HD / 16; ++kk) {
             uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
-            ldsm_x4(qbase + sw_off<HD>(kQRows, mt * 16 + (lm & 1) * 8 + lj, kk * 16 + (lm >> 1) * 8), a0, a1, a2,
-                    a3);
-            ldsm_x4(kb + kv_off<HD>(bs, t0 + (lm >> 1) * 8 + lj, kk * 16 + (lm & 1) * 8), b0, b1, b2, b3);
+            ldsm_x4(q_off[kk], a0, a1, a2, a3);
+            ldsm_x4(kb + k_off[sub][kk], b0, b1, b2, b3);
             mma16816(sc[0], a0, a1, a2, a3, b0, b1);
             mma16816(sc[1], a0, a1, a2, a3, b2, b3);
           }
+          // Masking only where the slice reaches past the row end or the causal
+          // limit of some row; interior slices just scale.
+          const bool interior = tok_abs + 15 < it.k_hi && tok_abs + 15 <= qpos_min;
           float mx0 = -INFINITY, mx1 = -INFINITY;
+          if (interior) {
 #pragma unroll
-          for (int n = 0; n < 2; ++n) {
+            for (int n = 0; n < 2; ++n) {
 #pragma unroll
-            for (int c = 0; c < 2; ++c) {
-              const int tok = tok_abs + n * 8 + 2 * tid4 + c;
-              const bool live = tok < it.k_hi;
-              sc[n][c] = (live && tok <= qpos0) ? sc[n][c] * a.scale_log2 : -INFINITY;
-              sc[n][2 + c] = (live && tok <= qpos1) ? sc[n][2 + c] * a.scale_log2 : -INFINITY;
-              mx0 = fmaxf(mx0, sc[n][c]);
-              mx1 = fmaxf(mx1, sc[n][2 + c]);
+              for (int c = 0; c < 4; ++c) sc[n][c] *= a.scale_log2;
+              mx0 = fmaxf(mx0, fmaxf(sc[n][0], sc[n][1]));
+              mx1 = fmaxf(mx1, fmaxf(sc[n][2], sc[n][3]));
+            }
+          } else {
+#pragma unroll
+            for (int n = 0; n < 2; ++n) {
+#pragma unroll
+              for (int c = 0; c < 2; ++c) {
+                const int tok = tok_abs + n * 8 + 2 * tid4 + c;
+                const bool live = tok < it.k_hi;
+                sc[n][c] = (live && tok <= qpos0) ? sc[n][c] * a.scale_log2 : -INFINITY;
+                sc[n][2 + c] = (live && tok <= qpos1) ? sc[n][2 + c] * a.scale_log2 : -INFINITY;
+                mx0 = fmaxf(mx0, sc[n][c]);
+                mx1 = fmaxf(mx1, sc[n][2 + c]);
+              }
             }
           }
           mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
@@ -394,7 +446,19 @@ __global__ void __launch_bounds__(kThreads) attn_tc_kernel(const __grid_constant
           mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
           const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
           const float ms0 = mn0 == -INFINITY ? 0.f : mn0, ms1 = mn1 == -INFINITY ? 0.f : mn1;
-          const float c0 = exp2f(m0 - ms0), c1 = exp2f(m1 - ms1);
+          // rescale the running output only when some row's maximum moved
+          if (__any_sync(0xffffffffu, mn0 != m0 || mn1 != m1)) {
+            const float c0 = exp2f(m0 - ms0), c1 = exp2f(m1 - ms1);
+            l0 *= c0;
+            l1 *= c1;
+#pragma unroll
+            for (int n = 0; n < HD / 8; ++n) {
+              o[n][0] *= c0;
+              o[n][1] *= c0;
+              o[n][2] *= c1;
+              o[n][3] *= c1;
+            }
+          }
           m0 = mn0;
           m1 = mn1;
           float p[2][4];
@@ -405,21 +469,14 @@ __global__ void __launch_bounds__(kThreads) attn_tc_kernel(const __grid_constant
             p[n][2] = exp2f(sc[n][2] - ms1);
             p[n][3] = exp2f(sc[n][3] - ms1);
           }
-          l0 = l0 * c0 + p[0][0] + p[0][1] + p[1][0] + p[1][1];
-          l1 = l1 * c1 + p[0][2] + p[0][3] + p[1][2] + p[1][3];
-#pragma unroll
-          for (int n = 0; n < HD / 8; ++n) {
-            o[n][0] *= c0;
-            o[n][1] *= c0;
-            o[n][2] *= c1;
-            o[n][3] *= c1;
-          }
+          l0 += p[0][0] + p[0][1] + p[1][0] + p[1][1];
+          l1 += p[0][2] + p[0][3] + p[1][2] + p[1][3];
           const uint32_t pa0 = pack_bf16(p[0][0], p[0][1]), pa1 = pack_bf16(p[0][2], p[0][3]);
           const uint32_t pa2 = pack_bf16(p[1][0], p[1][1]), pa3 = pack_bf16(p[1][2], p[1][3]);
 #pragma unroll
           for (int n2 = 0; n2 < HD / 16; ++n2) {
             uint32_t b0, b1, b2, b3;
-            ldsm_x4_t(vb + kv_off<HD>(bs, t0 + (lm & 1) * 8 + lj, n2 * 16 + (lm >> 1) * 8), b0, b1, b2, b3);
+            ldsm_x4_t(vb + v_off[sub][n2], b0, b1, b2, b3);
             mma16816(o[2 * n2], pa0, pa1, pa2, pa3, b0, b1);
             mma16816(o[2 * n2 + 1], pa0, pa1, pa2, pa3, b2, b3);
           }
