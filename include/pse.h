@@ -223,6 +223,15 @@ int pse_norm(const float *x, int64_t ldx, const void *gamma, const void *beta, i
              int32_t n_rows, int32_t d, float eps, int32_t rms, void *out, int64_t ldo,
              int32_t out_dtype, void *stream);
 
+/* Residual add fused with the next norm (engine/model.py:139-142 then
+ * :124-126 / :155), one warp per row: if y != NULL, x[r] += y[r] (+ bias),
+ * written back to x (fp32); then out[r] = LayerNorm(x[r]) (rms == 0; eps,
+ * biased variance, gamma / beta) or RMSNorm (rms != 0).  d <= 4096; y, the
+ * norm parameters and out share one dtype (y_dtype == param_dtype == out_dtype). */
+int pse_add_norm(float *x, int64_t ldx, const void *y, int64_t ldy, const void *bias, int32_t y_dtype,
+                 const void *gamma, const void *beta, int32_t param_dtype, int32_t n_rows, int32_t d, float eps,
+                 int32_t rms, void *out, int64_t ldo, int32_t out_dtype, void *stream);
+
 /* Elementwise epilogues on [n_rows, n] row-major data:
  * op 0: y = gelu(y + bias)            (engine/model.py:127-129, exact erf GELU)
  * op 1: x(fp32) += y + bias           (residual add, engine/model.py:140-141)

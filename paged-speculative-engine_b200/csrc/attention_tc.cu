@@ -33,15 +33,31 @@
 namespace pse {
 namespace tc {
 
-constexpr int kConsumers = 4;
+#ifndef PSE_TC_CONSUMERS
+#define PSE_TC_CONSUMERS 4
+#endif
+#ifndef PSE_TC_STAGES64
+#define PSE_TC_STAGES64 2
+#endif
+#ifndef PSE_TC_STAGES128
+#define PSE_TC_STAGES128 2
+#endif
+#ifndef PSE_TC_MINB64
+#define PSE_TC_MINB64 4
+#endif
+#ifndef PSE_TC_MINB128
+#define PSE_TC_MINB128 2
+#endif
+
+constexpr int kConsumers = PSE_TC_CONSUMERS;
 constexpr int kThreads = (kConsumers + 1) * 32;
-constexpr int kTile = 64;     // tokens per pipeline stage
+constexpr int kTile = 16 * kConsumers;  // tokens per pipeline stage (16 per consumer warp)
 constexpr uint32_t kSpinLimit = 1u << 22;
 
-// Ring depth: 3 x 16 KB stages for head_dim 64 (3 CTAs per SM), 2 x 32 KB for
+// Ring depth: 2 x 16 KB stages for head_dim 64 (4 CTAs per SM), 2 x 32 KB for
 // head_dim 128 (2 CTAs per SM); either keeps >= 128 KB of K/V in flight per SM,
 // and the persistent CTAs never let the ring drain between work items.
-__host__ __device__ constexpr int stages_for(int hd) { return hd == 64 ? 3 : 2; }
+__host__ __device__ constexpr int stages_for(int hd) { return hd == 64 ? PSE_TC_STAGES64 : PSE_TC_STAGES128; }
 
 struct Args {
   const int32_t* block_table;
@@ -176,7 +192,7 @@ __device__ __forceinline__ Item decode_item(const Args& a, int e) {
 constexpr int kFirst = 1, kLast = 2, kEmpty = 4, kEnd = 8;
 
 template <int HD, int MT>
-__global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2) attn_tc_kernel(const __grid_constant__ CUtensorMap tmk,
+__global__ void __launch_bounds__(kThreads, HD == 64 ? PSE_TC_MINB64 : PSE_TC_MINB128) attn_tc_kernel(const __grid_constant__ CUtensorMap tmk,
                                                           const __grid_constant__ CUtensorMap tmv, Args a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -220,7 +236,7 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2) attn_tc_kernel(con
     // first table chunk fetched while the current item's last chunk is being
     // issued, so no copy ever waits on a dependent global read.
     const unsigned FULL = 0xffffffffu;
-    const int ppt = kTile / bs;  // pages per tile (1, 2 or 4)
+    const int ppt = kTile / bs;  // pages per tile
     auto claim = [&]() -> int {
       int e = 0;
       if (lane == 0) e = atomicAdd(a.counter, 1);
@@ -286,9 +302,9 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2) attn_tc_kernel(con
         const int tiles_here = min(32 / ppt, it.n_tiles - c0 / ppt);
         for (int tl = 0; tl < tiles_here; ++tl) {
           const int tt = c0 / ppt + tl;
-          int blks[4];
+          int blks[kTile / 16];
 #pragma unroll
-          for (int p = 0; p < 4; ++p) blks[p] = __shfl_sync(FULL, cur, (tl * ppt + p) & 31);
+          for (int p = 0; p < kTile / 16; ++p) blks[p] = __shfl_sync(FULL, cur, (tl * ppt + p) & 31);
           int stop = 0;
           if (lane == 0) {
             if (!acquire(t)) {
@@ -301,7 +317,7 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2) attn_tc_kernel(con
               *issued = t + 1;
               mbar_expect_tx(&full[s], 2 * kTileBytes);
 #pragma unroll
-              for (int p = 0; p < 4; ++p) {
+              for (int p = 0; p < kTile / 16; ++p) {
                 if (p < ppt) {
                   const int y = blks[p] >= 0 ? (blks[p] * a.kv_heads + it.hk) * bs : a.oob_row;
 #pragma unroll

@@ -64,6 +64,92 @@ __global__ void __launch_bounds__(THREADS) norm_kernel(const float* x, int64_t l
   }
 }
 
+// Residual add fused with the following norm, one warp per row (the row
+// lives in registers; no block-wide synchronisation):
+//   if y:  x[r] += y[r] (+ bias)      (engine/model.py:140-141)
+//   out[r] = LayerNorm(x[r]) or RMSNorm(x[r])   (engine/model.py:124-126, 155)
+
+// One CTA per row, the row spread over the CTA's threads (<= 8 elements each,
+// held in registers): enough warps per row keep every load of the row in
+// flight at once.  Loads, math and stores are separate phases; the residual
+// row is written back only after all reads.
+template <int THREADS>
+__device__ __forceinline__ float cta_sum(float v, float* sh) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  v = warp_sum(v);
+  if (lane == 0) sh[warp] = v;
+  __syncthreads();
+  float t = 0.f;
+#pragma unroll
+  for (int w = 0; w < THREADS / 32; ++w) t += sh[w];
+  __syncthreads();
+  return t;
+}
+
+template <int THREADS, int EPT, typename T>
+__global__ void __launch_bounds__(THREADS) add_norm_kernel(float* __restrict__ x, int64_t ldx, const T* __restrict__ y,
+                                                           int64_t ldy, const T* __restrict__ bias,
+                                                           const T* __restrict__ gamma, const T* __restrict__ beta,
+                                                           int d, float eps, int rms, T* __restrict__ out,
+                                                           int64_t ldo) {
+  __shared__ float sh[THREADS / 32];
+  const int row = blockIdx.x;
+  float* xr = x + (int64_t)row * ldx;
+  float v[EPT], yv[EPT];
+#pragma unroll
+  for (int j = 0; j < EPT; ++j) {
+    const int c = threadIdx.x + THREADS * j;
+    v[j] = c < d ? xr[c] : 0.f;
+    yv[j] = (y && c < d) ? to_f32(y[(int64_t)row * ldy + c]) + (bias ? to_f32(bias[c]) : 0.f) : 0.f;
+  }
+  float s = 0.f;
+#pragma unroll
+  for (int j = 0; j < EPT; ++j) {
+    v[j] += yv[j];
+    s += v[j];
+  }
+  if (y) {
+#pragma unroll
+    for (int j = 0; j < EPT; ++j) {
+      const int c = threadIdx.x + THREADS * j;
+      if (c < d) xr[c] = v[j];
+    }
+  }
+  const float mean = rms ? 0.f : cta_sum<THREADS>(s, sh) / d;
+  float s2 = 0.f;
+#pragma unroll
+  for (int j = 0; j < EPT; ++j) {
+    const int c = threadIdx.x + THREADS * j;
+    const float z = c < d ? v[j] - mean : 0.f;
+    s2 += z * z;
+  }
+  const float inv = rsqrtf(cta_sum<THREADS>(s2, sh) / d + eps);
+#pragma unroll
+  for (int j = 0; j < EPT; ++j) {
+    const int c = threadIdx.x + THREADS * j;
+    if (c < d) {
+      float o = (v[j] - mean) * inv * to_f32(gamma[c]);
+      if (!rms && beta) o += to_f32(beta[c]);
+      out[(int64_t)row * ldo + c] = from_f32<T>(o);
+    }
+  }
+}
+
+template <int THREADS, int EPT>
+void launch_add_norm(int dtype, float* x, int64_t ldx, const void* y, int64_t ldy, const void* bias,
+                     const void* gamma, const void* beta, int n_rows, int d, float eps, int rms, void* out,
+                     int64_t ldo, cudaStream_t s) {
+  if (dtype == PSE_BF16)
+    add_norm_kernel<THREADS, EPT, __nv_bfloat16><<<n_rows, THREADS, 0, s>>>(
+        x, ldx, (const __nv_bfloat16*)y, ldy, (const __nv_bfloat16*)bias, (const __nv_bfloat16*)gamma,
+        (const __nv_bfloat16*)beta, d, eps, rms, (__nv_bfloat16*)out, ldo);
+  else
+    add_norm_kernel<THREADS, EPT, float><<<n_rows, THREADS, 0, s>>>(x, ldx, (const float*)y, ldy,
+                                                                     (const float*)bias, (const float*)gamma,
+                                                                     (const float*)beta, d, eps, rms, (float*)out,
+                                                                     ldo);
+}
+
 __device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.f + erff(x * 0.70710678118654752440f)); }
 
 __device__ __forceinline__ float silu(float x) { return x / (1.f + expf(-x)); }
@@ -86,6 +172,44 @@ __global__ void epilogue_kernel(int op, void* y, int64_t ldy, const void* bias, 
       const float g = load_as_f32(y, r * ldy + c, dtype);
       const float u = load_as_f32(y, r * ldy + n + c, dtype);
       store_from_f32(y2, r * ldy2 + c, silu(g) * u, dtype);
+    }
+  }
+}
+
+// bf16 fast path of ops 0 (bias + GELU, in place) and 2 (SwiGLU): 8 elements
+// (16 bytes) per thread.
+__global__ void epilogue_bf16x8_kernel(int op, __nv_bfloat16* y, int64_t ldy, const __nv_bfloat16* bias,
+                                       __nv_bfloat16* y2, int64_t ldy2, int n_rows, int n) {
+  const int vecs = n / 8;
+  const int64_t total = (int64_t)n_rows * vecs;
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = e / vecs;
+    const int c = (int)(e % vecs) * 8;
+    uint4 a = *reinterpret_cast<const uint4*>(y + r * ldy + c);
+    __nv_bfloat162* ah = reinterpret_cast<__nv_bfloat162*>(&a);
+    if (op == 0) {
+      uint4 b = make_uint4(0, 0, 0, 0);
+      if (bias) b = *reinterpret_cast<const uint4*>(bias + c);
+      const __nv_bfloat162* bh = reinterpret_cast<const __nv_bfloat162*>(&b);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float2 f = __bfloat1622float2(ah[q]);
+        float2 g = __bfloat1622float2(bh[q]);
+        ah[q] = __floats2bfloat162_rn(gelu_erf(f.x + g.x), gelu_erf(f.y + g.y));
+      }
+      *reinterpret_cast<uint4*>(y + r * ldy + c) = a;
+    } else {
+      uint4 u = *reinterpret_cast<const uint4*>(y + r * ldy + n + c);
+      const __nv_bfloat162* uh = reinterpret_cast<const __nv_bfloat162*>(&u);
+      uint4 o;
+      __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float2 g = __bfloat1622float2(ah[q]);
+        float2 v = __bfloat1622float2(uh[q]);
+        oh[q] = __floats2bfloat162_rn((g.x / (1.f + expf(-g.x))) * v.x, (g.y / (1.f + expf(-g.y))) * v.y);
+      }
+      *reinterpret_cast<uint4*>(y2 + r * ldy2 + c) = o;
     }
   }
 }
@@ -161,11 +285,43 @@ extern "C" int pse_norm(const float* x, int64_t ldx, const void* gamma, const vo
   return PSE_OK;
 }
 
+extern "C" int pse_add_norm(float* x, int64_t ldx, const void* y, int64_t ldy, const void* bias, int32_t y_dtype,
+                            const void* gamma, const void* beta, int32_t param_dtype, int32_t n_rows, int32_t d,
+                            float eps, int32_t rms, void* out, int64_t ldo, int32_t out_dtype, void* stream) {
+  if (n_rows < 0 || d <= 0 || d > 4096) return PSE_EINVAL;
+  if (n_rows == 0) return PSE_OK;
+  if (!x || !gamma || !out) return PSE_EINVAL;
+  // one element type for y, the norm parameters and the output (the engine's
+  // compute dtype); the residual stream is always fp32
+  if (y_dtype != param_dtype || out_dtype != param_dtype) return PSE_EINVAL;
+  cudaStream_t s = (cudaStream_t)stream;
+  const int dt = param_dtype;
+  if (d <= 256)
+    launch_add_norm<32, 8>(dt, x, ldx, y, ldy, bias, gamma, beta, n_rows, d, eps, rms, out, ldo, s);
+  else if (d <= 1024)
+    launch_add_norm<128, 8>(dt, x, ldx, y, ldy, bias, gamma, beta, n_rows, d, eps, rms, out, ldo, s);
+  else if (d <= 2048)
+    launch_add_norm<256, 8>(dt, x, ldx, y, ldy, bias, gamma, beta, n_rows, d, eps, rms, out, ldo, s);
+  else
+    launch_add_norm<512, 8>(dt, x, ldx, y, ldy, bias, gamma, beta, n_rows, d, eps, rms, out, ldo, s);
+  PSE_LAUNCH_CHECK();
+  return PSE_OK;
+}
+
 extern "C" int pse_epilogue(int32_t op, void* y, int64_t ldy, const void* bias, float* x, int64_t ldx, void* y2,
                             int64_t ldy2, int32_t n_rows, int32_t n, int32_t dtype, void* stream) {
   if (n_rows < 0 || n < 0 || op < 0 || op > 2) return PSE_EINVAL;
   if (n_rows == 0 || n == 0) return PSE_OK;
   if (!y || (op == 1 && !x) || (op == 2 && !y2)) return PSE_EINVAL;
+  const bool vec = dtype == PSE_BF16 && op != 1 && n % 8 == 0 && ldy % 8 == 0 && (op != 2 || ldy2 % 8 == 0) &&
+                   (reinterpret_cast<uintptr_t>(y) & 15) == 0 && (reinterpret_cast<uintptr_t>(bias) & 15) == 0 &&
+                   (reinterpret_cast<uintptr_t>(y2) & 15) == 0;
+  if (vec) {
+    epilogue_bf16x8_kernel<<<grid_for((int64_t)n_rows * (n / 8), 256), 256, 0, (cudaStream_t)stream>>>(
+        op, (__nv_bfloat16*)y, ldy, (const __nv_bfloat16*)bias, (__nv_bfloat16*)y2, ldy2, n_rows, n);
+    PSE_LAUNCH_CHECK();
+    return PSE_OK;
+  }
   epilogue_kernel<<<grid_for((int64_t)n_rows * n, 256), 256, 0, (cudaStream_t)stream>>>(op, y, ldy, bias, x, ldx, y2,
                                                                                          ldy2, n_rows, n, dtype);
   PSE_LAUNCH_CHECK();

@@ -112,15 +112,42 @@ __device__ __forceinline__ void argmax_combine(float& v, int& i, float ov, int o
   }
 }
 
+__device__ __forceinline__ void argmax_step(float x, int e, float& bv, int& bi) {
+  if (x > bv || (bi == INT_MAX && x == x)) {
+    bv = x;
+    bi = e;
+  }
+}
+
 __device__ int block_argmax(const float* row, int V, Scratch& sh) {
   float bv = -INFINITY;
   int bi = INT_MAX;
-  for (int e = threadIdx.x; e < V; e += blockDim.x) {
-    const float x = row[e];
-    if (x > bv || (bi == INT_MAX && x == x)) {
-      bv = x;
-      bi = e;
+  if ((V & 3) == 0 && (reinterpret_cast<uintptr_t>(row) & 15) == 0) {
+    // 16-byte loads, four rows of candidates per thread in index order
+    const float4* r4 = reinterpret_cast<const float4*>(row);
+    const int n4 = V >> 2;
+    int e = threadIdx.x;
+    for (; e + blockDim.x < n4; e += 2 * blockDim.x) {
+      const float4 a = r4[e], b = r4[e + blockDim.x];
+      argmax_step(a.x, 4 * e, bv, bi);
+      argmax_step(a.y, 4 * e + 1, bv, bi);
+      argmax_step(a.z, 4 * e + 2, bv, bi);
+      argmax_step(a.w, 4 * e + 3, bv, bi);
+      const int f = e + blockDim.x;
+      argmax_step(b.x, 4 * f, bv, bi);
+      argmax_step(b.y, 4 * f + 1, bv, bi);
+      argmax_step(b.z, 4 * f + 2, bv, bi);
+      argmax_step(b.w, 4 * f + 3, bv, bi);
     }
+    for (; e < n4; e += blockDim.x) {
+      const float4 a = r4[e];
+      argmax_step(a.x, 4 * e, bv, bi);
+      argmax_step(a.y, 4 * e + 1, bv, bi);
+      argmax_step(a.z, 4 * e + 2, bv, bi);
+      argmax_step(a.w, 4 * e + 3, bv, bi);
+    }
+  } else {
+    for (int e = threadIdx.x; e < V; e += blockDim.x) argmax_step(row[e], e, bv, bi);
   }
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 #pragma unroll

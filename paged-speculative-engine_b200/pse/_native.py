@@ -65,6 +65,8 @@ _PROTOS = {
                          c_i32, c_i32, c_i32, c_f32, c_p, c_p, c_p, c_p], 1),
     "pse_embed": ([c_p, c_p, c_i32, c_i32, c_p, c_p, c_i32, c_i32, c_i32, c_i32, c_p, c_p], 1),
     "pse_norm": ([c_p, c_i64, c_p, c_p, c_i32, c_i32, c_i32, c_f32, c_i32, c_p, c_i64, c_i32, c_p], 1),
+    "pse_add_norm": ([c_p, c_i64, c_p, c_i64, c_p, c_i32, c_p, c_p, c_i32, c_i32, c_i32, c_f32, c_i32, c_p, c_i64,
+                      c_i32, c_p], 1),
     "pse_epilogue": ([c_i32, c_p, c_i64, c_p, c_p, c_i64, c_p, c_i64, c_i32, c_i32, c_i32, c_p], 1),
     "pse_rope": ([c_p, c_i64, c_i32, c_i32, c_i32, c_i32, c_i32, c_p, c_f32, c_i32, c_p], 1),
     "pse_scatter_rows": ([c_p, c_i64, c_p, c_i32, c_i32, c_p, c_i64, c_i32, c_p], 1),

@@ -115,9 +115,11 @@ def forward(dm: DeviceModel, cache, slots: torch.Tensor, ids: torch.Tensor, rows
     sc.ensure_ws(ws_bytes)
     scale = 1.0 / math.sqrt(hd)
     rms = 1 if dm.kind == "llama" else 0
+    L0 = dm.layers[0]
+    N.call("pse_add_norm", x.data_ptr(), d, None, 0, None, dt, L0.norm1_w.data_ptr(), N.ptr(L0.norm1_b), dt, T, d,
+           dm.eps, rms, h.data_ptr(), d, dt, st)
+    n_layers = len(dm.layers)
     for li, L in enumerate(dm.layers):
-        N.call("pse_norm", x.data_ptr(), d, L.norm1_w.data_ptr(), N.ptr(L.norm1_b), dt, T, d, dm.eps, rms,
-               h.data_ptr(), d, dt, st)
         _mm(h, L.qkv_w, qkv, L.qkv_b)
         if dm.kind == "llama":
             N.call("pse_rope", qkv.data_ptr(), qkv.stride(0), rows, width, dm.q_heads, dm.kv_heads, hd,
@@ -130,9 +132,9 @@ def forward(dm: DeviceModel, cache, slots: torch.Tensor, ids: torch.Tensor, rows
                slots.data_ptr(), base_len.data_ptr(), rows, width, dm.q_heads, scale, max_ctx,
                sc.ws.data_ptr(), sc.ws.numel(), st)
         _mm(attn, L.out_w, tmp)
-        N.call("pse_epilogue", 1, tmp.data_ptr(), d, N.ptr(L.out_b), x.data_ptr(), d, None, 0, T, d, dt, st)
-        N.call("pse_norm", x.data_ptr(), d, L.norm2_w.data_ptr(), N.ptr(L.norm2_b), dt, T, d, dm.eps, rms,
-               h.data_ptr(), d, dt, st)
+        # x += attn-out (+ bias); h = norm2(x)
+        N.call("pse_add_norm", x.data_ptr(), d, tmp.data_ptr(), d, N.ptr(L.out_b), dt, L.norm2_w.data_ptr(),
+               N.ptr(L.norm2_b), dt, T, d, dm.eps, rms, h.data_ptr(), d, dt, st)
         _mm(h, L.up_w, up)
         if dm.kind == "llama":
             N.call("pse_epilogue", 2, up.data_ptr(), up.stride(0), None, None, 0, act.data_ptr(), act.stride(0),
@@ -141,18 +143,14 @@ def forward(dm: DeviceModel, cache, slots: torch.Tensor, ids: torch.Tensor, rows
             N.call("pse_epilogue", 0, up.data_ptr(), up.stride(0), N.ptr(L.up_b), None, 0, None, 0, T, dm.d_ff,
                    dt, st)
         _mm(act, L.down_w, tmp)
-        N.call("pse_epilogue", 1, tmp.data_ptr(), d, N.ptr(L.down_b), x.data_ptr(), d, None, 0, T, d, dt, st)
+        # x += mlp-out (+ bias); h = next layer's norm1(x), or the final norm after the last layer
+        if li + 1 < n_layers:
+            nw, nb = dm.layers[li + 1].norm1_w, dm.layers[li + 1].norm1_b
+        else:
+            nw, nb = dm.normf_w, dm.normf_b
+        N.call("pse_add_norm", x.data_ptr(), d, tmp.data_ptr(), d, N.ptr(L.down_b), dt, nw.data_ptr(), N.ptr(nb),
+               dt, T, d, dm.eps, rms, h.data_ptr(), d, dt, st)
     if logits_out is None:
         return
-    if last_only:
-        xs = x.view(rows, width, d)[:, width - 1]
-        n_out = rows
-        ldx = width * d
-    else:
-        xs = x
-        n_out = T
-        ldx = d
-    hf = h[:n_out]
-    N.call("pse_norm", xs.data_ptr(), ldx, dm.normf_w.data_ptr(), N.ptr(dm.normf_b), dt, n_out, d, dm.eps, rms,
-           hf.data_ptr(), d, dt, st)
+    hf = h.view(rows, width, d)[:, width - 1] if last_only else h
     lm_head(dm, hf, logits_out)
