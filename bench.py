@@ -135,11 +135,19 @@ def run_pse(args, rank, world, device):
     w = wl.WORKLOADS[args.workload]
     dtype = torch.bfloat16 if w.dtype == "bfloat16" else torch.float32
     B = args.rows or w.max_batch_size
+    from pse.dist import shard_requests
+    from pse.scheduler import Request
+
+    # The job is world x B requests (seeded prompts), sharded LPT-balanced by
+    # prompt + max_new tokens: every GPU holds ~B rows (weak scaling).
+    allreq = [Request(f"r{i}", p, w.max_new_tokens) for i, p in enumerate(wl.prompts(w, seed=0, n=B * world))]
+    mine = shard_requests(allreq, world, rank)
+    B = len(mine)
     d, t = build_pair(w, dtype, device)
     dc = cache_for(d, w, B, dtype, device, w.k + 2)
     tc = cache_for(t, w, B, dtype, device, w.k + 2)
-    prompts = wl.prompts(w, seed=rank, n=B)
-    rids = [f"g{rank}r{i}" for i in range(B)]
+    prompts = [r.prompt_ids for r in mine]
+    rids = [r.request_id for r in mine]
     dn, tn = {}, {}
     t0 = time.perf_counter()
     for r, p in zip(rids, prompts):
@@ -233,14 +241,10 @@ def run_pse(args, rank, world, device):
     esize = torch.finfo(dtype).bits // 8
     attn_bytes = int(ctx.sum().item()) * hk * hd * 2 * esize + 2 * q.numel() * esize + B * 4 * tc.max_blocks
 
-    stats = torch.tensor([committed, ms, e2e_tokens, e2e_ms], dtype=torch.float64, device=device)
-    if world > 1:
-        tot = stats.clone()
-        torch.distributed.all_reduce(tot, op=torch.distributed.ReduceOp.SUM)
-        mx = stats.clone()
-        torch.distributed.all_reduce(mx, op=torch.distributed.ReduceOp.MAX)
-        committed, e2e_tokens = int(tot[0].item()), int(tot[2].item())
-        ms, e2e_ms = float(mx[1].item()), float(mx[3].item())
+    from pse.dist import reduce_stats
+    committed, secs, _ = reduce_stats(committed, ms / 1000.0, device=device)
+    e2e_tokens, e2e_secs, _ = reduce_stats(e2e_tokens, e2e_ms / 1000.0, device=device)
+    ms, e2e_ms = secs * 1000.0, e2e_secs * 1000.0
     launches = sum(N.launches.values()) - launches_before
     return dict(committed=committed, ms=ms, e2e_tokens=e2e_tokens, e2e_ms=e2e_ms, attn_ms=attn_ms,
                 attn_bytes=attn_bytes, prefill_s=prefill_s, clocks=clk.summary(), B=B, k=k,
