@@ -368,6 +368,108 @@ def micro_attention(args, device):
                       "pool_bytes": 2 * c.k_pool.numel() * 2, "clocks": clk.summary()}), flush=True)
 
 
+def micro_accept(args, device):
+    """Accept / resample microbenchmark: fp32 target logits [R, k+1, V] and
+    draft logits [R, k, V] ~ N(0, 3^2), V = 128256, R = 1024, k = 8, drafts drawn
+    from the draft distributions with explicit uniforms.  Bytes counted are the
+    logit rows the rule has to read for the observed outcome: positions 0..n
+    of the target and 0..min(n, k-1) of the draft for a row that accepted n
+    (at T = 0 only the target rows); the formula figure (2k+1) R V 4 is
+    reported beside it."""
+    import pse._native as N
+    R, k, V, T = args.rows or 1024, 8, 128256, args.temperature
+    g = torch.Generator(device=device).manual_seed(0)
+    tgt = torch.randn(R, k + 1, V, device=device, generator=g).mul_(3.0)
+    drf = torch.randn(k, R, V, device=device, generator=g).mul_(3.0)  # position-major, as the step stores it
+    u = torch.rand(R, 2 * k + 1, device=device, dtype=torch.float64, generator=g)
+    drafts = torch.empty(R, k, dtype=torch.int32, device=device)
+    st = N.stream_ptr()
+    for j in range(k):
+        N.call("pse_sample_tokens", drf[j].data_ptr(), V, None, R, V, float(T), u.data_ptr(), 2 * k + 1, j,
+               drafts.data_ptr() + 4 * j, k, None, 0, st)
+    toks = torch.empty(R, k + 1, dtype=torch.int32, device=device)
+    nacc = torch.empty(R, dtype=torch.int32, device=device)
+    fin = torch.empty(R, dtype=torch.int32, device=device)
+
+    def launch():
+        N.call("pse_spec_accept", tgt.data_ptr(), (k + 1) * V, None, tgt.data_ptr() + 4 * V, (k + 1) * V, V,
+               drf.data_ptr(), V, None, drf.data_ptr() + 4 * R * V, V, R * V, drafts.data_ptr(), u.data_ptr(),
+               2 * k + 1, R, k, V, float(T), toks.data_ptr(), nacc.data_ptr(), fin.data_ptr(), st)
+
+    for _ in range(max(args.warmup, 3)):
+        launch()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        launch()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    n = nacc.long()
+    rows_read = (n + 1).sum().item() + (0 if T <= 0 else torch.minimum(n + 1, torch.tensor(k, device=device)).sum().item())
+    need = rows_read * V * 4
+    formula = (2 * k + 1) * R * V * 4
+    peak, kind = _peaks()
+    print(json.dumps({"metric": "accept/resample HBM GB/s", "value": need / (ms / 1000) / 1e9, "unit": "GB/s",
+                      "frac_of_peak": need / (ms / 1000) / 1e9 / peak, "peak": peak, "peak_kind": kind,
+                      "us_per_launch": ms * 1000, "bytes_needed": need, "bytes_formula_2k+1": formula,
+                      "formula_GBps": formula / (ms / 1000) / 1e9, "rows": R, "k": k, "vocab": V, "temperature": T,
+                      "mean_accepted": n.float().mean().item()}), flush=True)
+
+
+def micro_churn(args, device):
+    """Truncate churn: 1024 rows of block 16 with lengths U[512, 32768]; each
+    step reserves 8 tokens (verify), truncates every row to base + U{0..8}
+    and reserves 1 more (bonus), as one step of the engine commits.  1000
+    steps, device-resident, replayed from one CUDA graph; reports us/step and
+    host syncs per step (0)."""
+    import pse
+    import pse._native as N
+    R, bs, steps = args.rows or 1024, 16, args.steps if args.steps > 30 else 1000
+    rng = np.random.default_rng(0)
+    lens = rng.integers(512, 32769, size=R)
+    nb = int(((lens + 9 * steps + bs) // bs).sum()) + 64
+    c = pse.PagedKVCache(1, 1, 1, bs, nb, dtype=torch.float32, device=device, max_requests=R,
+                         max_blocks_per_request=int((lens.max() + 9 * steps) // bs + 2))
+    slots = torch.arange(R, dtype=torch.int32, device=device)
+    base = torch.empty(R, dtype=torch.int32, device=device)
+    base2 = torch.empty(R, dtype=torch.int32, device=device)
+    st = N.stream_ptr()
+    init = torch.from_numpy(lens.astype(np.int32)).to(device)
+    # initial lengths: one reserve per distinct length is slow; reserve row by row in one batched call per width
+    N.call("pse_kv_reserve", c.state, slots.data_ptr(), R, 0, base.data_ptr(), st)
+    for i in range(R):
+        N.call("pse_kv_reserve", c.state, slots[i:i + 1].data_ptr(), 1, int(lens[i]), base.data_ptr(), st)
+    acc = torch.from_numpy(rng.integers(0, 9, size=(steps, R)).astype(np.int32)).to(device)
+
+    def step(j):
+        N.call("pse_kv_reserve", c.state, slots.data_ptr(), R, 8, base.data_ptr(), st)
+        N.call("pse_kv_truncate", c.state, slots.data_ptr(), R, None, base.data_ptr(), acc[j].data_ptr(), st)
+        N.call("pse_kv_reserve", c.state, slots.data_ptr(), R, 1, base2.data_ptr(), st)
+
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        st = N.stream_ptr()
+        for j in range(steps):
+            step(j)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    status = int(c._blocks.status.item())
+    expect = init + (acc.sum(0) + steps).to(torch.int32)
+    ok = bool(torch.equal(c._blocks.seq_len[:R], expect)) and status == 0
+    print(json.dumps({"metric": "truncate churn us/step", "value": ms * 1000 / steps, "unit": "us/step",
+                      "higher_is_better": False, "rows": R, "block_size": bs, "steps": steps,
+                      "host_syncs_per_step": 0, "launches_per_step": 3, "lengths_ok": ok, "status": status,
+                      "free_blocks_end": int(c._blocks.free_top.item())}), flush=True)
+
+
 def config_block(args, w, B, world):
     return {"workload": f"{w.name}: {w.n_requests if args.rows is None else B} rows/GPU, prompts "
                         f"U[{w.prompt_lo},{w.prompt_hi}], k={w.k}, block {w.block_size}, "
@@ -389,7 +491,9 @@ def main():
     ap.add_argument("--cpu-rows", type=int, default=4)
     ap.add_argument("--cpu-steps", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--micro", choices=["attn"], default=None, help="kernel microbenchmark instead of the step")
+    ap.add_argument("--micro", choices=["attn", "accept", "churn"], default=None,
+                    help="kernel microbenchmark instead of the step")
+    ap.add_argument("--temperature", type=float, default=1.0, help="--micro accept: temperature")
     ap.add_argument("--attn-shape", default="gpt2-verify", choices=sorted(ATTN_SHAPES))
     ap.add_argument("--profile-step", action="store_true",
                     help="after warm-up run one eager step inside the NVTX range 'pse_step' and exit (for ncu)")
@@ -421,13 +525,20 @@ def main():
     if world > 1:
         import datetime
         torch.cuda.set_device(local)
-        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                             device_id=torch.device("cuda", local))
     device = torch.device("cuda", local if world > 1 else torch.cuda.current_device())
     torch.cuda.set_device(device)
     import pse._build
     pse._build.build()
     if args.micro == "attn":
         micro_attention(args, device)
+        return
+    if args.micro == "accept":
+        micro_accept(args, device)
+        return
+    if args.micro == "churn":
+        micro_churn(args, device)
         return
     r = run_pse(args, rank, world, device)
     if r is None:
