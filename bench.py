@@ -157,7 +157,7 @@ def run_pse(args, rank, world, device):
     k, T = w.k, w.temperature
 
     def api_step():
-        res = pse.batched_speculative_step(d, t, rids, dc, tc, dn, tn, k, T)
+        res = pse.batched_speculative_step(d, t, rids, dc, tc, dn, tn, k, T, defer_bonus=args.defer_bonus)
         for r in rids:
             dn[r] = res.draft_next_logits[r]
             tn[r] = res.target_next_logits[r]
@@ -172,7 +172,7 @@ def run_pse(args, rank, world, device):
     if args.profile_step:
         torch.cuda.synchronize()
         torch.cuda.nvtx.range_push("pse_step")
-        pse.batched_speculative_step(d, t, rids, dc, tc, dn, tn, k, T, use_graph=False)
+        pse.batched_speculative_step(d, t, rids, dc, tc, dn, tn, k, T, use_graph=False, defer_bonus=args.defer_bonus)
         torch.cuda.synchronize()
         torch.cuda.nvtx.range_pop()
         return None
@@ -494,6 +494,8 @@ def main():
     ap.add_argument("--micro", choices=["attn", "accept", "churn"], default=None,
                     help="kernel microbenchmark instead of the step")
     ap.add_argument("--temperature", type=float, default=1.0, help="--micro accept: temperature")
+    ap.add_argument("--defer-bonus", action="store_true",
+                    help="fold the target's bonus call into the next verify (one target pass per step)")
     ap.add_argument("--attn-shape", default="gpt2-verify", choices=sorted(ATTN_SHAPES))
     ap.add_argument("--profile-step", action="store_true",
                     help="after warm-up run one eager step inside the NVTX range 'pse_step' and exit (for ncu)")

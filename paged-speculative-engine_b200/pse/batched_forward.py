@@ -34,5 +34,6 @@ def batched_forward_append(model, cache, request_ids, new_input_ids: torch.Tenso
     logits = torch.empty(B * W, dm.vocab, dtype=torch.float32, device=cache.device)
     forward(dm, cache, slots, ids, B, W, base, max(longest, 1), logits)
     cache.note_append(request_ids, W)
+    cache.note_last_tokens(slots, ids, B, W)
     cache.check_status("batched_forward_append")
     return logits.view(B, W, dm.vocab)

@@ -155,6 +155,10 @@ class PagedKVCache:
         self._lengths: dict[str, int] = {}
         self.generation = 0  # bumped whenever device buffers move (captured graphs must be rebuilt)
         self._layer_structs = [self._layer_struct(l) for l in range(n_layers)]
+        # last token id appended to each slot by a forward (the deferred-bonus
+        # step re-runs it), and the slots whose last token is pending
+        self.last_token = torch.zeros(self._blocks.num_slots, dtype=torch.int32, device=self.device)
+        self.deferred_slots: set[int] = set()
 
     # ------------------------------------------------------------------ internals
     def _layer_struct(self, layer: int) -> N.KVLayer:
@@ -202,6 +206,9 @@ class PagedKVCache:
         self._free_slots = list(range(num_slots - 1, old.num_slots - 1, -1)) + self._free_slots
         self._blocks = new
         self.allocator._b = new
+        last = torch.zeros(num_slots, dtype=torch.int32, device=self.device)
+        last[: old.num_slots] = self.last_token
+        self.last_token = last
         self.generation += 1
 
     def ensure_capacity(self, request_ids, extra_tokens: int) -> None:
@@ -239,6 +246,10 @@ class PagedKVCache:
         for r in request_ids:
             self._lengths[r] += width
 
+    def note_last_tokens(self, slots: torch.Tensor, ids: torch.Tensor, rows: int, width: int) -> None:
+        """Record the last token id each row appended (device op, stream-ordered)."""
+        self.last_token.index_copy_(0, slots.long(), ids.view(rows, width)[:, width - 1].to(torch.int32))
+
     # ------------------------------------------------------------------ reference API
     def create_request(self, request_id: str) -> None:
         """engine/paged_cache.py:92-96."""
@@ -248,6 +259,7 @@ class PagedKVCache:
             self._grow(self._blocks.num_slots * 2, self._blocks.max_blocks)
         self._slot[request_id] = self._free_slots.pop()
         self._lengths[request_id] = 0
+        self.deferred_slots.discard(self._slot[request_id])
 
     def length(self, request_id: str) -> int:
         return self._lengths[request_id]
@@ -290,6 +302,7 @@ class PagedKVCache:
         """engine/paged_cache.py:156-160."""
         s = self._slot.pop(request_id)
         del self._lengths[request_id]
+        self.deferred_slots.discard(s)
         slots = torch.tensor([s], dtype=torch.int32).to(self.device, non_blocking=True)
         N.call("pse_kv_release", self.state, slots.data_ptr(), 1, N.stream_ptr())
         self._free_slots.append(s)
@@ -301,6 +314,7 @@ class PagedKVCache:
         slots = [self._slot.pop(r) for r in request_ids]
         for r in request_ids:
             del self._lengths[r]
+        self.deferred_slots.difference_update(slots)
         t = torch.tensor(slots, dtype=torch.int32).to(self.device, non_blocking=True)
         N.call("pse_kv_release", self.state, t.data_ptr(), len(slots), N.stream_ptr())
         self._free_slots.extend(slots)

@@ -49,9 +49,11 @@ class _Active:
 @torch.no_grad()
 def run_continuous_speculative_batches(draft_model, target_model, requests, draft_cache, target_cache,
                                        max_batch_size, k=4, temperature=0.0, generator=None, *,
-                                       uniform_fn=None, on_step=None, use_graph=None):
+                                       uniform_fn=None, on_step=None, use_graph=None, defer_bonus=False):
     """engine/scheduler.py:61-128.  ``uniform_fn(request_ids, steps, n)`` (optional)
-    supplies explicit uniforms per step; ``on_step(ids, result)`` observes steps."""
+    supplies explicit uniforms per step; ``on_step(ids, result)`` observes steps;
+    ``defer_bonus`` folds the target's bonus call into the next verify (see
+    ``batched_speculative_step``)."""
     queue = list(requests)
     active: dict[str, _Active] = {}
     steps_taken: dict[str, int] = {}
@@ -78,7 +80,7 @@ def run_continuous_speculative_batches(draft_model, target_model, requests, draf
         step = batched_speculative_step(
             draft_model, target_model, ids, draft_cache, target_cache,
             {r: active[r].draft_next_logits for r in ids}, {r: active[r].target_next_logits for r in ids},
-            k, temperature, generator, uniforms=u, use_graph=use_graph,
+            k, temperature, generator, uniforms=u, use_graph=use_graph, defer_bonus=defer_bonus,
         )
         if on_step is not None:
             on_step(ids, step)

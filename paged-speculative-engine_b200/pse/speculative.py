@@ -95,6 +95,7 @@ def prefill_request(draft_model, target_model, draft_cache, target_cache, reques
         base = torch.empty(1, dtype=torch.int32, device=cache.device)
         forward(dm, cache, slots, ids, 1, P, base, P, buf[slot:slot + 1], last_only=True)
         cache.note_append([request_id], P)
+        cache.note_last_tokens(slots, ids, 1, P)
         outs.append(buf[slot])
     draft_cache.check_status("prefill")
     target_cache.check_status("prefill")
@@ -119,6 +120,9 @@ class _StepBuffers:
         self.u = torch.zeros(B, 2 * k + 1, dtype=torch.float64, device=device)
         self.req_key = torch.empty(B, **i32)
         self.steps = torch.empty(B, **i32)
+        self.vids = None    # deferred-bonus mode: verify ids [B, k+1] and logits [B*(k+1), V]
+        self.vlog2 = None
+        self.nacc1 = torch.empty(B, **i32)
         n_pack = B * (k + 1) + B + 2
         self.pack = torch.empty(n_pack, **i32)
         self.host_pack = torch.empty(n_pack, dtype=torch.int32, pin_memory=True)
@@ -142,6 +146,7 @@ class StepRunner:
         self.use_graphs = USE_GRAPHS
         self.sc_d = Scratch(dm_d)
         self.sc_t = Scratch(dm_t)
+        self.tpending = None  # per target slot: token not yet appended (deferred-bonus mode)
 
     # ---------------------------------------------------------------- device program
     def _ctx_bound(self, cache, dm) -> int:
@@ -150,7 +155,8 @@ class StepRunner:
             bound = min(bound, dm.max_seq_len)
         return bound
 
-    def _program(self, b: _StepBuffers, T: float, philox: bool, max_ctx_d: int, max_ctx_t: int) -> None:
+    def _program(self, b: _StepBuffers, T: float, philox: bool, max_ctx_d: int, max_ctx_t: int,
+                 defer: bool = False) -> None:
         k, V, B = self.k, self.V, b.B
         st = N.stream_ptr()
         dnext = next_logits_buffer(self.dcache, V)
@@ -159,6 +165,7 @@ class StepRunner:
         if T > 0 and philox:
             N.call("pse_philox_uniforms", self.seed, b.req_key.data_ptr(), b.steps.data_ptr(), B, nu,
                    b.u.data_ptr(), st)
+        # draft rounds (engine/speculative.py:92-113)
         for j in range(k):
             if j == 0:
                 src, idx = dnext, b.slots_d.data_ptr()
@@ -168,33 +175,83 @@ class StepRunner:
                    b.drafts.data_ptr() + 4 * j, k, b.round_ids.data_ptr(), 1, st)
             forward(self.dm_d, self.dcache, b.slots_d, b.round_ids, B, 1, b.base[j], max_ctx_d, b.dlog[j],
                     scratch=self.sc_d)
-        forward(self.dm_t, self.tcache, b.slots_t, b.drafts.view(-1), B, k, b.base[k], max_ctx_t, b.vlog,
-                scratch=self.sc_t)
-        N.call("pse_spec_accept", tnext.data_ptr(), V, b.slots_t.data_ptr(), b.vlog.data_ptr(), k * V, V,
+        if not defer:
+            # verify: one width-k target call (engine/speculative.py:115-117)
+            forward(self.dm_t, self.tcache, b.slots_t, b.drafts.view(-1), B, k, b.base[k], max_ctx_t, b.vlog,
+                    scratch=self.sc_t)
+            t0, t0_stride, t0_index = tnext.data_ptr(), V, b.slots_t.data_ptr()
+            ver, v_row = b.vlog.data_ptr(), k * V
+        else:
+            # verify of width k+1: the previous step's final token (never appended
+            # to the target) followed by the k drafts; column 0 predicts what the
+            # reference's bonus call would have returned as target_next.
+            slots_t = b.slots_t.long()
+            b.vids[:, 0] = self.tpending.index_select(0, slots_t)
+            b.vids[:, 1:] = b.drafts
+            forward(self.dm_t, self.tcache, b.slots_t, b.vids.view(-1), B, k + 1, b.base[k], max_ctx_t, b.vlog2,
+                    scratch=self.sc_t)
+            t0, t0_stride, t0_index = b.vlog2.data_ptr(), (k + 1) * V, None
+            ver, v_row = b.vlog2.data_ptr() + 4 * V, (k + 1) * V
+        # accept / reject / resample (engine/speculative.py:119-157)
+        N.call("pse_spec_accept", t0, t0_stride, t0_index, ver, v_row, V,
                dnext.data_ptr(), V, b.slots_d.data_ptr(), b.dlog.data_ptr(), V, B * V,
                b.drafts.data_ptr(), b.u.data_ptr(), nu, B, k, V, float(T), b.tokens.data_ptr(),
                b.n_acc.data_ptr(), b.final.data_ptr(), st)
+        # commit (engine/speculative.py:159-164)
         N.call("pse_kv_truncate", self.dcache.state, b.slots_d.data_ptr(), B, None, b.base[0].data_ptr(),
                b.n_acc.data_ptr(), st)
-        N.call("pse_kv_truncate", self.tcache.state, b.slots_t.data_ptr(), B, None, b.base[k].data_ptr(),
-               b.n_acc.data_ptr(), st)
+        if not defer:
+            N.call("pse_kv_truncate", self.tcache.state, b.slots_t.data_ptr(), B, None, b.base[k].data_ptr(),
+                   b.n_acc.data_ptr(), st)
+        else:
+            torch.add(b.n_acc, 1, out=b.nacc1)
+            N.call("pse_kv_truncate", self.tcache.state, b.slots_t.data_ptr(), B, None, b.base[k].data_ptr(),
+                   b.nacc1.data_ptr(), st)
+            self.tpending.index_copy_(0, slots_t, b.final)
+        # bonus forwards (engine/speculative.py:166-177); the target's is folded
+        # into the next verify in deferred mode
         forward(self.dm_d, self.dcache, b.slots_d, b.final, B, 1, b.base[k + 1], max_ctx_d, b.blog,
                 scratch=self.sc_d)
         N.call("pse_scatter_rows", b.blog.data_ptr(), V, b.slots_d.data_ptr(), B, V, dnext.data_ptr(), V,
                dnext.shape[0], st)
-        forward(self.dm_t, self.tcache, b.slots_t, b.final, B, 1, b.base[k + 2], max_ctx_t, b.blog,
-                scratch=self.sc_t)
-        N.call("pse_scatter_rows", b.blog.data_ptr(), V, b.slots_t.data_ptr(), B, V, tnext.data_ptr(), V,
-               tnext.shape[0], st)
+        if not defer:
+            forward(self.dm_t, self.tcache, b.slots_t, b.final, B, 1, b.base[k + 2], max_ctx_t, b.blog,
+                    scratch=self.sc_t)
+            N.call("pse_scatter_rows", b.blog.data_ptr(), V, b.slots_t.data_ptr(), B, V, tnext.data_ptr(), V,
+                   tnext.shape[0], st)
+        self.dcache.last_token.index_copy_(0, b.slots_d.long(), b.final)
+        if not defer:
+            self.tcache.last_token.index_copy_(0, b.slots_t.long(), b.final)
         nt = B * (k + 1)
         b.pack[:nt].copy_(b.tokens.view(-1))
         b.pack[nt:nt + B].copy_(b.n_acc)
         b.pack[nt + B:nt + B + 1].copy_(self.dcache.status_tensor())
         b.pack[nt + B + 1:nt + B + 2].copy_(self.tcache.status_tensor())
 
+    def _enter_deferred(self, request_ids, slots_t) -> None:
+        """Move rows into the deferred-bonus state: the target forgets its last
+        token (truncate by one) and keeps it as the row's pending token, to be
+        re-run as column 0 of the next verify."""
+        tc = self.tcache
+        if self.tpending is None or self.tpending.shape[0] < tc.state.num_slots:
+            old = self.tpending
+            self.tpending = torch.zeros(tc.state.num_slots, dtype=torch.int32, device=self.device)
+            if old is not None:
+                self.tpending[: old.shape[0]] = old
+        new = [(r, s) for r, s in zip(request_ids, slots_t) if s not in tc.deferred_slots]
+        if not new:
+            return
+        idx = torch.tensor([s for _, s in new], dtype=torch.long).to(self.device)
+        self.tpending.index_copy_(0, idx, tc.last_token.index_select(0, idx))
+        for r, s in new:
+            if tc.length(r) < 1:
+                raise ValueError(f"request {r} has no token to defer")
+            tc.truncate(r, tc.length(r) - 1)
+            tc.deferred_slots.add(s)
+
     # ---------------------------------------------------------------- host side
     def step(self, request_ids, draft_next_logits, target_next_logits, temperature, generator=None,
-             uniforms=None, use_graph=None) -> BatchStepResult:
+             uniforms=None, use_graph=None, defer_bonus: bool = False) -> BatchStepResult:
         k, V = self.k, self.V
         B = len(request_ids)
         if B == 0:
@@ -202,6 +259,8 @@ class StepRunner:
         if len(set(request_ids)) != B:
             raise ValueError("request_ids must be unique")
         dc, tc = self.dcache, self.tcache
+        if not defer_bonus and any(tc.slot(r) in tc.deferred_slots for r in request_ids):
+            raise ValueError("request is in the deferred-bonus state: keep stepping it with defer_bonus=True")
         _check_positions(self.dm_d, dc, request_ids, k + 1)
         _check_positions(self.dm_t, tc, request_ids, k + 1)
         dc.ensure_capacity(request_ids, k + 1)
@@ -209,18 +268,24 @@ class StepRunner:
         b = self.bufs.get(B)
         if b is None:
             b = self.bufs[B] = _StepBuffers(B, k, V, self.device)
+        if defer_bonus and b.vids is None:
+            b.vids = torch.empty(B, k + 1, dtype=torch.int32, device=self.device)
+            b.vlog2 = torch.empty(B * (k + 1), V, dtype=torch.float32, device=self.device)
         dnext = next_logits_buffer(dc, V)
         tnext = next_logits_buffer(tc, V)
         sd = [dc.slot(r) for r in request_ids]
         stt = [tc.slot(r) for r in request_ids]
+        if defer_bonus:
+            self._enter_deferred(request_ids, stt)
         for r, s in zip(request_ids, sd):
             t = draft_next_logits[r]
             if t.data_ptr() != dnext[s].data_ptr():
                 dnext[s].copy_(t.reshape(-1), non_blocking=True)
-        for r, s in zip(request_ids, stt):
-            t = target_next_logits[r]
-            if t.data_ptr() != tnext[s].data_ptr():
-                tnext[s].copy_(t.reshape(-1), non_blocking=True)
+        if not defer_bonus:
+            for r, s in zip(request_ids, stt):
+                t = target_next_logits[r]
+                if t.data_ptr() != tnext[s].data_ptr():
+                    tnext[s].copy_(t.reshape(-1), non_blocking=True)
         T = float(temperature)
         philox = False
         hin = b.host_in
@@ -250,32 +315,34 @@ class StepRunner:
         if graphs:
             # size every buffer the program touches before the graph key is taken
             self.sc_d.ensure(B)
-            self.sc_t.ensure(B * k)
+            self.sc_t.ensure(B * (k + 1))
             dmd, dmt = self.dm_d, self.dm_t
             self.sc_d.ensure_ws(N.size_call("pse_paged_attention_workspace", B, 1, dmd.q_heads, dmd.kv_heads,
                                             dmd.head_dim, mcd))
             self.sc_t.ensure_ws(max(
+                N.size_call("pse_paged_attention_workspace", B, k + 1, dmt.q_heads, dmt.kv_heads, dmt.head_dim, mct),
                 N.size_call("pse_paged_attention_workspace", B, k, dmt.q_heads, dmt.kv_heads, dmt.head_dim, mct),
                 N.size_call("pse_paged_attention_workspace", B, 1, dmt.q_heads, dmt.kv_heads, dmt.head_dim, mct)))
-        key = (B, T, philox, dc.generation, tc.generation, self.sc_d.generation, self.sc_t.generation)
+        key = (B, T, philox, defer_bonus, dc.generation, tc.generation, self.sc_d.generation, self.sc_t.generation,
+               None if self.tpending is None else self.tpending.data_ptr())
         if graphs and key in self.graphs:
             self.graphs[key].replay()
         elif graphs and key in self.warm:
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g):
-                self._program(b, T, philox, mcd, mct)
+                self._program(b, T, philox, mcd, mct, defer_bonus)
             self.graphs[key] = g
             g.replay()
         else:
             if graphs:
                 # eager steps use the same context bound so the captured
                 # program's buffers (split-KV workspace) are already sized
-                self._program(b, T, philox, mcd, mct)
+                self._program(b, T, philox, mcd, mct, defer_bonus)
                 self.warm.add(key)
             else:
                 ld = max(dc.length(r) for r in request_ids) + k + 1
                 lt = max(tc.length(r) for r in request_ids) + k + 1
-                self._program(b, T, philox, ld, lt)
+                self._program(b, T, philox, ld, lt + 1, defer_bonus)
         hp = b.host_pack
         hp.copy_(b.pack, non_blocking=True)
         torch.cuda.current_stream().synchronize()
@@ -293,7 +360,7 @@ class StepRunner:
             accepted[r] = toks[i][: n + 1]
             n_acc[r] = n
             dn[r] = dnext[sd[i]]
-            tn[r] = tnext[stt[i]]
+            tn[r] = None if defer_bonus else tnext[stt[i]]
             self.request_steps[r] = self.request_steps.get(r, 0) + 1
         dc.note_lengths(request_ids, [dc.length(r) + n_acc[r] + 1 for r in request_ids])
         tc.note_lengths(request_ids, [tc.length(r) + n_acc[r] + 1 for r in request_ids])
@@ -314,8 +381,16 @@ def runner_for(draft_model, target_model, draft_cache, target_cache, k: int) -> 
 @torch.no_grad()
 def batched_speculative_step(draft_model, target_model, request_ids, draft_cache, target_cache,
                              draft_next_logits, target_next_logits, k, temperature, generator=None, *,
-                             uniforms=None, use_graph=None) -> BatchStepResult:
-    """engine/speculative.py:76-177 on the device."""
+                             uniforms=None, use_graph=None, defer_bonus=False) -> BatchStepResult:
+    """engine/speculative.py:76-177 on the device.
+
+    ``defer_bonus=True`` folds the target's width-1 bonus call into the next
+    step's verify, which then runs at width k+1 (the final token, then the k
+    drafts): one target pass per step instead of two, same accepted tokens.
+    In that mode ``target_next_logits`` in the result are ``None`` (the values
+    are computed, as column 0 of the next verify, but never materialised),
+    ``target_cache.length()`` is one less than the reference's (the final token
+    is pending), and the request must keep being stepped in this mode."""
     runner = runner_for(draft_model, target_model, draft_cache, target_cache, k)
     return runner.step(list(request_ids), draft_next_logits, target_next_logits, temperature, generator,
-                       uniforms, use_graph)
+                       uniforms, use_graph, defer_bonus)

@@ -93,8 +93,8 @@ def test_bf16_prompt_logits_within_tolerance(kind):
     assert worst < BF16_TOL, worst
 
 
-@pytest.mark.parametrize("k", [2, 4])
-def test_sampled_steps_match_oracle_draw_for_draw(k):
+@pytest.mark.parametrize("k,defer", [(2, False), (4, False), (4, True)])
+def test_sampled_steps_match_oracle_draw_for_draw(k, defer):
     """T = 1 with the same explicit Philox uniforms on both sides: identical
     accepted tokens at every step (fp32 TinyGPT pair)."""
     import pse
@@ -120,8 +120,32 @@ def test_sampled_steps_match_oracle_draw_for_draw(k):
     pdc = pse.PagedKVCache(2, 2, 32, 16, 256)
     ptc = pse.PagedKVCache(4, 4, 32, 16, 256)
     pres = pse.run_continuous_speculative_batches(
-        d, t, preqs, pdc, ptc, 4, k=k, temperature=1.0, uniform_fn=uniform_fn, use_graph=False,
+        d, t, preqs, pdc, ptc, 4, k=k, temperature=1.0, uniform_fn=uniform_fn, use_graph=False, defer_bonus=defer,
         on_step=lambda ids, r: device_steps.append({x: r.accepted_tokens[x] for x in ids}))
     assert device_steps == oracle_steps
     assert {r.request_id: r.output_ids for r in pres} == {r.request_id: r.output_ids for r in ores}
     assert any(len(v) > 1 for s in device_steps for v in s.values())  # some drafts were accepted
+
+
+def test_deferred_bonus_property_matches_solo_greedy():
+    """Scheduler property of the reference (every request == solo greedy) in
+    deferred-bonus mode, over seeded random workloads."""
+    import pse
+    rng = np.random.default_rng(7)
+    for trial in range(25):
+        torch.manual_seed(int(rng.integers(0, 1000)))
+        cfg = ModelConfig(vocab_size=32, d_model=12, n_layers=2, n_heads=2, d_ff=24, max_seq_len=256)
+        d, t = TinyGPT(cfg).eval(), TinyGPT(cfg).eval()
+        k, bs, mb = int(rng.integers(1, 6)), int(rng.integers(1, 6)), int(rng.integers(1, 5))
+        reqs = [pse.Request(f"r{i}", rng.integers(1, 32, size=int(rng.integers(1, 6))).tolist(), int(rng.integers(1, 9)))
+                for i in range(int(rng.integers(1, 7)))]
+        nb = sum(len(r.prompt_ids) + r.max_new_tokens + k + 2 for r in reqs) // bs * len(reqs) + 16
+        hd = cfg.d_model // cfg.n_heads
+        dc = pse.PagedKVCache(cfg.n_layers, cfg.n_heads, hd, bs, nb)
+        tc = pse.PagedKVCache(cfg.n_layers, cfg.n_heads, hd, bs, nb)
+        res = pse.run_continuous_speculative_batches(d, t, reqs, dc, tc, mb, k=k, temperature=0.0,
+                                                     use_graph=False, defer_bonus=True)
+        by = {r.request_id: r.output_ids for r in res}
+        for q in reqs:
+            assert by[q.request_id] == generate_cached(t, torch.tensor([q.prompt_ids]), q.max_new_tokens), (trial, q)
+        assert dc.allocator.num_free == nb and tc.allocator.num_free == nb
