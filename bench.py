@@ -228,7 +228,7 @@ def run_pse(args, rank, world, device):
         for li in range(dm.n_layers):
             N.call("pse_paged_attention", tc.state, tc.layer(li), q.data_ptr(), q.stride(0), out.data_ptr(),
                    out.stride(0), b.slots_t.data_ptr(), base.data_ptr(), B, k, hq, 1.0 / math.sqrt(hd), max_ctx,
-                   ws.data_ptr(), ws.numel(), st)
+                   None, ws.data_ptr(), ws.numel(), st)
 
     attn_all_layers()
     a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -343,7 +343,7 @@ def micro_attention(args, device):
 
     def launch():
         N.call("pse_paged_attention", c.state, c.layer(0), q.data_ptr(), q.stride(0), out.data_ptr(), out.stride(0),
-               slots.data_ptr(), base.data_ptr(), rows, width, hq, 1.0 / math.sqrt(hd), max_ctx, ws.data_ptr(),
+               slots.data_ptr(), base.data_ptr(), rows, width, hq, 1.0 / math.sqrt(hd), max_ctx, None, ws.data_ptr(),
                ws.numel(), st)
 
     for _ in range(max(args.warmup, 3)):

@@ -130,13 +130,16 @@ int pse_kv_gather(pse_block_state st, pse_kv_layer kv, const int32_t *slots, int
  * base_len[i] + w and attends to positions 0..base_len[i]+w of the row, whose
  * K/V are already in the pool.  Grouped heads: query head h reads KV head
  * h / (q_heads / kv_heads).  `max_ctx` bounds base_len[i] + width over rows
- * (it sizes the split-KV grid; rows may be shorter).  Output has the pool's
+ * (it sizes the split-KV grid; rows may be shorter).  row_order (nullable) is a
+ * permutation of 0..rows-1: the tensor-core kernel hands out rows in that order
+ * (longest first keeps the end of the launch from idling on one long row).
+ * Output has the pool's
  * dtype.  workspace: pse_paged_attention_workspace() bytes (at least 256: a
  * work counter the call zeroes on the stream, then split-KV partials). */
 int pse_paged_attention(pse_block_state st, pse_kv_layer kv, const void *q, int64_t q_tok_stride,
                         void *out, int64_t out_tok_stride, const int32_t *slots, const int32_t *base_len,
                         int32_t rows, int32_t width, int32_t q_heads, float scale, int32_t max_ctx,
-                        void *workspace, size_t workspace_bytes, void *stream);
+                        const int32_t *row_order, void *workspace, size_t workspace_bytes, void *stream);
 
 size_t pse_paged_attention_workspace(int32_t rows, int32_t width, int32_t q_heads, int32_t kv_heads,
                                      int32_t head_dim, int32_t max_ctx);
@@ -239,6 +242,16 @@ int pse_add_norm(float *x, int64_t ldx, const void *y, int64_t ldy, const void *
  * bias may be NULL. y has `dtype`. */
 int pse_epilogue(int32_t op, void *y, int64_t ldy, const void *bias, float *x, int64_t ldx, void *y2,
                  int64_t ldy2, int32_t n_rows, int32_t n, int32_t dtype, void *stream);
+
+/* The nn.Linear projections of engine/model.py:73-74, 127-129, 156 on the
+ * tcgen05 tensor cores: C[m, n] = A[m, k] . W[n, k]^T (+ bias[n]) (-> GELU if
+ * act == 1), A / W / bias bf16, fp32 accumulation, C bf16 (out_f32 == 0) or
+ * fp32.  k must be a multiple of 64; leading dimensions multiples of 8
+ * elements (4 for fp32 C); base pointers 16-byte aligned.  status (nullable)
+ * receives PSE_STATUS_TIMEOUT if a bounded in-kernel wait expires. */
+int pse_gemm_bf16(const void *a, int64_t lda, const void *w, int64_t ldw, const void *bias, void *c,
+                  int64_t ldc, int32_t m, int32_t n, int32_t k, int32_t act, int32_t out_f32, int32_t *status,
+                  void *stream);
 
 /* Rotate-half RoPE in place on the q and k heads of a fused qkv buffer
  * (q heads at column 0, k heads after them), position base_len[i] + w. */

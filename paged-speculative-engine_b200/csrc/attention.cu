@@ -404,7 +404,8 @@ int launch_d(const AttnArgs& a, const Plan& p, cudaStream_t s) {
 bool tc_eligible(const pse_block_state& st, const pse_kv_layer& kv, int q_heads, int width);
 int tc_attention(const pse_block_state& st, const pse_kv_layer& kv, const void* q, int64_t q_tok_stride, void* out,
                  int64_t out_tok_stride, const int32_t* slots, const int32_t* base_len, int rows, int width,
-                 int q_heads, float scale, int split_tokens, int n_splits, void* ws, int* counter, cudaStream_t s);
+                 int q_heads, float scale, int split_tokens, int n_splits, void* ws, int* counter,
+                 const int32_t* row_order, cudaStream_t s);
 
 }  // namespace pse
 
@@ -435,8 +436,8 @@ extern "C" size_t pse_paged_attention_workspace(int32_t rows, int32_t width, int
 
 extern "C" int pse_paged_attention(pse_block_state st, pse_kv_layer kv, const void* q, int64_t q_tok_stride, void* out,
                                    int64_t out_tok_stride, const int32_t* slots, const int32_t* base_len, int32_t rows,
-                                   int32_t width, int32_t q_heads, float scale, int32_t max_ctx, void* workspace,
-                                   size_t workspace_bytes, void* stream) {
+                                   int32_t width, int32_t q_heads, float scale, int32_t max_ctx,
+                                   const int32_t* row_order, void* workspace, size_t workspace_bytes, void* stream) {
   if (rows < 0 || width < 0) return PSE_EINVAL;
   if (rows == 0 || width == 0) return PSE_OK;
   if (!q || !out || !slots || !base_len || !kv.k_pool || !kv.v_pool || !st.block_table || !st.nblocks)
@@ -475,7 +476,7 @@ extern "C" int pse_paged_attention(pse_block_state st, pse_kv_layer kv, const vo
   cudaStream_t s = (cudaStream_t)stream;
   if (tc_eligible(st, kv, q_heads, width) && !g_force_generic) {
     int rc = tc_attention(st, kv, q, q_tok_stride, out, out_tok_stride, slots, base_len, rows, width, q_heads, scale,
-                          p.split_tokens, p.n_splits, a.ws, reinterpret_cast<int*>(workspace), s);
+                          p.split_tokens, p.n_splits, a.ws, reinterpret_cast<int*>(workspace), row_order, s);
     if (rc) return rc;
     if (p.n_splits > 1) {
       const int64_t items = (int64_t)rows * width * q_heads;
@@ -579,7 +580,7 @@ extern "C" int pse_paged_attention_noalloc(pse_block_state st, pse_kv_layer kv, 
   cudaStream_t s = (cudaStream_t)stream;
   if (tc_eligible(st, kv, q_heads, width)) {
     rc = tc_attention(st, kv, q, q_tok_stride, out, out_tok_stride, slots, base_len, rows, width, q_heads, scale,
-                      p.split_tokens, p.n_splits, a.ws, reinterpret_cast<int*>(scratch), s);
+                      p.split_tokens, p.n_splits, a.ws, reinterpret_cast<int*>(scratch), nullptr, s);
     if (rc) return rc;
     if (p.n_splits > 1) {
       const int64_t items = (int64_t)rows * width * q_heads;

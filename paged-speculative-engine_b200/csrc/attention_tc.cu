@@ -78,6 +78,7 @@ struct Args {
   int oob_row;  // first row index past the pool's 2-D view (zero-fill requests)
   int n_items;  // rows * kv_heads * n_qtiles * n_splits
   int* counter; // work counter (zeroed before the launch)
+  const int32_t* row_order;  // rows in the order items are handed out (nullable: 0..rows-1)
 };
 
 __device__ __forceinline__ uint32_t su32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -175,7 +176,7 @@ __device__ __forceinline__ Item decode_item(const Args& a, int e) {
   e /= a.n_qtiles;
   it.hk = e % a.kv_heads;
   e /= a.kv_heads;
-  it.i = e % a.rows;
+  it.i = a.row_order ? a.row_order[e % a.rows] : e % a.rows;
   it.split = e / a.rows;
   it.slot = a.slots[it.i];
   it.base = a.base_len[it.i];
@@ -650,7 +651,8 @@ bool tc_eligible(const pse_block_state& st, const pse_kv_layer& kv, int q_heads,
 
 int tc_attention(const pse_block_state& st, const pse_kv_layer& kv, const void* q, int64_t q_tok_stride, void* out,
                  int64_t out_tok_stride, const int32_t* slots, const int32_t* base_len, int rows, int width,
-                 int q_heads, float scale, int split_tokens, int n_splits, void* ws, int* counter, cudaStream_t s) {
+                 int q_heads, float scale, int split_tokens, int n_splits, void* ws, int* counter,
+                 const int32_t* row_order, cudaStream_t s) {
   const int n_qrows = (q_heads / kv.kv_heads) * width;
   const int MT = n_qrows <= 16 ? 1 : 2;
   tc::Args a;
@@ -680,6 +682,7 @@ int tc_attention(const pse_block_state& st, const pse_kv_layer& kv, const void* 
   a.oob_row = st.num_blocks * kv.kv_heads * st.block_size;
   a.n_items = rows * kv.kv_heads * a.n_qtiles * n_splits;
   a.counter = counter;
+  a.row_order = row_order;
   if (!counter) return PSE_EINVAL;
   CUtensorMap mk, mv;
   int rc = tc::tensor_map(kv.k_pool, st.num_blocks, kv.kv_heads, st.block_size, kv.head_dim, &mk);

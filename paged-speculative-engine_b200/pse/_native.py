@@ -58,7 +58,7 @@ _PROTOS = {
     "pse_kv_append": ([BlockState, KVLayer, c_p, c_p, c_i64, c_i64, c_p, c_p, c_i32, c_i32, c_p], 1),
     "pse_kv_gather": ([BlockState, KVLayer, c_p, c_i32, c_i32, c_p, c_p, c_p], 1),
     "pse_paged_attention": ([BlockState, KVLayer, c_p, c_i64, c_p, c_i64, c_p, c_p, c_i32, c_i32, c_i32,
-                             c_f32, c_i32, c_p, c_sz, c_p], 1),
+                             c_f32, c_i32, c_p, c_p, c_sz, c_p], 1),
     "pse_philox_uniforms": ([c_u64, c_p, c_p, c_i32, c_i32, c_p, c_p], 1),
     "pse_sample_tokens": ([c_p, c_i64, c_p, c_i32, c_i32, c_f32, c_p, c_i64, c_i32, c_p, c_i64, c_p, c_i64, c_p], 1),
     "pse_spec_accept": ([c_p, c_i64, c_p, c_p, c_i64, c_i64, c_p, c_i64, c_p, c_p, c_i64, c_i64, c_p, c_p, c_i64,
@@ -71,6 +71,7 @@ _PROTOS = {
     "pse_rope": ([c_p, c_i64, c_i32, c_i32, c_i32, c_i32, c_i32, c_p, c_f32, c_i32, c_p], 1),
     "pse_scatter_rows": ([c_p, c_i64, c_p, c_i32, c_i32, c_p, c_i64, c_i32, c_p], 1),
     "pse_attention_force_generic": ([c_i32], 0),
+    "pse_gemm_bf16": ([c_p, c_i64, c_p, c_i64, c_p, c_p, c_i64, c_i32, c_i32, c_i32, c_i32, c_i32, c_p, c_p], 1),
     "pse_paged_attention_noalloc": ([BlockState, KVLayer, c_p, c_i64, c_p, c_i64, c_p, c_p, c_i32, c_i32, c_i32,
                                      c_f32, c_i32, c_p], 1),
 }

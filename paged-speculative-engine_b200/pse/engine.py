@@ -74,25 +74,50 @@ def scratch_for(dm: DeviceModel) -> Scratch:
     return s
 
 
-def _mm(a: torch.Tensor, w: torch.Tensor, out: torch.Tensor, bias: torch.Tensor | None = None) -> None:
-    """out = a @ w^T (+ bias), cuBLAS via torch, no TF32."""
+USE_TC_GEMM = False  # bf16 projections on the tcgen05 GEMM (pse_gemm_bf16); off until it beats cuBLAS on these shapes
+
+
+def _tc_ok(a: torch.Tensor, w: torch.Tensor, out: torch.Tensor) -> bool:
+    """pse_gemm_bf16 takes bf16 operands, k in whole 64-element slabs, row
+    pitches in 16-byte units and 16-byte aligned bases."""
+    if not USE_TC_GEMM or a.dtype != torch.bfloat16 or w.dtype != torch.bfloat16:
+        return False
+    k = a.shape[1]
+    esz = out.element_size()
+    return (k % 64 == 0 and a.stride(1) == 1 and w.stride(1) == 1 and out.stride(1) == 1
+            and a.stride(0) % 8 == 0 and w.stride(0) % 8 == 0 and (out.stride(0) * esz) % 16 == 0
+            and a.data_ptr() % 16 == 0 and w.data_ptr() % 16 == 0 and out.data_ptr() % 16 == 0)
+
+
+def _mm(a: torch.Tensor, w: torch.Tensor, out: torch.Tensor, bias: torch.Tensor | None = None,
+        gelu: bool = False) -> bool:
+    """out = a @ w^T (+ bias).  With ``gelu`` the tensor-core path also applies
+    GELU; returns whether it did (the cuBLAS fallback never does)."""
+    if _tc_ok(a, w, out):
+        N.call("pse_gemm_bf16", a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0), N.ptr(bias), out.data_ptr(),
+               out.stride(0), a.shape[0], w.shape[0], a.shape[1], 1 if gelu else 0,
+               1 if out.dtype == torch.float32 else 0, None, N.stream_ptr())
+        return gelu
     if bias is not None:
         torch.addmm(bias, a, w.t(), out=out)
     else:
         torch.mm(a, w.t(), out=out)
+    return False
 
 
 def lm_head(dm: DeviceModel, h: torch.Tensor, out: torch.Tensor) -> None:
     """fp32 logits from the final normed hidden rows."""
     if dm.dtype == torch.float32:
         torch.mm(h, dm.lm_w.t(), out=out)
+    elif _tc_ok(h, dm.lm_w, out):
+        _mm(h, dm.lm_w, out)
     else:
         out.copy_(torch.mm(h, dm.lm_w.t(), out_dtype=torch.float32))
 
 
 def forward(dm: DeviceModel, cache, slots: torch.Tensor, ids: torch.Tensor, rows: int, width: int,
             base_len: torch.Tensor, max_ctx: int, logits_out: torch.Tensor | None, last_only: bool = False,
-            scratch: Scratch | None = None) -> None:
+            scratch: Scratch | None = None, row_order: torch.Tensor | None = None) -> None:
     """One paged forward.  ``slots`` int32 [rows]; ``ids`` int32 [rows*width];
     ``base_len`` int32 [rows] receives the rows' lengths before the call;
     ``max_ctx`` >= every row's length after it.  ``logits_out`` fp32
@@ -130,26 +155,25 @@ def forward(dm: DeviceModel, cache, slots: torch.Tensor, ids: torch.Tensor, rows
                base_len.data_ptr(), rows, width, st)
         N.call("pse_paged_attention", state, kvl, qkv.data_ptr(), qkv.stride(0), attn.data_ptr(), attn.stride(0),
                slots.data_ptr(), base_len.data_ptr(), rows, width, dm.q_heads, scale, max_ctx,
-               sc.ws.data_ptr(), sc.ws.numel(), st)
-        _mm(attn, L.out_w, tmp)
-        # x += attn-out (+ bias); h = norm2(x)
-        N.call("pse_add_norm", x.data_ptr(), d, tmp.data_ptr(), d, N.ptr(L.out_b), dt, L.norm2_w.data_ptr(),
+               N.ptr(row_order), sc.ws.data_ptr(), sc.ws.numel(), st)
+        _mm(attn, L.out_w, tmp, L.out_b)
+        # x += attn-out (bias already added by the GEMM); h = norm2(x)
+        N.call("pse_add_norm", x.data_ptr(), d, tmp.data_ptr(), d, None, dt, L.norm2_w.data_ptr(),
                N.ptr(L.norm2_b), dt, T, d, dm.eps, rms, h.data_ptr(), d, dt, st)
-        _mm(h, L.up_w, up)
         if dm.kind == "llama":
+            _mm(h, L.up_w, up)
             N.call("pse_epilogue", 2, up.data_ptr(), up.stride(0), None, None, 0, act.data_ptr(), act.stride(0),
                    T, dm.d_ff, dt, st)
-        else:
-            N.call("pse_epilogue", 0, up.data_ptr(), up.stride(0), N.ptr(L.up_b), None, 0, None, 0, T, dm.d_ff,
-                   dt, st)
-        _mm(act, L.down_w, tmp)
+        elif not _mm(h, L.up_w, up, L.up_b, gelu=True):
+            N.call("pse_epilogue", 0, up.data_ptr(), up.stride(0), None, None, 0, None, 0, T, dm.d_ff, dt, st)
+        _mm(act, L.down_w, tmp, L.down_b)
         # x += mlp-out (+ bias); h = next layer's norm1(x), or the final norm after the last layer
         if li + 1 < n_layers:
             nw, nb = dm.layers[li + 1].norm1_w, dm.layers[li + 1].norm1_b
         else:
             nw, nb = dm.normf_w, dm.normf_b
-        N.call("pse_add_norm", x.data_ptr(), d, tmp.data_ptr(), d, N.ptr(L.down_b), dt, nw.data_ptr(), N.ptr(nb),
-               dt, T, d, dm.eps, rms, h.data_ptr(), d, dt, st)
+        N.call("pse_add_norm", x.data_ptr(), d, tmp.data_ptr(), d, None, dt, nw.data_ptr(), N.ptr(nb), dt, T, d,
+               dm.eps, rms, h.data_ptr(), d, dt, st)
     if logits_out is None:
         return
     hf = h.view(rows, width, d)[:, width - 1] if last_only else h

@@ -123,10 +123,12 @@ class _StepBuffers:
         self.vids = None    # deferred-bonus mode: verify ids [B, k+1] and logits [B*(k+1), V]
         self.vlog2 = None
         self.nacc1 = torch.empty(B, **i32)
+        self.order_d = torch.arange(B, **i32)  # rows longest-first, refreshed every step
+        self.order_t = torch.arange(B, **i32)
         n_pack = B * (k + 1) + B + 2
         self.pack = torch.empty(n_pack, **i32)
         self.host_pack = torch.empty(n_pack, dtype=torch.int32, pin_memory=True)
-        self.host_in = torch.empty(4 * B, dtype=torch.int32, pin_memory=True)
+        self.host_in = torch.empty(6 * B, dtype=torch.int32, pin_memory=True)
 
 
 class StepRunner:
@@ -174,11 +176,11 @@ class StepRunner:
             N.call("pse_sample_tokens", src.data_ptr(), V, idx, B, V, float(T), b.u.data_ptr(), nu, j,
                    b.drafts.data_ptr() + 4 * j, k, b.round_ids.data_ptr(), 1, st)
             forward(self.dm_d, self.dcache, b.slots_d, b.round_ids, B, 1, b.base[j], max_ctx_d, b.dlog[j],
-                    scratch=self.sc_d)
+                    scratch=self.sc_d, row_order=b.order_d)
         if not defer:
             # verify: one width-k target call (engine/speculative.py:115-117)
             forward(self.dm_t, self.tcache, b.slots_t, b.drafts.view(-1), B, k, b.base[k], max_ctx_t, b.vlog,
-                    scratch=self.sc_t)
+                    scratch=self.sc_t, row_order=b.order_t)
             t0, t0_stride, t0_index = tnext.data_ptr(), V, b.slots_t.data_ptr()
             ver, v_row = b.vlog.data_ptr(), k * V
         else:
@@ -189,7 +191,7 @@ class StepRunner:
             b.vids[:, 0] = self.tpending.index_select(0, slots_t)
             b.vids[:, 1:] = b.drafts
             forward(self.dm_t, self.tcache, b.slots_t, b.vids.view(-1), B, k + 1, b.base[k], max_ctx_t, b.vlog2,
-                    scratch=self.sc_t)
+                    scratch=self.sc_t, row_order=b.order_t)
             t0, t0_stride, t0_index = b.vlog2.data_ptr(), (k + 1) * V, None
             ver, v_row = b.vlog2.data_ptr() + 4 * V, (k + 1) * V
         # accept / reject / resample (engine/speculative.py:119-157)
@@ -211,12 +213,12 @@ class StepRunner:
         # bonus forwards (engine/speculative.py:166-177); the target's is folded
         # into the next verify in deferred mode
         forward(self.dm_d, self.dcache, b.slots_d, b.final, B, 1, b.base[k + 1], max_ctx_d, b.blog,
-                scratch=self.sc_d)
+                scratch=self.sc_d, row_order=b.order_d)
         N.call("pse_scatter_rows", b.blog.data_ptr(), V, b.slots_d.data_ptr(), B, V, dnext.data_ptr(), V,
                dnext.shape[0], st)
         if not defer:
             forward(self.dm_t, self.tcache, b.slots_t, b.final, B, 1, b.base[k + 2], max_ctx_t, b.blog,
-                    scratch=self.sc_t)
+                    scratch=self.sc_t, row_order=b.order_t)
             N.call("pse_scatter_rows", b.blog.data_ptr(), V, b.slots_t.data_ptr(), B, V, tnext.data_ptr(), V,
                    tnext.shape[0], st)
         self.dcache.last_token.index_copy_(0, b.slots_d.long(), b.final)
@@ -304,6 +306,11 @@ class StepRunner:
                 hin[2 * B:3 * B] = torch.from_numpy(keys)
                 hin[3 * B:4 * B] = torch.tensor([self.request_steps.get(r, 0) for r in request_ids],
                                                 dtype=torch.int32)
+        # longest rows first: the attention kernels hand out work in this order
+        hin[4 * B:5 * B] = torch.from_numpy(np.argsort([-dc.length(r) for r in request_ids], kind="stable").astype(np.int32))
+        hin[5 * B:6 * B] = torch.from_numpy(np.argsort([-tc.length(r) for r in request_ids], kind="stable").astype(np.int32))
+        b.order_d.copy_(hin[4 * B:5 * B], non_blocking=True)
+        b.order_t.copy_(hin[5 * B:6 * B], non_blocking=True)
         b.slots_d.copy_(hin[:B], non_blocking=True)
         b.slots_t.copy_(hin[B:2 * B], non_blocking=True)
         if philox:

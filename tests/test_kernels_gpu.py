@@ -220,9 +220,11 @@ def test_paged_attention_matches_oracle(case, generic):
     ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device="cuda")
     N.call("pse_attention_force_generic", 1 if generic else 0)
     try:
+        # rows handed out longest-first (any permutation gives the same result)
+        order = torch.from_numpy(np.argsort(-base, kind="stable").astype(np.int32)).cuda()
         N.call("pse_paged_attention", c.state, c.layer(0), qd.data_ptr(), hq * hd, out.data_ptr(), hq * hd,
                slots.data_ptr(), base_d.data_ptr(), rows, width, hq, 1.0 / math.sqrt(hd), max_ctx,
-               ws.data_ptr(), ws.numel(), N.stream_ptr())
+               order.data_ptr(), ws.data_ptr(), ws.numel(), N.stream_ptr())
         torch.cuda.synchronize()
     finally:
         N.call("pse_attention_force_generic", 0)

@@ -67,7 +67,7 @@ def test_noalloc_matches_workspace_entry_point_twice(shape):
         got = torch.full_like(q, float("nan"))
         N.call("pse_paged_attention", c.state, c.layer(0), q.data_ptr(), hq * hd, want.data_ptr(), hq * hd,
                slots.data_ptr(), base_d.data_ptr(), rows, width, hq, 1.0 / math.sqrt(hd), max_ctx,
-               ws.data_ptr(), ws.numel(), st)
+               None, ws.data_ptr(), ws.numel(), st)
         N.call("pse_paged_attention_noalloc", c.state, c.layer(0), q.data_ptr(), hq * hd, got.data_ptr(), hq * hd,
                slots.data_ptr(), base_d.data_ptr(), rows, width, hq, 1.0 / math.sqrt(hd), max_ctx, st)
         torch.cuda.synchronize()
