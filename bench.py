@@ -144,8 +144,12 @@ def run_pse(args, rank, world, device):
     mine = shard_requests(allreq, world, rank)
     B = len(mine)
     d, t = build_pair(w, dtype, device)
-    dc = cache_for(d, w, B, dtype, device, w.k + 2)
-    tc = cache_for(t, w, B, dtype, device, w.k + 2)
+    # room for every step the run takes (two structures x (warm-up + K replays + K API steps)), each
+    # committing up to k+1 tokens, plus the roofline launch's k+1 reserved tokens
+    n_steps = 2 * (max(args.warmup, 3) + 2 * args.steps)
+    extra = (w.k + 1) * (n_steps + 1) + w.k + 2
+    dc = cache_for(d, w, B, dtype, device, extra)
+    tc = cache_for(t, w, B, dtype, device, extra)
     prompts = [r.prompt_ids for r in mine]
     rids = [r.request_id for r in mine]
     dn, tn = {}, {}
@@ -156,79 +160,94 @@ def run_pse(args, rank, world, device):
     prefill_s = time.perf_counter() - t0
     k, T = w.k, w.temperature
 
-    def api_step():
-        res = pse.batched_speculative_step(d, t, rids, dc, tc, dn, tn, k, T, defer_bonus=args.defer_bonus)
+    def api_step(defer):
+        res = pse.batched_speculative_step(d, t, rids, dc, tc, dn, tn, k, T, defer_bonus=defer)
         for r in rids:
             dn[r] = res.draft_next_logits[r]
             tn[r] = res.target_next_logits[r]
         return sum(len(v) for v in res.accepted_tokens.values())
 
-    before = sum(N.launches.values())
-    api_step()  # first step of this batch size runs eagerly: count its kernels
-    kernels_per_step = sum(N.launches.values()) - before
-    for _ in range(max(args.warmup, 3) - 1):
-        api_step()
     runner = runner_for(d, t, dc, tc, k)
-    if args.profile_step:
-        torch.cuda.synchronize()
-        torch.cuda.nvtx.range_push("pse_step")
-        pse.batched_speculative_step(d, t, rids, dc, tc, dn, tn, k, T, use_graph=False, defer_bonus=args.defer_bonus)
-        torch.cuda.synchronize()
-        torch.cuda.nvtx.range_pop()
-        return None
-    graph = [g for key, g in runner.graphs.items() if key[0] == B][0]
-    b = runner.bufs[B]
-    nacc_hist = torch.zeros(args.steps, B, dtype=torch.int32, device=device)
 
     def barrier():
         if world > 1:
             torch.distributed.barrier()
         torch.cuda.synchronize()
 
-    # ---- device-resident timed region: K graph replays ----
-    launches_before = sum(N.launches.values())
-    barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(device.index or 0) as clk:
-        e0.record()
-        for s in range(args.steps):
-            graph.replay()
-            nacc_hist[s].copy_(b.n_acc)
-        e1.record()
+    def sum_ctx(c, slots):
+        return int(c._blocks.seq_len[slots.long()].sum().item())
+
+    def measure(defer):
+        """W warm-up steps through the API (the first runs eagerly and counts its
+        kernels, the second captures the step's CUDA graph), K timed graph
+        replays (inputs resident), then K timed steps through the public API."""
+        before = sum(N.launches.values())
+        api_step(defer)
+        kernels = sum(N.launches.values()) - before
+        for _ in range(max(args.warmup, 3) - 1):
+            api_step(defer)
+        if args.profile_step:
+            torch.cuda.synchronize()
+            torch.cuda.nvtx.range_push("pse_step")
+            pse.batched_speculative_step(d, t, rids, dc, tc, dn, tn, k, T, use_graph=False, defer_bonus=defer)
+            torch.cuda.synchronize()
+            torch.cuda.nvtx.range_pop()
+            return None
+        graph = [g for key, g in runner.graphs.items() if key[0] == B and key[3] == defer][0]
+        b = runner.bufs[B]
+        nacc_hist = torch.zeros(args.steps, B, dtype=torch.int32, device=device)
+        ctx0 = (sum_ctx(dc, b.slots_d), sum_ctx(tc, b.slots_t))
         barrier()
-    ms = e0.elapsed_time(e1)
-    committed = int(nacc_hist.sum().item()) + args.steps * B
-    # host mirrors of the lengths after the replays
-    for c in (dc, tc):
-        c._resync_lengths()
-    # ---- e2e through the public API ----
-    barrier()
-    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    f0.record()
-    e2e_tokens = sum(api_step() for _ in range(args.steps))
-    f1.record()
-    barrier()
-    e2e_ms = f0.elapsed_time(f1)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(device.index or 0) as clk:
+            e0.record()
+            for s in range(args.steps):
+                graph.replay()
+                nacc_hist[s].copy_(b.n_acc)
+            e1.record()
+            barrier()
+        ms = e0.elapsed_time(e1)
+        ctx1 = (sum_ctx(dc, b.slots_d), sum_ctx(tc, b.slots_t))
+        committed = int(nacc_hist.sum().item()) + args.steps * B
+        for c in (dc, tc):  # host mirrors of the lengths after the replays
+            c._resync_lengths()
+        barrier()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record()
+        e2e_tokens = sum(api_step(defer) for _ in range(args.steps))
+        f1.record()
+        barrier()
+        return dict(ms=ms, committed=committed, e2e_ms=f0.elapsed_time(f1), e2e_tokens=e2e_tokens,
+                    clocks=clk.summary(), kernels=kernels, ctx_mean=((ctx0[0] + ctx1[0]) / 2, (ctx0[1] + ctx1[1]) / 2))
+
+    if args.profile_step:
+        return measure(not args.reference_structure)
+    ref = measure(False)  # the reference's step structure: 2 target + k+1 draft calls
+    head = ref if args.reference_structure else measure(True)  # 1 target call of width k+1 + k+1 draft calls
+    b = runner.bufs[B]
+    width = k if args.reference_structure else k + 1
 
     # ---- verify-attention kernel, timed live on the current target state ----
     dm = runner.dm_t
     hd, hq, hk = dm.head_dim, dm.q_heads, dm.kv_heads
     lens = tc._blocks.seq_len[b.slots_t.long()]
-    base = (lens - k).clamp(min=0).to(torch.int32)
-    ctx = (base + k).to(torch.int64)
+    base = lens.to(torch.int32)
+    ctx = (base + width).to(torch.int64)
     max_ctx = int(ctx.max().item())
-    q = torch.randn(B * k, hq * hd, dtype=dtype, device=device)
+    q = torch.randn(B * width, hq * hd, dtype=dtype, device=device)
     out = torch.empty_like(q)
-    wsb = N.size_call("pse_paged_attention_workspace", B, k, hq, hk, hd, max_ctx)
+    wsb = N.size_call("pse_paged_attention_workspace", B, width, hq, hk, hd, max_ctx)
     ws = torch.empty(max(wsb, 1), dtype=torch.uint8, device=device)
     st = N.stream_ptr()
     reps = 20
+    # the timed launches read blocks up to base + width: reserve them so every page read is a table entry
+    N.call("pse_kv_reserve", tc.state, b.slots_t.data_ptr(), B, width, b.base[0].data_ptr(), st)
 
     def attn_all_layers():
         for li in range(dm.n_layers):
             N.call("pse_paged_attention", tc.state, tc.layer(li), q.data_ptr(), q.stride(0), out.data_ptr(),
-                   out.stride(0), b.slots_t.data_ptr(), base.data_ptr(), B, k, hq, 1.0 / math.sqrt(hd), max_ctx,
-                   None, ws.data_ptr(), ws.numel(), st)
+                   out.stride(0), b.slots_t.data_ptr(), base.data_ptr(), B, width, hq, 1.0 / math.sqrt(hd),
+                   max_ctx, None, ws.data_ptr(), ws.numel(), st)
 
     attn_all_layers()
     a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -241,21 +260,34 @@ def run_pse(args, rank, world, device):
     esize = torch.finfo(dtype).bits // 8
     attn_bytes = int(ctx.sum().item()) * hk * hd * 2 * esize + 2 * q.numel() * esize + B * 4 * tc.max_blocks
 
+    # ---- KV + weight bytes of the minimal step (1 target pass of width k+1, k draft passes) ----
+    def kv_bytes_per_token(m):
+        c = m.cfg
+        return 2 * c.n_layers * getattr(c, "n_kv_heads", c.n_heads) * (c.d_model // c.n_heads) * esize
+
+    w_t = sum(p.numel() for p in t.parameters()) * esize
+    w_d = sum(p.numel() for p in d.parameters()) * esize
+    step_bytes = (w_t + head["ctx_mean"][1] * kv_bytes_per_token(t)
+                  + k * (w_d + head["ctx_mean"][0] * kv_bytes_per_token(d)))
+
     from pse.dist import reduce_stats
-    committed, secs, _ = reduce_stats(committed, ms / 1000.0, device=device)
-    e2e_tokens, e2e_secs, _ = reduce_stats(e2e_tokens, e2e_ms / 1000.0, device=device)
-    ms, e2e_ms = secs * 1000.0, e2e_secs * 1000.0
-    launches = sum(N.launches.values()) - launches_before
-    return dict(committed=committed, ms=ms, e2e_tokens=e2e_tokens, e2e_ms=e2e_ms, attn_ms=attn_ms,
-                attn_bytes=attn_bytes, prefill_s=prefill_s, clocks=clk.summary(), B=B, k=k,
-                kernels_per_step=kernels_per_step, launches_counted=launches, dtype=str(dtype),
-                h2d=2 * B * 4, d2h=(B * (k + 1) + B + 2) * 4)
+    out = {}
+    for name, m in (("ref", ref), ("head", head)):
+        c_, s_, _ = reduce_stats(m["committed"], m["ms"] / 1000.0, device=device)
+        e_, es_, _ = reduce_stats(m["e2e_tokens"], m["e2e_ms"] / 1000.0, device=device)
+        out[name] = dict(committed=c_, ms=s_ * 1000.0, e2e_tokens=e_, e2e_ms=es_ * 1000.0)
+    return dict(ref=out["ref"], head=out["head"], attn_ms=attn_ms, attn_bytes=attn_bytes, attn_width=width,
+                prefill_s=prefill_s, clocks=head["clocks"], B=B, k=k, kernels_per_step=head["kernels"],
+                dtype=str(dtype), h2d=2 * B * 4, d2h=(B * (k + 1) + B + 2) * 4, step_bytes=step_bytes,
+                tokens_per_step_mean=head["committed"] / args.steps / max(world, 1),
+                deferred=not args.reference_structure)
 
 
-def cpu_reference(args, sample_rows, sample_steps, threads):
+def cpu_reference(args, sample_rows, sample_steps, threads, warmup=0):
     """The reference's CPU path (the oracle port of engine/*.py, fp32) on a
-    bounded sample of the same workload: prefill is untimed, then
-    ``sample_steps`` batched speculative steps over ``sample_rows`` rows."""
+    bounded sample of the same workload: prefill and ``warmup`` steps are
+    untimed, then ``sample_steps`` batched speculative steps over
+    ``sample_rows`` rows."""
     from oracle.model import LlamaConfig, ModelConfig, TinyGPT, TinyLlama
     from oracle.paged_cache import PagedKVCache
     from oracle.speculative import batched_speculative_step, prefill_request
@@ -285,6 +317,9 @@ def cpu_reference(args, sample_rows, sample_steps, threads):
     dn, tn = {}, {}
     for r, p in zip(rids, prompts):
         dn[r], tn[r] = prefill_request(d, t, dc, tc, r, p)
+    for _ in range(warmup):
+        res = batched_speculative_step(d, t, rids, dc, tc, dn, tn, w.k, w.temperature)
+        dn, tn = res.draft_next_logits, res.target_next_logits
     tok = 0
     t0 = time.perf_counter()
     for _ in range(sample_steps):
@@ -297,9 +332,16 @@ def cpu_reference(args, sample_rows, sample_steps, threads):
                        f"workload (prompts from the same seed), fp32 oracle port, prefill untimed")
 
 
+# ncu dram__bytes_read.sum + dram__bytes_write.sum over the algorithmic bytes of
+# attn_tc_kernel, captured on the gpt2-verify microbench shape (the summary
+# with the command is profiles/attn_tc_gpt2-verify.md); keyed by (workload,
+# verify width).
+ATTN_TRAFFIC_RATIO: dict = {("gpt2-small", 6): (481367040 + 4925440) / 477461504}
+
 ATTN_SHAPES = {
     # name: rows, width, q_heads, kv_heads, head_dim, block, ctx_lo, ctx_hi (ctx includes the width queries)
-    "gpt2-verify": (256, 5, 12, 12, 64, 16, 133, 1029),
+    "gpt2-verify": (256, 6, 12, 12, 64, 16, 134, 1030),
+    "gpt2-verify5": (256, 5, 12, 12, 64, 16, 133, 1029),
     "gpt2-draft": (256, 1, 6, 6, 64, 16, 129, 1025),
     "verify-5a": (1024, 8, 32, 8, 128, 16, 512, 32768),
 }
@@ -489,13 +531,14 @@ def main():
     ap.add_argument("--workload", default="gpt2-small")
     ap.add_argument("--rows", type=int, default=None)
     ap.add_argument("--cpu-rows", type=int, default=4)
-    ap.add_argument("--cpu-steps", type=int, default=2)
+    ap.add_argument("--cpu-steps", type=int, default=10)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--micro", choices=["attn", "accept", "churn"], default=None,
                     help="kernel microbenchmark instead of the step")
     ap.add_argument("--temperature", type=float, default=1.0, help="--micro accept: temperature")
-    ap.add_argument("--defer-bonus", action="store_true",
-                    help="fold the target's bonus call into the next verify (one target pass per step)")
+    ap.add_argument("--reference-structure", action="store_true",
+                    help="headline the reference's step structure (2 target calls per step) instead of the "
+                         "deferred-bonus step (the target's bonus call folded into the next verify)")
     ap.add_argument("--attn-shape", default="gpt2-verify", choices=sorted(ATTN_SHAPES))
     ap.add_argument("--profile-step", action="store_true",
                     help="after warm-up run one eager step inside the NVTX range 'pse_step' and exit (for ncu)")
@@ -512,12 +555,13 @@ def main():
         if rank != 0:
             return
         threads = os.cpu_count() or 1
-        r = cpu_reference(args, args.cpu_rows, args.cpu_steps, threads)
+        # each step of this arm is one batched step over a bounded sample of the rows
+        r = cpu_reference(args, args.cpu_rows, args.steps, threads, warmup=args.warmup)
         line = {"impl": "reference", "metric": metric, "value": r["value"], "unit": "tokens/s", "n_gpus": args.gpus,
-                "steps": args.cpu_steps, "warmup": 0, "ms_per_step": 1000 * r["seconds"] / args.cpu_steps,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * r["seconds"] / args.steps,
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-                "data": "synthetic prompts, random-init weights",
-                "config": config_block(args, w, args.cpu_rows, 1),
+                "data": "synthetic prompts (seeded), random-init weights (seed 0)",
+                "config": config_block(args, w, w.max_batch_size if args.rows is None else args.rows, args.gpus),
                 "cpu_baseline": {"value": r["value"], "unit": "tokens/s", "cores": r["cores"], "kind": "port",
                                  "sample": r["sample"]},
                 "e2e": {"value": r["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -554,19 +598,37 @@ def main():
         torch.distributed.destroy_process_group()
     if rank != 0:
         return
-    value = r["committed"] / (r["ms"] / 1000.0)
+    hd_, rf_ = r["head"], r["ref"]
+    value = hd_["committed"] / (hd_["ms"] / 1000.0)
     achieved = r["attn_bytes"] / (r["attn_ms"] / 1000.0) / 1e9
+    per_gpu_tok_step = hd_["committed"] / args.steps / world
+    roof_tok_s = per_gpu_tok_step / (r["step_bytes"] / (peak * 1e9)) * world
+    ratio = ATTN_TRAFFIC_RATIO.get((args.workload, r["attn_width"]))
     line = {
         "metric": metric, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-        "warmup": max(args.warmup, 3), "ms_per_step": r["ms"] / args.steps, "higher_is_better": True,
+        "warmup": max(args.warmup, 3), "ms_per_step": hd_["ms"] / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16" if "bfloat16" in r["dtype"] else "f32",
         "data": "synthetic prompts (seeded), random-init weights (seed 0)",
         "config": config_block(args, w, r["B"], world),
-        "e2e": {"value": r["e2e_tokens"] / (r["e2e_ms"] / 1000.0), "unit": "tokens/s",
+        "step": ("deferred bonus: 1 target call of width k+1 + k+1 draft calls per step; token streams identical "
+                 "to the reference structure" if r["deferred"] else
+                 "reference structure: 2 target + k+1 draft calls per step"),
+        "e2e": {"value": hd_["e2e_tokens"] / (hd_["e2e_ms"] / 1000.0), "unit": "tokens/s",
                 "h2d_bytes_per_step": r["h2d"], "d2h_bytes_per_step": r["d2h"]},
-        "roofline": {"kernel": "pse_paged_attention (target verify, width k, all layers)", "bound": "hbm",
-                     "achieved": achieved, "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
-                     "frac": achieved / peak, "traffic": None, "avg_launch_us": r["attn_ms"] * 1000},
+        "reference_structure": {"value": rf_["committed"] / (rf_["ms"] / 1000.0),
+                                "ms_per_step": rf_["ms"] / args.steps,
+                                "e2e": rf_["e2e_tokens"] / (rf_["e2e_ms"] / 1000.0)},
+        "roofline": {"kernel": f"pse_paged_attention (target verify, width {r['attn_width']}, all layers)",
+                     "bound": "hbm", "achieved": achieved, "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
+                     "frac": achieved / peak,
+                     "traffic": None if ratio is None else ratio * r["attn_bytes"],
+                     "traffic_note": None if ratio is None else
+                     "ncu dram bytes / algorithmic bytes of the same kernel on the gpt2-verify microbench shape, "
+                     "scaled to this launch's algorithmic bytes",
+                     "avg_launch_us": r["attn_ms"] * 1000, "algorithmic_bytes": r["attn_bytes"]},
+        "step_roofline": {"bound": "hbm (KV + weights of 1 target pass of width k+1 and k draft passes)",
+                          "bytes_per_step_per_gpu": r["step_bytes"], "tokens_per_step_per_gpu": per_gpu_tok_step,
+                          "roofline_tokens_s": roof_tok_s, "frac": value / roof_tok_s},
         "cpu_baseline": None if cpu is None else {"value": cpu["value"], "unit": "tokens/s", "cores": cpu["cores"],
                                                   "kind": "port", "sample": cpu["sample"]},
         "clocks": r["clocks"],

@@ -191,7 +191,7 @@ int pse_sample_tokens(const float *logits, int64_t row_stride, const int32_t *in
                       int64_t out2_stride, void *stream);
 
 /* Fused accept / reject / residual / bonus of engine/speculative.py:119-157
- * (and _residual_sample, :43-50), one CTA per row.  Target position 0 is
+ * (and _residual_sample, :43-50).  Target position 0 is
  * target0 + (t0_index ? t0_index[i] : i) * t0_stride; positions 1..k are
  * verify + i*v_row + (j-1)*v_pos.  Draft position 0 is draft0 + (d0_index ?
  * d0_index[i] : i) * d0_stride; positions 1..k-1 are draft_rest + i*dr_row +
@@ -199,7 +199,10 @@ int pse_sample_tokens(const float *logits, int64_t row_stride, const int32_t *in
  * the drafted ids, u[i*u_stride + k + j] the accept uniforms and u[i*u_stride
  * + 2k] the residual / bonus uniform.  Writes tokens[i*(k+1) + 0..n] (the
  * accepted drafts then the corrected / bonus token), n_accepted[i] and
- * final_token[i] (= tokens[i*(k+1) + n_accepted[i]]). */
+ * final_token[i] (= tokens[i*(k+1) + n_accepted[i]]).
+ * T <= 0 runs one CTA per row; T > 0 with vocab <= 131072 runs one
+ * thread-block cluster (ceil(vocab / 16384) CTAs) per row with the row's
+ * logits held on chip, larger vocabularies one CTA per row. */
 int pse_spec_accept(const float *target0, int64_t t0_stride, const int32_t *t0_index,
                     const float *verify, int64_t v_row, int64_t v_pos,
                     const float *draft0, int64_t d0_stride, const int32_t *d0_index,
@@ -207,6 +210,11 @@ int pse_spec_accept(const float *target0, int64_t t0_stride, const int32_t *t0_i
                     const int32_t *drafts, const double *u, int64_t u_stride, int32_t rows,
                     int32_t k, int32_t vocab, float temperature, int32_t *tokens,
                     int32_t *n_accepted, int32_t *final_token, void *stream);
+
+/* on != 0 makes pse_spec_accept run the CTA-per-row kernel at every
+ * temperature (parity tests compare it with the cluster kernel); no
+ * counterpart in the reference. */
+int pse_accept_force_per_row(int32_t on);
 
 /* ------------------------------------------------------------------------ */
 /* Model pieces (TinyGPT engine/model.py:121-206; Llama-style variant)       */

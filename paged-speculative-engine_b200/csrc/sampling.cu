@@ -22,6 +22,9 @@ namespace pse {
 namespace {
 
 constexpr int kSampleThreads = 512;
+
+// Forces the CTA-per-row accept kernel at T > 0 (tests compare the two forms).
+int g_accept_per_row = 0;
 constexpr int kWarpsPerBlock = kSampleThreads / 32;
 
 // ---------------------------------------------------------------- Philox4x32-10
@@ -401,6 +404,485 @@ __global__ void __launch_bounds__(kSampleThreads) accept_kernel(AcceptArgs a) {
   }
 }
 
+// ---------------------------------------------------------------- accept / resample, T > 0, one cluster per row
+//
+// A thread-block cluster of C CTAs (C = ceil(V / 16384) <= 8) owns one request
+// row at a time.  The vocabulary is cut into C x 16 warp segments of 32 lane
+// runs of `run_len` consecutive entries (a multiple of 4, at most 32).  A lane keeps its run of
+// the current position's target logits in registers and of the draft logits
+// in shared memory (16-byte cp.async, no register staging), so every logit is
+// read from HBM once and the max / sum / residual passes of the rule run on
+// chip.
+//
+// Cluster reductions: every warp stores its partial (max, sum, last nonzero
+// index) straight into the mailbox of every CTA of the cluster (DSMEM
+// stores), then one cluster barrier; each warp then reduces the C x 16
+// partials from its own mailbox with the same fixed tree, so all CTAs hold
+// bit-identical totals, take identical decisions and keep their barriers
+// matched.  Mailboxes alternate between two slots: a slot is rewritten only
+// two reductions later, after every CTA has passed the barrier that follows
+// its reads of it.  Clusters are persistent over rows.
+//
+// Sums: a lane adds its run in index order; lanes, warps and CTAs combine by
+// fixed trees.  The inverse CDF descends warp segment (scan over the C x 16
+// segment sums) -> lane (scan over the warp's 32 run sums) -> entry (the
+// lane's run, in order).
+
+constexpr int kClThreads = 512;
+constexpr int kClWarps = kClThreads / 32;
+constexpr int kClRun = 32;                            // max entries per lane per vector
+constexpr int kClCtaCap = kClWarps * 32 * kClRun;     // 16384 vocabulary entries per CTA
+constexpr int kClMax = 8;                             // portable cluster size
+constexpr int kClSegs = kClMax * kClWarps;            // warp segments per cluster (max)
+constexpr int kClQStride = kClRun + 4;                // lane stride of the draft run in shared memory
+
+struct Mail {
+  float mx[2][kClSegs];     // maxima of s_p, s_q per warp segment
+  double sum[2][kClSegs];   // sums of w_p, w_q (or the residual in [1]) per segment
+  int last[2][kClSegs];     // last index of nonzero weight per segment
+  double xw[2];             // w_p[x], w_q[x] from the lane that holds x
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_id_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_count_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Address of `p` (this CTA's shared memory) in the shared memory of cluster rank `rank`.
+__device__ __forceinline__ uint32_t peer_addr(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void st_peer(uint32_t a, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(a), "f"(v) : "memory");
+}
+__device__ __forceinline__ void st_peer(uint32_t a, double v) {
+  asm volatile("st.shared::cluster.f64 [%0], %1;" ::"r"(a), "d"(v) : "memory");
+}
+__device__ __forceinline__ void st_peer(uint32_t a, int v) {
+  asm volatile("st.shared::cluster.s32 [%0], %1;" ::"r"(a), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ int warp_max_i(int v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = max(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+constexpr int kClG = kClSegs / 32;  // warp segments per lane in the descent (4)
+
+// Exclusive prefix over lanes of per-lane totals, plus `run`.
+__device__ __forceinline__ double lane_excl_prefix(double tot, double run) {
+  const int lane = threadIdx.x & 31;
+  const double incl = warp_inclusive_scan_d(tot);
+  const double ex = __shfl_up_sync(0xffffffffu, incl, 1);
+  return (lane == 0 ? 0.0 : ex) + run;
+}
+
+// Values v[0..G) of each lane, in lane-major order, form one sequence.  Finds
+// the first element at which `run + prefix` exceeds t; returns its index
+// (lane * G + j) and sets `run` to the prefix before it.  -1 (run unchanged)
+// if none.  Uniform over the warp.
+template <int G>
+__device__ __forceinline__ int group_cross(const double (&v)[G], double t, double& run) {
+  double tot = 0.0;
+#pragma unroll
+  for (int j = 0; j < G; ++j) tot += v[j];
+  double acc = lane_excl_prefix(tot, run);
+  int jh = -1;
+  double before = 0.0;
+#pragma unroll
+  for (int j = 0; j < G; ++j) {
+    if (jh < 0) {
+      if (acc + v[j] > t) {
+        jh = j;
+        before = acc;
+      } else {
+        acc += v[j];
+      }
+    }
+  }
+  const unsigned m = __ballot_sync(0xffffffffu, jh >= 0);
+  if (!m) return -1;
+  const int l = __ffs(m) - 1;
+  run = __shfl_sync(0xffffffffu, before, l);
+  return l * G + __shfl_sync(0xffffffffu, jh, l);
+}
+
+__device__ __forceinline__ double resid(float wp, float wq, double invp, double invq) {
+  // max(0, w_p / Z_p - w_q / Z_q) in fp64, products and difference rounded separately
+  const double r = __dsub_rn(__dmul_rn((double)wp, invp), __dmul_rn((double)wq, invq));
+  return r > 0.0 ? r : 0.0;
+}
+
+template <int C>
+__global__ void __launch_bounds__(kClThreads, 1) accept_cluster_kernel(AcceptArgs a, int rows, int run_len) {
+  __shared__ Mail box[2];
+  extern __shared__ __align__(16) float q_all[];  // [kClThreads][kClQStride] draft runs
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int rank = (int)cluster_ctarank();
+  const int n_cl = (int)cluster_count_x();
+  const int k = a.k, V = a.V;
+  const float T = a.T;
+  const int seg = 32 * run_len;                  // entries per warp segment
+  const int n_seg = C * kClWarps;
+  const int g = rank * kClWarps + warp;          // this warp's segment
+  const int e_lane = g * seg + lane * run_len;   // first entry of this lane's run
+  const int n4 = run_len >> 2;
+  float* qs = q_all + threadIdx.x * kClQStride;
+  float p[kClRun];
+  int ph = 0;
+  const uint32_t slot_bytes = sizeof(Mail);
+
+  auto load_p = [&](const float* row) {
+#pragma unroll
+    for (int c = 0; c < kClRun / 4; ++c) {
+      float4 v = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+      if (c < n4 && e_lane + 4 * c < V) v = __ldcs(reinterpret_cast<const float4*>(row + e_lane + 4 * c));
+      p[4 * c] = v.x;
+      p[4 * c + 1] = v.y;
+      p[4 * c + 2] = v.z;
+      p[4 * c + 3] = v.w;
+    }
+  };
+  auto load_q = [&](const float* row) {
+#pragma unroll
+    for (int c = 0; c < kClRun / 4; ++c) {
+      if (c < n4) {
+        const bool ok = e_lane + 4 * c < V;
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(qs + 4 * c)),
+                     "l"(ok ? row + e_lane + 4 * c : row), "r"(ok ? 16 : 0)
+                     : "memory");
+      }
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+
+  for (int i = (int)cluster_id_x(); i < rows; i += n_cl) {
+    const double* u = a.u + (int64_t)i * a.u_stride;
+    const int32_t* drafted = a.drafts + (int64_t)i * k;
+    int32_t* toks = a.tokens + (int64_t)i * (k + 1);
+    load_q(draft_row(a, i, 0));
+    load_p(target_row(a, i, 0));
+    for (int j = 0; j <= k; ++j) {
+      const bool bonus = j == k;  // every draft accepted: sample target[k]
+      if (j > 0) {
+        if (!bonus) load_q(draft_row(a, i, j));
+        load_p(target_row(a, i, j));
+      }
+      // ---- maxima of s = l / T (s kept in place)
+      float mp = -INFINITY, mq = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < kClRun; ++c) {
+        if (T != 1.0f) p[c] = p[c] / T;  // l / 1 is l: skip the division
+        mp = fmaxf(mp, p[c]);
+      }
+      if (!bonus) {
+        asm volatile("cp.async.wait_group 0;" ::: "memory");
+#pragma unroll
+        for (int c = 0; c < kClRun / 4; ++c) {
+          if (c < n4) {
+            float4 v = *reinterpret_cast<float4*>(qs + 4 * c);
+            const bool ok = e_lane + 4 * c < V;
+            if (T != 1.0f) {
+              v.x = v.x / T;
+              v.y = v.y / T;
+              v.z = v.z / T;
+              v.w = v.w / T;
+            }
+            if (!ok) v.x = v.y = v.z = v.w = -INFINITY;
+            *reinterpret_cast<float4*>(qs + 4 * c) = v;
+            mq = fmaxf(mq, fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w)));
+          }
+        }
+      }
+      mp = warp_max(mp);
+      mq = warp_max(mq);
+      if (lane < C) {
+        const uint32_t b = peer_addr(&box[0], lane) + ph * slot_bytes;
+        st_peer(b + (uint32_t)offsetof(Mail, mx[0][0]) + 4u * g, mp);
+        st_peer(b + (uint32_t)offsetof(Mail, mx[1][0]) + 4u * g, mq);
+      }
+      cluster_sync_all();
+      {
+        const Mail& m = box[ph];
+        float x0 = -INFINITY, y0 = -INFINITY;
+#pragma unroll
+        for (int jj = 0; jj < kClG; ++jj) {
+          const int sg = kClG * lane + jj;
+          if (sg < n_seg) {
+            x0 = fmaxf(x0, m.mx[0][sg]);
+            y0 = fmaxf(y0, m.mx[1][sg]);
+          }
+        }
+        mp = warp_max(x0);
+        mq = warp_max(y0);
+      }
+      ph ^= 1;
+      // ---- weights w = expf(s - m) in place; run sums; last nonzero; w[x]
+      const int x = bonus ? -1 : drafted[j];
+      const bool x_ok = x >= 0 && x < V;
+      double sp = 0.0, sq = 0.0;
+      int lp = -1;
+#pragma unroll
+      for (int c = 0; c < kClRun; ++c) {
+        const float wp = expf(p[c] - mp);
+        p[c] = wp;
+        sp += (double)wp;
+        if (wp > 0.f) lp = e_lane + c;
+      }
+      if (!bonus) {
+#pragma unroll
+        for (int c = 0; c < kClRun / 4; ++c) {
+          if (c < n4) {
+            float4 v = *reinterpret_cast<float4*>(qs + 4 * c);
+            v.x = expf(v.x - mq);
+            v.y = expf(v.y - mq);
+            v.z = expf(v.z - mq);
+            v.w = expf(v.w - mq);
+            *reinterpret_cast<float4*>(qs + 4 * c) = v;
+            sq += (double)v.x;
+            sq += (double)v.y;
+            sq += (double)v.z;
+            sq += (double)v.w;
+          }
+        }
+      }
+      // lane sums in lane order within the warp (fixed tree)
+      const double sp_lane = sp;
+      sp = warp_sum_d(sp);
+      sq = warp_sum_d(sq);
+      lp = warp_max_i(lp);
+      const bool x_here = x_ok && x >= e_lane && x < e_lane + run_len;
+      if (lane < C) {
+        const uint32_t b = peer_addr(&box[0], lane) + ph * slot_bytes;
+        st_peer(b + (uint32_t)offsetof(Mail, sum[0][0]) + 8u * g, sp);
+        st_peer(b + (uint32_t)offsetof(Mail, sum[1][0]) + 8u * g, sq);
+        st_peer(b + (uint32_t)offsetof(Mail, last[0][0]) + 4u * g, lp);
+      }
+      if (x_here) {
+        const int c = x - e_lane;
+        float wpx = 0.f;
+#pragma unroll
+        for (int c2 = 0; c2 < kClRun; ++c2)
+          if (c2 == c) wpx = p[c2];
+        const float wqx = qs[c];
+        for (int r = 0; r < C; ++r) {
+          const uint32_t b = peer_addr(&box[0], r) + ph * slot_bytes;
+          st_peer(b + (uint32_t)offsetof(Mail, xw[0]), (double)wpx);
+          st_peer(b + (uint32_t)offsetof(Mail, xw[1]), (double)wqx);
+        }
+      }
+      cluster_sync_all();
+      // segment sums stay in registers for the descent (lane l: segments kClG*l ..)
+      double segp[kClG];
+      int lastseg[kClG];
+      int last_p = -1;
+      double wpx = 0.0, wqx = 0.0;
+      double Zp = 0.0, Zq = 0.0;
+      {
+        const Mail& m = box[ph];
+#pragma unroll
+        for (int jj = 0; jj < kClG; ++jj) {
+          const int sg = kClG * lane + jj;
+          segp[jj] = sg < n_seg ? m.sum[0][sg] : 0.0;
+          lastseg[jj] = sg < n_seg ? m.last[0][sg] : -1;
+          Zp += segp[jj];
+          Zq += sg < n_seg ? m.sum[1][sg] : 0.0;
+          last_p = max(last_p, lastseg[jj]);
+        }
+        last_p = warp_max_i(last_p);
+        if (x_ok) {
+          wpx = m.xw[0];
+          wqx = m.xw[1];
+        }
+      }
+      ph ^= 1;
+      Zp = warp_sum_d(Zp);
+      Zq = warp_sum_d(Zq);
+      bool use_resid = false;
+      double t = 0.0, invp = 0.0, invq = 0.0;
+      double sr_lane = 0.0;
+      int n_acc = k;
+      if (!bonus) {
+        // engine/speculative.py:133-142
+        double prob = 0.0;
+        if (x_ok && wqx > 0.0) {
+          const double ratio = __ddiv_rn(__dmul_rn(wpx, Zq), __dmul_rn(wqx, Zp));
+          prob = ratio < 1.0 ? ratio : 1.0;
+        }
+        if (u[k + j] < prob) {
+          if (rank == 0 && threadIdx.x == 0) toks[j] = x;
+          continue;
+        }
+        // engine/speculative.py:43-50: residual max(0, p - q), or p if it is empty
+        n_acc = j;
+        invp = 1.0 / Zp;
+        invq = 1.0 / Zq;
+        int lr = -1;
+#pragma unroll
+        for (int c4 = 0; c4 < kClRun / 4; ++c4) {
+          if (c4 < n4) {
+            const float4 w4 = *reinterpret_cast<const float4*>(qs + 4 * c4);
+            const float wq4[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc) {
+              const double r = resid(p[4 * c4 + cc], wq4[cc], invp, invq);
+              sr_lane += r;
+              if (r > 0.0) lr = e_lane + 4 * c4 + cc;
+            }
+          }
+        }
+        const double sr = warp_sum_d(sr_lane);
+        lr = warp_max_i(lr);
+        if (lane < C) {
+          const uint32_t b = peer_addr(&box[0], lane) + ph * slot_bytes;
+          st_peer(b + (uint32_t)offsetof(Mail, sum[1][0]) + 8u * g, sr);
+          st_peer(b + (uint32_t)offsetof(Mail, last[1][0]) + 4u * g, lr);
+        }
+        cluster_sync_all();
+        double segr[kClG];
+        int lastr_seg[kClG];
+        int last_r = -1;
+        double R = 0.0;
+        {
+          const Mail& m = box[ph];
+#pragma unroll
+          for (int jj = 0; jj < kClG; ++jj) {
+            const int sg = kClG * lane + jj;
+            segr[jj] = sg < n_seg ? m.sum[1][sg] : 0.0;
+            lastr_seg[jj] = sg < n_seg ? m.last[1][sg] : -1;
+            R += segr[jj];
+            last_r = max(last_r, lastr_seg[jj]);
+          }
+          last_r = warp_max_i(last_r);
+        }
+        ph ^= 1;
+        R = warp_sum_d(R);
+        if (R > 0.0) {
+          use_resid = true;
+          t = u[2 * k] * R;
+#pragma unroll
+          for (int jj = 0; jj < kClG; ++jj) {  // descend over the residual sums
+            segp[jj] = segr[jj];
+            lastseg[jj] = lastr_seg[jj];
+          }
+          last_p = last_r;
+        }
+      }
+      if (!use_resid) t = u[2 * k] * Zp;
+      // ---- inverse CDF: warp segment -> lane run -> entry
+      double run = 0.0;
+      const int g_hit = group_cross<kClG>(segp, t, run);
+      int fin = last_p >= 0 ? last_p : 0;  // fallback: last entry of nonzero weight
+      const int writer = g_hit >= 0 ? g_hit : 0;  // the segment whose lane 0 writes the row
+      if (g_hit >= 0) {
+        // the hit segment's last nonzero entry, in case rounding leaves no crossing inside it
+        int ls = -1;
+#pragma unroll
+        for (int jj = 0; jj < kClG; ++jj)
+          if (jj == g_hit % kClG) ls = lastseg[jj];
+        ls = __shfl_sync(0xffffffffu, ls, g_hit / kClG);
+        if (ls >= 0) fin = ls;
+      }
+      if (g == writer) {
+        if (g_hit >= 0) {
+          const double mine[1] = {use_resid ? sr_lane : sp_lane};
+          const int l_hit = group_cross<1>(mine, t, run);
+          int found = -1;
+          if (l_hit >= 0 && lane == l_hit) {
+            double acc = run;
+#pragma unroll
+            for (int c = 0; c < kClRun; ++c) {
+              if (found < 0 && c < run_len && e_lane + c < V) {
+                acc += use_resid ? resid(p[c], qs[c], invp, invq) : (double)p[c];
+                if (acc > t) found = e_lane + c;
+              }
+            }
+          }
+          found = warp_max_i(found);
+          if (found >= 0) fin = found;
+        }
+        if (lane == 0) {
+          toks[n_acc] = fin;
+          for (int jj = n_acc + 1; jj <= k; ++jj) toks[jj] = -1;
+          a.n_accepted[i] = n_acc;
+          a.final_token[i] = fin;
+        }
+      }
+      break;  // the row is finished (rejection or bonus)
+    }
+  }
+  // no CTA leaves while a peer may still store into or read its mailbox
+  cluster_sync_all();
+}
+
+template <int C>
+int launch_accept_cluster(const AcceptArgs& a, int rows, int run_len, cudaStream_t stream) {
+  static int max_clusters[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -1;
+  const size_t smem = (size_t)kClThreads * kClQStride * sizeof(float);
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = C;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(kClThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (max_clusters[dev] == 0) {
+    if (cudaFuncSetAttribute(accept_cluster_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+        cudaSuccess) {
+      cudaGetLastError();
+      return -1;
+    }
+    int sms = kNumSMs;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cfg.gridDim = dim3((unsigned)(C * (sms / C)), 1, 1);
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, accept_cluster_kernel<C>, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      return -1;
+    }
+    max_clusters[dev] = n;
+  }
+  const int n_cl = rows < max_clusters[dev] ? rows : max_clusters[dev];
+  cfg.gridDim = dim3((unsigned)(C * n_cl), 1, 1);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, accept_cluster_kernel<C>, a, rows, run_len);
+  return e == cudaSuccess ? 0 : (int)e;
+}
+
+// The cluster kernel reads 16-byte vectors: every logits row must start on a
+// 16-byte boundary (base pointers aligned, strides and vocab multiples of 4),
+// and the vocabulary must fit 8 CTAs.
+bool cluster_accept_ok(const AcceptArgs& a) {
+  auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  auto m4 = [](int64_t v) { return (v & 3) == 0; };
+  if (a.V > kClMax * kClCtaCap || !m4(a.V)) return false;
+  if (!al(a.target0) || !al(a.verify) || !al(a.draft0) || (a.k > 1 && !al(a.draft_rest))) return false;
+  return m4(a.t0_stride) && m4(a.v_row) && m4(a.v_pos) && m4(a.d0_stride) && (a.k <= 1 || (m4(a.dr_row) && m4(a.dr_pos)));
+}
+
 }  // namespace
 }  // namespace pse
 
@@ -432,6 +914,11 @@ extern "C" int pse_sample_tokens(const float* logits, int64_t row_stride, const 
   return PSE_OK;
 }
 
+extern "C" int pse_accept_force_per_row(int32_t on) {
+  g_accept_per_row = on ? 1 : 0;
+  return PSE_OK;
+}
+
 extern "C" int pse_spec_accept(const float* target0, int64_t t0_stride, const int32_t* t0_index, const float* verify,
                                int64_t v_row, int64_t v_pos, const float* draft0, int64_t d0_stride,
                                const int32_t* d0_index, const float* draft_rest, int64_t dr_row, int64_t dr_pos,
@@ -444,6 +931,26 @@ extern "C" int pse_spec_accept(const float* target0, int64_t t0_stride, const in
   if (temperature > 0.f && (!u || !draft0 || (k > 1 && !draft_rest))) return PSE_EINVAL;
   AcceptArgs a{target0, t0_stride, t0_index, verify, v_row, v_pos, draft0, d0_stride, d0_index, draft_rest,
                dr_row, dr_pos, drafts, u, u_stride, k, vocab, temperature, tokens, n_accepted, final_token};
+  if (temperature > 0.f && !g_accept_per_row && cluster_accept_ok(a)) {
+    // one cluster per row with the row held on chip (vocabularies up to 8 x 16384)
+    const int C = (vocab + kClCtaCap - 1) / kClCtaCap;
+    const int per_lane = (vocab + C * kClThreads - 1) / (C * kClThreads);
+    const int run_len = (per_lane + 3) & ~3;  // <= 64
+    int rc = -1;
+    switch (C) {
+      case 1: rc = launch_accept_cluster<1>(a, rows, run_len, (cudaStream_t)stream); break;
+      case 2: rc = launch_accept_cluster<2>(a, rows, run_len, (cudaStream_t)stream); break;
+      case 3: rc = launch_accept_cluster<3>(a, rows, run_len, (cudaStream_t)stream); break;
+      case 4: rc = launch_accept_cluster<4>(a, rows, run_len, (cudaStream_t)stream); break;
+      case 5: rc = launch_accept_cluster<5>(a, rows, run_len, (cudaStream_t)stream); break;
+      case 6: rc = launch_accept_cluster<6>(a, rows, run_len, (cudaStream_t)stream); break;
+      case 7: rc = launch_accept_cluster<7>(a, rows, run_len, (cudaStream_t)stream); break;
+      default: rc = launch_accept_cluster<8>(a, rows, run_len, (cudaStream_t)stream); break;
+    }
+    if (rc > 0) return rc;
+    if (rc == 0) return PSE_OK;
+    // rc < 0: no cluster of this size fits on the device; the CTA-per-row kernel below handles it
+  }
   accept_kernel<<<rows, kSampleThreads, 0, (cudaStream_t)stream>>>(a);
   PSE_LAUNCH_CHECK();
   return PSE_OK;
