@@ -49,10 +49,16 @@ def _peaks():
 class ClockSampler:
     """nvidia-smi clock / throttle sampling during the timed region."""
 
-    def __init__(self, index: int):
+    def __init__(self, index: int, interval_ms: int = 20):
         self.index = index
+        self.interval_ms = interval_ms
         self.proc = None
-        self.lines: list[str] = []
+        self.lines: list[tuple[float, str]] = []
+        self.marks: list[float] = []
+
+    def mark(self) -> None:
+        """Start / end of a timed region (call in pairs)."""
+        self.marks.append(time.perf_counter())
 
     def __enter__(self):
         try:
@@ -61,7 +67,7 @@ class ClockSampler:
                  "--query-gpu=clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
                  "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
                  "clocks_event_reasons.sw_power_cap",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
+                 "--format=csv,noheader,nounits", "-lms", str(self.interval_ms)],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
@@ -71,7 +77,7 @@ class ClockSampler:
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.perf_counter(), line.strip()))
 
     def __exit__(self, *a):
         if self.proc is not None:
@@ -84,7 +90,11 @@ class ClockSampler:
     def summary(self):
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        windows = list(zip(self.marks[0::2], self.marks[1::2]))
+        # a sample reports the interval that ends at its arrival: keep the ones that overlap a timed region
+        slack = self.interval_ms / 1000.0
+        inside = [ln for t, ln in self.lines if not windows or any(a <= t <= b + slack for a, b in windows)]
+        for ln in inside:
             parts = [x.strip() for x in ln.split(",")]
             if len(parts) < 7:
                 continue
@@ -97,7 +107,7 @@ class ClockSampler:
                 if v.lower() == "active":
                     reasons.add(n)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm), "interval_ms": self.interval_ms}
 
 
 def build_pair(workload, dtype, device, seed=0):
@@ -199,13 +209,14 @@ def run_pse(args, rank, world, device):
         ctx0 = (sum_ctx(dc, b.slots_d), sum_ctx(tc, b.slots_t))
         barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        with ClockSampler(device.index or 0) as clk:
-            e0.record()
-            for s in range(args.steps):
-                graph.replay()
-                nacc_hist[s].copy_(b.n_acc)
-            e1.record()
-            barrier()
+        clk.mark()
+        e0.record()
+        for s in range(args.steps):
+            graph.replay()
+            nacc_hist[s].copy_(b.n_acc)
+        e1.record()
+        barrier()
+        clk.mark()
         ms = e0.elapsed_time(e1)
         ctx1 = (sum_ctx(dc, b.slots_d), sum_ctx(tc, b.slots_t))
         committed = int(nacc_hist.sum().item()) + args.steps * B
@@ -218,12 +229,16 @@ def run_pse(args, rank, world, device):
         f1.record()
         barrier()
         return dict(ms=ms, committed=committed, e2e_ms=f0.elapsed_time(f1), e2e_tokens=e2e_tokens,
-                    clocks=clk.summary(), kernels=kernels, ctx_mean=((ctx0[0] + ctx1[0]) / 2, (ctx0[1] + ctx1[1]) / 2))
+                    kernels=kernels, ctx_mean=((ctx0[0] + ctx1[0]) / 2, (ctx0[1] + ctx1[1]) / 2))
 
     if args.profile_step:
         return measure(not args.reference_structure)
-    ref = measure(False)  # the reference's step structure: 2 target + k+1 draft calls
-    head = ref if args.reference_structure else measure(True)  # 1 target call of width k+1 + k+1 draft calls
+    # clocks are sampled from before the first warm-up to the end of the last timed region;
+    # the summary keeps the samples taken inside the timed regions
+    with ClockSampler(device.index or 0) as clk:
+        ref = measure(False)  # the reference's step structure: 2 target + k+1 draft calls
+        head = ref if args.reference_structure else measure(True)  # 1 target call of width k+1 + k+1 draft calls
+    head["clocks"] = clk.summary()
     b = runner.bufs[B]
     width = k if args.reference_structure else k + 1
 
@@ -278,7 +293,7 @@ def run_pse(args, rank, world, device):
         out[name] = dict(committed=c_, ms=s_ * 1000.0, e2e_tokens=e_, e2e_ms=es_ * 1000.0)
     return dict(ref=out["ref"], head=out["head"], attn_ms=attn_ms, attn_bytes=attn_bytes, attn_width=width,
                 prefill_s=prefill_s, clocks=head["clocks"], B=B, k=k, kernels_per_step=head["kernels"],
-                dtype=str(dtype), h2d=2 * B * 4, d2h=(B * (k + 1) + B + 2) * 4, step_bytes=step_bytes,
+                dtype=str(dtype), h2d=6 * B * 4, d2h=(B * (k + 1) + B + 2) * 4, step_bytes=step_bytes,
                 tokens_per_step_mean=head["committed"] / args.steps / max(world, 1),
                 deferred=not args.reference_structure)
 

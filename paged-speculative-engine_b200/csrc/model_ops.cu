@@ -135,6 +135,95 @@ __global__ void __launch_bounds__(THREADS) add_norm_kernel(float* __restrict__ x
   }
 }
 
+// bf16 fast path: one CTA per row, one thread per 8 contiguous columns (two
+// float4 of the fp32 residual, one 16-byte vector of y / bias / gamma / beta /
+// out), blockDim = d / 8 rounded up to whole warps.
+__device__ __forceinline__ float cta_sum_dyn(float v, float* sh) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  v = warp_sum(v);
+  if (lane == 0) sh[warp] = v;
+  __syncthreads();
+  float t = 0.f;
+  for (int w = 0; w < nw; ++w) t += sh[w];
+  __syncthreads();
+  return t;
+}
+
+__device__ __forceinline__ void bf16x8_to_f32(const uint4& a, float* f) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&a);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const float2 t = __bfloat1622float2(h[q]);
+    f[2 * q] = t.x;
+    f[2 * q + 1] = t.y;
+  }
+}
+
+__global__ void __launch_bounds__(1024) add_norm_bf16x8_kernel(float* __restrict__ x, int64_t ldx,
+                                                               const __nv_bfloat16* __restrict__ y, int64_t ldy,
+                                                               const __nv_bfloat16* __restrict__ bias,
+                                                               const __nv_bfloat16* __restrict__ gamma,
+                                                               const __nv_bfloat16* __restrict__ beta, int d,
+                                                               float eps, int rms, __nv_bfloat16* __restrict__ out,
+                                                               int64_t ldo) {
+  __shared__ float sh[32];
+  const int row = blockIdx.x;
+  const int c = threadIdx.x * 8;
+  const bool on = c < d;
+  float v[8];
+  float* xr = x + (int64_t)row * ldx + c;
+  if (on) {
+    const float4 a = *reinterpret_cast<const float4*>(xr);
+    const float4 b = *reinterpret_cast<const float4*>(xr + 4);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    if (y) {
+      float t[8];
+      bf16x8_to_f32(*reinterpret_cast<const uint4*>(y + (int64_t)row * ldy + c), t);
+      if (bias) {
+        float bb[8];
+        bf16x8_to_f32(*reinterpret_cast<const uint4*>(bias + c), bb);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) t[j] += bb[j];
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] += t[j];
+      *reinterpret_cast<float4*>(xr) = make_float4(v[0], v[1], v[2], v[3]);
+      *reinterpret_cast<float4*>(xr + 4) = make_float4(v[4], v[5], v[6], v[7]);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = 0.f;
+  }
+  float s = 0.f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) s += v[j];
+  const float mean = rms ? 0.f : cta_sum_dyn(s, sh) / d;
+  float s2 = 0.f;
+  if (on) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s2 += (v[j] - mean) * (v[j] - mean);
+  }
+  const float inv = rsqrtf(cta_sum_dyn(s2, sh) / d + eps);
+  if (on) {
+    float g[8], bt[8];
+    bf16x8_to_f32(*reinterpret_cast<const uint4*>(gamma + c), g);
+    if (!rms && beta) {
+      bf16x8_to_f32(*reinterpret_cast<const uint4*>(beta + c), bt);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) bt[j] = 0.f;
+    }
+    uint4 o;
+    __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      oh[q] = __floats2bfloat162_rn((v[2 * q] - mean) * inv * g[2 * q] + bt[2 * q],
+                                    (v[2 * q + 1] - mean) * inv * g[2 * q + 1] + bt[2 * q + 1]);
+    *reinterpret_cast<uint4*>(out + (int64_t)row * ldo + c) = o;
+  }
+}
+
 template <int THREADS, int EPT>
 void launch_add_norm(int dtype, float* x, int64_t ldx, const void* y, int64_t ldy, const void* bias,
                      const void* gamma, const void* beta, int n_rows, int d, float eps, int rms, void* out,
@@ -296,6 +385,17 @@ extern "C" int pse_add_norm(float* x, int64_t ldx, const void* y, int64_t ldy, c
   if (y_dtype != param_dtype || out_dtype != param_dtype) return PSE_EINVAL;
   cudaStream_t s = (cudaStream_t)stream;
   const int dt = param_dtype;
+  auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  if (dt == PSE_BF16 && d % 8 == 0 && ldx % 4 == 0 && ldy % 8 == 0 && ldo % 8 == 0 && al16(x) && al16(y) &&
+      al16(bias) && al16(gamma) && al16(beta) && al16(out)) {
+    const int threads = ((d / 8 + 31) / 32) * 32;  // d <= 4096: at most 512
+    add_norm_bf16x8_kernel<<<n_rows, threads, 0, s>>>(x, ldx, (const __nv_bfloat16*)y, ldy,
+                                                      (const __nv_bfloat16*)bias, (const __nv_bfloat16*)gamma,
+                                                      (const __nv_bfloat16*)beta, d, eps, rms, (__nv_bfloat16*)out,
+                                                      ldo);
+    PSE_LAUNCH_CHECK();
+    return PSE_OK;
+  }
   if (d <= 256)
     launch_add_norm<32, 8>(dt, x, ldx, y, ldy, bias, gamma, beta, n_rows, d, eps, rms, out, ldo, s);
   else if (d <= 1024)

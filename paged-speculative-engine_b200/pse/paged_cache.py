@@ -213,9 +213,12 @@ class PagedKVCache:
 
     def ensure_capacity(self, request_ids, extra_tokens: int) -> None:
         """Widen the block table if a row could outgrow it by ``extra_tokens``."""
-        need = 0
-        for r in request_ids:
-            need = max(need, _blocks_for(self._lengths[r] + extra_tokens, self.block_size))
+        longest = max((self._lengths[r] for r in request_ids), default=0)
+        self.ensure_capacity_len(longest + extra_tokens)
+
+    def ensure_capacity_len(self, tokens: int) -> None:
+        """Widen the block table so a row of ``tokens`` tokens fits."""
+        need = _blocks_for(tokens, self.block_size)
         if need > self._blocks.max_blocks:
             width = self._blocks.max_blocks
             while width < need:
@@ -239,8 +242,7 @@ class PagedKVCache:
             self._lengths[r] = int(lens[s])
 
     def note_lengths(self, request_ids, lengths) -> None:
-        for r, n in zip(request_ids, lengths):
-            self._lengths[r] = int(n)
+        self._lengths.update(zip(request_ids, lengths))
 
     def note_append(self, request_ids, width: int) -> None:
         for r in request_ids:

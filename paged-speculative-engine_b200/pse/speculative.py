@@ -62,6 +62,18 @@ def next_logits_buffer(cache, vocab: int) -> torch.Tensor:
     return cache._next_logits
 
 
+def next_logits_views(cache, vocab: int) -> list:
+    """One view per slot of ``next_logits_buffer`` (row s is request slot s's
+    next-token logits), built once per buffer allocation: handing a request's
+    row back to the caller costs a list lookup instead of a tensor index."""
+    buf = next_logits_buffer(cache, vocab)
+    cached = getattr(cache, "_next_views", None)
+    if cached is None or cached[0] is not buf:
+        cached = (buf, list(buf.unbind(0)))
+        cache._next_views = cached
+    return cached[1]
+
+
 def _check_ids(ids, vocab: int) -> None:
     if len(ids) and (min(ids) < 0 or max(ids) >= vocab):
         raise IndexError(f"token id out of range for vocabulary of {vocab}")
@@ -106,8 +118,10 @@ class _StepBuffers:
     def __init__(self, B: int, k: int, V: int, device):
         i32 = dict(dtype=torch.int32, device=device)
         self.B = B
-        self.slots_d = torch.empty(B, **i32)
-        self.slots_t = torch.empty(B, **i32)
+        # the step's per-row host inputs, copied to the device in one transfer:
+        # [slots_d | slots_t | req_key | steps | order_d | order_t]
+        self.dev_in = torch.zeros(6 * B, **i32)
+        self.slots_d, self.slots_t, self.req_key, self.steps, self.order_d, self.order_t = self.dev_in.view(6, B)
         self.base = torch.empty(k + 3, B, **i32)
         self.round_ids = torch.empty(B, **i32)
         self.drafts = torch.empty(B, k, **i32)
@@ -118,17 +132,15 @@ class _StepBuffers:
         self.n_acc = torch.empty(B, **i32)
         self.final = torch.empty(B, **i32)
         self.u = torch.zeros(B, 2 * k + 1, dtype=torch.float64, device=device)
-        self.req_key = torch.empty(B, **i32)
-        self.steps = torch.empty(B, **i32)
         self.vids = None    # deferred-bonus mode: verify ids [B, k+1] and logits [B*(k+1), V]
         self.vlog2 = None
         self.nacc1 = torch.empty(B, **i32)
-        self.order_d = torch.arange(B, **i32)  # rows longest-first, refreshed every step
-        self.order_t = torch.arange(B, **i32)
         n_pack = B * (k + 1) + B + 2
         self.pack = torch.empty(n_pack, **i32)
         self.host_pack = torch.empty(n_pack, dtype=torch.int32, pin_memory=True)
         self.host_in = torch.empty(6 * B, dtype=torch.int32, pin_memory=True)
+        self.host_pack_np = self.host_pack.numpy()  # same pinned memory
+        self.host_in_np = self.host_in.numpy()
 
 
 class StepRunner:
@@ -263,36 +275,47 @@ class StepRunner:
         dc, tc = self.dcache, self.tcache
         if not defer_bonus and any(tc.slot(r) in tc.deferred_slots for r in request_ids):
             raise ValueError("request is in the deferred-bonus state: keep stepping it with defer_bonus=True")
-        _check_positions(self.dm_d, dc, request_ids, k + 1)
-        _check_positions(self.dm_t, tc, request_ids, k + 1)
-        dc.ensure_capacity(request_ids, k + 1)
-        tc.ensure_capacity(request_ids, k + 1)
+        sd_np = np.fromiter((dc._slot[r] for r in request_ids), np.int32, B)
+        st_np = np.fromiter((tc._slot[r] for r in request_ids), np.int32, B)
+        len_d = np.fromiter((dc._lengths[r] for r in request_ids), np.int64, B)
+        len_t = np.fromiter((tc._lengths[r] for r in request_ids), np.int64, B)
+        for dm, c, lens in ((self.dm_d, dc, len_d), (self.dm_t, tc, len_t)):
+            longest = int(lens.max()) + k + 1
+            if dm.pos_emb is not None and longest > dm.max_seq_len:
+                raise IndexError(f"position {longest - 1} beyond max_seq_len {dm.max_seq_len}")
+            c.ensure_capacity_len(longest)
         b = self.bufs.get(B)
         if b is None:
             b = self.bufs[B] = _StepBuffers(B, k, V, self.device)
         if defer_bonus and b.vids is None:
             b.vids = torch.empty(B, k + 1, dtype=torch.int32, device=self.device)
             b.vlog2 = torch.empty(B * (k + 1), V, dtype=torch.float32, device=self.device)
-        dnext = next_logits_buffer(dc, V)
-        tnext = next_logits_buffer(tc, V)
-        sd = [dc.slot(r) for r in request_ids]
-        stt = [tc.slot(r) for r in request_ids]
+        dviews = next_logits_views(dc, V)
+        tviews = next_logits_views(tc, V)
+        sd = sd_np.tolist()
+        stt = st_np.tolist()
         if defer_bonus:
+            n_before = len(tc.deferred_slots)
             self._enter_deferred(request_ids, stt)
+            if len(tc.deferred_slots) != n_before:  # rows entered the deferred state: lengths moved
+                len_t = np.fromiter((tc._lengths[r] for r in request_ids), np.int64, B)
         for r, s in zip(request_ids, sd):
             t = draft_next_logits[r]
-            if t.data_ptr() != dnext[s].data_ptr():
-                dnext[s].copy_(t.reshape(-1), non_blocking=True)
+            v = dviews[s]
+            if t is not v and t.data_ptr() != v.data_ptr():
+                v.copy_(t.reshape(-1), non_blocking=True)
         if not defer_bonus:
             for r, s in zip(request_ids, stt):
                 t = target_next_logits[r]
-                if t.data_ptr() != tnext[s].data_ptr():
-                    tnext[s].copy_(t.reshape(-1), non_blocking=True)
+                v = tviews[s]
+                if t is not v and t.data_ptr() != v.data_ptr():
+                    v.copy_(t.reshape(-1), non_blocking=True)
         T = float(temperature)
         philox = False
         hin = b.host_in
-        hin[:B] = torch.tensor(sd, dtype=torch.int32)
-        hin[B:2 * B] = torch.tensor(stt, dtype=torch.int32)
+        hnp = b.host_in_np
+        hnp[:B] = sd_np
+        hnp[B:2 * B] = st_np
         if T > 0:
             if uniforms is not None:
                 u = torch.as_tensor(np.asarray(uniforms, dtype=np.float64) if not torch.is_tensor(uniforms)
@@ -302,20 +325,12 @@ class StepRunner:
                 b.u.copy_(torch.rand(B, 2 * k + 1, generator=generator, dtype=torch.float64), non_blocking=True)
             else:
                 philox = True
-                keys = np.array([_fnv1a(r) for r in request_ids], dtype=np.uint32).view(np.int32)
-                hin[2 * B:3 * B] = torch.from_numpy(keys)
-                hin[3 * B:4 * B] = torch.tensor([self.request_steps.get(r, 0) for r in request_ids],
-                                                dtype=torch.int32)
+                hnp[2 * B:3 * B] = np.array([_fnv1a(r) for r in request_ids], dtype=np.uint32).view(np.int32)
+                hnp[3 * B:4 * B] = np.fromiter((self.request_steps.get(r, 0) for r in request_ids), np.int32, B)
         # longest rows first: the attention kernels hand out work in this order
-        hin[4 * B:5 * B] = torch.from_numpy(np.argsort([-dc.length(r) for r in request_ids], kind="stable").astype(np.int32))
-        hin[5 * B:6 * B] = torch.from_numpy(np.argsort([-tc.length(r) for r in request_ids], kind="stable").astype(np.int32))
-        b.order_d.copy_(hin[4 * B:5 * B], non_blocking=True)
-        b.order_t.copy_(hin[5 * B:6 * B], non_blocking=True)
-        b.slots_d.copy_(hin[:B], non_blocking=True)
-        b.slots_t.copy_(hin[B:2 * B], non_blocking=True)
-        if philox:
-            b.req_key.copy_(hin[2 * B:3 * B], non_blocking=True)
-            b.steps.copy_(hin[3 * B:4 * B], non_blocking=True)
+        hnp[4 * B:5 * B] = np.argsort(-len_d, kind="stable")
+        hnp[5 * B:6 * B] = np.argsort(-len_t, kind="stable")
+        b.dev_in.copy_(hin, non_blocking=True)
 
         graphs = self.use_graphs if use_graph is None else use_graph
         mcd, mct = self._ctx_bound(dc, self.dm_d), self._ctx_bound(tc, self.dm_t)
@@ -359,18 +374,19 @@ class StepRunner:
             for c, s in ((dc, status_d), (tc, status_t)):
                 if s:
                     c.check_status("speculative step")
-        toks = hp[:nt].view(B, k + 1).tolist()
-        nacc = hp[nt:nt + B].tolist()
-        accepted, n_acc, dn, tn = {}, {}, {}, {}
-        for i, r in enumerate(request_ids):
-            n = nacc[i]
-            accepted[r] = toks[i][: n + 1]
-            n_acc[r] = n
-            dn[r] = dnext[sd[i]]
-            tn[r] = None if defer_bonus else tnext[stt[i]]
-            self.request_steps[r] = self.request_steps.get(r, 0) + 1
-        dc.note_lengths(request_ids, [dc.length(r) + n_acc[r] + 1 for r in request_ids])
-        tc.note_lengths(request_ids, [tc.length(r) + n_acc[r] + 1 for r in request_ids])
+        hpn = b.host_pack_np
+        toks = hpn[:nt].reshape(B, k + 1).tolist()
+        nacc_np = hpn[nt:nt + B].astype(np.int64)
+        nacc = nacc_np.tolist()
+        accepted = {r: toks[i][: nacc[i] + 1] for i, r in enumerate(request_ids)}
+        n_acc = dict(zip(request_ids, nacc))
+        dn = {r: dviews[s] for r, s in zip(request_ids, sd)}
+        tn = dict.fromkeys(request_ids) if defer_bonus else {r: tviews[s] for r, s in zip(request_ids, stt)}
+        steps = self.request_steps
+        for r in request_ids:
+            steps[r] = steps.get(r, 0) + 1
+        dc.note_lengths(request_ids, (len_d + nacc_np + 1).tolist())
+        tc.note_lengths(request_ids, (len_t + nacc_np + 1).tolist())
         return BatchStepResult(accepted, n_acc, dn, tn)
 
 
