@@ -378,7 +378,7 @@ def micro_attention(args, device):
     nb = int(need.sum())
     c = pse.PagedKVCache(1, hk, hd, bs, nb, dtype=torch.bfloat16, device=device, max_requests=rows,
                          max_blocks_per_request=int(need.max()))
-    perm = torch.from_numpy(rng.permutation(nb).astype(np.int32))
+    perm = torch.from_numpy((rng.permutation(nb) if args.attn_pages == "permuted" else np.arange(nb)).astype(np.int32))
     table = torch.full((rows, int(need.max())), -1, dtype=torch.int32)
     o = 0
     for i, n in enumerate(need):
@@ -421,7 +421,7 @@ def micro_attention(args, device):
     print(json.dumps({"metric": "paged attention HBM GB/s", "shape": args.attn_shape, "value": gbs, "unit": "GB/s",
                       "frac_of_peak": gbs / peak, "peak": peak, "peak_kind": kind, "us_per_launch": ms * 1000,
                       "algorithmic_bytes": alg, "rows": rows, "width": width, "q_heads": hq, "kv_heads": hk,
-                      "head_dim": hd, "block_size": bs, "ctx_mean": float(ctx.mean()),
+                      "head_dim": hd, "block_size": bs, "ctx_mean": float(ctx.mean()), "pages": args.attn_pages,
                       "pool_bytes": 2 * c.k_pool.numel() * 2, "clocks": clk.summary()}), flush=True)
 
 
@@ -555,6 +555,8 @@ def main():
                     help="headline the reference's step structure (2 target calls per step) instead of the "
                          "deferred-bonus step (the target's bonus call folded into the next verify)")
     ap.add_argument("--attn-shape", default="gpt2-verify", choices=sorted(ATTN_SHAPES))
+    ap.add_argument("--attn-pages", default="permuted", choices=["permuted", "contiguous"],
+                    help="--micro attn: block tables a random permutation of the pool, or consecutive blocks")
     ap.add_argument("--profile-step", action="store_true",
                     help="after warm-up run one eager step inside the NVTX range 'pse_step' and exit (for ncu)")
     args = ap.parse_args()

@@ -9,7 +9,7 @@
 // KV split).  The producer walks the row's block table and, for every page of
 // a 64-token tile, issues 2-D TMA loads (cp.async.bulk.tensor, 128-byte
 // swizzle) of the page's K and V boxes [block_size x 64 columns] into a
-// 4-stage shared-memory ring, completing on an mbarrier with the transaction
+// 3-stage shared-memory ring, completing on an mbarrier with the transaction
 // byte count.  Pages past the row's end are requested at an out-of-range row,
 // so the TMA unit fills them with zeros and the byte count never changes.
 // Consumers run S = Q K^T and O += P V with mma.sync m16n8k16 (bf16 in, fp32
@@ -17,7 +17,8 @@
 // swizzle makes every ldmatrix conflict-free), an exp2-domain online softmax
 // per row, and release the stage through an "empty" mbarrier.  Warps split
 // the tile's tokens (and, with 32 query rows, the two 16-row m-tiles); their
-// partial (max, sum, O) are merged through shared memory at the end.
+// partial (max, sum, O) are merged at the item's last tile, through that
+// tile's own stage buffers, before the stage is released.
 //
 // Every mbarrier wait is bounded; on expiry the kernel latches
 // PSE_STATUS_TIMEOUT in the cache status word and stops issuing work.
@@ -37,10 +38,10 @@ namespace tc {
 #define PSE_TC_CONSUMERS 4
 #endif
 #ifndef PSE_TC_STAGES64
-#define PSE_TC_STAGES64 2
+#define PSE_TC_STAGES64 3
 #endif
 #ifndef PSE_TC_STAGES128
-#define PSE_TC_STAGES128 2
+#define PSE_TC_STAGES128 3
 #endif
 #ifndef PSE_TC_MINB64
 #define PSE_TC_MINB64 4
@@ -50,13 +51,17 @@ namespace tc {
 #endif
 
 constexpr int kConsumers = PSE_TC_CONSUMERS;
+static_assert(kConsumers % 2 == 0, "the item merge puts half the consumer warps' partials in each stage buffer");
 constexpr int kThreads = (kConsumers + 1) * 32;
 constexpr int kTile = 16 * kConsumers;  // tokens per pipeline stage (16 per consumer warp)
 constexpr uint32_t kSpinLimit = 1u << 22;
 
-// Ring depth: 2 x 16 KB stages for head_dim 64 (4 CTAs per SM), 2 x 32 KB for
-// head_dim 128 (2 CTAs per SM); either keeps >= 128 KB of K/V in flight per SM,
-// and the persistent CTAs never let the ring drain between work items.
+// Ring depth: 3 x 16 KB stages for head_dim 64 (4 CTAs per SM), 3 x 32 KB for
+// head_dim 128 (2 CTAs per SM): up to 192 KB of K/V in flight per SM.  HBM
+// needs ~200+ KB in flight per SM to approach its peak (a 128 KB ring reached
+// ~60% of it), so the ring takes nearly all of shared memory; the item merge
+// reuses the last tile's stage instead of a buffer of its own.  The persistent
+// CTAs never let the ring drain between work items.
 __host__ __device__ constexpr int stages_for(int hd) { return hd == 64 ? PSE_TC_STAGES64 : PSE_TC_STAGES128; }
 
 struct Args {
@@ -205,8 +210,7 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? PSE_TC_MINB64 : PSE_TC_MI
   uint8_t* q_s = smem + 2 * kStages * kTileBytes;   // [kQRows x HD] swizzled
   float* mw = reinterpret_cast<float*>(q_s + kQRows * HD * 2);  // [kConsumers][16]
   float* lw = mw + kConsumers * 16;                               // [kConsumers][16]
-  float* ow = lw + kConsumers * 16;                               // [kConsumers][16][HD]
-  uint64_t* full = reinterpret_cast<uint64_t*>(ow + kConsumers * 16 * HD);
+  uint64_t* full = reinterpret_cast<uint64_t*>(lw + kConsumers * 16);
   uint64_t* empty = full + kStages;
   int* desc_item = reinterpret_cast<int*>(empty + kStages);
   int* desc_tile = desc_item + kStages;
@@ -500,26 +504,37 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? PSE_TC_MINB64 : PSE_TC_MI
         }
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[s]);
-      if (flags & kLast) {
-        // merge the warps' partial (max, sum, O) of this item and write it out
+      if (!(flags & kLast)) {
+        if (lane == 0) mbar_arrive(&empty[s]);
+      } else {
+        // Merge the warps' partial (max, sum, O) of this item and write it out.
+        // The partial O go through this tile's own stage buffers (K and V, two
+        // warps each), which stay with the consumers until the merge is done.
         float L0 = l0 + __shfl_xor_sync(0xffffffffu, l0, 1);
         L0 += __shfl_xor_sync(0xffffffffu, L0, 2);
         float L1 = l1 + __shfl_xor_sync(0xffffffffu, l1, 1);
         L1 += __shfl_xor_sync(0xffffffffu, L1, 2);
+        constexpr int kHalf = kConsumers / 2;  // warps per stage buffer
+        float* const ow_k = reinterpret_cast<float*>(stage_k + s * kTileBytes);
+        float* const ow_v = reinterpret_cast<float*>(stage_v + s * kTileBytes);
+        auto ow_at = [&](int w2, int r) -> float* {
+          return (w2 < kHalf ? ow_k : ow_v) + ((w2 % kHalf) * 16 + r) * HD;
+        };
+        // every consumer warp is done with this stage's K / V and with the previous item's merge
+        asm volatile("bar.sync 1, %0;" ::"r"(kConsumers * 32));
         if (tid4 == 0) {
           mw[warp * 16 + gid] = m0;
           mw[warp * 16 + gid + 8] = m1;
           lw[warp * 16 + gid] = L0;
           lw[warp * 16 + gid + 8] = L1;
         }
+        float* const own0 = ow_at(warp, gid);
+        float* const own1 = ow_at(warp, gid + 8);
 #pragma unroll
         for (int n = 0; n < HD / 8; ++n) {
           const int d = n * 8 + 2 * tid4;
-          ow[(warp * 16 + gid) * HD + d] = o[n][0];
-          ow[(warp * 16 + gid) * HD + d + 1] = o[n][1];
-          ow[(warp * 16 + gid + 8) * HD + d] = o[n][2];
-          ow[(warp * 16 + gid + 8) * HD + d + 1] = o[n][3];
+          *reinterpret_cast<float2*>(own0 + d) = make_float2(o[n][0], o[n][1]);
+          *reinterpret_cast<float2*>(own1 + d) = make_float2(o[n][2], o[n][3]);
         }
         asm volatile("bar.sync 1, %0;" ::"r"(kConsumers * 32));
         for (int e = tid; e < it.nr * HD; e += kConsumers * 32) {
@@ -531,7 +546,7 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? PSE_TC_MINB64 : PSE_TC_MI
           for (int w2 = mtr; w2 < kConsumers; w2 += MT) {
             const float f = M == -INFINITY ? 0.f : exp2f(mw[w2 * 16 + rl] - M);
             L += lw[w2 * 16 + rl] * f;
-            acc += ow[(w2 * 16 + rl) * HD + d] * f;
+            acc += ow_at(w2, rl)[d] * f;
           }
           const int rr = it.r0 + r, w = rr / group, g = rr % group, h = it.hk * group + g;
           const int64_t tokrow = (int64_t)it.i * a.width + w;
@@ -546,6 +561,11 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? PSE_TC_MINB64 : PSE_TC_MI
             }
           }
         }
+        // the merge wrote the stage with generic-proxy stores: order them before
+        // the producer's next TMA write into it, then release the stage
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
       }
     }
   }
@@ -604,8 +624,7 @@ int tensor_map(const void* pool, int num_blocks, int kv_heads, int bs, int hd, C
 template <int HD>
 constexpr size_t smem_bytes(int mt) {
   return 1024 + 2 * stages_for(HD) * (size_t)kTile * HD * 2 + (size_t)16 * mt * HD * 2 +
-         (size_t)(2 * kConsumers * 16 + kConsumers * 16 * HD) * 4 + 2 * stages_for(HD) * 8 + 3 * stages_for(HD) * 4 +
-         16;
+         (size_t)(2 * kConsumers * 16) * 4 + 2 * stages_for(HD) * 8 + 3 * stages_for(HD) * 4 + 16;
 }
 
 // Persistent launch: as many CTAs as fit on the GPU at once (never more than

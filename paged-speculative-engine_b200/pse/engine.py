@@ -112,16 +112,19 @@ def lm_head(dm: DeviceModel, h: torch.Tensor, out: torch.Tensor) -> None:
     elif _tc_ok(h, dm.lm_w, out):
         _mm(h, dm.lm_w, out)
     else:
-        out.copy_(torch.mm(h, dm.lm_w.t(), out_dtype=torch.float32))
+        torch.mm(h, dm.lm_w.t(), out_dtype=torch.float32, out=out)  # bf16 in, fp32 logits out, no temporary
 
 
 def forward(dm: DeviceModel, cache, slots: torch.Tensor, ids: torch.Tensor, rows: int, width: int,
             base_len: torch.Tensor, max_ctx: int, logits_out: torch.Tensor | None, last_only: bool = False,
-            scratch: Scratch | None = None, row_order: torch.Tensor | None = None) -> None:
+            scratch: Scratch | None = None, row_order: torch.Tensor | None = None, reserve: bool = True) -> None:
     """One paged forward.  ``slots`` int32 [rows]; ``ids`` int32 [rows*width];
     ``base_len`` int32 [rows] receives the rows' lengths before the call;
     ``max_ctx`` >= every row's length after it.  ``logits_out`` fp32
-    [rows*width, V] (or [rows, V] with ``last_only``) or None."""
+    [rows*width, V] (or [rows, V] with ``last_only``) or None.  With
+    ``reserve=False`` nothing is allocated: ``base_len`` gives each row's first
+    position, and K/V of positions in blocks the row does not hold are dropped.
+    The final normed hidden rows stay in the scratch's ``h``."""
     T = rows * width
     sc = scratch or scratch_for(dm)
     sc.ensure(T)
@@ -130,7 +133,8 @@ def forward(dm: DeviceModel, cache, slots: torch.Tensor, ids: torch.Tensor, rows
     dt = N.dtype_code(dm.dtype)
     d, hd = dm.d_model, dm.head_dim
     nq, nk = dm.q_heads * hd, dm.kv_heads * hd
-    N.call("pse_kv_reserve", state, slots.data_ptr(), rows, width, base_len.data_ptr(), st)
+    if reserve:
+        N.call("pse_kv_reserve", state, slots.data_ptr(), rows, width, base_len.data_ptr(), st)
     x, h, qkv, attn, tmp, up, act = (sc.x[:T], sc.h[:T], sc.qkv[:T], sc.attn[:T], sc.tmp[:T], sc.up[:T],
                                       sc.act[:T])
     N.call("pse_embed", ids.data_ptr(), base_len.data_ptr(), rows, width, dm.tok_emb.data_ptr(),

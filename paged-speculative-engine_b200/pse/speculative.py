@@ -27,7 +27,7 @@ import torch
 
 from . import _native as N
 from .device_model import device_model
-from .engine import Scratch, forward
+from .engine import Scratch, forward, lm_head
 
 DEFAULT_SEED = 0x5EED5EED
 USE_GRAPHS = True  # replay steps from CUDA graphs (from the second step of a batch size on)
@@ -115,14 +115,21 @@ def prefill_request(draft_model, target_model, draft_cache, target_cache, reques
 
 
 class _StepBuffers:
-    def __init__(self, B: int, k: int, V: int, device):
+    def __init__(self, B: int, k: int, V: int, device, d_draft: int, draft_dtype):
         i32 = dict(dtype=torch.int32, device=device)
         self.B = B
+        # the draft's tail call (its last round + its bonus, width 2): ids, the
+        # row each request's next logits come from, those hidden rows
+        self.nclamp = torch.empty(B, **i32)
+        self.ids2 = torch.empty(B, 2, **i32)
+        self.sel = torch.empty(B, dtype=torch.int64, device=device)
+        self.even = torch.arange(0, 2 * B, 2, dtype=torch.int64, device=device)
+        self.hsel = torch.empty(B, d_draft, dtype=draft_dtype, device=device)
         # the step's per-row host inputs, copied to the device in one transfer:
         # [slots_d | slots_t | req_key | steps | order_d | order_t]
         self.dev_in = torch.zeros(6 * B, **i32)
         self.slots_d, self.slots_t, self.req_key, self.steps, self.order_d, self.order_t = self.dev_in.view(6, B)
-        self.base = torch.empty(k + 3, B, **i32)
+        self.base = torch.empty(k + 4, B, **i32)  # per-call base lengths (rounds, verify, bonus calls)
         self.round_ids = torch.empty(B, **i32)
         self.drafts = torch.empty(B, k, **i32)
         self.dlog = torch.empty(k, B, V, dtype=torch.float32, device=device)
@@ -179,7 +186,9 @@ class StepRunner:
         if T > 0 and philox:
             N.call("pse_philox_uniforms", self.seed, b.req_key.data_ptr(), b.steps.data_ptr(), B, nu,
                    b.u.data_ptr(), st)
-        # draft rounds (engine/speculative.py:92-113)
+        # draft rounds (engine/speculative.py:92-113).  The last round's draft
+        # call is not made here: its logits are never tested, and its KV write
+        # merges with the bonus call below into one width-2 call.
         for j in range(k):
             if j == 0:
                 src, idx = dnext, b.slots_d.data_ptr()
@@ -187,8 +196,13 @@ class StepRunner:
                 src, idx = b.dlog[j - 1], None
             N.call("pse_sample_tokens", src.data_ptr(), V, idx, B, V, float(T), b.u.data_ptr(), nu, j,
                    b.drafts.data_ptr() + 4 * j, k, b.round_ids.data_ptr(), 1, st)
-            forward(self.dm_d, self.dcache, b.slots_d, b.round_ids, B, 1, b.base[j], max_ctx_d, b.dlog[j],
-                    scratch=self.sc_d, row_order=b.order_d)
+            if j + 1 < k:
+                forward(self.dm_d, self.dcache, b.slots_d, b.round_ids, B, 1, b.base[j], max_ctx_d, b.dlog[j],
+                        scratch=self.sc_d, row_order=b.order_d)
+            else:
+                # the last round's position is still allocated here, so the draft's
+                # block tables and free list follow the reference's sequence exactly
+                N.call("pse_kv_reserve", self.dcache.state, b.slots_d.data_ptr(), B, 1, b.base[j].data_ptr(), st)
         if not defer:
             # verify: one width-k target call (engine/speculative.py:115-117)
             forward(self.dm_t, self.tcache, b.slots_t, b.drafts.view(-1), B, k, b.base[k], max_ctx_t, b.vlog,
@@ -214,18 +228,34 @@ class StepRunner:
         # commit (engine/speculative.py:159-164)
         N.call("pse_kv_truncate", self.dcache.state, b.slots_d.data_ptr(), B, None, b.base[0].data_ptr(),
                b.n_acc.data_ptr(), st)
+        torch.add(b.n_acc, 1, out=b.nacc1)
         if not defer:
             N.call("pse_kv_truncate", self.tcache.state, b.slots_t.data_ptr(), B, None, b.base[k].data_ptr(),
                    b.n_acc.data_ptr(), st)
         else:
-            torch.add(b.n_acc, 1, out=b.nacc1)
             N.call("pse_kv_truncate", self.tcache.state, b.slots_t.data_ptr(), B, None, b.base[k].data_ptr(),
                    b.nacc1.data_ptr(), st)
             self.tpending.index_copy_(0, slots_t, b.final)
         # bonus forwards (engine/speculative.py:166-177); the target's is folded
-        # into the next verify in deferred mode
-        forward(self.dm_d, self.dcache, b.slots_d, b.final, B, 1, b.base[k + 1], max_ctx_d, b.blog,
-                scratch=self.sc_d, row_order=b.order_d)
+        # into the next verify in deferred mode.  The draft's is one width-2
+        # call: [x_{k-1}, final] when every draft was accepted (the last round's
+        # token was never computed), else [final, final] whose second position
+        # lies past the row's length (its K/V lands in a block the row holds
+        # and is overwritten by the next append, or is dropped); the next
+        # logits are those after `final`.  The bonus position is allocated first
+        # (as the reference's bonus append does), then the call runs at
+        # base + min(n, k-1) without allocating.
+        N.call("pse_kv_reserve", self.dcache.state, b.slots_d.data_ptr(), B, 1, b.base[k + 1].data_ptr(), st)
+        full = b.n_acc.eq(k)
+        torch.where(full, b.drafts[:, k - 1], b.final, out=b.ids2[:, 0])
+        b.ids2[:, 1].copy_(b.final)
+        torch.clamp(b.n_acc, max=k - 1, out=b.nclamp)
+        torch.add(b.base[0], b.nclamp, out=b.base[k + 3])
+        forward(self.dm_d, self.dcache, b.slots_d, b.ids2.view(-1), B, 2, b.base[k + 3], max_ctx_d, None,
+                scratch=self.sc_d, row_order=b.order_d, reserve=False)
+        torch.add(b.even, full, out=b.sel)
+        torch.index_select(self.sc_d.h[:2 * B], 0, b.sel, out=b.hsel)
+        lm_head(self.dm_d, b.hsel, b.blog)
         N.call("pse_scatter_rows", b.blog.data_ptr(), V, b.slots_d.data_ptr(), B, V, dnext.data_ptr(), V,
                dnext.shape[0], st)
         if not defer:
@@ -286,7 +316,7 @@ class StepRunner:
             c.ensure_capacity_len(longest)
         b = self.bufs.get(B)
         if b is None:
-            b = self.bufs[B] = _StepBuffers(B, k, V, self.device)
+            b = self.bufs[B] = _StepBuffers(B, k, V, self.device, self.dm_d.d_model, self.dm_d.dtype)
         if defer_bonus and b.vids is None:
             b.vids = torch.empty(B, k + 1, dtype=torch.int32, device=self.device)
             b.vlog2 = torch.empty(B * (k + 1), V, dtype=torch.float32, device=self.device)
@@ -336,11 +366,12 @@ class StepRunner:
         mcd, mct = self._ctx_bound(dc, self.dm_d), self._ctx_bound(tc, self.dm_t)
         if graphs:
             # size every buffer the program touches before the graph key is taken
-            self.sc_d.ensure(B)
+            self.sc_d.ensure(2 * B)
             self.sc_t.ensure(B * (k + 1))
             dmd, dmt = self.dm_d, self.dm_t
-            self.sc_d.ensure_ws(N.size_call("pse_paged_attention_workspace", B, 1, dmd.q_heads, dmd.kv_heads,
-                                            dmd.head_dim, mcd))
+            self.sc_d.ensure_ws(max(
+                N.size_call("pse_paged_attention_workspace", B, 1, dmd.q_heads, dmd.kv_heads, dmd.head_dim, mcd),
+                N.size_call("pse_paged_attention_workspace", B, 2, dmd.q_heads, dmd.kv_heads, dmd.head_dim, mcd)))
             self.sc_t.ensure_ws(max(
                 N.size_call("pse_paged_attention_workspace", B, k + 1, dmt.q_heads, dmt.kv_heads, dmt.head_dim, mct),
                 N.size_call("pse_paged_attention_workspace", B, k, dmt.q_heads, dmt.kv_heads, dmt.head_dim, mct),
