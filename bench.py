@@ -351,7 +351,7 @@ def cpu_reference(args, sample_rows, sample_steps, threads, warmup=0):
 # attn_tc_kernel, captured on the gpt2-verify microbench shape (the summary
 # with the command is profiles/attn_tc_gpt2-verify.md); keyed by (workload,
 # verify width).
-ATTN_TRAFFIC_RATIO: dict = {("gpt2-small", 6): (481367040 + 4925440) / 477461504}
+ATTN_TRAFFIC_RATIO: dict = {("gpt2-small", 6): (481297920 + 5749760) / 477461504}
 
 ATTN_SHAPES = {
     # name: rows, width, q_heads, kv_heads, head_dim, block, ctx_lo, ctx_hi (ctx includes the width queries)
