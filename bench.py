@@ -448,6 +448,8 @@ def micro_accept(args, device):
     nacc = torch.empty(R, dtype=torch.int32, device=device)
     fin = torch.empty(R, dtype=torch.int32, device=device)
 
+    N.load().pse_accept_select(args.accept_kernel)
+
     def launch():
         N.call("pse_spec_accept", tgt.data_ptr(), (k + 1) * V, None, tgt.data_ptr() + 4 * V, (k + 1) * V, V,
                drf.data_ptr(), V, None, drf.data_ptr() + 4 * R * V, V, R * V, drafts.data_ptr(), u.data_ptr(),
@@ -472,7 +474,10 @@ def micro_accept(args, device):
                       "frac_of_peak": need / (ms / 1000) / 1e9 / peak, "peak": peak, "peak_kind": kind,
                       "us_per_launch": ms * 1000, "bytes_needed": need, "bytes_formula_2k+1": formula,
                       "formula_GBps": formula / (ms / 1000) / 1e9, "rows": R, "k": k, "vocab": V, "temperature": T,
-                      "mean_accepted": n.float().mean().item()}), flush=True)
+                      "mean_accepted": n.float().mean().item(),
+                      "kernel": ["streaming CTA per row", "CTA per row (scalar)", "cluster per row"][args.accept_kernel]
+                      if T > 0 else "CTA per row (argmax)"}), flush=True)
+    N.load().pse_accept_select(0)
 
 
 def micro_churn(args, device):
@@ -551,6 +556,8 @@ def main():
     ap.add_argument("--micro", choices=["attn", "accept", "churn"], default=None,
                     help="kernel microbenchmark instead of the step")
     ap.add_argument("--temperature", type=float, default=1.0, help="--micro accept: temperature")
+    ap.add_argument("--accept-kernel", type=int, default=0, choices=[0, 1, 2],
+                    help="--micro accept at T > 0: 0 streaming CTA per row, 1 scalar CTA per row, 2 cluster per row")
     ap.add_argument("--reference-structure", action="store_true",
                     help="headline the reference's step structure (2 target calls per step) instead of the "
                          "deferred-bonus step (the target's bonus call folded into the next verify)")

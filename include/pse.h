@@ -200,9 +200,10 @@ int pse_sample_tokens(const float *logits, int64_t row_stride, const int32_t *in
  * + 2k] the residual / bonus uniform.  Writes tokens[i*(k+1) + 0..n] (the
  * accepted drafts then the corrected / bonus token), n_accepted[i] and
  * final_token[i] (= tokens[i*(k+1) + n_accepted[i]]).
- * T <= 0 runs one CTA per row; T > 0 with vocab <= 131072 runs one
- * thread-block cluster (ceil(vocab / 16384) CTAs) per row with the row's
- * logits held on chip, larger vocabularies one CTA per row. */
+ * T <= 0 runs one CTA per row.  T > 0 with 16-byte aligned rows (vocab and
+ * strides multiples of 4) runs persistent 1024-thread CTAs, one row each, with
+ * the rows in flight kept resident in L2 so every needed logit crosses HBM
+ * once; other rows run the CTA-per-row scalar kernel. */
 int pse_spec_accept(const float *target0, int64_t t0_stride, const int32_t *t0_index,
                     const float *verify, int64_t v_row, int64_t v_pos,
                     const float *draft0, int64_t d0_stride, const int32_t *d0_index,
@@ -211,10 +212,12 @@ int pse_spec_accept(const float *target0, int64_t t0_stride, const int32_t *t0_i
                     int32_t k, int32_t vocab, float temperature, int32_t *tokens,
                     int32_t *n_accepted, int32_t *final_token, void *stream);
 
-/* on != 0 makes pse_spec_accept run the CTA-per-row kernel at every
- * temperature (parity tests compare it with the cluster kernel); no
- * counterpart in the reference. */
-int pse_accept_force_per_row(int32_t on);
+/* Which kernel pse_spec_accept runs at T > 0: 0 the default (L2-resident
+ * streaming CTA per row), 1 the CTA-per-row scalar kernel, 2 one thread-block
+ * cluster of ceil(vocab / 16384) CTAs per row with the row held on chip
+ * (vocab <= 131072).  All three give the same tokens; parity tests compare
+ * them.  No counterpart in the reference. */
+int pse_accept_select(int32_t kernel);
 
 /* ------------------------------------------------------------------------ */
 /* Model pieces (TinyGPT engine/model.py:121-206; Llama-style variant)       */

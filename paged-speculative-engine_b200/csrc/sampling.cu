@@ -23,8 +23,9 @@ namespace {
 
 constexpr int kSampleThreads = 512;
 
-// Forces the CTA-per-row accept kernel at T > 0 (tests compare the two forms).
-int g_accept_per_row = 0;
+// Which accept kernel runs at T > 0 (tests compare the forms): 0 the default
+// (streaming), 1 the CTA-per-row scalar kernel, 2 the cluster kernel.
+int g_accept_kernel = 0;
 constexpr int kWarpsPerBlock = kSampleThreads / 32;
 
 // ---------------------------------------------------------------- Philox4x32-10
@@ -872,13 +873,318 @@ int launch_accept_cluster(const AcceptArgs& a, int rows, int run_len, cudaStream
   return e == cudaSuccess ? 0 : (int)e;
 }
 
-// The cluster kernel reads 16-byte vectors: every logits row must start on a
-// 16-byte boundary (base pointers aligned, strides and vocab multiples of 4),
-// and the vocabulary must fit 8 CTAs.
-bool cluster_accept_ok(const AcceptArgs& a) {
+// ---------------------------------------------------------------- accept / resample, T > 0, one CTA per row, L2-resident
+//
+// One CTA of 1024 threads owns a request row at a time; CTAs are persistent and
+// at most ACCEPT_ROWS_IN_FLIGHT rows are worked on at once, so the rows being
+// worked on (about 1 MB each at vocab 128k: target + draft) stay in L2.  The
+// first pass over a position (maxima) streams from HBM; the exp / sum pass, the
+// residual pass and the inverse-CDF walk re-read from L2 (ld.global.cg), so
+// each needed logit crosses HBM once.  Reductions are CTA-local.
+//
+// Layout: warp w owns the vocabulary segment [w*seg, (w+1)*seg), seg a
+// multiple of 128; its lanes read it as consecutive 128-entry rows, lane l
+// taking entries 4l..4l+3 of each row with one 16-byte load (coalesced).
+// Index order inside a segment is (row, lane, component).  Sums: a lane adds
+// its entries in index order, warps combine by butterfly, the CTA adds its 32
+// warp sums in warp order.  The inverse CDF descends warp segment (in order)
+// -> 128-entry row (warp scan of the lanes' 4-entry sums) -> entry.
+
+#ifndef PSE_ACCEPT_ROWS_IN_FLIGHT
+#define PSE_ACCEPT_ROWS_IN_FLIGHT 148
+#endif
+
+constexpr int kStThreads = 1024;
+constexpr int kStWarps = kStThreads / 32;
+
+struct StShared {
+  float wm[2][kStWarps];
+  double ws[2][kStWarps];
+  int wl[2][kStWarps];
+  double xw[2];
+  float m[2];
+  double z[2];
+  int last[2];
+  double cross_run;
+  int cross_warp;
+};
+
+__device__ __forceinline__ float4 ld_l2(const float* p) { return __ldcg(reinterpret_cast<const float4*>(p)); }
+
+__device__ __forceinline__ float4 scale_s(float4 v, float T) {
+  if (T != 1.0f) {  // l / 1 is l
+    v.x = v.x / T;
+    v.y = v.y / T;
+    v.z = v.z / T;
+    v.w = v.w / T;
+  }
+  return v;
+}
+
+__device__ __forceinline__ float4 weights4(float4 l, float T, float m) {
+  const float4 sv = scale_s(l, T);
+  return make_float4(expf(sv.x - m), expf(sv.y - m), expf(sv.z - m), expf(sv.w - m));
+}
+
+// CTA reduction of two per-warp values already stored in sh.ws / sh.wl (lane 0
+// of every warp wrote them): ordered sums and max of the last-nonzero indices.
+__device__ __forceinline__ void st_reduce_sums(StShared& sh, int n) {
+  if (threadIdx.x == 0) {
+    for (int v = 0; v < n; ++v) {
+      double z = 0.0;
+      int last = -1;
+      for (int w = 0; w < kStWarps; ++w) {
+        z += sh.ws[v][w];
+        last = max(last, sh.wl[v][w]);
+      }
+      sh.z[v] = z;
+      sh.last[v] = last;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kStThreads, 1) accept_stream_kernel(AcceptArgs a, int rows, int seg) {
+  __shared__ StShared sh;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int V = a.V, k = a.k;
+  const float T = a.T;
+  const int e_w = warp * seg;  // this warp's segment
+  const int n_c = seg >> 7;    // 128-entry rows in a segment
+  for (int i = blockIdx.x; i < rows; i += gridDim.x) {
+    const double* u = a.u + (int64_t)i * a.u_stride;
+    const int32_t* drafted = a.drafts + (int64_t)i * k;
+    int32_t* toks = a.tokens + (int64_t)i * (k + 1);
+    for (int j = 0; j <= k; ++j) {
+      const bool bonus = j == k;  // every draft accepted: sample target[k]
+      const float* P = target_row(a, i, j);
+      const float* Q = bonus ? P : draft_row(a, i, j);
+      // ---- maxima of s = l / T
+      float mp = -INFINITY, mq = -INFINITY;
+#pragma unroll 4
+      for (int c = 0; c < n_c; ++c) {
+        const int e = e_w + c * 128 + lane * 4;
+        if (e < V) {
+          const float4 sp = scale_s(ld_l2(P + e), T);
+          mp = fmaxf(mp, fmaxf(fmaxf(sp.x, sp.y), fmaxf(sp.z, sp.w)));
+          if (!bonus) {
+            const float4 sq = scale_s(ld_l2(Q + e), T);
+            mq = fmaxf(mq, fmaxf(fmaxf(sq.x, sq.y), fmaxf(sq.z, sq.w)));
+          }
+        }
+      }
+      mp = warp_max(mp);
+      mq = warp_max(mq);
+      if (lane == 0) {
+        sh.wm[0][warp] = mp;
+        sh.wm[1][warp] = mq;
+      }
+      __syncthreads();
+      if (warp == 0) {
+        const float x = warp_max(sh.wm[0][lane]);
+        const float y = warp_max(sh.wm[1][lane]);
+        if (lane == 0) {
+          sh.m[0] = x;
+          sh.m[1] = y;
+        }
+      }
+      __syncthreads();
+      mp = sh.m[0];
+      mq = sh.m[1];
+      // ---- weights: sums, last nonzero, w[x]
+      const int x = bonus ? -1 : drafted[j];
+      const bool x_ok = x >= 0 && x < V;
+      double zp = 0.0, zq = 0.0;
+      int lp = -1;
+#pragma unroll 4
+      for (int c = 0; c < n_c; ++c) {
+        const int e = e_w + c * 128 + lane * 4;
+        if (e < V) {
+          const float4 wp = weights4(ld_l2(P + e), T, mp);
+          zp += (double)wp.x;
+          zp += (double)wp.y;
+          zp += (double)wp.z;
+          zp += (double)wp.w;
+          if (wp.w > 0.f) lp = e + 3;
+          else if (wp.z > 0.f) lp = e + 2;
+          else if (wp.y > 0.f) lp = e + 1;
+          else if (wp.x > 0.f) lp = e;
+          if (!bonus) {
+            const float4 wq = weights4(ld_l2(Q + e), T, mq);
+            zq += (double)wq.x;
+            zq += (double)wq.y;
+            zq += (double)wq.z;
+            zq += (double)wq.w;
+            if (x_ok && x >= e && x < e + 4) {
+              const int q = x - e;
+              sh.xw[0] = (double)(q == 0 ? wp.x : q == 1 ? wp.y : q == 2 ? wp.z : wp.w);
+              sh.xw[1] = (double)(q == 0 ? wq.x : q == 1 ? wq.y : q == 2 ? wq.z : wq.w);
+            }
+          }
+        }
+      }
+      zp = warp_sum_d(zp);
+      zq = warp_sum_d(zq);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) lp = max(lp, __shfl_xor_sync(0xffffffffu, lp, o));
+      if (lane == 0) {
+        sh.ws[0][warp] = zp;
+        sh.ws[1][warp] = zq;
+        sh.wl[0][warp] = lp;
+        sh.wl[1][warp] = -1;
+      }
+      __syncthreads();
+      st_reduce_sums(sh, 2);
+      __syncthreads();
+      const double Zp = sh.z[0], Zq = sh.z[1];
+      int n_acc = k;
+      bool use_resid = false;
+      double t, invp = 0.0, invq = 0.0;
+      if (!bonus) {
+        // engine/speculative.py:133-142
+        const double wpx = x_ok ? sh.xw[0] : 0.0, wqx = x_ok ? sh.xw[1] : 0.0;
+        double prob = 0.0;
+        if (x_ok && wqx > 0.0) {
+          const double ratio = __ddiv_rn(__dmul_rn(wpx, Zq), __dmul_rn(wqx, Zp));
+          prob = ratio < 1.0 ? ratio : 1.0;
+        }
+        if (u[k + j] < prob) {
+          if (threadIdx.x == 0) toks[j] = x;
+          continue;
+        }
+        // engine/speculative.py:43-50: residual max(0, p - q), or p if it is empty
+        n_acc = j;
+        invp = 1.0 / Zp;
+        invq = 1.0 / Zq;
+        double zr = 0.0;
+        int lr = -1;
+#pragma unroll 4
+        for (int c = 0; c < n_c; ++c) {
+          const int e = e_w + c * 128 + lane * 4;
+          if (e < V) {
+            const float4 wp = weights4(ld_l2(P + e), T, mp);
+            const float4 wq = weights4(ld_l2(Q + e), T, mq);
+            const double r0 = resid(wp.x, wq.x, invp, invq), r1 = resid(wp.y, wq.y, invp, invq);
+            const double r2 = resid(wp.z, wq.z, invp, invq), r3 = resid(wp.w, wq.w, invp, invq);
+            zr += r0;
+            zr += r1;
+            zr += r2;
+            zr += r3;
+            if (r3 > 0.0) lr = e + 3;
+            else if (r2 > 0.0) lr = e + 2;
+            else if (r1 > 0.0) lr = e + 1;
+            else if (r0 > 0.0) lr = e;
+          }
+        }
+        zr = warp_sum_d(zr);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) lr = max(lr, __shfl_xor_sync(0xffffffffu, lr, o));
+        if (lane == 0) {
+          sh.ws[1][warp] = zr;  // draft sums are done with: the residual's go here
+          sh.wl[1][warp] = lr;
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+          double z = 0.0;
+          int last = -1;
+          for (int w = 0; w < kStWarps; ++w) {
+            z += sh.ws[1][w];
+            last = max(last, sh.wl[1][w]);
+          }
+          sh.z[1] = z;
+          sh.last[1] = last;
+        }
+        __syncthreads();
+        use_resid = sh.z[1] > 0.0;
+      }
+      const int v = use_resid ? 1 : 0;
+      t = u[2 * k] * sh.z[v];
+      // ---- inverse CDF: warp segment -> 128-entry row -> entry
+      if (threadIdx.x == 0) {
+        double run = 0.0;
+        int hit = -1;
+        for (int w = 0; w < kStWarps; ++w) {
+          if (run + sh.ws[v][w] > t) {
+            hit = w;
+            break;
+          }
+          run += sh.ws[v][w];
+        }
+        sh.cross_warp = hit;
+        sh.cross_run = run;
+      }
+      __syncthreads();
+      const int w_hit = sh.cross_warp;
+      const int last_all = sh.last[v];
+      if (w_hit < 0) {
+        if (threadIdx.x == 0) {  // rounding left no crossing: the last entry of nonzero weight
+          const int fin = last_all >= 0 ? last_all : 0;
+          toks[n_acc] = fin;
+          for (int jj = n_acc + 1; jj <= k; ++jj) toks[jj] = -1;
+          a.n_accepted[i] = n_acc;
+          a.final_token[i] = fin;
+        }
+      } else if (warp == w_hit) {
+        double run = sh.cross_run;
+        int found = -1;
+        for (int c = 0; c < n_c && found < 0; ++c) {
+          const int e = e_w + c * 128 + lane * 4;
+          double w4[4] = {0.0, 0.0, 0.0, 0.0};
+          if (e < V) {
+            const float4 wp = weights4(ld_l2(P + e), T, mp);
+            if (use_resid) {
+              const float4 wq = weights4(ld_l2(Q + e), T, mq);
+              w4[0] = resid(wp.x, wq.x, invp, invq);
+              w4[1] = resid(wp.y, wq.y, invp, invq);
+              w4[2] = resid(wp.z, wq.z, invp, invq);
+              w4[3] = resid(wp.w, wq.w, invp, invq);
+            } else {
+              w4[0] = wp.x;
+              w4[1] = wp.y;
+              w4[2] = wp.z;
+              w4[3] = wp.w;
+            }
+          }
+          const double mine = ((w4[0] + w4[1]) + w4[2]) + w4[3];
+          const double incl = warp_inclusive_scan_d(mine) + run;
+          const unsigned hit = __ballot_sync(0xffffffffu, incl > t);
+          if (hit) {
+            const int l = __ffs(hit) - 1;
+            if (lane == l) {
+              double acc = incl - mine;
+              for (int q = 0; q < 4 && found < 0; ++q) {
+                acc += w4[q];
+                if (acc > t) found = e + q;
+              }
+              if (found < 0) {  // rounding: the lane's last entry of nonzero weight
+                for (int q = 3; q >= 0 && found < 0; --q)
+                  if (w4[q] > 0.0) found = e + q;
+              }
+            }
+            found = __shfl_sync(0xffffffffu, found, l);
+            if (found < 0) found = sh.wl[v][warp] >= 0 ? sh.wl[v][warp] : (last_all >= 0 ? last_all : 0);
+          }
+          run = __shfl_sync(0xffffffffu, incl, 31);
+        }
+        if (found < 0) found = sh.wl[v][warp] >= 0 ? sh.wl[v][warp] : (last_all >= 0 ? last_all : 0);
+        if (lane == 0) {
+          toks[n_acc] = found;
+          for (int jj = n_acc + 1; jj <= k; ++jj) toks[jj] = -1;
+          a.n_accepted[i] = n_acc;
+          a.final_token[i] = found;
+        }
+      }
+      __syncthreads();  // sh is rewritten by the next row
+      break;            // the row is finished (rejection or bonus)
+    }
+  }
+}
+
+// The vector kernels read 16-byte vectors: every logits row must start on a
+// 16-byte boundary (base pointers aligned, strides and vocab multiples of 4).
+bool vec_accept_ok(const AcceptArgs& a) {
   auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
   auto m4 = [](int64_t v) { return (v & 3) == 0; };
-  if (a.V > kClMax * kClCtaCap || !m4(a.V)) return false;
+  if (!m4(a.V)) return false;
   if (!al(a.target0) || !al(a.verify) || !al(a.draft0) || (a.k > 1 && !al(a.draft_rest))) return false;
   return m4(a.t0_stride) && m4(a.v_row) && m4(a.v_pos) && m4(a.d0_stride) && (a.k <= 1 || (m4(a.dr_row) && m4(a.dr_pos)));
 }
@@ -914,8 +1220,9 @@ extern "C" int pse_sample_tokens(const float* logits, int64_t row_stride, const 
   return PSE_OK;
 }
 
-extern "C" int pse_accept_force_per_row(int32_t on) {
-  g_accept_per_row = on ? 1 : 0;
+extern "C" int pse_accept_select(int32_t kernel) {
+  if (kernel < 0 || kernel > 2) return PSE_EINVAL;
+  g_accept_kernel = kernel;
   return PSE_OK;
 }
 
@@ -931,11 +1238,22 @@ extern "C" int pse_spec_accept(const float* target0, int64_t t0_stride, const in
   if (temperature > 0.f && (!u || !draft0 || (k > 1 && !draft_rest))) return PSE_EINVAL;
   AcceptArgs a{target0, t0_stride, t0_index, verify, v_row, v_pos, draft0, d0_stride, d0_index, draft_rest,
                dr_row, dr_pos, drafts, u, u_stride, k, vocab, temperature, tokens, n_accepted, final_token};
-  if (temperature > 0.f && !g_accept_per_row && cluster_accept_ok(a)) {
+  const bool vec = temperature > 0.f && vec_accept_ok(a);
+  if (vec && g_accept_kernel == 0) {
+    const int seg = ((vocab + kStWarps - 1) / kStWarps + 127) & ~127;
+    int sms = kNumSMs, dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    int grid = rows < PSE_ACCEPT_ROWS_IN_FLIGHT ? rows : PSE_ACCEPT_ROWS_IN_FLIGHT;
+    if (grid > sms) grid = sms;
+    accept_stream_kernel<<<grid, kStThreads, 0, (cudaStream_t)stream>>>(a, rows, seg);
+    PSE_LAUNCH_CHECK();
+    return PSE_OK;
+  }
+  if (vec && g_accept_kernel == 2 && vocab <= kClMax * kClCtaCap) {
     // one cluster per row with the row held on chip (vocabularies up to 8 x 16384)
     const int C = (vocab + kClCtaCap - 1) / kClCtaCap;
     const int per_lane = (vocab + C * kClThreads - 1) / (C * kClThreads);
-    const int run_len = (per_lane + 3) & ~3;  // <= 64
+    const int run_len = (per_lane + 3) & ~3;  // <= 32
     int rc = -1;
     switch (C) {
       case 1: rc = launch_accept_cluster<1>(a, rows, run_len, (cudaStream_t)stream); break;

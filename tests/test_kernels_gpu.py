@@ -323,25 +323,28 @@ def test_accept_resample_matches_oracle(k, vocab, temp, agree):
 
 @pytest.mark.parametrize("rows,k,vocab,temp,agree", [
     (24, 4, 128256, 1.0, 0.97),   # cluster of 8 CTAs per row
-    (16, 3, 100000, 0.7, 0.99),   # cluster of 7 (segment padded to 896)
-    (300, 2, 32000, 1.0, 0.95),   # more rows than co-resident clusters: persistent clusters
-    (40, 8, 16385, 1.0, 0.98),    # one entry past a single CTA's capacity
+    (16, 3, 100000, 0.7, 0.99),   # cluster of 7; streaming segments padded to 3200
+    (300, 2, 32000, 1.0, 0.95),   # more rows than CTAs / clusters in flight: persistent
+    (40, 8, 16388, 1.0, 0.98),    # just past a single cluster CTA's capacity
+    (20, 3, 200000, 1.0, 0.97),   # beyond the cluster kernel's reach (it falls back to the scalar kernel)
 ])
-def test_cluster_accept_matches_oracle_and_per_row_kernel(rows, k, vocab, temp, agree):
-    """T > 0 runs one thread-block cluster per row; the CTA-per-row kernel is
-    the other form.  Both must give the oracle's tokens exactly."""
+def test_accept_kernels_match_oracle(rows, k, vocab, temp, agree):
+    """T > 0 has three kernels (L2-resident streaming CTA per row, the default;
+    CTA-per-row scalar; one thread-block cluster per row).  Each must give the
+    oracle's tokens exactly."""
     N = _N()
     tgt, drf, u, drafts = _accept_inputs(rows, k, vocab, temp, seed=rows + k + vocab, agree=agree)
-    got = _run_accept(N, tgt, drf, u, drafts, temp)
-    N.load().pse_accept_force_per_row(1)
+    outs = []
     try:
-        per_row = _run_accept(N, tgt, drf, u, drafts, temp)
+        for kern in (0, 1, 2):
+            N.load().pse_accept_select(kern)
+            outs.append(_run_accept(N, tgt, drf, u, drafts, temp))
     finally:
-        N.load().pse_accept_force_per_row(0)
+        N.load().pse_accept_select(0)
     seen = set()
     for i in range(rows):
         want, n = accept_row(tgt[i].numpy(), drf[i].numpy(), drafts[i], u[i].numpy(), k, temp)
-        for toks, nacc, fin in (got, per_row):
+        for toks, nacc, fin in outs:
             assert nacc[i] == n, (i, nacc[i], n)
             assert toks[i, : n + 1].tolist() == want and fin[i] == want[-1]
             assert (toks[i, n + 1:] == -1).all()
