@@ -163,11 +163,14 @@ def run_pse(args, rank, world, device):
     prompts = [r.prompt_ids for r in mine]
     rids = [r.request_id for r in mine]
     dn, tn = {}, {}
+    torch.cuda.synchronize()
     t0 = time.perf_counter()
-    for r, p in zip(rids, prompts):
-        dn[r], tn[r] = pse.prefill_request(d, t, dc, tc, r, p)
+    out = pse.prefill_requests(d, t, dc, tc, rids, prompts)  # batched; same caches as one-by-one calls
+    for r in rids:
+        dn[r], tn[r] = out[r]
     torch.cuda.synchronize()
     prefill_s = time.perf_counter() - t0
+    prefill_tokens = sum(len(p) for p in prompts)
     k, T = w.k, w.temperature
 
     def api_step(defer):
@@ -292,7 +295,7 @@ def run_pse(args, rank, world, device):
         e_, es_, _ = reduce_stats(m["e2e_tokens"], m["e2e_ms"] / 1000.0, device=device)
         out[name] = dict(committed=c_, ms=s_ * 1000.0, e2e_tokens=e_, e2e_ms=es_ * 1000.0)
     return dict(ref=out["ref"], head=out["head"], attn_ms=attn_ms, attn_bytes=attn_bytes, attn_width=width,
-                prefill_s=prefill_s, clocks=head["clocks"], B=B, k=k, kernels_per_step=head["kernels"],
+                prefill_s=prefill_s, prefill_tokens=prefill_tokens, clocks=head["clocks"], B=B, k=k, kernels_per_step=head["kernels"],
                 dtype=str(dtype), h2d=6 * B * 4, d2h=(B * (k + 1) + B + 2) * 4, step_bytes=step_bytes,
                 tokens_per_step_mean=head["committed"] / args.steps / max(world, 1),
                 deferred=not args.reference_structure)
@@ -480,6 +483,44 @@ def micro_accept(args, device):
     N.load().pse_accept_select(0)
 
 
+def micro_prefill(args, device):
+    """Batched prefill (prefill_requests) against one-by-one prefill_request
+    calls on the workload's first ``--rows`` requests (default 64), each into
+    fresh caches: wall time with device sync, prompt tokens/s, and whether the
+    two left identical block tables and free lists."""
+    import pse
+    from pse import workload as wl
+    w = wl.WORKLOADS[args.workload]
+    dtype = torch.bfloat16 if w.dtype == "bfloat16" else torch.float32
+    n = args.rows or 64
+    prompts = wl.prompts(w, seed=0, n=n)
+    ids = [f"r{i}" for i in range(n)]
+    d, t = build_pair(w, dtype, device)
+    res = {}
+    for mode in ("one_by_one", "batched", "batched_again"):
+        dc = cache_for(d, w, n, dtype, device, w.k + 2)
+        tc = cache_for(t, w, n, dtype, device, w.k + 2)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        if mode == "one_by_one":
+            for r, p in zip(ids, prompts):
+                pse.prefill_request(d, t, dc, tc, r, p)
+        else:
+            pse.prefill_requests(d, t, dc, tc, ids, prompts)
+        torch.cuda.synchronize()
+        res[mode] = (time.perf_counter() - t0, [dc.block_table(r) for r in ids] + [tc.block_table(r) for r in ids],
+                     dc.allocator.free_list(), tc.allocator.free_list())
+        del dc, tc
+    tokens = sum(len(p) for p in prompts)
+    same = res["one_by_one"][1:] == res["batched"][1:]
+    print(json.dumps({"metric": "prefill prompt tokens/s", "workload": w.name, "requests": n, "prompt_tokens": tokens,
+                      "one_by_one_s": res["one_by_one"][0], "batched_s": res["batched_again"][0],
+                      "one_by_one_tokens_per_s": tokens / res["one_by_one"][0],
+                      "batched_tokens_per_s": tokens / res["batched_again"][0],
+                      "speedup": res["one_by_one"][0] / res["batched_again"][0],
+                      "identical_tables_and_free_lists": same}), flush=True)
+
+
 def micro_churn(args, device):
     """Truncate churn: 1024 rows of block 16 with lengths U[512, 32768]; each
     step reserves 8 tokens (verify), truncates every row to base + U{0..8}
@@ -553,7 +594,7 @@ def main():
     ap.add_argument("--cpu-rows", type=int, default=4)
     ap.add_argument("--cpu-steps", type=int, default=10)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--micro", choices=["attn", "accept", "churn"], default=None,
+    ap.add_argument("--micro", choices=["attn", "accept", "churn", "prefill"], default=None,
                     help="kernel microbenchmark instead of the step")
     ap.add_argument("--temperature", type=float, default=1.0, help="--micro accept: temperature")
     ap.add_argument("--accept-kernel", type=int, default=0, choices=[0, 1, 2],
@@ -610,6 +651,9 @@ def main():
     if args.micro == "churn":
         micro_churn(args, device)
         return
+    if args.micro == "prefill":
+        micro_prefill(args, device)
+        return
     r = run_pse(args, rank, world, device)
     if r is None:
         return
@@ -657,7 +701,8 @@ def main():
                                                   "kind": "port", "sample": cpu["sample"]},
         "clocks": r["clocks"],
         "gpu_launches": r["kernels_per_step"] * args.steps,
-        "prefill_s": r["prefill_s"],
+        "prefill": {"requests": r["B"], "prompt_tokens": r["prefill_tokens"], "seconds": r["prefill_s"],
+                    "tokens_per_s": r["prefill_tokens"] / r["prefill_s"], "mode": "batched (prefill_requests)"},
     }
     print(json.dumps(line), flush=True)
 

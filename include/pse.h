@@ -96,6 +96,14 @@ int pse_block_free_one(pse_block_state st, const int32_t *block_id, void *stream
 int pse_kv_reserve(pse_block_state st, const int32_t *slots, int32_t rows, int32_t width,
                    int32_t *base_len, void *stream);
 
+/* pse_kv_reserve with a width per row (widths[i] >= 0; a negative one latches
+ * PSE_STATUS_BAD_BLOCK and changes nothing): the allocation half of one
+ * PagedKVCache.append per row, rows in call order -- what prefilling requests
+ * one after another (engine/speculative.py:53-73, engine/scheduler.py:78-90)
+ * allocates, in one launch. */
+int pse_kv_reserve_rows(pse_block_state st, const int32_t *slots, int32_t rows, const int32_t *widths,
+                        int32_t *base_len, void *stream);
+
 /* PagedKVCache.truncate (engine/paged_cache.py:140-154) for many rows in call
  * order, as the commit loop of engine/speculative.py:162-164 runs it.  New
  * length of row i = new_len[i] if new_len != NULL, else base_len[i] +

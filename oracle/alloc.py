@@ -49,9 +49,10 @@ class BlockState:
     def free_list(self) -> list[int]:
         return self.stack[: self.top].tolist()
 
-    def reserve(self, slots, width: int):
-        """Make room for ``width`` more tokens in every row and advance the rows'
-        lengths; returns the lengths before the call.
+    def reserve(self, slots, width):
+        """Make room for ``width`` more tokens in every row (an int, or one per
+        row: one append per row in row order) and advance the rows' lengths;
+        returns the lengths before the call.
 
         On exhaustion the state is the reference's after its ``MemoryError``
         (engine/paged_cache.py:46-47 raised inside the per-row append loop of
@@ -59,6 +60,7 @@ class BlockState:
         complete, the failing row keeps the blocks it got before the pool ran
         dry, its length and every later row are untouched."""
         slots = np.asarray(slots, dtype=np.int64)
+        width = np.broadcast_to(np.asarray(width, dtype=np.int64), slots.shape)  # one width, or one per row
         base = self.seq_len[slots].copy()
         want = blocks_for(base + width, self.block_size)
         if np.any(want > self.table.shape[1]):
@@ -75,7 +77,7 @@ class BlockState:
                 self.block_free[blk] = False
             self.nblocks[s] += got[i]
             if complete[i]:
-                self.seq_len[s] = base[i] + width
+                self.seq_len[s] = base[i] + width[i]
         self.top -= int(got.sum())
         if not complete.all():
             self.status |= OOM

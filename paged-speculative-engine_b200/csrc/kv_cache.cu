@@ -70,7 +70,7 @@ __global__ void block_free_one_kernel(pse_block_state st, const int32_t* block_i
 
 // engine/paged_cache.py:116-130 for every row of one forward, rows in order.
 __global__ void __launch_bounds__(kScanThreads) reserve_kernel(pse_block_state st, const int32_t* slots, int rows,
-                                                              int width, int32_t* base_len) {
+                                                              int width, const int32_t* widths, int32_t* base_len) {
   __shared__ int scan_tmp[33];
   const int tid = threadIdx.x;
   const bool latched = *st.status != 0;
@@ -86,7 +86,11 @@ __global__ void __launch_bounds__(kScanThreads) reserve_kernel(pse_block_state s
     }
     int len = st.seq_len[slot];
     base_len[i] = len;
-    if (blocks_for(len + width, st.block_size) > st.max_blocks) bad |= PSE_STATUS_TABLE_OVERFLOW;
+    const int w = widths ? widths[i] : width;
+    if (w < 0)
+      bad |= PSE_STATUS_BAD_BLOCK;
+    else if (blocks_for(len + w, st.block_size) > st.max_blocks)
+      bad |= PSE_STATUS_TABLE_OVERFLOW;
   }
   bad = __syncthreads_or(bad) ? 1 : 0;
   if (bad || latched) {
@@ -99,7 +103,11 @@ __global__ void __launch_bounds__(kScanThreads) reserve_kernel(pse_block_state s
           bits |= PSE_STATUS_BAD_BLOCK;
           continue;
         }
-        if (blocks_for(st.seq_len[slot] + width, st.block_size) > st.max_blocks) bits |= PSE_STATUS_TABLE_OVERFLOW;
+        const int w = widths ? widths[i] : width;
+        if (w < 0)
+          bits |= PSE_STATUS_BAD_BLOCK;
+        else if (blocks_for(st.seq_len[slot] + w, st.block_size) > st.max_blocks)
+          bits |= PSE_STATUS_TABLE_OVERFLOW;
       }
       atomicOr(st.status, bits);
     }
@@ -110,12 +118,13 @@ __global__ void __launch_bounds__(kScanThreads) reserve_kernel(pse_block_state s
   int oom = 0;
   for (int c0 = 0; c0 < rows; c0 += blockDim.x) {
     const int i = c0 + tid;
-    int slot = 0, len = 0, nb = 0, need = 0;
+    int slot = 0, len = 0, nb = 0, need = 0, w = 0;
     if (i < rows) {
       slot = slots[i];
       len = base_len[i];
       nb = st.nblocks[slot];
-      need = max(blocks_for(len + width, st.block_size) - nb, 0);
+      w = widths ? widths[i] : width;
+      need = max(blocks_for(len + w, st.block_size) - nb, 0);
     }
     int total = 0;
     const int off = block_exclusive_scan(need, scan_tmp, &total) + running;
@@ -129,7 +138,7 @@ __global__ void __launch_bounds__(kScanThreads) reserve_kernel(pse_block_state s
       }
       st.nblocks[slot] = nb + got;
       if (off + need <= top)
-        st.seq_len[slot] = len + width;
+        st.seq_len[slot] = len + w;
       else
         oom = 1;
     }
@@ -343,7 +352,16 @@ extern "C" int pse_kv_reserve(pse_block_state st, const int32_t* slots, int32_t 
                               int32_t* base_len, void* stream) {
   if (!state_ok(st) || rows < 0 || width < 0 || (rows > 0 && (!slots || !base_len))) return PSE_EINVAL;
   if (rows == 0) return PSE_OK;
-  reserve_kernel<<<1, kScanThreads, 0, (cudaStream_t)stream>>>(st, slots, rows, width, base_len);
+  reserve_kernel<<<1, kScanThreads, 0, (cudaStream_t)stream>>>(st, slots, rows, width, nullptr, base_len);
+  PSE_LAUNCH_CHECK();
+  return PSE_OK;
+}
+
+extern "C" int pse_kv_reserve_rows(pse_block_state st, const int32_t* slots, int32_t rows, const int32_t* widths,
+                                   int32_t* base_len, void* stream) {
+  if (!state_ok(st) || rows < 0 || (rows > 0 && (!slots || !widths || !base_len))) return PSE_EINVAL;
+  if (rows == 0) return PSE_OK;
+  reserve_kernel<<<1, kScanThreads, 0, (cudaStream_t)stream>>>(st, slots, rows, 0, widths, base_len);
   PSE_LAUNCH_CHECK();
   return PSE_OK;
 }

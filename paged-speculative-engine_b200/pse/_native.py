@@ -53,6 +53,7 @@ _PROTOS = {
     "pse_block_alloc_one": ([BlockState, c_p, c_p], 1),
     "pse_block_free_one": ([BlockState, c_p, c_p], 1),
     "pse_kv_reserve": ([BlockState, c_p, c_i32, c_i32, c_p, c_p], 1),
+    "pse_kv_reserve_rows": ([BlockState, c_p, c_i32, c_p, c_p, c_p], 1),
     "pse_kv_truncate": ([BlockState, c_p, c_i32, c_p, c_p, c_p, c_p], 1),
     "pse_kv_release": ([BlockState, c_p, c_i32, c_p], 1),
     "pse_kv_append": ([BlockState, KVLayer, c_p, c_p, c_i64, c_i64, c_p, c_p, c_i32, c_i32, c_p], 1),

@@ -14,7 +14,7 @@ from dataclasses import dataclass, field
 
 import torch
 
-from .speculative import batched_speculative_step, prefill_request
+from .speculative import batched_speculative_step, prefill_requests
 
 
 @dataclass
@@ -61,10 +61,18 @@ def run_continuous_speculative_batches(draft_model, target_model, requests, draf
     t_start = time.perf_counter()
 
     def admit() -> None:
-        while queue and len(active) < max_batch_size:
-            req = queue.pop(0)
-            dn, tn = prefill_request(draft_model, target_model, draft_cache, target_cache,
-                                     req.request_id, req.prompt_ids)
+        # FIFO admission up to the batch size (engine/scheduler.py:78-90); the
+        # admitted requests are prefilled together, leaving the caches as
+        # one-by-one prefills would
+        take = []
+        while queue and len(active) + len(take) < max_batch_size:
+            take.append(queue.pop(0))
+        if not take:
+            return
+        out = prefill_requests(draft_model, target_model, draft_cache, target_cache,
+                               [q.request_id for q in take], [q.prompt_ids for q in take])
+        for req in take:
+            dn, tn = out[req.request_id]
             active[req.request_id] = _Active(req, list(req.prompt_ids), dn, tn, submitted_at=t_start)
             steps_taken[req.request_id] = 0
 

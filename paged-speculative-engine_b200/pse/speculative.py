@@ -27,7 +27,7 @@ import torch
 
 from . import _native as N
 from .device_model import device_model
-from .engine import Scratch, forward, lm_head
+from .engine import Scratch, forward, lm_head, scratch_for
 
 DEFAULT_SEED = 0x5EED5EED
 USE_GRAPHS = True  # replay steps from CUDA graphs (from the second step of a batch size on)
@@ -112,6 +112,100 @@ def prefill_request(draft_model, target_model, draft_cache, target_cache, reques
     draft_cache.check_status("prefill")
     target_cache.check_status("prefill")
     return outs[0], outs[1]
+
+
+def _batch_prefill_safe(pairs, request_ids, prompts) -> bool:
+    """True when prefilling these requests one by one could not raise part-way
+    (so one batched pass leaves exactly the same state)."""
+    if len(set(request_ids)) != len(request_ids):
+        return False
+    for dm, cache in pairs:
+        bs = cache.block_size
+        need = 0
+        for r, p in zip(request_ids, prompts):
+            if r in cache._slot or not p:
+                return False
+            if min(p) < 0 or max(p) >= dm.vocab:
+                return False
+            if dm.pos_emb is not None and len(p) > dm.max_seq_len:
+                return False
+            need += (len(p) + bs - 1) // bs
+        if need > cache.allocator.num_free:
+            return False
+    return True
+
+
+@torch.no_grad()
+def prefill_requests(draft_model, target_model, draft_cache, target_cache, request_ids, prompts,
+                     max_tokens_per_call: int = 32768) -> dict:
+    """Batched ``prefill_request`` (engine/speculative.py:53-73) for many
+    requests, as the scheduler admits them (engine/scheduler.py:78-90).
+
+    The result and the cache state are those of calling ``prefill_request``
+    for each request in order: requests are created in order, and each cache
+    reserves every prompt's blocks in one launch with rows in request order
+    (``pse_kv_reserve_rows``), so block tables and free lists are the
+    one-by-one calls'.  The forwards then run over groups of similar-length
+    prompts, each padded to its longest (padding is never allocated: its K/V
+    lands past the row's length in a block the row holds, or is dropped).
+    Returns ``{request_id: (draft_logits, target_logits)}`` (device views of
+    the per-slot next-logits rows).  Inputs for which the one-by-one calls
+    would raise part-way (bad ids, positions past ``max_seq_len``, a pool too
+    small, duplicate or existing ids, empty prompts) take the one-by-one path,
+    which raises at the same request."""
+    ids = list(request_ids)
+    prompts = [list(p) for p in prompts]
+    if len(ids) != len(prompts):
+        raise ValueError("one prompt per request id")
+    pairs = [(device_model(m, c.dtype, c.device), c) for m, c in ((draft_model, draft_cache),
+                                                                   (target_model, target_cache))]
+    if len(ids) <= 1 or not _batch_prefill_safe(pairs, ids, prompts):
+        return {r: prefill_request(draft_model, target_model, draft_cache, target_cache, r, p)
+                for r, p in zip(ids, prompts)}
+    for r in ids:
+        draft_cache.create_request(r)
+        target_cache.create_request(r)
+    n = len(ids)
+    P = np.array([len(p) for p in prompts], dtype=np.int64)
+    order = np.argsort(-P, kind="stable")  # groups of similar length, longest first
+    st = N.stream_ptr()
+    for dm, cache in pairs:
+        dev = cache.device
+        cache.ensure_capacity_len(int(P.max()))
+        slots_np = np.fromiter((cache.slot(r) for r in ids), np.int32, n)
+        slots = torch.from_numpy(slots_np).to(dev)
+        widths = torch.from_numpy(P.astype(np.int32)).to(dev)
+        base = torch.empty(n, dtype=torch.int32, device=dev)
+        N.call("pse_kv_reserve_rows", cache.state, slots.data_ptr(), n, widths.data_ptr(), base.data_ptr(), st)
+        buf = next_logits_buffer(cache, dm.vocab)
+        sc = scratch_for(dm)
+        i0 = 0
+        while i0 < n:
+            W = int(P[order[i0]])
+            grp = order[i0:i0 + max(1, max_tokens_per_call // W)]
+            i0 += len(grp)
+            g = len(grp)
+            ids_pad = np.zeros((g, W), dtype=np.int32)
+            for j, idx in enumerate(grp):
+                ids_pad[j, : P[idx]] = prompts[idx]
+            gids = torch.from_numpy(ids_pad).to(dev)
+            gslots = torch.from_numpy(slots_np[grp]).to(dev)
+            gbase = torch.zeros(g, dtype=torch.int32, device=dev)
+            forward(dm, cache, gslots, gids.view(-1), g, W, gbase, W, None, scratch=sc, reserve=False)
+            last = torch.from_numpy(np.arange(g, dtype=np.int64) * W + P[grp] - 1).to(dev)
+            hsel = torch.index_select(sc.h[: g * W], 0, last)
+            logits = torch.empty(g, dm.vocab, dtype=torch.float32, device=dev)
+            lm_head(dm, hsel, logits)
+            N.call("pse_scatter_rows", logits.data_ptr(), dm.vocab, gslots.data_ptr(), g, dm.vocab,
+                   buf.data_ptr(), dm.vocab, buf.shape[0], st)
+            last_tok = torch.from_numpy(np.array([prompts[idx][-1] for idx in grp], dtype=np.int32)).to(dev)
+            cache.last_token.index_copy_(0, gslots.long(), last_tok)
+        cache.note_lengths(ids, P.tolist())
+    draft_cache.check_status("prefill")
+    target_cache.check_status("prefill")
+    dv = next_logits_views(draft_cache, pairs[0][0].vocab)
+    tv = next_logits_views(target_cache, pairs[1][0].vocab)
+    return {r: (dv[draft_cache.slot(r)], tv[target_cache.slot(r)]) for r in ids}
 
 
 class _StepBuffers:

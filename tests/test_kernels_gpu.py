@@ -60,14 +60,19 @@ def test_batched_reserve_truncate_release_bit_exact(seed):
             rows = [int(x) for x in pick] + ([int(x) for x in rng.choice(live, size=min(len(live), 3),
                                                                          replace=False)] if live else [])
             rng.shuffle(rows)
-            w = int(rng.integers(1, 12))
-            if any((ref.seq_len[s] + w + bs - 1) // bs > width for s in rows):
+            ragged = bool(rng.integers(0, 2))  # pse_kv_reserve_rows: one width per row
+            w = rng.integers(0, 12, size=len(rows)) if ragged else int(rng.integers(1, 12))
+            if any((ref.seq_len[s] + ww + bs - 1) // bs > width for s, ww in zip(rows, np.broadcast_to(w, len(rows)))):
                 continue
             ref.status = 0
             base_ref = ref.reserve(rows, w)
             slots = torch.tensor(rows, dtype=torch.int32, device="cuda")
             base = torch.empty(len(rows), dtype=torch.int32, device="cuda")
-            N.call("pse_kv_reserve", c.state, slots.data_ptr(), len(rows), w, base.data_ptr(), st)
+            if ragged:
+                wd = torch.tensor(w.tolist(), dtype=torch.int32, device="cuda")
+                N.call("pse_kv_reserve_rows", c.state, slots.data_ptr(), len(rows), wd.data_ptr(), base.data_ptr(), st)
+            else:
+                N.call("pse_kv_reserve", c.state, slots.data_ptr(), len(rows), w, base.data_ptr(), st)
             assert base.cpu().tolist() == base_ref.tolist()
             for s in rows:
                 if s not in live:
