@@ -521,6 +521,72 @@ def micro_prefill(args, device):
                       "identical_tables_and_free_lists": same}), flush=True)
 
 
+def micro_scheduler(args, device):
+    """The whole workload through run_continuous_speculative_batches (FIFO
+    admission up to the batch size, batched prefill, steps until every request
+    has max_new_tokens, as the reference's own benchmark drives it): committed
+    tokens / wall time, device-synchronised, after one untimed run of the same
+    workload (graph capture, allocation).  T > 0 draws its uniforms from the
+    device Philox stream."""
+    import pse
+    from pse import workload as wl
+    from pse.scheduler import Request
+    w = wl.WORKLOADS[args.workload]
+    dtype = torch.bfloat16 if w.dtype == "bfloat16" else torch.float32
+    n = args.rows or w.n_requests
+    prompts = wl.prompts(w, seed=0, n=n)
+    d, t = build_pair(w, dtype, device)
+    out = {}
+    for run in ("warm", "timed"):
+        reqs = [Request(f"{run}{i}", p, w.max_new_tokens) for i, p in enumerate(prompts)]
+        dc = cache_for(d, w, n, dtype, device, w.k + 2)
+        tc = cache_for(t, w, n, dtype, device, w.k + 2)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        res = pse.run_continuous_speculative_batches(d, t, reqs, dc, tc, w.max_batch_size, k=w.k,
+                                                     temperature=w.temperature,
+                                                     defer_bonus=not args.reference_structure)
+        torch.cuda.synchronize()
+        out[run] = (time.perf_counter() - t0, sum(len(r.output_ids) - len(p) for r, p in
+                                                   zip(sorted(res, key=lambda r: int(r.request_id[len(run):])),
+                                                       prompts)))
+        del dc, tc
+    secs, toks = out["timed"]
+    cpu = None
+    if not args.no_cpu_baseline:
+        # the reference's CPU path (oracle port, fp32) on the same whole workload, all host threads
+        from oracle import scheduler as OS
+        from oracle.model import ModelConfig as OMC, TinyGPT as OTG, LlamaConfig as OLC, TinyLlama as OTL
+        from oracle.paged_cache import PagedKVCache as OPC
+        torch.set_num_threads(os.cpu_count() or 1)
+        torch.manual_seed(0)
+        pr = w.pair
+        mk = (lambda c: OTG(OMC(vocab_size=pr.vocab, **c))) if pr.kind == "gpt" else \
+            (lambda c: OTL(OLC(vocab_size=pr.vocab, **c)))
+        od, ot = mk(pr.draft).eval(), mk(pr.target).eval()
+
+        def ocache(m):
+            c = m.cfg
+            per = w.prompt_hi + w.max_new_tokens + w.k + 2
+            return OPC(c.n_layers, getattr(c, "n_kv_heads", c.n_heads), c.d_model // c.n_heads, w.block_size,
+                       n * ((per + w.block_size - 1) // w.block_size) + 8)
+
+        oreqs = [OS.Request(f"c{i}", p, w.max_new_tokens) for i, p in enumerate(prompts)]
+        g = torch.Generator().manual_seed(0)
+        t0 = time.perf_counter()
+        ores = OS.run_continuous_speculative_batches(od, ot, oreqs, ocache(od), ocache(ot), w.max_batch_size,
+                                                     k=w.k, temperature=w.temperature, generator=g)
+        csecs = time.perf_counter() - t0
+        ctoks = sum(len(r.output_ids) for r in ores) - sum(len(p) for p in prompts)
+        cpu = {"value": ctoks / csecs, "unit": "tokens/s", "cores": os.cpu_count() or 1, "kind": "port",
+               "sample": f"the whole {w.name} workload ({n} requests), fp32 oracle port"}
+    print(json.dumps({"metric": "committed tokens/s (scheduler, whole workload)", "workload": w.name, "k": w.k,
+                      "temperature": w.temperature, "requests": n, "max_batch_size": w.max_batch_size,
+                      "step": "reference structure" if args.reference_structure else "deferred bonus",
+                      "generated_tokens": toks, "seconds": secs, "value": toks / secs, "unit": "tokens/s",
+                      "cpu_baseline": cpu}), flush=True)
+
+
 def micro_churn(args, device):
     """Truncate churn: 1024 rows of block 16 with lengths U[512, 32768]; each
     step reserves 8 tokens (verify), truncates every row to base + U{0..8}
@@ -591,10 +657,11 @@ def main():
     ap.add_argument("--impl", default="pse", choices=["pse", "reference"])
     ap.add_argument("--workload", default="gpt2-small")
     ap.add_argument("--rows", type=int, default=None)
+    ap.add_argument("--k", type=int, default=None, help="draft length (default: the workload's)")
     ap.add_argument("--cpu-rows", type=int, default=4)
     ap.add_argument("--cpu-steps", type=int, default=10)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--micro", choices=["attn", "accept", "churn", "prefill"], default=None,
+    ap.add_argument("--micro", choices=["attn", "accept", "churn", "prefill", "scheduler"], default=None,
                     help="kernel microbenchmark instead of the step")
     ap.add_argument("--temperature", type=float, default=1.0, help="--micro accept: temperature")
     ap.add_argument("--accept-kernel", type=int, default=0, choices=[0, 1, 2],
@@ -610,6 +677,9 @@ def main():
     args = ap.parse_args()
 
     from pse import workload as wl
+    if args.k is not None:  # e.g. the k sweep of the T = 1 workload
+        import dataclasses
+        wl.WORKLOADS[args.workload] = dataclasses.replace(wl.WORKLOADS[args.workload], k=args.k)
     w = wl.WORKLOADS[args.workload]
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -653,6 +723,9 @@ def main():
         return
     if args.micro == "prefill":
         micro_prefill(args, device)
+        return
+    if args.micro == "scheduler":
+        micro_scheduler(args, device)
         return
     r = run_pse(args, rank, world, device)
     if r is None:
