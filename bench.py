@@ -658,6 +658,8 @@ def main():
     ap.add_argument("--workload", default="gpt2-small")
     ap.add_argument("--rows", type=int, default=None)
     ap.add_argument("--k", type=int, default=None, help="draft length (default: the workload's)")
+    ap.add_argument("--step-temperature", type=float, default=None,
+                    help="sampling temperature of the step (default: the workload's)")
     ap.add_argument("--cpu-rows", type=int, default=4)
     ap.add_argument("--cpu-steps", type=int, default=10)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -677,9 +679,12 @@ def main():
     args = ap.parse_args()
 
     from pse import workload as wl
-    if args.k is not None:  # e.g. the k sweep of the T = 1 workload
+    if args.k is not None or args.step_temperature is not None:  # e.g. the k sweep of the T = 1 workload
         import dataclasses
-        wl.WORKLOADS[args.workload] = dataclasses.replace(wl.WORKLOADS[args.workload], k=args.k)
+        w0 = wl.WORKLOADS[args.workload]
+        wl.WORKLOADS[args.workload] = dataclasses.replace(
+            w0, k=w0.k if args.k is None else args.k,
+            temperature=w0.temperature if args.step_temperature is None else args.step_temperature)
     w = wl.WORKLOADS[args.workload]
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

@@ -217,21 +217,18 @@ __global__ void __launch_bounds__(kScanThreads) free_rows_kernel(pse_block_state
 }
 
 // Scatter of new K/V tokens into their blocks (engine/paged_cache.py:131-136).
-// One thread per VEC elements of one (row, w, head).
+// CTAs walk the new tokens (row, w); a token's block is looked up once and its
+// threads copy one VEC-element piece of one head each (32-bit index math).
 template <typename T, int VEC>
 __global__ void append_kernel(pse_block_state st, T* __restrict__ k_pool, T* __restrict__ v_pool, int kv_heads,
                               int head_dim, const T* __restrict__ k_src, const T* __restrict__ v_src,
                               int64_t tok_stride, int64_t head_stride, const int32_t* __restrict__ slots,
                               const int32_t* __restrict__ base_len, int rows, int width) {
   const int vecs = head_dim / VEC;
-  const int64_t total = (int64_t)rows * width * kv_heads * vecs;
-  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
-    const int v = (int)(e % vecs);
-    int64_t r = e / vecs;
-    const int h = (int)(r % kv_heads);
-    r /= kv_heads;
-    const int w = (int)(r % width);
-    const int i = (int)(r / width);
+  const int per_tok = kv_heads * vecs;
+  const int n_tok = rows * width;
+  for (int tkn = blockIdx.x; tkn < n_tok; tkn += gridDim.x) {
+    const int i = tkn / width, w = tkn - (tkn / width) * width;
     const int slot = slots[i];
     if (slot < 0 || slot >= st.num_slots) continue;
     const int pos = base_len[i] + w;
@@ -240,16 +237,21 @@ __global__ void append_kernel(pse_block_state st, T* __restrict__ k_pool, T* __r
     if (bi >= st.nblocks[slot]) continue;  // block never reserved (pool exhausted)
     const int blk = st.block_table[(int64_t)slot * st.max_blocks + bi];
     if (blk < 0 || blk >= st.num_blocks) continue;
-    const int64_t dst = (((int64_t)blk * kv_heads + h) * st.block_size + pos % st.block_size) * head_dim + v * VEC;
-    const int64_t src = ((int64_t)i * width + w) * tok_stride + (int64_t)h * head_stride + v * VEC;
-    if constexpr (VEC * sizeof(T) == 16) {
-      *reinterpret_cast<uint4*>(k_pool + dst) = *reinterpret_cast<const uint4*>(k_src + src);
-      *reinterpret_cast<uint4*>(v_pool + dst) = *reinterpret_cast<const uint4*>(v_src + src);
-    } else {
+    const int64_t dst_tok = ((int64_t)blk * kv_heads * st.block_size + pos % st.block_size) * head_dim;
+    const int64_t src_tok = (int64_t)tkn * tok_stride;
+    for (int e = threadIdx.x; e < per_tok; e += blockDim.x) {
+      const int h = e / vecs, v = e - (e / vecs) * vecs;
+      const int64_t dst = dst_tok + (int64_t)h * st.block_size * head_dim + v * VEC;
+      const int64_t src = src_tok + (int64_t)h * head_stride + v * VEC;
+      if constexpr (VEC * sizeof(T) == 16) {
+        *reinterpret_cast<uint4*>(k_pool + dst) = *reinterpret_cast<const uint4*>(k_src + src);
+        *reinterpret_cast<uint4*>(v_pool + dst) = *reinterpret_cast<const uint4*>(v_src + src);
+      } else {
 #pragma unroll
-      for (int q = 0; q < VEC; ++q) {
-        k_pool[dst + q] = k_src[src + q];
-        v_pool[dst + q] = v_src[src + q];
+        for (int q = 0; q < VEC; ++q) {
+          k_pool[dst + q] = k_src[src + q];
+          v_pool[dst + q] = v_src[src + q];
+        }
       }
     }
   }
@@ -304,17 +306,21 @@ int launch_append(const pse_block_state& st, const pse_kv_layer& kv, const void*
   const bool vec_ok = kv.head_dim % V16 == 0 && tok_stride % V16 == 0 && head_stride % V16 == 0 &&
                       reinterpret_cast<uintptr_t>(k_src) % 16 == 0 && reinterpret_cast<uintptr_t>(v_src) % 16 == 0 &&
                       reinterpret_cast<uintptr_t>(kv.k_pool) % 16 == 0 && reinterpret_cast<uintptr_t>(kv.v_pool) % 16 == 0;
-  const int threads = 256;
+  if ((int64_t)rows * width >= (1ll << 31)) return PSE_EINVAL;
+  const int n_tok = rows * width;
+  const int grid = n_tok < kNumSMs * 16 ? n_tok : kNumSMs * 16;
   if (vec_ok) {
-    const int64_t work = (int64_t)rows * width * kv.kv_heads * (kv.head_dim / V16);
-    append_kernel<T, V16><<<grid_for(work, threads), threads, 0, s>>>(
-        st, (T*)kv.k_pool, (T*)kv.v_pool, kv.kv_heads, kv.head_dim, (const T*)k_src, (const T*)v_src, tok_stride,
-        head_stride, slots, base_len, rows, width);
+    const int per_tok = kv.kv_heads * (kv.head_dim / V16);
+    const int threads = per_tok >= 256 ? 256 : ((per_tok + 31) / 32) * 32;
+    append_kernel<T, V16><<<grid, threads, 0, s>>>(st, (T*)kv.k_pool, (T*)kv.v_pool, kv.kv_heads, kv.head_dim,
+                                                   (const T*)k_src, (const T*)v_src, tok_stride, head_stride, slots,
+                                                   base_len, rows, width);
   } else {
-    const int64_t work = (int64_t)rows * width * kv.kv_heads * kv.head_dim;
-    append_kernel<T, 1><<<grid_for(work, threads), threads, 0, s>>>(
-        st, (T*)kv.k_pool, (T*)kv.v_pool, kv.kv_heads, kv.head_dim, (const T*)k_src, (const T*)v_src, tok_stride,
-        head_stride, slots, base_len, rows, width);
+    const int per_tok = kv.kv_heads * kv.head_dim;
+    const int threads = per_tok >= 256 ? 256 : ((per_tok + 31) / 32) * 32;
+    append_kernel<T, 1><<<grid, threads, 0, s>>>(st, (T*)kv.k_pool, (T*)kv.v_pool, kv.kv_heads, kv.head_dim,
+                                                 (const T*)k_src, (const T*)v_src, tok_stride, head_stride, slots,
+                                                 base_len, rows, width);
   }
   PSE_LAUNCH_CHECK();
   return PSE_OK;

@@ -243,10 +243,14 @@ __device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.f + er
 
 __device__ __forceinline__ float silu(float x) { return x / (1.f + expf(-x)); }
 
+// Grid-stride kernels below take their flat index type I: 32-bit whenever the
+// element count fits (integer division by a runtime value is several times
+// cheaper in 32 bits), 64-bit otherwise.
+template <typename I>
 __global__ void epilogue_kernel(int op, void* y, int64_t ldy, const void* bias, float* x, int64_t ldx, void* y2,
                                 int64_t ldy2, int n_rows, int n, int dtype) {
-  const int64_t total = (int64_t)n_rows * n;
-  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+  const I total = (I)n_rows * n;
+  for (I e = blockIdx.x * (I)blockDim.x + threadIdx.x; e < total; e += (I)gridDim.x * blockDim.x) {
     const int64_t r = e / n;
     const int c = (int)(e % n);
     if (op == 0) {
@@ -267,11 +271,12 @@ __global__ void epilogue_kernel(int op, void* y, int64_t ldy, const void* bias, 
 
 // bf16 fast path of ops 0 (bias + GELU, in place) and 2 (SwiGLU): 8 elements
 // (16 bytes) per thread.
+template <typename I>
 __global__ void epilogue_bf16x8_kernel(int op, __nv_bfloat16* y, int64_t ldy, const __nv_bfloat16* bias,
                                        __nv_bfloat16* y2, int64_t ldy2, int n_rows, int n) {
   const int vecs = n / 8;
-  const int64_t total = (int64_t)n_rows * vecs;
-  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+  const I total = (I)n_rows * vecs;
+  for (I e = blockIdx.x * (I)blockDim.x + threadIdx.x; e < total; e += (I)gridDim.x * blockDim.x) {
     const int64_t r = e / vecs;
     const int c = (int)(e % vecs) * 8;
     uint4 a = *reinterpret_cast<const uint4*>(y + r * ldy + c);
@@ -304,12 +309,13 @@ __global__ void epilogue_bf16x8_kernel(int op, __nv_bfloat16* y, int64_t ldy, co
 }
 
 // Rotate-half RoPE on the q heads and k heads of a fused qkv row.
+template <typename I>
 __global__ void rope_kernel(void* qkv, int64_t ld, int width, int q_heads, int kv_heads, int hd,
-                            const int32_t* base_len, float theta, int dtype, int64_t total) {
+                            const int32_t* base_len, float theta, int dtype, I total) {
   const int half = hd / 2;
-  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+  for (I e = blockIdx.x * (I)blockDim.x + threadIdx.x; e < total; e += (I)gridDim.x * blockDim.x) {
     const int p = (int)(e % half);
-    int64_t r = e / half;
+    I r = e / half;
     const int h = (int)(r % (q_heads + kv_heads));
     const int64_t t = r / (q_heads + kv_heads);
     const int64_t pos = (int64_t)base_len[t / width] + t % width;
@@ -324,10 +330,11 @@ __global__ void rope_kernel(void* qkv, int64_t ld, int width, int q_heads, int k
   }
 }
 
-__global__ void scatter_rows_kernel(const float* src, int64_t ld_src, const int32_t* index, int rows, int n,
-                                    float* dst, int64_t ld_dst, int n_dst_rows) {
-  const int64_t total = (int64_t)rows * n;
-  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+template <typename I, typename E>
+__global__ void scatter_rows_kernel(const E* src, int64_t ld_src, const int32_t* index, int rows, int n, E* dst,
+                                    int64_t ld_dst, int n_dst_rows) {
+  const I total = (I)rows * n;
+  for (I e = blockIdx.x * (I)blockDim.x + threadIdx.x; e < total; e += (I)gridDim.x * blockDim.x) {
     const int64_t i = e / n;
     const int c = (int)(e % n);
     const int r = index[i];
@@ -340,6 +347,10 @@ inline int grid_for(int64_t work, int threads) {
   if (g > (int64_t)kNumSMs * 32) g = (int64_t)kNumSMs * 32;
   return g < 1 ? 1 : (int)g;
 }
+
+// Element counts below this use 32-bit flat indices (the grid-stride step,
+// at most kNumSMs * 32 * 256 threads, cannot overflow them).
+constexpr int64_t kIdx32 = 1ll << 30;
 
 }  // namespace
 }  // namespace pse
@@ -416,14 +427,24 @@ extern "C" int pse_epilogue(int32_t op, void* y, int64_t ldy, const void* bias, 
   const bool vec = dtype == PSE_BF16 && op != 1 && n % 8 == 0 && ldy % 8 == 0 && (op != 2 || ldy2 % 8 == 0) &&
                    (reinterpret_cast<uintptr_t>(y) & 15) == 0 && (reinterpret_cast<uintptr_t>(bias) & 15) == 0 &&
                    (reinterpret_cast<uintptr_t>(y2) & 15) == 0;
+  cudaStream_t s = (cudaStream_t)stream;
   if (vec) {
-    epilogue_bf16x8_kernel<<<grid_for((int64_t)n_rows * (n / 8), 256), 256, 0, (cudaStream_t)stream>>>(
-        op, (__nv_bfloat16*)y, ldy, (const __nv_bfloat16*)bias, (__nv_bfloat16*)y2, ldy2, n_rows, n);
+    const int64_t work = (int64_t)n_rows * (n / 8);
+    if (work < kIdx32)
+      epilogue_bf16x8_kernel<int><<<grid_for(work, 256), 256, 0, s>>>(
+          op, (__nv_bfloat16*)y, ldy, (const __nv_bfloat16*)bias, (__nv_bfloat16*)y2, ldy2, n_rows, n);
+    else
+      epilogue_bf16x8_kernel<int64_t><<<grid_for(work, 256), 256, 0, s>>>(
+          op, (__nv_bfloat16*)y, ldy, (const __nv_bfloat16*)bias, (__nv_bfloat16*)y2, ldy2, n_rows, n);
     PSE_LAUNCH_CHECK();
     return PSE_OK;
   }
-  epilogue_kernel<<<grid_for((int64_t)n_rows * n, 256), 256, 0, (cudaStream_t)stream>>>(op, y, ldy, bias, x, ldx, y2,
-                                                                                         ldy2, n_rows, n, dtype);
+  const int64_t work = (int64_t)n_rows * n;
+  if (work < kIdx32)
+    epilogue_kernel<int><<<grid_for(work, 256), 256, 0, s>>>(op, y, ldy, bias, x, ldx, y2, ldy2, n_rows, n, dtype);
+  else
+    epilogue_kernel<int64_t><<<grid_for(work, 256), 256, 0, s>>>(op, y, ldy, bias, x, ldx, y2, ldy2, n_rows, n,
+                                                                 dtype);
   PSE_LAUNCH_CHECK();
   return PSE_OK;
 }
@@ -434,8 +455,14 @@ extern "C" int pse_rope(void* qkv, int64_t ld, int32_t rows, int32_t width, int3
   if (rows == 0 || width == 0) return PSE_OK;
   if (!qkv || !base_len) return PSE_EINVAL;
   const int64_t total = (int64_t)rows * width * (q_heads + kv_heads) * (head_dim / 2);
-  rope_kernel<<<grid_for(total, 256), 256, 0, (cudaStream_t)stream>>>(qkv, ld, width, q_heads, kv_heads, head_dim,
-                                                                      base_len, theta, dtype, total);
+  if (total < kIdx32)
+    rope_kernel<int><<<grid_for(total, 256), 256, 0, (cudaStream_t)stream>>>(qkv, ld, width, q_heads, kv_heads,
+                                                                           head_dim, base_len, theta, dtype,
+                                                                           (int)total);
+  else
+    rope_kernel<int64_t><<<grid_for(total, 256), 256, 0, (cudaStream_t)stream>>>(qkv, ld, width, q_heads, kv_heads,
+                                                                               head_dim, base_len, theta, dtype,
+                                                                               total);
   PSE_LAUNCH_CHECK();
   return PSE_OK;
 }
@@ -445,8 +472,21 @@ extern "C" int pse_scatter_rows(const float* src, int64_t ld_src, const int32_t*
   if (rows < 0 || n < 0) return PSE_EINVAL;
   if (rows == 0 || n == 0) return PSE_OK;
   if (!src || !index || !dst) return PSE_EINVAL;
-  scatter_rows_kernel<<<grid_for((int64_t)rows * n, 256), 256, 0, (cudaStream_t)stream>>>(src, ld_src, index, rows, n,
-                                                                                          dst, ld_dst, n_dst_rows);
+  cudaStream_t s = (cudaStream_t)stream;
+  const bool v4 = n % 4 == 0 && ld_src % 4 == 0 && ld_dst % 4 == 0 && (reinterpret_cast<uintptr_t>(src) & 15) == 0 &&
+                  (reinterpret_cast<uintptr_t>(dst) & 15) == 0;
+  if (v4 && (int64_t)rows * (n / 4) < kIdx32) {
+    // 16-byte rows: one float4 per element of the index space
+    scatter_rows_kernel<int><<<grid_for((int64_t)rows * (n / 4), 256), 256, 0, s>>>(
+        reinterpret_cast<const float4*>(src), ld_src / 4, index, rows, n / 4, reinterpret_cast<float4*>(dst),
+        ld_dst / 4, n_dst_rows);
+  } else if ((int64_t)rows * n < kIdx32) {
+    scatter_rows_kernel<int><<<grid_for((int64_t)rows * n, 256), 256, 0, s>>>(src, ld_src, index, rows, n, dst, ld_dst,
+                                                                             n_dst_rows);
+  } else {
+    scatter_rows_kernel<int64_t><<<grid_for((int64_t)rows * n, 256), 256, 0, s>>>(src, ld_src, index, rows, n, dst,
+                                                                                 ld_dst, n_dst_rows);
+  }
   PSE_LAUNCH_CHECK();
   return PSE_OK;
 }
