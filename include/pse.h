@@ -224,7 +224,9 @@ int pse_spec_accept(const float *target0, int64_t t0_stride, const int32_t *t0_i
  * streaming CTA per row), 1 the CTA-per-row scalar kernel, 2 one thread-block
  * cluster of ceil(vocab / 16384) CTAs per row with the row held on chip
  * (vocab <= 131072).  All three give the same tokens; parity tests compare
- * them.  No counterpart in the reference. */
+ * them.  Draft sampling (pse_sample_tokens) at T > 0 likewise runs a streaming
+ * CTA per row for 0 and the scalar kernel otherwise.  No counterpart in the
+ * reference. */
 int pse_accept_select(int32_t kernel);
 
 /* ------------------------------------------------------------------------ */

@@ -24,7 +24,9 @@ namespace {
 constexpr int kSampleThreads = 512;
 
 // Which accept kernel runs at T > 0 (tests compare the forms): 0 the default
-// (streaming), 1 the CTA-per-row scalar kernel, 2 the cluster kernel.
+// (streaming), 1 the CTA-per-row scalar kernel, 2 the cluster kernel.  Draft
+// sampling at T > 0 uses the streaming kernel when this is 0, the scalar
+// kernel otherwise.
 int g_accept_kernel = 0;
 constexpr int kWarpsPerBlock = kSampleThreads / 32;
 
@@ -1179,6 +1181,136 @@ __global__ void __launch_bounds__(kStThreads, 1) accept_stream_kernel(AcceptArgs
   }
 }
 
+// ---------------------------------------------------------------- draft sampling, T > 0, one CTA per row
+//
+// The streaming kernel's layout for one logits row: the max pass, one exp /
+// sum pass that also leaves each warp segment's sum, then the inverse-CDF
+// descent walks only the crossing segment (weights recomputed there).
+__global__ void __launch_bounds__(kStThreads, 1) sample_stream_kernel(const float* logits, int64_t row_stride,
+                                                                      const int32_t* index, int rows, int V, float T,
+                                                                      const double* u, int64_t u_stride, int u_col,
+                                                                      int32_t* out, int64_t out_stride,
+                                                                      int32_t* out2, int64_t out2_stride, int seg) {
+  __shared__ StShared sh;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int e_w = warp * seg;
+  const int n_c = seg >> 7;
+  for (int i = blockIdx.x; i < rows; i += gridDim.x) {
+    const float* P = logits + (int64_t)(index ? index[i] : i) * row_stride;
+    float mp = -INFINITY;
+#pragma unroll 4
+    for (int c = 0; c < n_c; ++c) {
+      const int e = e_w + c * 128 + lane * 4;
+      if (e < V) {
+        const float4 sp = scale_s(ld_l2(P + e), T);
+        mp = fmaxf(mp, fmaxf(fmaxf(sp.x, sp.y), fmaxf(sp.z, sp.w)));
+      }
+    }
+    mp = warp_max(mp);
+    if (lane == 0) sh.wm[0][warp] = mp;
+    __syncthreads();
+    if (warp == 0) {
+      const float x = warp_max(sh.wm[0][lane]);
+      if (lane == 0) sh.m[0] = x;
+    }
+    __syncthreads();
+    mp = sh.m[0];
+    double zp = 0.0;
+    int lp = -1;
+#pragma unroll 4
+    for (int c = 0; c < n_c; ++c) {
+      const int e = e_w + c * 128 + lane * 4;
+      if (e < V) {
+        const float4 wp = weights4(ld_l2(P + e), T, mp);
+        zp += (double)wp.x;
+        zp += (double)wp.y;
+        zp += (double)wp.z;
+        zp += (double)wp.w;
+        if (wp.w > 0.f) lp = e + 3;
+        else if (wp.z > 0.f) lp = e + 2;
+        else if (wp.y > 0.f) lp = e + 1;
+        else if (wp.x > 0.f) lp = e;
+      }
+    }
+    zp = warp_sum_d(zp);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) lp = max(lp, __shfl_xor_sync(0xffffffffu, lp, o));
+    if (lane == 0) {
+      sh.ws[0][warp] = zp;
+      sh.wl[0][warp] = lp;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      double z = 0.0;
+      int last = -1;
+      for (int w = 0; w < kStWarps; ++w) {
+        z += sh.ws[0][w];
+        last = max(last, sh.wl[0][w]);
+      }
+      const double t = u[(int64_t)i * u_stride + u_col] * z;
+      double run = 0.0;
+      int hit = -1;
+      for (int w = 0; w < kStWarps; ++w) {
+        if (run + sh.ws[0][w] > t) {
+          hit = w;
+          break;
+        }
+        run += sh.ws[0][w];
+      }
+      sh.z[0] = t;
+      sh.last[0] = last;
+      sh.cross_warp = hit;
+      sh.cross_run = run;
+    }
+    __syncthreads();
+    const int w_hit = sh.cross_warp;
+    const int last_all = sh.last[0];
+    const double t = sh.z[0];
+    int tok = -1;
+    if (w_hit < 0) {
+      tok = last_all >= 0 ? last_all : 0;  // rounding left no crossing: the last entry of nonzero weight
+    } else if (warp == w_hit) {
+      double run = sh.cross_run;
+      int found = -1;
+      for (int c = 0; c < n_c && found < 0; ++c) {
+        const int e = e_w + c * 128 + lane * 4;
+        double w4[4] = {0.0, 0.0, 0.0, 0.0};
+        if (e < V) {
+          const float4 wp = weights4(ld_l2(P + e), T, mp);
+          w4[0] = wp.x;
+          w4[1] = wp.y;
+          w4[2] = wp.z;
+          w4[3] = wp.w;
+        }
+        const double mine = ((w4[0] + w4[1]) + w4[2]) + w4[3];
+        const double incl = warp_inclusive_scan_d(mine) + run;
+        const unsigned hit = __ballot_sync(0xffffffffu, incl > t);
+        if (hit) {
+          const int l = __ffs(hit) - 1;
+          if (lane == l) {
+            double acc = incl - mine;
+            for (int q = 0; q < 4 && found < 0; ++q) {
+              acc += w4[q];
+              if (acc > t) found = e + q;
+            }
+            for (int q = 3; q >= 0 && found < 0; --q)
+              if (w4[q] > 0.0) found = e + q;
+          }
+          found = __shfl_sync(0xffffffffu, found, l);
+          if (found < 0) found = sh.wl[0][warp] >= 0 ? sh.wl[0][warp] : (last_all >= 0 ? last_all : 0);
+        }
+        run = __shfl_sync(0xffffffffu, incl, 31);
+      }
+      tok = found >= 0 ? found : (sh.wl[0][warp] >= 0 ? sh.wl[0][warp] : (last_all >= 0 ? last_all : 0));
+    }
+    if ((w_hit < 0 && threadIdx.x == 0) || (w_hit >= 0 && warp == w_hit && lane == 0)) {
+      out[(int64_t)i * out_stride] = tok;
+      if (out2) out2[(int64_t)i * out2_stride] = tok;
+    }
+    __syncthreads();  // sh is rewritten by the next row
+  }
+}
+
 // The vector kernels read 16-byte vectors: every logits row must start on a
 // 16-byte boundary (base pointers aligned, strides and vocab multiples of 4).
 bool vec_accept_ok(const AcceptArgs& a) {
@@ -1213,6 +1345,15 @@ extern "C" int pse_sample_tokens(const float* logits, int64_t row_stride, const 
   if (rows < 0 || vocab <= 0) return PSE_EINVAL;
   if (rows == 0) return PSE_OK;
   if (!logits || !out || (temperature > 0.f && !u)) return PSE_EINVAL;
+  if (temperature > 0.f && g_accept_kernel == 0 && vocab % 4 == 0 && row_stride % 4 == 0 &&
+      (reinterpret_cast<uintptr_t>(logits) & 15) == 0) {
+    const int seg = ((vocab + kStWarps - 1) / kStWarps + 127) & ~127;
+    sample_stream_kernel<<<rows, kStThreads, 0, (cudaStream_t)stream>>>(logits, row_stride, index, rows, vocab,
+                                                                       temperature, u, u_stride, u_col, out, out_stride,
+                                                                       out2, out2_stride, seg);
+    PSE_LAUNCH_CHECK();
+    return PSE_OK;
+  }
   sample_kernel<<<rows, kSampleThreads, 0, (cudaStream_t)stream>>>(logits, row_stride, index, vocab, temperature, u,
                                                                     u_stride, u_col, out, out_stride, out2,
                                                                     out2_stride);

@@ -255,8 +255,9 @@ def test_philox_uniforms_bit_exact():
     assert np.array_equal(out.cpu().numpy(), want)
 
 
-@pytest.mark.parametrize("vocab,temp", [(257, 0.0), (257, 1.0), (32000, 0.7), (128256, 1.0)])
-def test_sample_tokens_matches_oracle(vocab, temp):
+@pytest.mark.parametrize("kern", [0, 1])
+@pytest.mark.parametrize("vocab,temp", [(257, 0.0), (257, 1.0), (256, 1.0), (32000, 0.7), (128256, 1.0)])
+def test_sample_tokens_matches_oracle(vocab, temp, kern):
     N = _N()
     rows = 48
     g = torch.Generator().manual_seed(vocab)
@@ -265,9 +266,13 @@ def test_sample_tokens_matches_oracle(vocab, temp):
     u = torch.rand(rows, 3, generator=g, dtype=torch.float64)
     out = torch.empty(rows, dtype=torch.int32, device="cuda")
     ld, ud = logits.cuda(), u.cuda()
-    N.call("pse_sample_tokens", ld.data_ptr(), vocab, None, rows, vocab, temp, ud.data_ptr(), 3, 1,
-           out.data_ptr(), 1, None, 0, N.stream_ptr())
-    got = out.cpu().tolist()
+    N.load().pse_accept_select(2 * kern)  # 0: streaming sampler (vocab % 4 == 0), 2: the scalar one
+    try:
+        N.call("pse_sample_tokens", ld.data_ptr(), vocab, None, rows, vocab, temp, ud.data_ptr(), 3, 1,
+               out.data_ptr(), 1, None, 0, N.stream_ptr())
+        got = out.cpu().tolist()
+    finally:
+        N.load().pse_accept_select(0)
     want = [sample_with_uniform(logits[i].numpy(), temp, float(u[i, 1])) for i in range(rows)]
     assert got == want
     if temp == 0:
