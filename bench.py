@@ -536,6 +536,8 @@ def micro_scheduler(args, device):
     n = args.rows or w.n_requests
     prompts = wl.prompts(w, seed=0, n=n)
     d, t = build_pair(w, dtype, device)
+    if args.sched_mode == "self":
+        d = t  # draft == target: every draft accepted (the reference benchmark's ceiling configuration)
     out = {}
     for run in ("warm", "timed"):
         reqs = [Request(f"{run}{i}", p, w.max_new_tokens) for i, p in enumerate(prompts)]
@@ -543,9 +545,12 @@ def micro_scheduler(args, device):
         tc = cache_for(t, w, n, dtype, device, w.k + 2)
         torch.cuda.synchronize()
         t0 = time.perf_counter()
-        res = pse.run_continuous_speculative_batches(d, t, reqs, dc, tc, w.max_batch_size, k=w.k,
-                                                     temperature=w.temperature,
-                                                     defer_bonus=not args.reference_structure)
+        if args.sched_mode == "plain":
+            res = pse.run_plain_continuous_batches(t, reqs, tc, w.max_batch_size)
+        else:
+            res = pse.run_continuous_speculative_batches(d, t, reqs, dc, tc, w.max_batch_size, k=w.k,
+                                                         temperature=w.temperature,
+                                                         defer_bonus=not args.reference_structure)
         torch.cuda.synchronize()
         out[run] = (time.perf_counter() - t0, sum(len(r.output_ids) - len(p) for r, p in
                                                    zip(sorted(res, key=lambda r: int(r.request_id[len(run):])),
@@ -553,7 +558,7 @@ def micro_scheduler(args, device):
         del dc, tc
     secs, toks = out["timed"]
     cpu = None
-    if not args.no_cpu_baseline:
+    if not args.no_cpu_baseline and args.sched_mode == "spec":
         # the reference's CPU path (oracle port, fp32) on the same whole workload, all host threads
         from oracle import scheduler as OS
         from oracle.model import ModelConfig as OMC, TinyGPT as OTG, LlamaConfig as OLC, TinyLlama as OTL
@@ -583,6 +588,8 @@ def micro_scheduler(args, device):
     print(json.dumps({"metric": "committed tokens/s (scheduler, whole workload)", "workload": w.name, "k": w.k,
                       "temperature": w.temperature, "requests": n, "max_batch_size": w.max_batch_size,
                       "step": "reference structure" if args.reference_structure else "deferred bonus",
+                      "mode": {"spec": "speculative, independent draft", "self": "speculative, draft = target",
+                               "plain": "plain continuous batching, no speculation"}[args.sched_mode],
                       "generated_tokens": toks, "seconds": secs, "value": toks / secs, "unit": "tokens/s",
                       "cpu_baseline": cpu}), flush=True)
 
@@ -658,6 +665,8 @@ def main():
     ap.add_argument("--workload", default="gpt2-small")
     ap.add_argument("--rows", type=int, default=None)
     ap.add_argument("--k", type=int, default=None, help="draft length (default: the workload's)")
+    ap.add_argument("--sched-mode", default="spec", choices=["spec", "self", "plain"],
+                    help="--micro scheduler: independent draft, draft = target, or no speculation")
     ap.add_argument("--step-temperature", type=float, default=None,
                     help="sampling temperature of the step (default: the workload's)")
     ap.add_argument("--cpu-rows", type=int, default=4)

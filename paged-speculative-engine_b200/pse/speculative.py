@@ -136,39 +136,34 @@ def _batch_prefill_safe(pairs, request_ids, prompts) -> bool:
 
 
 @torch.no_grad()
-def prefill_requests(draft_model, target_model, draft_cache, target_cache, request_ids, prompts,
-                     max_tokens_per_call: int = 32768) -> dict:
-    """Batched ``prefill_request`` (engine/speculative.py:53-73) for many
-    requests, as the scheduler admits them (engine/scheduler.py:78-90).
-
-    The result and the cache state are those of calling ``prefill_request``
-    for each request in order: requests are created in order, and each cache
-    reserves every prompt's blocks in one launch with rows in request order
-    (``pse_kv_reserve_rows``), so block tables and free lists are the
-    one-by-one calls'.  The forwards then run over groups of similar-length
-    prompts, each padded to its longest (padding is never allocated: its K/V
-    lands past the row's length in a block the row holds, or is dropped).
-    Returns ``{request_id: (draft_logits, target_logits)}`` (device views of
-    the per-slot next-logits rows).  Inputs for which the one-by-one calls
-    would raise part-way (bad ids, positions past ``max_seq_len``, a pool too
-    small, duplicate or existing ids, empty prompts) take the one-by-one path,
+def prefill_many(models_caches, request_ids, prompts, max_tokens_per_call: int = 32768):
+    """Batched prompt prefill of ``request_ids`` into every (model, cache) pair,
+    leaving each cache as one-by-one appends of the prompts in request order
+    would: requests are created in order, each cache reserves every prompt's
+    blocks in one launch with rows in request order (``pse_kv_reserve_rows``),
+    and the forwards run over groups of similar-length prompts padded to the
+    group's longest (padding is never allocated: its K/V lands past the row's
+    length in a block the row holds, or is dropped).  Returns, per pair, the
+    list of the requests' next-token logits rows (device views), or None --
+    having changed nothing -- when one-by-one prefills could raise part-way
+    (bad ids, positions past ``max_seq_len``, a pool too small, duplicate or
+    existing ids, empty prompts): the caller then takes the one-by-one path,
     which raises at the same request."""
     ids = list(request_ids)
     prompts = [list(p) for p in prompts]
     if len(ids) != len(prompts):
         raise ValueError("one prompt per request id")
-    pairs = [(device_model(m, c.dtype, c.device), c) for m, c in ((draft_model, draft_cache),
-                                                                   (target_model, target_cache))]
+    pairs = [(device_model(m, c.dtype, c.device), c) for m, c in models_caches]
     if len(ids) <= 1 or not _batch_prefill_safe(pairs, ids, prompts):
-        return {r: prefill_request(draft_model, target_model, draft_cache, target_cache, r, p)
-                for r, p in zip(ids, prompts)}
+        return None
     for r in ids:
-        draft_cache.create_request(r)
-        target_cache.create_request(r)
+        for _, cache in pairs:
+            cache.create_request(r)
     n = len(ids)
     P = np.array([len(p) for p in prompts], dtype=np.int64)
     order = np.argsort(-P, kind="stable")  # groups of similar length, longest first
     st = N.stream_ptr()
+    out = []
     for dm, cache in pairs:
         dev = cache.device
         cache.ensure_capacity_len(int(P.max()))
@@ -201,11 +196,31 @@ def prefill_requests(draft_model, target_model, draft_cache, target_cache, reque
             last_tok = torch.from_numpy(np.array([prompts[idx][-1] for idx in grp], dtype=np.int32)).to(dev)
             cache.last_token.index_copy_(0, gslots.long(), last_tok)
         cache.note_lengths(ids, P.tolist())
-    draft_cache.check_status("prefill")
-    target_cache.check_status("prefill")
-    dv = next_logits_views(draft_cache, pairs[0][0].vocab)
-    tv = next_logits_views(target_cache, pairs[1][0].vocab)
-    return {r: (dv[draft_cache.slot(r)], tv[target_cache.slot(r)]) for r in ids}
+    for _, cache in pairs:
+        cache.check_status("prefill")
+    for dm, cache in pairs:
+        views = next_logits_views(cache, dm.vocab)
+        out.append([views[cache.slot(r)] for r in ids])
+    return out
+
+
+@torch.no_grad()
+def prefill_requests(draft_model, target_model, draft_cache, target_cache, request_ids, prompts,
+                     max_tokens_per_call: int = 32768) -> dict:
+    """Batched ``prefill_request`` (engine/speculative.py:53-73) for many
+    requests, as the scheduler admits them (engine/scheduler.py:78-90): the
+    result and both caches' state are those of calling ``prefill_request`` for
+    each request in order (see ``prefill_many``).  Returns
+    ``{request_id: (draft_logits, target_logits)}`` (device views of the
+    per-slot next-logits rows)."""
+    ids = list(request_ids)
+    prompts = [list(p) for p in prompts]
+    out = prefill_many([(draft_model, draft_cache), (target_model, target_cache)], ids, prompts,
+                       max_tokens_per_call)
+    if out is None:
+        return {r: prefill_request(draft_model, target_model, draft_cache, target_cache, r, p)
+                for r, p in zip(ids, prompts)}
+    return {r: (dv, tv) for r, dv, tv in zip(ids, out[0], out[1])}
 
 
 class _StepBuffers:
