@@ -25,6 +25,9 @@ cache state then equals the reference's state after its exception.
 """
 from __future__ import annotations
 
+from collections.abc import Mapping
+
+import numpy as np
 import torch
 
 from . import _native as N
@@ -65,6 +68,22 @@ class _DeviceBlocks:
     @property
     def scratch_id(self) -> torch.Tensor:
         return self.scalars[2:3]
+
+
+class _LengthView(Mapping):
+    """Read-only ``{request_id: length}`` over a cache's per-slot mirror."""
+
+    def __init__(self, cache):
+        self._c = cache
+
+    def __getitem__(self, request_id):
+        return int(self._c._len_np[self._c._slot[request_id]])
+
+    def __iter__(self):
+        return iter(self._c._slot)
+
+    def __len__(self):
+        return len(self._c._slot)
 
 
 def _raise_for_status(bits: int, where: str) -> None:
@@ -152,7 +171,10 @@ class PagedKVCache:
         self.allocator = BlockAllocator(num_blocks, self.device, _blocks=self._blocks)
         self._slot: dict[str, int] = {}
         self._free_slots = list(range(self._blocks.num_slots - 1, -1, -1))
-        self._lengths: dict[str, int] = {}
+        # host mirror of the rows' lengths, one entry per slot (the device
+        # seq_len is the truth; every mutation updates both)
+        self._len_np = np.zeros(self._blocks.num_slots, dtype=np.int64)
+        self.slot_version = 0  # bumped whenever a request id gets or loses a slot
         self.generation = 0  # bumped whenever device buffers move (captured graphs must be rebuilt)
         self._layer_structs = [self._layer_struct(l) for l in range(n_layers)]
         # last token id appended to each slot by a forward (the deferred-bonus
@@ -209,11 +231,14 @@ class PagedKVCache:
         last = torch.zeros(num_slots, dtype=torch.int32, device=self.device)
         last[: old.num_slots] = self.last_token
         self.last_token = last
+        lens = np.zeros(num_slots, dtype=np.int64)
+        lens[: old.num_slots] = self._len_np
+        self._len_np = lens
         self.generation += 1
 
     def ensure_capacity(self, request_ids, extra_tokens: int) -> None:
         """Widen the block table if a row could outgrow it by ``extra_tokens``."""
-        longest = max((self._lengths[r] for r in request_ids), default=0)
+        longest = max((self.length(r) for r in request_ids), default=0)
         self.ensure_capacity_len(longest + extra_tokens)
 
     def ensure_capacity_len(self, tokens: int) -> None:
@@ -237,16 +262,27 @@ class PagedKVCache:
         return self._blocks.status
 
     def _resync_lengths(self) -> None:
-        lens = self._blocks.seq_len.tolist()
-        for r, s in self._slot.items():
-            self._lengths[r] = int(lens[s])
+        self._len_np[:] = self._blocks.seq_len.cpu().numpy()
+
+    @property
+    def _lengths(self) -> "_LengthView":
+        """request id -> length (a read-only mapping over the per-slot mirror)."""
+        return _LengthView(self)
+
+    def slots_np(self, request_ids) -> np.ndarray:
+        return np.fromiter((self._slot[r] for r in request_ids), np.int32, len(request_ids))
+
+    def lengths_np(self, slots: np.ndarray) -> np.ndarray:
+        return self._len_np[slots]
 
     def note_lengths(self, request_ids, lengths) -> None:
-        self._lengths.update(zip(request_ids, lengths))
+        self._len_np[self.slots_np(request_ids)] = np.asarray(lengths, dtype=np.int64)
+
+    def note_lengths_slots(self, slots: np.ndarray, lengths: np.ndarray) -> None:
+        self._len_np[slots] = lengths
 
     def note_append(self, request_ids, width: int) -> None:
-        for r in request_ids:
-            self._lengths[r] += width
+        self._len_np[self.slots_np(request_ids)] += width
 
     def note_last_tokens(self, slots: torch.Tensor, ids: torch.Tensor, rows: int, width: int) -> None:
         """Record the last token id each row appended (device op, stream-ordered)."""
@@ -260,11 +296,12 @@ class PagedKVCache:
         if not self._free_slots:
             self._grow(self._blocks.num_slots * 2, self._blocks.max_blocks)
         self._slot[request_id] = self._free_slots.pop()
-        self._lengths[request_id] = 0
+        self._len_np[self._slot[request_id]] = 0
+        self.slot_version += 1
         self.deferred_slots.discard(self._slot[request_id])
 
     def length(self, request_id: str) -> int:
-        return self._lengths[request_id]
+        return int(self._len_np[self._slot[request_id]])
 
     def num_blocks_in_use(self, request_id: str) -> int:
         return int(self._blocks.nblocks[self._slot[request_id]].item())
@@ -287,23 +324,24 @@ class PagedKVCache:
             v = new_v[layer].to(device=self.device, dtype=self.dtype).contiguous()
             N.call("pse_kv_append", self.state, self.layer(layer), k.data_ptr(), v.data_ptr(),
                    self.head_dim, n * self.head_dim, slots.data_ptr(), base.data_ptr(), 1, n, st)
-        self._lengths[request_id] += n
+        self._len_np[self._slot[request_id]] += n
         self.check_status("append")
 
     def truncate(self, request_id: str, new_length: int) -> None:
         """engine/paged_cache.py:140-154."""
-        old = self._lengths[request_id]
+        old = self.length(request_id)
         if new_length > old:
             raise ValueError(f"truncate({new_length}) > current length {old}")
         slots = torch.tensor([self._slot[request_id]], dtype=torch.int32).to(self.device, non_blocking=True)
         lens = torch.tensor([new_length], dtype=torch.int32).to(self.device, non_blocking=True)
         N.call("pse_kv_truncate", self.state, slots.data_ptr(), 1, lens.data_ptr(), None, None, N.stream_ptr())
-        self._lengths[request_id] = new_length
+        self._len_np[self._slot[request_id]] = new_length
 
     def free_request(self, request_id: str) -> None:
         """engine/paged_cache.py:156-160."""
         s = self._slot.pop(request_id)
-        del self._lengths[request_id]
+        self._len_np[s] = 0
+        self.slot_version += 1
         self.deferred_slots.discard(s)
         slots = torch.tensor([s], dtype=torch.int32).to(self.device, non_blocking=True)
         N.call("pse_kv_release", self.state, slots.data_ptr(), 1, N.stream_ptr())
@@ -314,8 +352,8 @@ class PagedKVCache:
         if not request_ids:
             return
         slots = [self._slot.pop(r) for r in request_ids]
-        for r in request_ids:
-            del self._lengths[r]
+        self._len_np[slots] = 0
+        self.slot_version += 1
         self.deferred_slots.difference_update(slots)
         t = torch.tensor(slots, dtype=torch.int32).to(self.device, non_blocking=True)
         N.call("pse_kv_release", self.state, t.data_ptr(), len(slots), N.stream_ptr())
@@ -324,7 +362,7 @@ class PagedKVCache:
     def gather(self, request_ids):
         """engine/paged_cache.py:162-198: padded per-layer [B, H, max_len, hd]
         K and V, the [B, max_len] padding mask and the [B] lengths (device tensors)."""
-        lengths = torch.tensor([self._lengths[r] for r in request_ids], dtype=torch.long)
+        lengths = torch.tensor([self.length(r) for r in request_ids], dtype=torch.long)
         max_len = int(lengths.max().item()) if len(lengths) else 0
         batch = len(request_ids)
         mask = torch.arange(max_len).view(1, -1) < lengths.view(-1, 1)

@@ -87,8 +87,8 @@ class DecodeRunner:
     def step(self, request_ids, use_graph: bool = True) -> list[int]:
         c, dm = self.cache, self.dm
         B = len(request_ids)
-        slots_np = np.fromiter((c._slot[r] for r in request_ids), np.int32, B)
-        lens = np.fromiter((c._lengths[r] for r in request_ids), np.int64, B)
+        slots_np = c.slots_np(request_ids)
+        lens = c.lengths_np(slots_np)
         longest = int(lens.max()) + 1
         if dm.pos_emb is not None and longest > dm.max_seq_len:
             raise IndexError(f"position {longest - 1} beyond max_seq_len {dm.max_seq_len}")
@@ -120,7 +120,7 @@ class DecodeRunner:
         torch.cuda.current_stream().synchronize()
         if int(b.host_pack_np[B]):
             c.check_status("decode step")
-        c.note_lengths(request_ids, (lens + 1).tolist())
+        c.note_lengths_slots(slots_np, lens + 1)
         return b.host_pack_np[:B].tolist()
 
 

@@ -277,6 +277,7 @@ class StepRunner:
         self.sc_d = Scratch(dm_d)
         self.sc_t = Scratch(dm_t)
         self.tpending = None  # per target slot: token not yet appended (deferred-bonus mode)
+        self._slots_key, self._slots_ids, self._slots_np = None, None, None
 
     # ---------------------------------------------------------------- device program
     def _ctx_bound(self, cache, dm) -> int:
@@ -391,6 +392,8 @@ class StepRunner:
             self.tpending = torch.zeros(tc.state.num_slots, dtype=torch.int32, device=self.device)
             if old is not None:
                 self.tpending[: old.shape[0]] = old
+        if len(tc.deferred_slots) >= len(slots_t) and tc.deferred_slots.issuperset(slots_t):
+            return
         new = [(r, s) for r, s in zip(request_ids, slots_t) if s not in tc.deferred_slots]
         if not new:
             return
@@ -414,10 +417,15 @@ class StepRunner:
         dc, tc = self.dcache, self.tcache
         if not defer_bonus and any(tc.slot(r) in tc.deferred_slots for r in request_ids):
             raise ValueError("request is in the deferred-bonus state: keep stepping it with defer_bonus=True")
-        sd_np = np.fromiter((dc._slot[r] for r in request_ids), np.int32, B)
-        st_np = np.fromiter((tc._slot[r] for r in request_ids), np.int32, B)
-        len_d = np.fromiter((dc._lengths[r] for r in request_ids), np.int64, B)
-        len_t = np.fromiter((tc._lengths[r] for r in request_ids), np.int64, B)
+        # slot arrays: reused while the request list and the slot assignment are unchanged
+        skey = (dc.slot_version, tc.slot_version)
+        if self._slots_key == skey and self._slots_ids == request_ids:
+            sd_np, st_np = self._slots_np
+        else:
+            sd_np, st_np = dc.slots_np(request_ids), tc.slots_np(request_ids)
+            self._slots_key, self._slots_ids, self._slots_np = skey, list(request_ids), (sd_np, st_np)
+        len_d = dc.lengths_np(sd_np)
+        len_t = tc.lengths_np(st_np)
         for dm, c, lens in ((self.dm_d, dc, len_d), (self.dm_t, tc, len_t)):
             longest = int(lens.max()) + k + 1
             if dm.pos_emb is not None and longest > dm.max_seq_len:
@@ -437,7 +445,7 @@ class StepRunner:
             n_before = len(tc.deferred_slots)
             self._enter_deferred(request_ids, stt)
             if len(tc.deferred_slots) != n_before:  # rows entered the deferred state: lengths moved
-                len_t = np.fromiter((tc._lengths[r] for r in request_ids), np.int64, B)
+                len_t = tc.lengths_np(st_np)
         for r, s in zip(request_ids, sd):
             t = draft_next_logits[r]
             v = dviews[s]
@@ -525,8 +533,8 @@ class StepRunner:
         steps = self.request_steps
         for r in request_ids:
             steps[r] = steps.get(r, 0) + 1
-        dc.note_lengths(request_ids, (len_d + nacc_np + 1).tolist())
-        tc.note_lengths(request_ids, (len_t + nacc_np + 1).tolist())
+        dc.note_lengths_slots(sd_np, len_d + nacc_np + 1)
+        tc.note_lengths_slots(st_np, len_t + nacc_np + 1)
         return BatchStepResult(accepted, n_acc, dn, tn)
 
 
