@@ -594,6 +594,68 @@ def micro_scheduler(args, device):
                       "cpu_baseline": cpu}), flush=True)
 
 
+GEMM_SHAPES = {
+    # name: (M, K, N, bias, gelu, fp32 out) -- the gpt2-small step's projections
+    "t.qkv": (1536, 768, 2304, True, False, False), "t.out": (1536, 768, 768, True, False, False),
+    "t.fc1": (1536, 768, 3072, True, True, False), "t.fc2": (1536, 3072, 768, True, False, False),
+    "t.lm_head": (1536, 768, 32000, False, False, True),
+    "d.qkv": (256, 384, 1152, True, False, False), "d.out": (256, 384, 384, True, False, False),
+    "d.fc1": (256, 384, 1536, True, True, False), "d.fc2": (256, 1536, 384, True, False, False),
+    "d.lm_head": (256, 384, 32000, False, False, True),
+}
+
+
+def micro_gemm(args, device):
+    """The step's projection GEMMs, cuBLAS (torch, bias fused, GELU as a
+    separate pass) against pse_gemm_bf16 (tcgen05, bias and GELU fused): device
+    us per call (50 calls captured in a CUDA graph, replayed 4 times, CUDA
+    events) and TFLOP/s."""
+    import pse._native as N
+    rows = []
+    g = torch.Generator(device=device).manual_seed(0)
+    for name, (M, K, Nn, bias, gelu, f32) in GEMM_SHAPES.items():
+        a = torch.randn(M, K, device=device, generator=g).to(torch.bfloat16)
+        w = (torch.randn(Nn, K, device=device, generator=g) * 0.05).to(torch.bfloat16)
+        b = torch.randn(Nn, device=device, generator=g).to(torch.bfloat16) if bias else None
+        c = torch.empty(M, Nn, device=device, dtype=torch.float32 if f32 else torch.bfloat16)
+
+        def cublas():
+            if f32:
+                torch.mm(a, w.t(), out_dtype=torch.float32, out=c)
+            elif b is not None:
+                torch.addmm(b, a, w.t(), out=c)
+                if gelu:
+                    c.copy_(torch.nn.functional.gelu(c))
+            else:
+                torch.mm(a, w.t(), out=c)
+
+        def ours():
+            N.call("pse_gemm_bf16", a.data_ptr(), K, w.data_ptr(), K, None if b is None else b.data_ptr(),
+                   c.data_ptr(), Nn, M, Nn, K, 1 if gelu else 0, 1 if f32 else 0, None, N.stream_ptr())
+
+        res = {}
+        for label, fn in (("cublas", cublas), ("tcgen05", ours)):
+            for _ in range(5):
+                fn()
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()  # device time: 50 calls captured, no host dispatch in the timing
+            with torch.cuda.graph(graph):
+                for _ in range(50):
+                    fn()
+            graph.replay()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(4):
+                graph.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) / 200 * 1000
+            res[label] = {"us": round(us, 2), "tflops": round(2 * M * K * Nn / (us * 1e-6) / 1e12, 1)}
+        rows.append({"gemm": name, "M": M, "K": K, "N": Nn, **res})
+    print(json.dumps({"metric": "projection GEMMs", "rows": rows}), flush=True)
+
+
 def micro_churn(args, device):
     """Truncate churn: 1024 rows of block 16 with lengths U[512, 32768]; each
     step reserves 8 tokens (verify), truncates every row to base + U{0..8}
@@ -672,7 +734,7 @@ def main():
     ap.add_argument("--cpu-rows", type=int, default=4)
     ap.add_argument("--cpu-steps", type=int, default=10)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--micro", choices=["attn", "accept", "churn", "prefill", "scheduler"], default=None,
+    ap.add_argument("--micro", choices=["attn", "accept", "churn", "prefill", "scheduler", "gemm"], default=None,
                     help="kernel microbenchmark instead of the step")
     ap.add_argument("--temperature", type=float, default=1.0, help="--micro accept: temperature")
     ap.add_argument("--accept-kernel", type=int, default=0, choices=[0, 1, 2],
@@ -740,6 +802,9 @@ def main():
         return
     if args.micro == "scheduler":
         micro_scheduler(args, device)
+        return
+    if args.micro == "gemm":
+        micro_gemm(args, device)
         return
     r = run_pse(args, rank, world, device)
     if r is None:
