@@ -255,7 +255,7 @@ def run_pse(args, rank, world, device):
     q = torch.randn(B * width, hq * hd, dtype=dtype, device=device)
     out = torch.empty_like(q)
     wsb = N.size_call("pse_paged_attention_workspace", B, width, hq, hk, hd, max_ctx)
-    ws = torch.empty(max(wsb, 1), dtype=torch.uint8, device=device)
+    ws = torch.zeros(max(wsb, 1), dtype=torch.uint8, device=device)
     st = N.stream_ptr()
     reps = 20
     # the timed launches read blocks up to base + width: reserve them so every page read is a table entry
@@ -360,6 +360,8 @@ ATTN_SHAPES = {
     # name: rows, width, q_heads, kv_heads, head_dim, block, ctx_lo, ctx_hi (ctx includes the width queries)
     "gpt2-verify": (256, 6, 12, 12, 64, 16, 134, 1030),
     "gpt2-verify5": (256, 5, 12, 12, 64, 16, 133, 1029),
+    "gpt2-verify-bs64": (256, 6, 12, 12, 64, 64, 134, 1030),
+    "gpt2-draft-bs64": (256, 1, 6, 6, 64, 64, 129, 1025),
     "gpt2-draft": (256, 1, 6, 6, 64, 16, 129, 1025),
     "verify-5a": (1024, 8, 32, 8, 128, 16, 512, 32768),
 }
@@ -369,7 +371,9 @@ def micro_attention(args, device):
     """Verify-attention kernel microbenchmark: one layer's pools, block tables a
     random permutation of a shared pool, Q/K/V ~ N(0,1), bf16.  Bytes are the
     algorithmic K/V bytes (sum of contexts x kv_heads x head_dim x 2 x 2 B) plus
-    Q and O; each timed launch reads a pool far larger than L2."""
+    Q and O; each timed launch reads a pool far larger than L2 (except the small
+    row counts of a size sweep).  ``--steps`` launches are captured in one CUDA
+    graph and timed as one replay (device time)."""
     import pse
     import pse._native as N
     rows, width, hq, hk, hd, bs, lo, hi = ATTN_SHAPES[args.attn_shape]
@@ -398,22 +402,28 @@ def micro_attention(args, device):
     base = torch.from_numpy((ctx - width).astype(np.int32)).to(device)
     max_ctx = int(ctx.max())
     wsb = N.size_call("pse_paged_attention_workspace", rows, width, hq, hk, hd, max_ctx)
-    ws = torch.empty(wsb, dtype=torch.uint8, device=device)
+    ws = torch.zeros(wsb, dtype=torch.uint8, device=device)
     st = N.stream_ptr()
 
     def launch():
         N.call("pse_paged_attention", c.state, c.layer(0), q.data_ptr(), q.stride(0), out.data_ptr(), out.stride(0),
                slots.data_ptr(), base.data_ptr(), rows, width, hq, 1.0 / math.sqrt(hd), max_ctx, None, ws.data_ptr(),
-               ws.numel(), st)
+               ws.numel(), N.stream_ptr())
 
     for _ in range(max(args.warmup, 3)):
         launch()
     torch.cuda.synchronize()
+    # device time: the launches captured in one CUDA graph (no host dispatch between them)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for _ in range(args.steps):
+            launch()
+    graph.replay()
+    torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(device.index or 0) as clk:
         e0.record()
-        for _ in range(args.steps):
-            launch()
+        graph.replay()
         e1.record()
         torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / args.steps

@@ -142,8 +142,12 @@ int pse_kv_gather(pse_block_state st, pse_kv_layer kv, const int32_t *slots, int
  * permutation of 0..rows-1: the tensor-core kernel hands out rows in that order
  * (longest first keeps the end of the launch from idling on one long row).
  * Output has the pool's
- * dtype.  workspace: pse_paged_attention_workspace() bytes (at least 256: a
- * work counter the call zeroes on the stream, then split-KV partials). */
+ * dtype.  workspace: pse_paged_attention_workspace() bytes (at least 256: the
+ * kernel's work counters, then split-KV partials).  The first 256 bytes must
+ * be zero before the first call with a workspace (e.g. one cudaMemsetAsync
+ * when it is allocated); every call leaves them zero, so a workspace kept for
+ * many calls (or captured in a CUDA graph) needs no per-call clearing.  Calls
+ * that share a workspace must not overlap on the GPU. */
 int pse_paged_attention(pse_block_state st, pse_kv_layer kv, const void *q, int64_t q_tok_stride,
                         void *out, int64_t out_tok_stride, const int32_t *slots, const int32_t *base_len,
                         int32_t rows, int32_t width, int32_t q_heads, float scale, int32_t max_ctx,

@@ -405,7 +405,7 @@ bool tc_eligible(const pse_block_state& st, const pse_kv_layer& kv, int q_heads,
 int tc_attention(const pse_block_state& st, const pse_kv_layer& kv, const void* q, int64_t q_tok_stride, void* out,
                  int64_t out_tok_stride, const int32_t* slots, const int32_t* base_len, int rows, int width,
                  int q_heads, float scale, int split_tokens, int n_splits, void* ws, int* counter,
-                 const int32_t* row_order, cudaStream_t s);
+                 const int32_t* row_order, bool self_reset, cudaStream_t s);
 
 }  // namespace pse
 
@@ -421,8 +421,8 @@ extern "C" int pse_attention_force_generic(int32_t on) {
   return PSE_OK;
 }
 
-// Workspace layout: a 256-byte header (the persistent kernel's work counter,
-// zeroed by every call) followed by the split-KV partials
+// Workspace layout: a 256-byte header (the persistent kernel's work counters,
+// zero before a call and left zero by it) followed by the split-KV partials
 // [n_splits][rows*width][q_heads][head_dim + 2] floats when the call splits.
 constexpr size_t kWsHeader = 256;
 
@@ -476,7 +476,8 @@ extern "C" int pse_paged_attention(pse_block_state st, pse_kv_layer kv, const vo
   cudaStream_t s = (cudaStream_t)stream;
   if (tc_eligible(st, kv, q_heads, width) && !g_force_generic) {
     int rc = tc_attention(st, kv, q, q_tok_stride, out, out_tok_stride, slots, base_len, rows, width, q_heads, scale,
-                          p.split_tokens, p.n_splits, a.ws, reinterpret_cast<int*>(workspace), row_order, s);
+                          p.split_tokens, p.n_splits, a.ws, reinterpret_cast<int*>(workspace), row_order,
+                          /*self_reset=*/true, s);
     if (rc) return rc;
     if (p.n_splits > 1) {
       const int64_t items = (int64_t)rows * width * q_heads;
@@ -580,7 +581,8 @@ extern "C" int pse_paged_attention_noalloc(pse_block_state st, pse_kv_layer kv, 
   cudaStream_t s = (cudaStream_t)stream;
   if (tc_eligible(st, kv, q_heads, width)) {
     rc = tc_attention(st, kv, q, q_tok_stride, out, out_tok_stride, slots, base_len, rows, width, q_heads, scale,
-                      p.split_tokens, p.n_splits, a.ws, reinterpret_cast<int*>(scratch), nullptr, s);
+                      p.split_tokens, p.n_splits, a.ws, reinterpret_cast<int*>(scratch), nullptr,
+                      /*self_reset=*/false, s);
     if (rc) return rc;
     if (p.n_splits > 1) {
       const int64_t items = (int64_t)rows * width * q_heads;

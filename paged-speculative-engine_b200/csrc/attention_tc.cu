@@ -84,6 +84,7 @@ struct Args {
   int n_items;  // rows * kv_heads * n_qtiles * n_splits
   int* counter; // work counter (zeroed before the launch)
   const int32_t* row_order;  // rows in the order items are handed out (nullable: 0..rows-1)
+  int self_reset;            // the last CTA zeroes counter[0..1] (counter[1] counts CTAs done)
 };
 
 __device__ __forceinline__ uint32_t su32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -570,6 +571,15 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? PSE_TC_MINB64 : PSE_TC_MI
     }
   }
   __syncthreads();
+  // With self_reset the work counter is left zero for the next call: the
+  // last CTA to finish (every CTA has stopped claiming by then) zeroes it.
+  if (a.self_reset && tid == 0) {
+    __threadfence();
+    if (atomicAdd(a.counter + 1, 1) == (int)gridDim.x - 1) {
+      a.counter[0] = 0;
+      a.counter[1] = 0;
+    }
+  }
   // Error path only: before the CTA's shared memory is released, wait (bounded)
   // for the copies of the last tiles the producer issued.
   if (tid == kConsumers * 32 && *reinterpret_cast<volatile int*>(abort_flag)) {
@@ -647,8 +657,10 @@ int launch(const CUtensorMap& mk, const CUtensorMap& mv, const Args& a, cudaStre
   int dev = 0;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int grid = a.n_items < per_sm * sms ? a.n_items : per_sm * sms;
-  cudaError_t e = cudaMemsetAsync(a.counter, 0, sizeof(int), s);
-  if (e != cudaSuccess) return (int)e;
+  if (!a.self_reset) {
+    cudaError_t e = cudaMemsetAsync(a.counter, 0, sizeof(int), s);
+    if (e != cudaSuccess) return (int)e;
+  }
   kern<<<grid, kThreads, smem, s>>>(mk, mv, a);
   PSE_LAUNCH_CHECK();
   return PSE_OK;
@@ -671,7 +683,7 @@ bool tc_eligible(const pse_block_state& st, const pse_kv_layer& kv, int q_heads,
 int tc_attention(const pse_block_state& st, const pse_kv_layer& kv, const void* q, int64_t q_tok_stride, void* out,
                  int64_t out_tok_stride, const int32_t* slots, const int32_t* base_len, int rows, int width,
                  int q_heads, float scale, int split_tokens, int n_splits, void* ws, int* counter,
-                 const int32_t* row_order, cudaStream_t s) {
+                 const int32_t* row_order, bool self_reset, cudaStream_t s) {
   const int n_qrows = (q_heads / kv.kv_heads) * width;
   const int MT = n_qrows <= 16 ? 1 : 2;
   tc::Args a;
@@ -701,6 +713,7 @@ int tc_attention(const pse_block_state& st, const pse_kv_layer& kv, const void* 
   a.oob_row = st.num_blocks * kv.kv_heads * st.block_size;
   a.n_items = rows * kv.kv_heads * a.n_qtiles * n_splits;
   a.counter = counter;
+  a.self_reset = self_reset ? 1 : 0;
   a.row_order = row_order;
   if (!counter) return PSE_EINVAL;
   CUtensorMap mk, mv;

@@ -62,7 +62,8 @@ class Scratch:
 
     def ensure_ws(self, nbytes: int) -> None:
         if nbytes > self.ws.numel():
-            self.ws = torch.empty(max(nbytes, 2 * self.ws.numel()), dtype=torch.uint8, device=self.dm.device)
+            # zeroed: its first 256 bytes are the attention kernel's work counters (left zero by every call)
+            self.ws = torch.zeros(max(nbytes, 2 * self.ws.numel()), dtype=torch.uint8, device=self.dm.device)
             self.generation += 1
 
 

@@ -222,7 +222,7 @@ def test_paged_attention_matches_oracle(case, generic):
     base_d = torch.tensor(base, dtype=torch.int32, device="cuda")
     max_ctx = int(base.max()) + width
     ws_bytes = N.size_call("pse_paged_attention_workspace", rows, width, hq, hk, hd, max_ctx)
-    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device="cuda")
+    ws = torch.zeros(max(ws_bytes, 1), dtype=torch.uint8, device="cuda")
     N.call("pse_attention_force_generic", 1 if generic else 0)
     try:
         # rows handed out longest-first (any permutation gives the same result)

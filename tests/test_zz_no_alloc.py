@@ -57,7 +57,7 @@ def test_noalloc_matches_workspace_entry_point_twice(shape):
     N, c, slots, base_d, max_ctx = _setup(rows, width, hq, hk, hd, bs, max_len, dtype, seed=11)
     ws_bytes = N.size_call("pse_paged_attention_workspace", rows, width, hq, hk, hd, max_ctx)
     assert 0 < ws_bytes <= N.NOALLOC_SCRATCH_BYTES  # the shape really uses scratch
-    ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
+    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device="cuda")
     tol = F32_TOL if dtype == torch.float32 else BF16_TOL
     g = torch.Generator().manual_seed(5)
     st = N.stream_ptr()
