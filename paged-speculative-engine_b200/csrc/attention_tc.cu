@@ -270,6 +270,10 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? PSE_TC_MINB64 : PSE_TC_MI
       it = decode_item<kQRows>(a, e);
       cur = page_block(it, lane);
     }
+    // Everything above reads data the kernels before the K/V append wrote; the
+    // pages themselves may come from that append, which this launch is allowed
+    // to overlap (programmatic dependent launch): wait for it to finish here.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     bool run = true;
     while (run && e < a.n_items) {
       const int e_next = claim();
@@ -362,6 +366,8 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? PSE_TC_MINB64 : PSE_TC_MI
     }
   } else {
     // ------------------------------------------------------------ consumers
+    // Q (and the output rows) may belong to the kernel just before this launch
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const int mt = warp % MT;                       // this warp's 16-row m-tile
     const int tok_base = (warp / MT) * (16 * MT);   // this warp's token slice of a tile
     const int gid = lane >> 2, tid4 = lane & 3;
@@ -661,7 +667,21 @@ int launch(const CUtensorMap& mk, const CUtensorMap& mv, const Args& a, cudaStre
     cudaError_t e = cudaMemsetAsync(a.counter, 0, sizeof(int), s);
     if (e != cudaSuccess) return (int)e;
   }
-  kern<<<grid, kThreads, smem, s>>>(mk, mv, a);
+  // Programmatic dependent launch: the CTAs may start (and run their
+  // prologue) while the preceding kernel -- the K/V append, which signals
+  // early -- finishes; the producer waits for it before its first page copy.
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.gridDim = dim3((unsigned)grid, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t le = cudaLaunchKernelEx(&cfg, kern, mk, mv, a);
+  if (le != cudaSuccess) return (int)le;
   PSE_LAUNCH_CHECK();
   return PSE_OK;
 }

@@ -224,6 +224,9 @@ __global__ void append_kernel(pse_block_state st, T* __restrict__ k_pool, T* __r
                               int head_dim, const T* __restrict__ k_src, const T* __restrict__ v_src,
                               int64_t tok_stride, int64_t head_stride, const int32_t* __restrict__ slots,
                               const int32_t* __restrict__ base_len, int rows, int width) {
+  // the attention kernel that follows may launch now (it waits for this
+  // kernel's writes before it copies any page)
+  asm volatile("griddepcontrol.launch_dependents;");
   const int vecs = head_dim / VEC;
   const int per_tok = kv_heads * vecs;
   const int n_tok = rows * width;
