@@ -256,7 +256,8 @@ def test_philox_uniforms_bit_exact():
 
 
 @pytest.mark.parametrize("kern", [0, 1])
-@pytest.mark.parametrize("vocab,temp", [(257, 0.0), (257, 1.0), (256, 1.0), (32000, 0.7), (128256, 1.0)])
+@pytest.mark.parametrize("vocab,temp", [(257, 0.0), (257, 1.0), (256, 1.0), (32000, 0.7), (128256, 1.0),
+                                        (13, 1.0)])
 def test_sample_tokens_matches_oracle(vocab, temp, kern):
     N = _N()
     rows = 48
@@ -315,6 +316,8 @@ def _run_accept(N, tgt, drf, u, drafts, temp):
 @pytest.mark.parametrize("k,vocab,temp,agree", [
     (1, 64, 0.0, 0.0), (4, 256, 0.0, 0.0), (8, 1000, 0.0, 0.0),
     (3, 64, 1.0, 0.9), (5, 1000, 1.0, 0.97), (8, 4096, 0.8, 0.99), (2, 32000, 1.0, 0.0),
+    (1, 1000, 1.0, 0.9),     # one draft: no draft rows past the first
+    (3, 1001, 1.0, 0.95),    # vocab not a multiple of 4: the scalar kernel takes the row
 ])
 def test_accept_resample_matches_oracle(k, vocab, temp, agree):
     N = _N()
