@@ -261,11 +261,14 @@ def run_pse(args, rank, world, device):
     # the timed launches read blocks up to base + width: reserve them so every page read is a table entry
     N.call("pse_kv_reserve", tc.state, b.slots_t.data_ptr(), B, width, b.base[0].data_ptr(), st)
 
+    # rows handed out longest first, as the step's own attention calls do
+    order = torch.argsort(-base.to(torch.int64), stable=True).to(torch.int32)
+
     def attn_all_layers():
         for li in range(dm.n_layers):
             N.call("pse_paged_attention", tc.state, tc.layer(li), q.data_ptr(), q.stride(0), out.data_ptr(),
                    out.stride(0), b.slots_t.data_ptr(), base.data_ptr(), B, width, hq, 1.0 / math.sqrt(hd),
-                   max_ctx, None, ws.data_ptr(), ws.numel(), st)
+                   max_ctx, order.data_ptr(), ws.data_ptr(), ws.numel(), st)
 
     attn_all_layers()
     a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -361,6 +364,7 @@ ATTN_SHAPES = {
     "gpt2-verify": (256, 6, 12, 12, 64, 16, 134, 1030),
     "gpt2-verify5": (256, 5, 12, 12, 64, 16, 133, 1029),
     "gpt2-verify-bs64": (256, 6, 12, 12, 64, 64, 134, 1030),
+    "llama-verify": (512, 5, 32, 8, 64, 32, 133, 8197),
     "gpt2-draft-bs64": (256, 1, 6, 6, 64, 64, 129, 1025),
     "gpt2-draft": (256, 1, 6, 6, 64, 16, 129, 1025),
     "verify-5a": (1024, 8, 32, 8, 128, 16, 512, 32768),
