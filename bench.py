@@ -520,7 +520,11 @@ def micro_prefill(args, device):
             for r, p in zip(ids, prompts):
                 pse.prefill_request(d, t, dc, tc, r, p)
         else:
+            if mode == "batched_again":
+                torch.cuda.nvtx.range_push("prefill_batched")
             pse.prefill_requests(d, t, dc, tc, ids, prompts)
+            if mode == "batched_again":
+                torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize()
         res[mode] = (time.perf_counter() - t0, [dc.block_table(r) for r in ids] + [tc.block_table(r) for r in ids],
                      dc.allocator.free_list(), tc.allocator.free_list())

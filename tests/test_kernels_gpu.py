@@ -181,7 +181,9 @@ ATTN_CASES = [
     (2, 4, 32, 8, 64, 32, 3000, torch.bfloat16),   # long context: split-KV path
     (1, 1, 4, 4, 128, 16, 9000, torch.float32),    # single row, many splits
     (1, 37, 2, 2, 16, 4, 60, torch.float32),       # prefill-like width, several query tiles
-    (1, 40, 4, 4, 64, 16, 50, torch.bfloat16),     # prefill-like width on the tensor-core path
+    (1, 40, 4, 4, 64, 16, 50, torch.bfloat16),     # prefill-like width on the tensor-core path (64-row items)
+    (3, 23, 8, 2, 64, 32, 400, torch.bfloat16),    # GQA 4 x width 23 = 92 rows: two 64-row items, one padded
+    (2, 33, 4, 4, 64, 16, 3000, torch.bfloat16),   # 33 rows just past a 32-row item, long context, splits
     (4, 1, 6, 6, 64, 64, 500, torch.bfloat16),     # block 64
     (2, 5, 12, 12, 64, 32, 2100, torch.bfloat16),  # block 32, splits
     (5, 6, 16, 4, 128, 16, 300, torch.bfloat16),   # GQA 4 x width 6 = 24 rows (two m-tiles, one padded)
