@@ -568,7 +568,8 @@ def micro_scheduler(args, device):
         else:
             res = pse.run_continuous_speculative_batches(d, t, reqs, dc, tc, w.max_batch_size, k=w.k,
                                                          temperature=w.temperature,
-                                                         defer_bonus=not args.reference_structure)
+                                                         defer_bonus=not args.reference_structure,
+                                                         device_bookkeeping=not args.sched_host_loop)
         torch.cuda.synchronize()
         out[run] = (time.perf_counter() - t0, sum(len(r.output_ids) - len(p) for r, p in
                                                    zip(sorted(res, key=lambda r: int(r.request_id[len(run):])),
@@ -606,6 +607,7 @@ def micro_scheduler(args, device):
     print(json.dumps({"metric": "committed tokens/s (scheduler, whole workload)", "workload": w.name, "k": w.k,
                       "temperature": w.temperature, "requests": n, "max_batch_size": w.max_batch_size,
                       "step": "reference structure" if args.reference_structure else "deferred bonus",
+                      "bookkeeping": "host" if args.sched_host_loop else "device",
                       "mode": {"spec": "speculative, independent draft", "self": "speculative, draft = target",
                                "plain": "plain continuous batching, no speculation"}[args.sched_mode],
                       "generated_tokens": toks, "seconds": secs, "value": toks / secs, "unit": "tokens/s",
@@ -747,6 +749,9 @@ def main():
     ap.add_argument("--k", type=int, default=None, help="draft length (default: the workload's)")
     ap.add_argument("--sched-mode", default="spec", choices=["spec", "self", "plain"],
                     help="--micro scheduler: independent draft, draft = target, or no speculation")
+    ap.add_argument("--sched-host-loop", action="store_true",
+                    help="--micro scheduler: per-row bookkeeping on the host (the reference's loop) instead of "
+                         "on the device")
     ap.add_argument("--step-temperature", type=float, default=None,
                     help="sampling temperature of the step (default: the workload's)")
     ap.add_argument("--cpu-rows", type=int, default=4)

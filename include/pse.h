@@ -288,6 +288,24 @@ int pse_rope(void *qkv, int64_t ld, int32_t rows, int32_t width, int32_t q_heads
 int pse_scatter_rows(const float *src, int64_t ld_src, const int32_t *index, int32_t rows, int32_t n,
                      float *dst, int64_t ld_dst, int32_t n_dst_rows, void *stream);
 
+/* ------------------------------------------------------------------------ */
+/* Scheduler bookkeeping                                                    */
+/* ------------------------------------------------------------------------ */
+
+/* The per-row loop of run_continuous_speculative_batches after a step
+ * (engine/scheduler.py:107-126) on the device.  Row i of the step belongs to
+ * request ordinal ords[i]; its n_acc[i] + 1 accepted tokens (tokens[i *
+ * tok_stride + j], n_acc[i] + 1 <= tok_stride) extend the request's output at
+ * out[out_off[o] + generated[o] ...], keeping only the first max_new[o]
+ * (the reference trims the overshoot when the request finishes), and
+ * generated[o] grows by n_acc[i] + 1.  finished[0] receives the number of rows
+ * with generated >= max_new after the step and finished[1..] those rows'
+ * indices in row order (the order the reference reports and frees them).
+ * Every ords[i] must index out_off / max_new / generated; rows <= 2^30. */
+int pse_sched_commit(const int32_t *tokens, int32_t tok_stride, const int32_t *n_acc, const int32_t *ords,
+                     int32_t rows, const int64_t *out_off, const int32_t *max_new, int32_t *generated,
+                     int32_t *out, int32_t *finished, void *stream);
+
 /* Number of kernels the library registers (load check) and a version tag. */
 int pse_version(void);
 int pse_warmup(void);

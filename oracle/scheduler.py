@@ -99,3 +99,25 @@ def run_continuous_speculative_batches(draft_model, target_model, requests, draf
             target_cache.free_request(r)
         admit()
     return results
+
+
+def commit_rows(tokens, n_acc, ords, generated, max_new, outputs):
+    """engine/scheduler.py:107-126 on one step's row arrays: row i, owned by
+    request ordinal ``ords[i]``, extends ``outputs[o]`` with
+    ``tokens[i][:n_acc[i] + 1]`` and ``generated[o]`` by as many; rows whose
+    request reaches ``generated >= max_new`` finish and their overshoot is
+    trimmed from the end (:119-121).  Updates ``generated`` and ``outputs`` in
+    place and returns the finished rows in row order."""
+    fin = []
+    for i, o in enumerate(ords):
+        acc = list(tokens[i][: n_acc[i] + 1])
+        outputs[o].extend(acc)
+        generated[o] += len(acc)
+        if generated[o] >= max_new[o]:
+            fin.append(i)
+    for i in fin:
+        o = ords[i]
+        over = generated[o] - max_new[o]
+        if over > 0:
+            del outputs[o][len(outputs[o]) - over:]
+    return fin

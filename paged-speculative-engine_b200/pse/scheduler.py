@@ -2,19 +2,30 @@
 driving the device engine.
 
 The loop is the reference's: FIFO admission while fewer than
-``max_batch_size`` requests are active (each prefilled on its own), one
-batched speculative step over every active request, finish once a request has
-``generated >= max_new_tokens`` (overshoot trimmed), free both caches,
-backfill immediately.  Only the calls underneath run on the GPU.
+``max_batch_size`` requests are active, one batched speculative step over
+every active request, finish once a request has ``generated >=
+max_new_tokens`` (overshoot trimmed), free both caches, backfill immediately.
+Admitted requests are prefilled together (``prefill_requests``), leaving the
+caches as one-by-one prefills would.
+
+Unless a caller observes every step (``on_step``), the per-row bookkeeping
+also runs on the device: each step's accepted tokens are appended to a device
+output arena, counted and tested against ``max_new_tokens`` by a kernel inside
+the step's graph (``pse_sched_commit``), and the host reads back only the
+accepted counts and the finished rows.  Host work per step is then
+independent of the number of active rows except for a few array operations.
 """
 from __future__ import annotations
 
 import time
+from collections import deque
 from dataclasses import dataclass, field
+from numbers import Integral
 
+import numpy as np
 import torch
 
-from .speculative import batched_speculative_step, prefill_requests
+from .speculative import _fnv1a, batched_speculative_step, prefill_requests, runner_for, CommitArena
 
 
 @dataclass
@@ -49,11 +60,21 @@ class _Active:
 @torch.no_grad()
 def run_continuous_speculative_batches(draft_model, target_model, requests, draft_cache, target_cache,
                                        max_batch_size, k=4, temperature=0.0, generator=None, *,
-                                       uniform_fn=None, on_step=None, use_graph=None, defer_bonus=False):
+                                       uniform_fn=None, on_step=None, use_graph=None, defer_bonus=False,
+                                       device_bookkeeping=None):
     """engine/scheduler.py:61-128.  ``uniform_fn(request_ids, steps, n)`` (optional)
     supplies explicit uniforms per step; ``on_step(ids, result)`` observes steps;
     ``defer_bonus`` folds the target's bonus call into the next verify (see
-    ``batched_speculative_step``)."""
+    ``batched_speculative_step``); ``device_bookkeeping`` (default: whenever
+    ``on_step`` is not given) keeps the per-row token lists and finish tests
+    on the device, False runs them on the host as the reference does."""
+    requests = list(requests)
+    if device_bookkeeping and on_step is not None:
+        raise ValueError("on_step needs every step's result on the host: device_bookkeeping must be off")
+    if (device_bookkeeping is None or device_bookkeeping) and on_step is None and \
+            all(isinstance(q.max_new_tokens, Integral) and q.max_new_tokens >= 0 for q in requests):
+        return _run_device_bookkeeping(draft_model, target_model, requests, draft_cache, target_cache,
+                                       max_batch_size, k, temperature, generator, uniform_fn, use_graph, defer_bonus)
     queue = list(requests)
     active: dict[str, _Active] = {}
     steps_taken: dict[str, int] = {}
@@ -111,4 +132,91 @@ def run_continuous_speculative_batches(draft_model, target_model, requests, draf
             draft_cache.free_request(r)
             target_cache.free_request(r)
         admit()
+    return results
+
+
+def _run_device_bookkeeping(draft_model, target_model, requests, draft_cache, target_cache, max_batch_size, k,
+                            temperature, generator, uniform_fn, use_graph, defer_bonus) -> list:
+    """The loop above with engine/scheduler.py:107-126 on the device: request
+    ordinal o (its index in ``requests``) owns ``max_new_tokens`` entries of the
+    runner's commit arena; the host keeps the active rows as arrays (slots in
+    both caches, ordinals) in ``active`` order, which is the reference's dict
+    order (finished rows leave, admitted ones join at the end)."""
+    runner = runner_for(draft_model, target_model, draft_cache, target_cache, k)
+    n = len(requests)
+    max_new = np.array([q.max_new_tokens for q in requests], dtype=np.int64)
+    if runner.commit is None:
+        runner.commit = CommitArena(runner.device)
+    arena = runner.commit
+    arena.reset(max_new)
+    T = float(temperature)
+    philox = T > 0 and uniform_fn is None and generator is None
+    key_by_ord = np.zeros(n, dtype=np.int32)
+    steps_by_ord = np.zeros(n, dtype=np.int32)  # the runner's per-request step count (Philox key)
+    taken_by_ord = np.zeros(n, dtype=np.int32)  # steps taken in this run (uniform_fn's argument)
+    queue = deque(range(n))
+    ids: list = []
+    ords = np.zeros(0, dtype=np.int32)
+    sd = np.zeros(0, dtype=np.int32)
+    st = np.zeros(0, dtype=np.int32)
+    finished_at: list = []  # (ordinal, completion time) in completion order
+    t_start = time.perf_counter()
+
+    def admit() -> None:
+        nonlocal ords, sd, st
+        take = []
+        while queue and len(ids) + len(take) < max_batch_size:
+            take.append(queue.popleft())
+        if not take:
+            return
+        new_ids = [requests[o].request_id for o in take]
+        prefill_requests(draft_model, target_model, draft_cache, target_cache, new_ids,
+                         [requests[o].prompt_ids for o in take])
+        ids.extend(new_ids)
+        t_ords = np.array(take, dtype=np.int32)
+        ords = np.concatenate([ords, t_ords])
+        sd = np.concatenate([sd, draft_cache.slots_np(new_ids)])
+        st = np.concatenate([st, target_cache.slots_np(new_ids)])
+        steps_by_ord[t_ords] = [runner.request_steps.get(r, 0) for r in new_ids]
+        if philox:
+            key_by_ord[t_ords] = np.array([_fnv1a(r) for r in new_ids], dtype=np.uint32).view(np.int32)
+
+    try:
+        admit()
+        while ids or queue:
+            if not ids:
+                admit()
+                continue
+            u = None
+            if uniform_fn is not None and T > 0:
+                u = uniform_fn(list(ids), taken_by_ord[ords].tolist(), 2 * k + 1)
+            _, fin = runner.step_rows(ids, sd, st, ords, arena, T, generator, u, use_graph, defer_bonus,
+                                      key_by_ord[ords] if philox else None, steps_by_ord[ords] if philox else None)
+            steps_by_ord[ords] += 1
+            taken_by_ord[ords] += 1
+            if len(fin):
+                now = time.perf_counter()
+                fin_ids = [ids[i] for i in fin.tolist()]
+                for o, r in zip(ords[fin].tolist(), fin_ids):
+                    finished_at.append((o, now))
+                    runner.request_steps[r] = int(steps_by_ord[o])
+                draft_cache.free_requests(fin_ids)
+                target_cache.free_requests(fin_ids)
+                keep = np.ones(len(ids), dtype=bool)
+                keep[fin] = False
+                ids[:] = [r for r, kp in zip(ids, keep.tolist()) if kp]
+                ords, sd, st = ords[keep], sd[keep], st[keep]
+            admit()
+    finally:
+        # requests still active (an exception ended the run) keep their step counts
+        for r, o in zip(ids, ords.tolist()):
+            runner.request_steps[r] = int(steps_by_ord[o])
+    out = arena.out[: int(max_new.sum())].cpu().numpy() if n else np.zeros(0, dtype=np.int32)
+    off = np.zeros(n + 1, dtype=np.int64)
+    np.cumsum(max_new, out=off[1:])
+    results = []
+    for o, t_done in finished_at:
+        q = requests[o]
+        results.append(RequestResult(q.request_id, list(q.prompt_ids) + out[off[o]:off[o + 1]].tolist(),
+                                     t_start, t_done))
     return results

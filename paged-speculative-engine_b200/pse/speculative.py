@@ -235,9 +235,11 @@ class _StepBuffers:
         self.even = torch.arange(0, 2 * B, 2, dtype=torch.int64, device=device)
         self.hsel = torch.empty(B, d_draft, dtype=draft_dtype, device=device)
         # the step's per-row host inputs, copied to the device in one transfer:
-        # [slots_d | slots_t | req_key | steps | order_d | order_t]
-        self.dev_in = torch.zeros(6 * B, **i32)
-        self.slots_d, self.slots_t, self.req_key, self.steps, self.order_d, self.order_t = self.dev_in.view(6, B)
+        # [slots_d | slots_t | req_key | steps | order_d | order_t | ords]
+        # (ords: each row's request ordinal in the scheduler's output arena)
+        self.dev_in = torch.zeros(7 * B, **i32)
+        (self.slots_d, self.slots_t, self.req_key, self.steps, self.order_d, self.order_t,
+         self.ords) = self.dev_in.view(7, B)
         self.base = torch.empty(k + 4, B, **i32)  # per-call base lengths (rounds, verify, bonus calls)
         self.round_ids = torch.empty(B, **i32)
         self.drafts = torch.empty(B, k, **i32)
@@ -251,12 +253,50 @@ class _StepBuffers:
         self.vids = None    # deferred-bonus mode: verify ids [B, k+1] and logits [B*(k+1), V]
         self.vlog2 = None
         self.nacc1 = torch.empty(B, **i32)
-        n_pack = B * (k + 1) + B + 2
+        # the step's result, copied to pinned host memory in one transfer:
+        # [tokens B*(k+1) | n_acc B | status_d | status_t | finished count | finished rows B]
+        # (the last two only when the scheduler's commit runs in the step)
+        n_pack = B * (k + 1) + B + 3 + B
         self.pack = torch.empty(n_pack, **i32)
         self.host_pack = torch.empty(n_pack, dtype=torch.int32, pin_memory=True)
-        self.host_in = torch.empty(6 * B, dtype=torch.int32, pin_memory=True)
+        self.host_in = torch.empty(7 * B, dtype=torch.int32, pin_memory=True)
         self.host_pack_np = self.host_pack.numpy()  # same pinned memory
         self.host_in_np = self.host_in.numpy()
+
+
+class CommitArena:
+    """Device output arena of a scheduler run (engine/scheduler.py:107-126
+    kept on the device): request ordinal o owns ``max_new[o]`` int32 entries at
+    ``off[o]``; ``generated[o]`` counts its accepted tokens, overshoot
+    included.  Buffers are reused across runs while they are large enough
+    (``generation`` changes when they move, so captured steps are rebuilt)."""
+
+    def __init__(self, device):
+        self.device = device
+        self.generation = 0
+        self.cap_req = 0
+        self.cap_out = 0
+        self.off = self.max_new = self.generated = self.out = None
+
+    def reset(self, max_new: np.ndarray) -> None:
+        n = int(max_new.shape[0])
+        off = np.zeros(n, dtype=np.int64)
+        if n > 1:
+            np.cumsum(max_new[:-1], out=off[1:])
+        total = int(max_new.sum()) if n else 0
+        if n > self.cap_req or total > self.cap_out or self.off is None:
+            self.cap_req = max(n, 2 * self.cap_req, 64)
+            self.cap_out = max(total, 2 * self.cap_out, 1024)
+            i32 = dict(dtype=torch.int32, device=self.device)
+            self.off = torch.zeros(self.cap_req, dtype=torch.int64, device=self.device)
+            self.max_new = torch.zeros(self.cap_req, **i32)
+            self.generated = torch.zeros(self.cap_req, **i32)
+            self.out = torch.zeros(self.cap_out, **i32)
+            self.generation += 1
+        if n:
+            self.off[:n].copy_(torch.from_numpy(off))
+            self.max_new[:n].copy_(torch.from_numpy(max_new.astype(np.int32)))
+        self.generated.zero_()
 
 
 class StepRunner:
@@ -277,6 +317,7 @@ class StepRunner:
         self.sc_d = Scratch(dm_d)
         self.sc_t = Scratch(dm_t)
         self.tpending = None  # per target slot: token not yet appended (deferred-bonus mode)
+        self.commit: CommitArena | None = None  # the scheduler's device output arena
         self._slots_key, self._slots_ids, self._slots_np = None, None, None
 
     # ---------------------------------------------------------------- device program
@@ -287,7 +328,7 @@ class StepRunner:
         return bound
 
     def _program(self, b: _StepBuffers, T: float, philox: bool, max_ctx_d: int, max_ctx_t: int,
-                 defer: bool = False) -> None:
+                 defer: bool = False, commit: CommitArena | None = None) -> None:
         k, V, B = self.k, self.V, b.B
         st = N.stream_ptr()
         dnext = next_logits_buffer(self.dcache, V)
@@ -335,6 +376,12 @@ class StepRunner:
                dnext.data_ptr(), V, b.slots_d.data_ptr(), b.dlog.data_ptr(), V, B * V,
                b.drafts.data_ptr(), b.u.data_ptr(), nu, B, k, V, float(T), b.tokens.data_ptr(),
                b.n_acc.data_ptr(), b.final.data_ptr(), st)
+        if commit is not None:
+            # the scheduler's per-row bookkeeping (engine/scheduler.py:107-126)
+            nt = B * (k + 1)
+            N.call("pse_sched_commit", b.tokens.data_ptr(), k + 1, b.n_acc.data_ptr(), b.ords.data_ptr(), B,
+                   commit.off.data_ptr(), commit.max_new.data_ptr(), commit.generated.data_ptr(),
+                   commit.out.data_ptr(), b.pack.data_ptr() + 4 * (nt + B + 2), st)
         # commit (engine/speculative.py:159-164)
         N.call("pse_kv_truncate", self.dcache.state, b.slots_d.data_ptr(), B, None, b.base[0].data_ptr(),
                b.n_acc.data_ptr(), st)
@@ -415,8 +462,6 @@ class StepRunner:
         if len(set(request_ids)) != B:
             raise ValueError("request_ids must be unique")
         dc, tc = self.dcache, self.tcache
-        if not defer_bonus and any(tc.slot(r) in tc.deferred_slots for r in request_ids):
-            raise ValueError("request is in the deferred-bonus state: keep stepping it with defer_bonus=True")
         # slot arrays: reused while the request list and the slot assignment are unchanged
         skey = (dc.slot_version, tc.slot_version)
         if self._slots_key == skey and self._slots_ids == request_ids:
@@ -424,6 +469,68 @@ class StepRunner:
         else:
             sd_np, st_np = dc.slots_np(request_ids), tc.slots_np(request_ids)
             self._slots_key, self._slots_ids, self._slots_np = skey, list(request_ids), (sd_np, st_np)
+        dviews = next_logits_views(dc, V)
+        tviews = next_logits_views(tc, V)
+        sd = sd_np.tolist()
+        stt = st_np.tolist()
+        if not defer_bonus and tc.deferred_slots and not tc.deferred_slots.isdisjoint(stt):
+            raise ValueError("request is in the deferred-bonus state: keep stepping it with defer_bonus=True")
+        for r, s in zip(request_ids, sd):
+            t = draft_next_logits[r]
+            v = dviews[s]
+            if t is not v and t.data_ptr() != v.data_ptr():
+                v.copy_(t.reshape(-1), non_blocking=True)
+        if not defer_bonus:
+            for r, s in zip(request_ids, stt):
+                t = target_next_logits[r]
+                v = tviews[s]
+                if t is not v and t.data_ptr() != v.data_ptr():
+                    v.copy_(t.reshape(-1), non_blocking=True)
+        steps = self.request_steps
+        key_np = steps_np = None
+        if float(temperature) > 0 and uniforms is None and generator is None:
+            key_np = np.array([_fnv1a(r) for r in request_ids], dtype=np.uint32).view(np.int32)
+            steps_np = np.fromiter((steps.get(r, 0) for r in request_ids), np.int32, B)
+        b, nacc_np = self._run(request_ids, sd_np, st_np, temperature, generator, uniforms, use_graph, defer_bonus,
+                               key_np, steps_np)
+        hpn = b.host_pack_np
+        toks = hpn[:B * (k + 1)].reshape(B, k + 1).tolist()
+        nacc = nacc_np.tolist()
+        accepted = {r: toks[i][: nacc[i] + 1] for i, r in enumerate(request_ids)}
+        n_acc = dict(zip(request_ids, nacc))
+        dn = {r: dviews[s] for r, s in zip(request_ids, sd)}
+        tn = dict.fromkeys(request_ids) if defer_bonus else {r: tviews[s] for r, s in zip(request_ids, stt)}
+        for r in request_ids:
+            steps[r] = steps.get(r, 0) + 1
+        return BatchStepResult(accepted, n_acc, dn, tn)
+
+    def step_rows(self, request_ids, sd_np, st_np, ords_np, commit: CommitArena, temperature, generator=None,
+                  uniforms=None, use_graph=None, defer_bonus: bool = False, req_key_np=None, steps_np=None):
+        """The scheduler's form of ``step``: rows come as slot arrays, each
+        request's next logits are already in its slot's row (as prefill and
+        every step leave them), the accepted tokens stay on the device in
+        ``commit`` (row i extends request ordinal ``ords_np[i]``) and nothing
+        per row is built on the host.  ``req_key_np`` / ``steps_np`` key the
+        device Philox stream when T > 0 and neither ``uniforms`` nor
+        ``generator`` is given.  Returns (n_acc [B] int64, finished row
+        indices in row order)."""
+        B = len(request_ids)
+        b, nacc_np = self._run(request_ids, sd_np, st_np, temperature, generator, uniforms, use_graph, defer_bonus,
+                               req_key_np, steps_np, ords_np, commit)
+        at = B * (self.k + 1) + B + 2
+        nfin = int(b.host_pack_np[at])
+        return nacc_np, b.host_pack_np[at + 1:at + 1 + nfin].copy()
+
+    def _run(self, request_ids, sd_np, st_np, temperature, generator, uniforms, use_graph, defer_bonus,
+             req_key_np=None, steps_np=None, ords_np=None, commit: CommitArena | None = None):
+        """Launch one step (replaying its graph when captured), copy its result
+        to the host, raise a latched device error, update the host length
+        mirrors.  Returns the step's buffers and n_acc as int64."""
+        k, V = self.k, self.V
+        B = len(request_ids)
+        dc, tc = self.dcache, self.tcache
+        if not defer_bonus and tc.deferred_slots and not tc.deferred_slots.isdisjoint(st_np.tolist()):
+            raise ValueError("request is in the deferred-bonus state: keep stepping it with defer_bonus=True")
         len_d = dc.lengths_np(sd_np)
         len_t = tc.lengths_np(st_np)
         for dm, c, lens in ((self.dm_d, dc, len_d), (self.dm_t, tc, len_t)):
@@ -437,26 +544,11 @@ class StepRunner:
         if defer_bonus and b.vids is None:
             b.vids = torch.empty(B, k + 1, dtype=torch.int32, device=self.device)
             b.vlog2 = torch.empty(B * (k + 1), V, dtype=torch.float32, device=self.device)
-        dviews = next_logits_views(dc, V)
-        tviews = next_logits_views(tc, V)
-        sd = sd_np.tolist()
-        stt = st_np.tolist()
         if defer_bonus:
             n_before = len(tc.deferred_slots)
-            self._enter_deferred(request_ids, stt)
+            self._enter_deferred(request_ids, st_np.tolist())
             if len(tc.deferred_slots) != n_before:  # rows entered the deferred state: lengths moved
                 len_t = tc.lengths_np(st_np)
-        for r, s in zip(request_ids, sd):
-            t = draft_next_logits[r]
-            v = dviews[s]
-            if t is not v and t.data_ptr() != v.data_ptr():
-                v.copy_(t.reshape(-1), non_blocking=True)
-        if not defer_bonus:
-            for r, s in zip(request_ids, stt):
-                t = target_next_logits[r]
-                v = tviews[s]
-                if t is not v and t.data_ptr() != v.data_ptr():
-                    v.copy_(t.reshape(-1), non_blocking=True)
         T = float(temperature)
         philox = False
         hin = b.host_in
@@ -472,11 +564,13 @@ class StepRunner:
                 b.u.copy_(torch.rand(B, 2 * k + 1, generator=generator, dtype=torch.float64), non_blocking=True)
             else:
                 philox = True
-                hnp[2 * B:3 * B] = np.array([_fnv1a(r) for r in request_ids], dtype=np.uint32).view(np.int32)
-                hnp[3 * B:4 * B] = np.fromiter((self.request_steps.get(r, 0) for r in request_ids), np.int32, B)
+                hnp[2 * B:3 * B] = req_key_np
+                hnp[3 * B:4 * B] = steps_np
         # longest rows first: the attention kernels hand out work in this order
         hnp[4 * B:5 * B] = np.argsort(-len_d, kind="stable")
         hnp[5 * B:6 * B] = np.argsort(-len_t, kind="stable")
+        if ords_np is not None:
+            hnp[6 * B:7 * B] = ords_np
         b.dev_in.copy_(hin, non_blocking=True)
 
         graphs = self.use_graphs if use_graph is None else use_graph
@@ -494,48 +588,42 @@ class StepRunner:
                 N.size_call("pse_paged_attention_workspace", B, k, dmt.q_heads, dmt.kv_heads, dmt.head_dim, mct),
                 N.size_call("pse_paged_attention_workspace", B, 1, dmt.q_heads, dmt.kv_heads, dmt.head_dim, mct)))
         key = (B, T, philox, defer_bonus, dc.generation, tc.generation, self.sc_d.generation, self.sc_t.generation,
-               None if self.tpending is None else self.tpending.data_ptr())
+               None if self.tpending is None else self.tpending.data_ptr(),
+               None if commit is None else (id(commit), commit.generation))
         if graphs and key in self.graphs:
             self.graphs[key].replay()
         elif graphs and key in self.warm:
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g):
-                self._program(b, T, philox, mcd, mct, defer_bonus)
+                self._program(b, T, philox, mcd, mct, defer_bonus, commit)
             self.graphs[key] = g
             g.replay()
         else:
             if graphs:
                 # eager steps use the same context bound so the captured
                 # program's buffers (split-KV workspace) are already sized
-                self._program(b, T, philox, mcd, mct, defer_bonus)
+                self._program(b, T, philox, mcd, mct, defer_bonus, commit)
                 self.warm.add(key)
             else:
-                ld = max(dc.length(r) for r in request_ids) + k + 1
-                lt = max(tc.length(r) for r in request_ids) + k + 1
-                self._program(b, T, philox, ld, lt + 1, defer_bonus)
-        hp = b.host_pack
-        hp.copy_(b.pack, non_blocking=True)
-        torch.cuda.current_stream().synchronize()
+                ld = int(len_d.max()) + k + 1
+                lt = int(len_t.max()) + k + 1
+                self._program(b, T, philox, ld, lt + 1, defer_bonus, commit)
         nt = B * (k + 1)
-        status_d, status_t = int(hp[nt + B]), int(hp[nt + B + 1])
+        if commit is None:
+            b.host_pack.copy_(b.pack, non_blocking=True)
+        else:  # the tokens stay on the device
+            b.host_pack[nt:].copy_(b.pack[nt:], non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        hpn = b.host_pack_np
+        status_d, status_t = int(hpn[nt + B]), int(hpn[nt + B + 1])
         if status_d or status_t:
             for c, s in ((dc, status_d), (tc, status_t)):
                 if s:
                     c.check_status("speculative step")
-        hpn = b.host_pack_np
-        toks = hpn[:nt].reshape(B, k + 1).tolist()
         nacc_np = hpn[nt:nt + B].astype(np.int64)
-        nacc = nacc_np.tolist()
-        accepted = {r: toks[i][: nacc[i] + 1] for i, r in enumerate(request_ids)}
-        n_acc = dict(zip(request_ids, nacc))
-        dn = {r: dviews[s] for r, s in zip(request_ids, sd)}
-        tn = dict.fromkeys(request_ids) if defer_bonus else {r: tviews[s] for r, s in zip(request_ids, stt)}
-        steps = self.request_steps
-        for r in request_ids:
-            steps[r] = steps.get(r, 0) + 1
         dc.note_lengths_slots(sd_np, len_d + nacc_np + 1)
         tc.note_lengths_slots(st_np, len_t + nacc_np + 1)
-        return BatchStepResult(accepted, n_acc, dn, tn)
+        return b, nacc_np
 
 
 def runner_for(draft_model, target_model, draft_cache, target_cache, k: int) -> StepRunner:

@@ -195,3 +195,28 @@ def test_first_token_distributions_match_reference():
         with torch.no_grad():
             probs = torch.softmax(target(torch.tensor([case["prompt"]]))[0][0, -1], -1)
         assert torch.allclose(probs, torch.tensor(case["probs"]), atol=1e-6)
+
+
+def test_commit_rows_replays_golden_trace_to_golden_outputs():
+    """The scheduler's per-row bookkeeping restated on row arrays (the check of
+    pse_sched_commit) turns the reference's per-step accepted tokens into the
+    reference's outputs, finishing each request at the step the trace drops it."""
+    from oracle.scheduler import commit_rows
+    g = _load("tiny_greedy.json")
+    tiny = wl.WORKLOADS["tiny"]
+    ids = g["request_ids"]
+    ordinal = {r: i for i, r in enumerate(ids)}
+    outputs = [[] for _ in ids]
+    generated = [0] * len(ids)
+    max_new = [tiny.max_new_tokens] * len(ids)
+    steps = g["steps"]
+    for n, step in enumerate(steps):
+        rows = step["ids"]
+        width = max(len(v) for v in step["accepted"].values())
+        tokens = [step["accepted"][r] + [-1] * (width - len(step["accepted"][r])) for r in rows]
+        n_acc = [len(step["accepted"][r]) - 1 for r in rows]
+        fin = commit_rows(tokens, n_acc, [ordinal[r] for r in rows], generated, max_new, outputs)
+        still = set(steps[n + 1]["ids"]) if n + 1 < len(steps) else set()
+        assert [rows[i] for i in fin] == [r for r in rows if r not in still]
+    for r, p in zip(ids, g["prompts"]):
+        assert p + outputs[ordinal[r]] == g["outputs"][r]

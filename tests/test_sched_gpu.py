@@ -1,0 +1,160 @@
+"""Scheduler bookkeeping on the device (engine/scheduler.py:107-126):
+``pse_sched_commit`` against the oracle's ``commit_rows`` on random step
+sequences (bit-exact: arena contents, generated counts, finished rows in row
+order), and the scheduler's device-bookkeeping loop against its per-row host
+loop and the reference's golden outputs.  GPU only."""
+from __future__ import annotations
+
+import json
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import GOLDEN
+from oracle.model import ModelConfig, TinyGPT
+from oracle.scheduler import commit_rows
+
+pytestmark = pytest.mark.gpu
+
+
+def _commit_case(n_req, max_rows, k, seed, steps=60):
+    import pse._native as N
+    rng = np.random.default_rng(seed)
+    dev = torch.device("cuda")
+    max_new = rng.integers(0, 40, size=n_req)
+    max_new[rng.random(n_req) < 0.05] = 0
+    off = np.zeros(n_req, dtype=np.int64)
+    np.cumsum(max_new[:-1], out=off[1:])
+    d_off = torch.from_numpy(off).to(dev)
+    d_max = torch.from_numpy(max_new.astype(np.int32)).to(dev)
+    d_gen = torch.zeros(n_req, dtype=torch.int32, device=dev)
+    d_out = torch.full((max(1, int(max_new.sum())),), -7, dtype=torch.int32, device=dev)
+    generated = [0] * n_req
+    outputs = [[] for _ in range(n_req)]
+    done = np.zeros(n_req, dtype=bool)
+    st = N.stream_ptr()
+    for _ in range(steps):
+        live = np.flatnonzero(~done)
+        if len(live) == 0:
+            break
+        rows = int(min(len(live), rng.integers(1, max_rows + 1)))
+        ords = rng.permutation(live)[:rows].astype(np.int32)
+        tokens = rng.integers(0, 50000, size=(rows, k + 1)).astype(np.int32)
+        n_acc = rng.integers(0, k + 1, size=rows).astype(np.int32)
+        d_tok = torch.from_numpy(tokens).to(dev)
+        d_nacc = torch.from_numpy(n_acc).to(dev)
+        d_ords = torch.from_numpy(ords).to(dev)
+        d_fin = torch.full((rows + 1,), -1, dtype=torch.int32, device=dev)
+        N.call("pse_sched_commit", d_tok.data_ptr(), k + 1, d_nacc.data_ptr(), d_ords.data_ptr(), rows,
+               d_off.data_ptr(), d_max.data_ptr(), d_gen.data_ptr(), d_out.data_ptr(), d_fin.data_ptr(), st)
+        fin = commit_rows(tokens.tolist(), n_acc.tolist(), ords.tolist(), generated, max_new.tolist(), outputs)
+        got = d_fin.cpu().numpy()
+        assert got[0] == len(fin)
+        assert got[1:1 + len(fin)].tolist() == fin
+        done[ords[fin]] = True
+    assert d_gen.cpu().tolist() == generated
+    out = d_out.cpu().numpy()
+    for o in range(n_req):
+        m = min(generated[o], int(max_new[o]))
+        assert out[off[o]:off[o] + m].tolist() == outputs[o][:m], o
+
+
+@pytest.mark.parametrize("n_req,max_rows,k,seed", [
+    (40, 16, 4, 0),       # small batches, many steps per request
+    (3000, 2500, 5, 1),   # more rows than one CTA pass (the finished list carries across passes)
+    (1100, 1024, 1, 2),   # exactly one full pass, k = 1
+    (200, 200, 8, 3),
+])
+def test_sched_commit_matches_oracle(n_req, max_rows, k, seed):
+    _commit_case(n_req, max_rows, k, seed)
+
+
+def test_sched_commit_zero_rows_and_bad_args():
+    import pse._native as N
+    dev = torch.device("cuda")
+    fin = torch.full((1,), 5, dtype=torch.int32, device=dev)
+    N.call("pse_sched_commit", None, 1, None, None, 0, None, None, None, None, fin.data_ptr(), N.stream_ptr())
+    assert fin.item() == 0
+    lib = N.load()
+    assert lib.pse_sched_commit(None, 0, None, None, 0, None, None, None, None, fin.data_ptr(), None) != 0
+    assert lib.pse_sched_commit(None, 2, None, None, 3, None, None, None, None, fin.data_ptr(), None) != 0
+
+
+def _pair(vocab=64, seed=0):
+    torch.manual_seed(seed)
+    dcfg = ModelConfig(vocab_size=vocab, d_model=32, n_layers=2, n_heads=2, d_ff=64, max_seq_len=256)
+    tcfg = ModelConfig(vocab_size=vocab, d_model=64, n_layers=3, n_heads=4, d_ff=128, max_seq_len=256)
+    return TinyGPT(dcfg).eval(), TinyGPT(tcfg).eval()
+
+
+def _run(d, t, reqs, mb, k, T, *, device_bookkeeping, **kw):
+    import pse
+    dc = pse.PagedKVCache(2, 2, 16, 8, 600)
+    tc = pse.PagedKVCache(3, 4, 16, 8, 600)
+    res = pse.run_continuous_speculative_batches(d, t, reqs, dc, tc, mb, k=k, temperature=T,
+                                                 device_bookkeeping=device_bookkeeping, **kw)
+    return ([(r.request_id, r.output_ids) for r in res], dc.allocator.free_list(), tc.allocator.free_list())
+
+
+@pytest.mark.parametrize("T,defer,graphs,source", [
+    (0.0, False, True, None), (0.0, True, True, None), (0.0, False, False, None),
+    (1.0, False, True, "philox"), (1.0, True, True, "philox"), (1.0, False, True, "uniform_fn"),
+    (0.8, True, False, "generator"),
+])
+def test_device_bookkeeping_equals_host_loop(T, defer, graphs, source):
+    """Same requests, same order of results, same tokens and free lists whether
+    the per-row bookkeeping runs on the device or on the host."""
+    import pse
+    from oracle.philox import request_key, step_uniforms
+    d, t = _pair()
+    rng = np.random.default_rng(5)
+    k = 3
+    prompts = [rng.integers(0, 64, size=int(rng.integers(3, 20))).tolist() for _ in range(11)]
+    max_new = [int(x) for x in rng.integers(0, 30, size=11)]
+    outs = []
+    for dev_bk in (True, False):
+        reqs = [pse.Request(f"q{i}", p, m) for i, (p, m) in enumerate(zip(prompts, max_new))]
+        kw = dict(use_graph=graphs, defer_bonus=defer)
+        if source == "uniform_fn":
+            kw["uniform_fn"] = lambda ids, steps, n: step_uniforms(77, [request_key(r) for r in ids], steps, n)
+        if source == "generator":
+            kw["generator"] = torch.Generator().manual_seed(3)
+        outs.append(_run(d, t, reqs, 4, k, T, device_bookkeeping=dev_bk, **kw))
+    assert outs[0] == outs[1]
+    assert sorted(r for r, _ in outs[0][0]) == sorted(f"q{i}" for i in range(11))
+
+
+def test_device_bookkeeping_reproduces_golden_outputs():
+    """The reference's tiny workload (golden outputs and final free lists)
+    through the default scheduler loop, which keeps the bookkeeping on the device."""
+    import pse
+    from pse import workload as wl
+    with open(os.path.join(GOLDEN, "tiny_greedy.json")) as f:
+        g = json.load(f)
+    tiny = wl.WORKLOADS["tiny"]
+    torch.manual_seed(0)
+    d = TinyGPT(ModelConfig(vocab_size=tiny.pair.vocab, **tiny.pair.draft)).eval()
+    t = TinyGPT(ModelConfig(vocab_size=tiny.pair.vocab, **tiny.pair.target)).eval()
+    pd, pt = tiny.pair.draft, tiny.pair.target
+    for defer in (False, True):
+        dc = pse.PagedKVCache(pd["n_layers"], pd["n_heads"], pd["d_model"] // pd["n_heads"], tiny.block_size,
+                              g["num_blocks"])
+        tc = pse.PagedKVCache(pt["n_layers"], pt["n_heads"], pt["d_model"] // pt["n_heads"], tiny.block_size,
+                              g["num_blocks"])
+        reqs = [pse.Request(r, p, tiny.max_new_tokens) for r, p in zip(g["request_ids"], g["prompts"])]
+        res = pse.run_continuous_speculative_batches(d, t, reqs, dc, tc, tiny.max_batch_size, k=tiny.k,
+                                                     temperature=0.0, defer_bonus=defer)
+        assert {r.request_id: r.output_ids for r in res} == g["outputs"]
+        if not defer:
+            assert dc.allocator.free_list() == g["final_free"]["draft"]
+            assert tc.allocator.free_list() == g["final_free"]["target"]
+        assert dc.allocator.num_free == g["num_blocks"] and tc.allocator.num_free == g["num_blocks"]
+
+
+def test_on_step_with_device_bookkeeping_is_refused():
+    import pse
+    d, t = _pair()
+    with pytest.raises(ValueError):
+        _run(d, t, [pse.Request("a", [1, 2], 3)], 2, 2, 0.0, device_bookkeeping=True, on_step=lambda i, r: None)
