@@ -46,6 +46,17 @@ def _peaks():
         return 6650.0, "fallback"
 
 
+def _tensor_peak():
+    """Dense bf16 tensor-core peak in TFLOP/s: the measured burst figure, else
+    the fallback measured earlier on this hardware."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["bf16_tflops"]), "measured"
+    except Exception:
+        return 1590.0, "fallback"
+
+
 class ClockSampler:
     """nvidia-smi clock / throttle sampling during the timed region."""
 
@@ -368,6 +379,10 @@ ATTN_SHAPES = {
     "gpt2-draft-bs64": (256, 1, 6, 6, 64, 64, 129, 1025),
     "gpt2-draft": (256, 1, 6, 6, 64, 16, 129, 1025),
     "verify-5a": (1024, 8, 32, 8, 128, 16, 512, 32768),
+    # prompt prefill (width = context: each prompt attends to itself, causal)
+    "gpt2-prefill": (32, 512, 12, 12, 64, 16, 512, 512),
+    "llama-prefill": (8, 2048, 32, 8, 64, 32, 2048, 2048),
+    "prefill-hd128": (8, 2048, 32, 8, 128, 16, 2048, 2048),
 }
 
 
@@ -409,6 +424,10 @@ def micro_attention(args, device):
     ws = torch.zeros(wsb, dtype=torch.uint8, device=device)
     st = N.stream_ptr()
 
+    # the rows' lengths: everything up to and including the last query
+    c._blocks.seq_len.copy_(torch.from_numpy(ctx.astype(np.int32)))
+    N.call("pse_attention_prefill_select", 1 if args.prefill_kernel == "off" else 0)
+
     def launch():
         N.call("pse_paged_attention", c.state, c.layer(0), q.data_ptr(), q.stride(0), out.data_ptr(), out.stride(0),
                slots.data_ptr(), base.data_ptr(), rows, width, hq, 1.0 / math.sqrt(hd), max_ctx, None, ws.data_ptr(),
@@ -435,8 +454,14 @@ def micro_attention(args, device):
     alg = kv_bytes + 2 * q.numel() * 2 + rows * 4 * int(need.max())
     peak, kind = _peaks()
     gbs = alg / (ms / 1000) / 1e9
+    # causal QK^T and PV flops: query w of row i sees base_i + w + 1 keys
+    keys = int(sum(int(b) * width + width * (width + 1) // 2 for b in (ctx - width)))
+    tflops = 4 * hq * hd * keys / (ms / 1000) / 1e12
+    N.call("pse_attention_prefill_select", 0)
     print(json.dumps({"metric": "paged attention HBM GB/s", "shape": args.attn_shape, "value": gbs, "unit": "GB/s",
                       "frac_of_peak": gbs / peak, "peak": peak, "peak_kind": kind, "us_per_launch": ms * 1000,
+                      "tflops": tflops, "tflops_frac_of_bf16_peak": tflops / _tensor_peak()[0],
+                      "prefill_kernel": args.prefill_kernel,
                       "algorithmic_bytes": alg, "rows": rows, "width": width, "q_heads": hq, "kv_heads": hk,
                       "head_dim": hd, "block_size": bs, "ctx_mean": float(ctx.mean()), "pages": args.attn_pages,
                       "pool_bytes": 2 * c.k_pool.numel() * 2, "clocks": clk.summary()}), flush=True)
@@ -729,8 +754,10 @@ def micro_churn(args, device):
 
 
 def config_block(args, w, B, world):
+    dist = (f"lognormal(median {w.lognormal_median:g}, sigma {w.lognormal_sigma:g}) clipped to "
+            f"[{w.prompt_lo},{w.prompt_hi}]" if w.lognormal_sigma > 0 else f"U[{w.prompt_lo},{w.prompt_hi}]")
     return {"workload": f"{w.name}: {w.n_requests if args.rows is None else B} rows/GPU, prompts "
-                        f"U[{w.prompt_lo},{w.prompt_hi}], k={w.k}, block {w.block_size}, "
+                        f"{dist}, k={w.k}, block {w.block_size}, "
                         f"{'greedy' if w.temperature == 0 else 'T=%g' % w.temperature}",
             "rows_per_gpu": B, "k": w.k, "block_size": w.block_size,
             "target": w.pair.target, "draft": w.pair.draft, "vocab": w.pair.vocab,
@@ -766,6 +793,8 @@ def main():
                     help="headline the reference's step structure (2 target calls per step) instead of the "
                          "deferred-bonus step (the target's bonus call folded into the next verify)")
     ap.add_argument("--attn-shape", default="gpt2-verify", choices=sorted(ATTN_SHAPES))
+    ap.add_argument("--prefill-kernel", default="tc", choices=["tc", "off"],
+                    help="wide attention calls (prefill) on the tcgen05 kernel, or on the mma.sync kernel")
     ap.add_argument("--attn-pages", default="permuted", choices=["permuted", "contiguous"],
                     help="--micro attn: block tables a random permutation of the pool, or consecutive blocks")
     ap.add_argument("--profile-step", action="store_true",

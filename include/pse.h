@@ -182,6 +182,15 @@ int pse_paged_attention_noalloc(pse_block_state st, pse_kv_layer kv, const void 
  * two); no counterpart in the reference. */
 int pse_attention_force_generic(int32_t on);
 
+/* Wide calls (at least 64 query rows per row and KV head: prompt prefill, a
+ * wide batched append) with bf16 pools, head_dim 64/128, block_size 16..128
+ * dividing 128 and 16-byte aligned q / out rows run a tcgen05 kernel (scores
+ * and output accumulator in tensor memory, 128 query rows x 128 keys per
+ * tile); query tokens at or past the row's length (seq_len) get zero output
+ * there.  mode 0: that kernel for wide calls (default); 1: never (the calls
+ * take the kernels above).  No counterpart in the reference. */
+int pse_attention_prefill_select(int32_t mode);
+
 /* ------------------------------------------------------------------------ */
 /* Sampling, accept/resample                                                */
 /* ------------------------------------------------------------------------ */

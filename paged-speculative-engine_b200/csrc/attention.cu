@@ -407,17 +407,36 @@ int tc_attention(const pse_block_state& st, const pse_kv_layer& kv, const void* 
                  int q_heads, float scale, int split_tokens, int n_splits, void* ws, int* counter,
                  const int32_t* row_order, bool self_reset, cudaStream_t s);
 
+bool prefill_eligible(const pse_block_state& st, const pse_kv_layer& kv, const void* q, int64_t q_tok_stride,
+                      const void* out, int64_t out_tok_stride, int q_heads, int width);
+int prefill_attention(const pse_block_state& st, const pse_kv_layer& kv, const void* q, int64_t q_tok_stride,
+                      void* out, int64_t out_tok_stride, const int32_t* slots, const int32_t* base_len, int rows,
+                      int width, int q_heads, float scale, const int32_t* row_order, cudaStream_t s);
+
 }  // namespace pse
 
 using namespace pse;
 
 namespace {
 bool g_force_generic = false;
+bool g_prefill_off = false;
+
+bool use_prefill(const pse_block_state& st, const pse_kv_layer& kv, const void* q, int64_t q_tok_stride,
+                 const void* out, int64_t out_tok_stride, int q_heads, int width) {
+  return !g_force_generic && !g_prefill_off &&
+         prefill_eligible(st, kv, q, q_tok_stride, out, out_tok_stride, q_heads, width);
 }
+}  // namespace
 
 /* Test hook: route every call to the generic kernel (1) or let the shape pick (0). */
 extern "C" int pse_attention_force_generic(int32_t on) {
   g_force_generic = on != 0;
+  return PSE_OK;
+}
+
+extern "C" int pse_attention_prefill_select(int32_t mode) {
+  if (mode < 0 || mode > 1) return PSE_EINVAL;
+  g_prefill_off = mode == 1;
   return PSE_OK;
 }
 
@@ -474,6 +493,9 @@ extern "C" int pse_paged_attention(pse_block_state st, pse_kv_layer kv, const vo
   a.n_qtiles = p.n_qtiles;
   a.ws = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(workspace) + kWsHeader);
   cudaStream_t s = (cudaStream_t)stream;
+  if (use_prefill(st, kv, q, q_tok_stride, out, out_tok_stride, q_heads, width))
+    return prefill_attention(st, kv, q, q_tok_stride, out, out_tok_stride, slots, base_len, rows, width, q_heads,
+                             scale, row_order, s);
   if (tc_eligible(st, kv, q_heads, width) && !g_force_generic) {
     int rc = tc_attention(st, kv, q, q_tok_stride, out, out_tok_stride, slots, base_len, rows, width, q_heads, scale,
                           p.split_tokens, p.n_splits, a.ws, reinterpret_cast<int*>(workspace), row_order,
@@ -579,6 +601,9 @@ extern "C" int pse_paged_attention_noalloc(pse_block_state st, pse_kv_layer kv, 
   // reads it, so stale contents from an earlier call never leak in.
   a.ws = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(scratch) + kWsHeader);
   cudaStream_t s = (cudaStream_t)stream;
+  if (use_prefill(st, kv, q, q_tok_stride, out, out_tok_stride, q_heads, width))
+    return prefill_attention(st, kv, q, q_tok_stride, out, out_tok_stride, slots, base_len, rows, width, q_heads,
+                             scale, nullptr, s);
   if (tc_eligible(st, kv, q_heads, width)) {
     rc = tc_attention(st, kv, q, q_tok_stride, out, out_tok_stride, slots, base_len, rows, width, q_heads, scale,
                       p.split_tokens, p.n_splits, a.ws, reinterpret_cast<int*>(scratch), nullptr,

@@ -12,7 +12,7 @@ CSRC = os.path.join(ROOT, "csrc")
 INCLUDE = os.path.join(REPO, "include")
 LIB = os.path.join(PKG, "lib", "libpse.so")
 
-SOURCES = ["kv_cache.cu", "attention.cu", "attention_tc.cu", "gemm_tc.cu", "sampling.cu", "model_ops.cu", "sched.cu"]
+SOURCES = ["kv_cache.cu", "attention.cu", "attention_tc.cu", "attention_prefill.cu", "gemm_tc.cu", "sampling.cu", "model_ops.cu", "sched.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
