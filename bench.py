@@ -426,7 +426,7 @@ def micro_attention(args, device):
 
     # the rows' lengths: everything up to and including the last query
     c._blocks.seq_len.copy_(torch.from_numpy(ctx.astype(np.int32)))
-    N.call("pse_attention_prefill_select", 1 if args.prefill_kernel == "off" else 0)
+    N.call("pse_attention_prefill_select", {"tc": 0, "off": 1, "single": 2}[args.prefill_kernel])
 
     def launch():
         N.call("pse_paged_attention", c.state, c.layer(0), q.data_ptr(), q.stride(0), out.data_ptr(), out.stride(0),
@@ -793,8 +793,9 @@ def main():
                     help="headline the reference's step structure (2 target calls per step) instead of the "
                          "deferred-bonus step (the target's bonus call folded into the next verify)")
     ap.add_argument("--attn-shape", default="gpt2-verify", choices=sorted(ATTN_SHAPES))
-    ap.add_argument("--prefill-kernel", default="tc", choices=["tc", "off"],
-                    help="wide attention calls (prefill) on the tcgen05 kernel, or on the mma.sync kernel")
+    ap.add_argument("--prefill-kernel", default="tc", choices=["tc", "off", "single"],
+                    help="wide attention calls (prefill) on the tcgen05 kernels, on the mma.sync kernel, or on the "
+                         "one-query-tile tcgen05 kernel at every head_dim")
     ap.add_argument("--attn-pages", default="permuted", choices=["permuted", "contiguous"],
                     help="--micro attn: block tables a random permutation of the pool, or consecutive blocks")
     ap.add_argument("--profile-step", action="store_true",

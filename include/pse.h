@@ -187,8 +187,10 @@ int pse_attention_force_generic(int32_t on);
  * dividing 128 and 16-byte aligned q / out rows run a tcgen05 kernel (scores
  * and output accumulator in tensor memory, 128 query rows x 128 keys per
  * tile); query tokens at or past the row's length (seq_len) get zero output
- * there.  mode 0: that kernel for wide calls (default); 1: never (the calls
- * take the kernels above).  No counterpart in the reference. */
+ * there.  head_dim 64 runs two query tiles per CTA (one per softmax
+ * warpgroup, sharing the K/V tiles).  mode 0: those kernels for wide calls
+ * (default); 1: never (the calls take the kernels above); 2: one query tile
+ * per CTA at every head_dim.  No counterpart in the reference. */
 int pse_attention_prefill_select(int32_t mode);
 
 /* ------------------------------------------------------------------------ */

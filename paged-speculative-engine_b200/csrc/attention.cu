@@ -407,6 +407,7 @@ int tc_attention(const pse_block_state& st, const pse_kv_layer& kv, const void* 
                  int q_heads, float scale, int split_tokens, int n_splits, void* ws, int* counter,
                  const int32_t* row_order, bool self_reset, cudaStream_t s);
 
+extern bool g_prefill_pair;
 bool prefill_eligible(const pse_block_state& st, const pse_kv_layer& kv, const void* q, int64_t q_tok_stride,
                       const void* out, int64_t out_tok_stride, int q_heads, int width);
 int prefill_attention(const pse_block_state& st, const pse_kv_layer& kv, const void* q, int64_t q_tok_stride,
@@ -435,8 +436,9 @@ extern "C" int pse_attention_force_generic(int32_t on) {
 }
 
 extern "C" int pse_attention_prefill_select(int32_t mode) {
-  if (mode < 0 || mode > 1) return PSE_EINVAL;
+  if (mode < 0 || mode > 2) return PSE_EINVAL;
   g_prefill_off = mode == 1;
+  pse::g_prefill_pair = mode == 0;
   return PSE_OK;
 }
 

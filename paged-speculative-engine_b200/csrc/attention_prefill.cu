@@ -4,28 +4,39 @@
 // Same contract as pse_paged_attention (engine/model.py:99-116 over the paged
 // layout of engine/paged_cache.py:83-88) for calls with many query rows per
 // (row, KV head): the K/V of a prompt is re-read by every query tile from L2,
-// so these calls are bound by math and by the softmax, not by HBM.
+// so these calls are bound by the tensor cores, the softmax's exponentials and
+// shared-memory traffic, not by HBM.
 //
-// Work item = (row, KV head, 128-query-row tile); the 128 query rows are the
-// GQA group's heads over 128 / group consecutive tokens, head-major.
-// Persistent CTAs take items round-robin, heaviest (last query tile) first.
-// Per CTA:
-//   warp 4       TMA producer: loads each item's Q tile into one of two
-//                buffers ahead of use, walks the row's block table and copies
-//                the K and V pages of each 128-key tile into a shared-memory
-//                ring (128-byte swizzle; each head_dim half of the 128 keys is
-//                one 16 KB K-major block), completing on mbarriers;
-//   warp 5       allocates 512 TMEM columns and issues tcgen05.mma from one
-//                thread: S = Q K^T (M 128, N 128, K 16) into one of two TMEM
-//                score buffers, then O += P V (M 128, N head_dim, K 16) into
-//                the TMEM output accumulator with V as an MN-major operand;
-//                tcgen05.commit hands each result to the next stage;
-//   warps 0..3   one thread per query row (its TMEM lane): tcgen05.ld of the
-//                row's 128 scores, causal mask, exp2 online softmax (max and
-//                sum over 8 independent chains, ex2.approx), P as bf16
-//                into shared memory for the second MMA, rescale of the row's
-//                TMEM output when its running maximum grows by more than 2^8,
-//                and at the item's end O / l to global memory.
+// A query tile is 128 rows: the GQA group's heads over 128 / group consecutive
+// tokens, head-major (tile row r = group head r / (128 / group), token
+// r % (128 / group)).  Persistent CTAs take work items round-robin, heaviest
+// first.  Warp roles:
+//   warp 8       TMA producer: each item's Q tile(s) into one of two buffers
+//                ahead of use, and the K and V pages of each 128-key tile into
+//                a shared-memory ring (128-byte swizzle; each head_dim half of
+//                a tile's 128 keys is one 16 KB K-major block), completing on
+//                mbarriers;
+//   warp 9       allocates the 512 TMEM columns and issues tcgen05.mma from
+//                one thread: S = Q K^T (M 128, N 128, K 16; Q and K in shared
+//                memory) into a TMEM score buffer, O += P V (M 128, N
+//                head_dim, K 16; P in TMEM, V in shared memory as an MN-major
+//                operand) into the TMEM output; tcgen05.commit hands each
+//                result on;
+//   warps 0..7   the softmax, one thread per (tile row, warpgroup): tcgen05.ld
+//                of the scores, causal mask, exp2 online softmax (max and sum
+//                over 8 independent chains, ex2.approx), P as bf16 pairs into
+//                TMEM with tcgen05.st, rescale of the row's TMEM output when
+//                its reference maximum grows by more than 2^8, and at the
+//                item's end O / l to global memory.
+// P never touches shared memory: with K, V and Q the only operands read from
+// it, shared-memory bandwidth (which bounds these small-N MMAs) goes to them.
+// Two arrangements of the softmax warpgroups:
+//   prefill_attn_kernel (head_dim 64 or 128): one query tile per item; the two
+//                warpgroups split its 128 key columns and exchange each row's
+//                maximum every tile;
+//   prefill_pair_kernel (head_dim 64): two query tiles per item (tiles 2m and
+//                2m + 1 of one row and KV head), one per warpgroup, sharing
+//                every K/V tile.
 // Scores of tile j+1 are computed while the softmax of tile j runs, P V of
 // tile j while the softmax of tile j+1 runs, and the next item's Q and first
 // scores while this item's output is written.
@@ -46,16 +57,26 @@ namespace pf {
 
 constexpr int BQ = 128;   // query rows per item = TMEM lanes
 constexpr int BKV = 128;  // keys per tile
-constexpr int kProducerWarp = 4, kMmaWarp = 5;  // warps 0..3: softmax
-constexpr int kThreads = 6 * 32;
+// warps 0..7: softmax (warp w handles TMEM lanes 32 * (w % 4) .. +31 and key
+// columns 64 * (w / 4) .. +63 of each tile); warp 8: TMA; warp 9: MMA
+constexpr int kSoftmaxThreads = 256;
+constexpr int kProducerWarp = 8, kMmaWarp = 9;
+constexpr int kThreads = 10 * 32;
 constexpr uint32_t kSpinLimit = 1u << 22;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 0;    // score buffers at columns 0 and 128
 constexpr uint32_t kColO = 256;  // output accumulator
+constexpr uint32_t kColP = 384;  // P (bf16 pairs, 64 columns): the A operand of O += P V
 constexpr int kHalfBytes = BKV * 128;  // one 64-column half of a 128-row tile (16 KB)
 
+#ifndef PSE_PF_STAGES64
+#define PSE_PF_STAGES64 3
+#endif
 template <int HD>
-__host__ __device__ constexpr int n_stages() { return HD == 64 ? 3 : 2; }
+__host__ __device__ constexpr int n_stages() { return HD == 64 ? PSE_PF_STAGES64 : 2; }
+// Q tiles in flight: two (the next item's Q lands while this one runs).
+template <int HD>
+__host__ __device__ constexpr int n_qbufs() { return 2; }
 
 struct Args {
   const int32_t* block_table;
@@ -180,6 +201,16 @@ __device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t a, uint64_t b
       "l"(a), "l"(b), "r"(idesc), "r"(acc)
       : "memory");
 }
+// A operand in tensor memory: row r of A is lane r, 16-bit elements packed two
+// to a 32-bit column (K = 16 per instruction = 8 columns).
+__device__ __forceinline__ void mma_bf16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t b, uint32_t idesc,
+                                            uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(su32(bar))
                : "memory");
@@ -215,18 +246,12 @@ __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
-// Byte offset of 16-byte chunk c (8 bf16 columns) of row r in a K-major
-// 128-row operand made of 64-column halves (16 KB each), 128-byte swizzle.
-__device__ __forceinline__ uint32_t chunk_off(int r, int c) {
-  return (uint32_t)((c >> 3) * kHalfBytes + r * 128 + (((c & 7) ^ (r & 7)) << 4));
-}
 
 __device__ __forceinline__ float ex2(float x) {
   float y;
@@ -236,8 +261,10 @@ __device__ __forceinline__ float ex2(float x) {
 
 template <int HD>
 constexpr size_t smem_bytes() {
-  // align slack + Q (two buffers) + P + ring (K and V per stage) + barriers
-  return 1024 + (size_t)2 * BQ * HD * 2 + (size_t)BQ * BKV * 2 + (size_t)n_stages<HD>() * 2 * BKV * HD * 2 + 256;
+  // align slack + Q buffers + ring (K and V per stage) + barriers + the two
+  // softmax warpgroups' row exchange (2 x 2 x 128 maxima, 2 x 128 sums)
+  return 1024 + (size_t)n_qbufs<HD>() * BQ * HD * 2 + (size_t)n_stages<HD>() * 2 * BKV * HD * 2 + 256 +
+         (size_t)6 * BQ * 4;
 }
 
 template <int HD>
@@ -250,21 +277,24 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int kHalves = HD / 64;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* q_s = smem;                        // [2][128 x HD] K-major
-  uint8_t* p_s = q_s + 2 * kQBytes;           // [128 x 128] K-major
-  uint8_t* ring = p_s + BQ * BKV * 2;         // [S][K tile | V tile]
+  constexpr int QB = n_qbufs<HD>();
+  uint8_t* q_s = smem;                        // [QB][128 x HD] K-major
+  uint8_t* ring = q_s + QB * kQBytes;         // [S][K tile | V tile]
   uint64_t* full = reinterpret_cast<uint64_t*>(ring + S * 2 * kTileBytes);
   uint64_t* empty = full + S;
   uint64_t* s_full = empty + S;     // [2] scores of a tile ready (one per score buffer)
-  uint64_t* q_full = s_full + 2;    // [2] an item's Q landed (one per Q buffer)
-  uint64_t* q_empty = q_full + 2;   // [2] an item's score MMAs retired: its Q buffer is free
+  uint64_t* q_full = s_full + 2;    // [QB] an item's Q landed (one per Q buffer)
+  uint64_t* q_empty = q_full + 2;   // [QB] an item's score MMAs retired: its Q buffer is free
   uint64_t* p_full = q_empty + 2;   // P written, output rescaled (128 arrivals)
   uint64_t* pv_done = p_full + 1;   // O += P V of a tile retired
   uint64_t* final_bar = pv_done + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(final_bar + 1);
+  uint64_t* pair_bar = final_bar + 1;  // [4] softmax warp pairs' exchanges (64 arrivals)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pair_bar + 4);
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
   int* issued = abort_flag + 1;   // K/V tiles whose copies the producer issued
   int* issued_q = issued + 1;     // Q tiles whose copies the producer issued
+  float* xmax = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(full) + 256);  // [2 tiles][2 halves][128]
+  float* xsum = xmax + 4 * BQ;                                                      // [2 halves][128]
   volatile int* vabort = abort_flag;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -278,9 +308,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&q_full[b], 1);
       mbar_init(&q_empty[b], 1);
     }
-    mbar_init(p_full, BQ);
+    mbar_init(p_full, kSoftmaxThreads);
     mbar_init(pv_done, 1);
     mbar_init(final_bar, 1);
+    for (int x = 0; x < 4; ++x) mbar_init(&pair_bar[x], 64);
     *abort_flag = 0;
     *issued = 0;
     *issued_q = 0;
@@ -306,8 +337,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (it.n_tiles == 0) continue;
       // the item's Q: one [tpt tokens x 64 columns] box per group head and half
       if (lane == 0) {
-        const int qb = nq & 1;
-        if (!mbar_wait(&q_empty[qb], ((nq >> 1) & 1) ^ 1, vabort)) {
+        const int qb = nq % QB;
+        if (!mbar_wait(&q_empty[qb], ((nq / QB) & 1) ^ 1, vabort)) {
           run = false;
         } else {
           mbar_expect_tx(&q_full[qb], kQBytes);
@@ -374,14 +405,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       // V's head_dim halves are 16 KB apart; with one half the field is unused
       // and gets the 8-row-group stride, so no reading of it leaves the tile
       constexpr uint32_t kVAtomStride = HD == 128 ? (uint32_t)kHalfBytes : 1024u;
-      const uint32_t p_base = su32(p_s);
       int g = 0, items = 0;
       bool run = true;
       for (int e = blockIdx.x; run && e < a.n_items; e += gridDim.x) {
         const Item it = decode(a, e);
         if (it.n_tiles == 0) continue;
-        const int qb = items & 1;
-        if (!mbar_wait(&q_full[qb], (items >> 1) & 1, vabort)) break;
+        const int qb = items % QB;
+        if (!mbar_wait(&q_full[qb], (items / QB) & 1, vabort)) break;
         tc_fence_after();
         const uint32_t q_base = su32(q_s + qb * kQBytes);
         int s_prev = 0;
@@ -413,11 +443,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             const uint32_t vb = su32(ring + s_prev * 2 * kTileBytes + kTileBytes);
 #pragma unroll
-            for (int kk = 0; kk < BKV / 16; ++kk) {
-              const uint32_t poff = (uint32_t)((kk >> 2) * kHalfBytes + (kk & 3) * 32);
-              mma_bf16(tmem + kColO, desc_kmajor(p_base + poff), desc_mnmajor(vb + kk * 16 * 128, kVAtomStride),
-                       idesc_o, (j > 1 || kk > 0) ? 1u : 0u);
-            }
+            for (int kk = 0; kk < BKV / 16; ++kk)
+              mma_bf16_ts(tmem + kColO, tmem + kColP + kk * 8, desc_mnmajor(vb + kk * 16 * 128, kVAtomStride),
+                          idesc_o, (j > 1 || kk > 0) ? 1u : 0u);
             mma_commit(pv_done);
             mma_commit(&empty[s_prev]);
           }
@@ -432,10 +460,24 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ softmax
-    const int r = tid;  // tile row = TMEM lane
-    const uint32_t lane_base = tmem + ((uint32_t)(32 * warp) << 16);
+    // Warps w and w + 4 share tile rows 32 * (w % 4) .. +31: each takes 64 of
+    // a tile's 128 key columns, half of P and half of the output columns; the
+    // pair exchanges the row maximum every tile (and the row sum at the end)
+    // through shared memory behind the pair's mbarrier (a bounded wait: a warp
+    // that gives up never leaves its partner blocked).
+    const int half = warp >> 2, q4 = warp & 3;
+    const int r = 32 * q4 + lane;  // tile row = TMEM lane
+    const uint32_t lane_base = tmem + ((uint32_t)(32 * q4) << 16);
     const int gq = r / a.tpt, wr = r % a.tpt;
     const float sl2 = a.scale_log2;
+    constexpr int kCols = BKV / 2;   // key columns of this warp
+    constexpr int kOCols = HD / 2;   // output columns of this warp
+    int nx = 0;  // exchanges so far (the pair's barrier phase)
+    auto pair_wait = [&]() -> bool {  // after this thread's arrive: wait for the partner's
+      const bool ok = mbar_wait(&pair_bar[q4], nx & 1, vabort);
+      ++nx;
+      return __all_sync(0xffffffffu, ok);
+    };
     int g = 0;
     bool run = true;
     for (int e = blockIdx.x; run && e < a.n_items; e += gridDim.x) {
@@ -445,11 +487,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int pos = it.base + w;
       const bool valid = row_ok && pos < it.len;
       const int h = it.hk * a.group + gq;
-      __nv_bfloat16* orow = a.out + ((int64_t)it.i * a.width + w) * a.out_tok_stride + (int64_t)h * HD;
+      __nv_bfloat16* orow = a.out + ((int64_t)it.i * a.width + w) * a.out_tok_stride + (int64_t)h * HD + half * kOCols;
       if (it.n_tiles == 0) {
         if (row_ok) {
 #pragma unroll
-          for (int c = 0; c < HD / 8; ++c) *reinterpret_cast<uint4*>(orow + c * 8) = make_uint4(0, 0, 0, 0);
+          for (int c = 0; c < kOCols / 8; ++c) *reinterpret_cast<uint4*>(orow + c * 8) = make_uint4(0, 0, 0, 0);
         }
         continue;
       }
@@ -462,44 +504,67 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         tc_fence_after();
-        float sc[BKV];
-        {
+        float sc[kCols];
+        const int key0 = j * BKV + half * kCols;
+        auto load_scores = [&]() {  // this warp's 64 raw scores of the tile, masked
           uint32_t* u = reinterpret_cast<uint32_t*>(sc);
-          const uint32_t col = kColS + (uint32_t)(g & 1) * BKV;
+          const uint32_t col = kColS + (uint32_t)(g & 1) * BKV + half * kCols;
 #pragma unroll
-          for (int c = 0; c < BKV / 32; ++c) tmem_ld32(lane_base + col + c * 32, u + c * 32);
+          for (int c = 0; c < kCols / 32; ++c) tmem_ld32(lane_base + col + c * 32, u + c * 32);
           tmem_wait_ld();
-        }
-        const int key0 = j * BKV;
-        if (key0 + BKV > lim) {
+          if (key0 + kCols > lim) {
 #pragma unroll
-          for (int c = 0; c < BKV; ++c) sc[c] = key0 + c < lim ? sc[c] : -INFINITY;
-        }
-        // maximum of the raw scores (8 independent chains)
+            for (int c = 0; c < kCols; ++c) sc[c] = key0 + c < lim ? sc[c] : -INFINITY;
+          }
+        };
+        float s8[8];
+        auto exps = [&](float msub) {  // sc <- 2^(score * scale - msub), partial sums in s8
+#pragma unroll
+          for (int x = 0; x < 8; ++x) s8[x] = 0.f;
+#pragma unroll
+          for (int c = 0; c < kCols; ++c) {
+            sc[c] = ex2(fmaf(sc[c], sl2, -msub));
+            s8[c & 7] += sc[c];
+          }
+        };
+        load_scores();
+        // maximum of the raw scores (8 independent chains), published to the pair
         float m8[8];
 #pragma unroll
         for (int x = 0; x < 8; ++x) m8[x] = sc[x];
 #pragma unroll
-        for (int c = 8; c < BKV; ++c) m8[c & 7] = fmaxf(m8[c & 7], sc[c]);
-        const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
-                               fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7]))) * sl2;
+        for (int c = 8; c < kCols; ++c) m8[c & 7] = fmaxf(m8[c & 7], sc[c]);
+        const float pm = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                               fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+        float* xm = xmax + (g & 1) * 2 * BQ;
+        xm[half * BQ + r] = pm;
+        mbar_arrive(&pair_bar[q4]);
+        // From the second tile on, the exponentials are taken against the
+        // row's current reference maximum while the partner's maximum is in
+        // flight; they are redone (from the scores, still in TMEM) only when
+        // the pair's maximum moved past that reference.
+        if (j > 0) exps(m_used == -INFINITY ? 0.f : m_used);
+        if (!pair_wait()) {
+          run = false;
+          break;
+        }
+        const float mx = fmaxf(pm, xm[(half ^ 1) * BQ + r]) * sl2;
         // the row's reference maximum moves only when it would grow by more
-        // than 8 (exponents stay <= 2^8); the output is rescaled then
+        // than 8 (exponents stay <= 2^8); the output is rescaled then.  Both
+        // warps of the pair see the same maximum, so they decide alike.
         float corr = 1.f;
         bool rescale = false;
-        if (mx > m_used + 8.f) {
+        const bool moved = mx > m_used + 8.f;
+        if (moved) {
           if (m_used != -INFINITY) {
             corr = ex2(m_used - mx);
             rescale = j > 0;
           }
           m_used = mx;
         }
-        const float msub = m_used == -INFINITY ? 0.f : m_used;
-        float s8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int c = 0; c < BKV; ++c) {
-          sc[c] = ex2(fmaf(sc[c], sl2, -msub));
-          s8[c & 7] += sc[c];
+        if (j == 0 || __any_sync(0xffffffffu, moved)) {
+          if (j > 0) load_scores();
+          exps(m_used == -INFINITY ? 0.f : m_used);
         }
         l = l * corr + (((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7])));
         // the previous tile's P V has retired: P's buffer and the output are free
@@ -510,39 +575,43 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         if (__any_sync(0xffffffffu, rescale)) {
 #pragma unroll
-          for (int c = 0; c < HD / 32; ++c) {
+          for (int c = 0; c < kOCols / 32; ++c) {
             uint32_t o[32];
-            tmem_ld32(lane_base + kColO + c * 32, o);
+            const uint32_t ta = lane_base + kColO + half * kOCols + c * 32;
+            tmem_ld32(ta, o);
             tmem_wait_ld();
 #pragma unroll
             for (int x = 0; x < 32; ++x) o[x] = __float_as_uint(__uint_as_float(o[x]) * corr);
-            tmem_st32(lane_base + kColO + c * 32, o);
+            tmem_st32(ta, o);
           }
           tmem_wait_st();
         }
+        {
+          // this warp's 64 keys of P as bf16 pairs into TMEM (the PV MMA's A operand)
+          uint32_t pk[kCols / 2];
 #pragma unroll
-        for (int c = 0; c < BKV / 8; ++c) {
-          uint4 v;
-          v.x = pack_bf16(sc[8 * c + 0], sc[8 * c + 1]);
-          v.y = pack_bf16(sc[8 * c + 2], sc[8 * c + 3]);
-          v.z = pack_bf16(sc[8 * c + 4], sc[8 * c + 5]);
-          v.w = pack_bf16(sc[8 * c + 6], sc[8 * c + 7]);
-          *reinterpret_cast<uint4*>(p_s + chunk_off(r, c)) = v;
+          for (int c = 0; c < kCols / 2; ++c) pk[c] = pack_bf16(sc[2 * c], sc[2 * c + 1]);
+          tmem_st32(lane_base + kColP + half * (kCols / 2), pk);
+          tmem_wait_st();
         }
-        fence_async_smem();
         tc_fence_before();
         mbar_arrive(p_full);
         ++g;
       }
       if (!run) break;
-      // the item's output: O / l once the last P V has retired
+      // the item's output: O / l once the last P V has retired; the row's sum
+      // is the pair's two partial sums (same reference maximum)
+      xsum[half * BQ + r] = l;
+      mbar_arrive(&pair_bar[q4]);
+      if (!pair_wait()) break;
+      const float L = l + xsum[(half ^ 1) * BQ + r];
       if (!__all_sync(0xffffffffu, mbar_wait(pv_done, (g - 1) & 1, vabort))) break;
       tc_fence_after();
-      const float inv = valid && l > 0.f ? 1.f / l : 0.f;
+      const float inv = valid && L > 0.f ? 1.f / L : 0.f;
 #pragma unroll
-      for (int c = 0; c < HD / 32; ++c) {
+      for (int c = 0; c < kOCols / 32; ++c) {
         uint32_t o[32];
-        tmem_ld32(lane_base + kColO + c * 32, o);
+        tmem_ld32(lane_base + kColO + half * kOCols + c * 32, o);
         tmem_wait_ld();
         if (row_ok) {
 #pragma unroll
@@ -568,7 +637,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int n = *issued;
       for (int t = n > S ? n - S : 0; t < n; ++t) mbar_drain(&full[t % S], (t / S) & 1);
       const int nq = *issued_q;
-      for (int t = nq > 2 ? nq - 2 : 0; t < nq; ++t) mbar_drain(&q_full[t & 1], (t >> 1) & 1);
+      for (int t = nq > QB ? nq - QB : 0; t < nq; ++t) mbar_drain(&q_full[t % QB], (t / QB) & 1);
     }
   }
   if (warp == kMmaWarp) {
@@ -596,6 +665,412 @@ int launch(const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mq, 
   return PSE_OK;
 }
 
+// ---------------------------------------------------------------- two query tiles per CTA
+// head_dim 64: each softmax warpgroup owns one query tile of a pair (tiles 2m
+// and 2m + 1 of one row and KV head), so the pair shares every K/V tile, no
+// row statistics cross warpgroups, and one warpgroup's waits overlap the
+// other's exponentials on the SMSP's MUFU.
+
+struct PairItem {
+  int i, hk, slot, base, len;
+  int w0[2], w_end[2], kmax[2], n[2];
+  int kmax_all, n_max;
+};
+
+__device__ __forceinline__ PairItem decode_pair(const Args& a, int e) {
+  PairItem it;
+  const int per = a.rows * a.kv_heads;
+  const int n_pairs = (a.n_qtiles + 1) / 2;
+  const int m = n_pairs - 1 - e / per;  // heaviest pair first
+  const int rem = e % per;
+  const int ri = rem / a.kv_heads;
+  it.hk = rem % a.kv_heads;
+  it.i = a.row_order ? a.row_order[ri] : ri;
+  it.slot = a.slots[it.i];
+  it.base = a.base_len[it.i];
+  const bool ok = it.slot >= 0 && it.slot < a.num_slots && it.base >= 0;
+  it.len = ok ? a.seq_len[it.slot] : 0;
+  it.kmax_all = 0;
+  it.n_max = 0;
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    it.w0[k] = (2 * m + k) * a.tpt;
+    it.w_end[k] = min(it.w0[k] + a.tpt, a.width);
+    it.kmax[k] = min(it.base + it.w_end[k], it.len);
+    it.n[k] = (ok && it.w_end[k] > it.w0[k] && it.base + it.w0[k] < it.len && it.kmax[k] > 0)
+                  ? (it.kmax[k] + BKV - 1) / BKV
+                  : 0;
+    if (it.n[k] > 0) it.kmax_all = max(it.kmax_all, it.kmax[k]);
+    it.n_max = max(it.n_max, it.n[k]);
+  }
+  return it;
+}
+
+// Warp roles as in the one-tile kernel: warps 0..3 and 4..7 are the two
+// softmax warpgroups, warp 8 TMA, warp 9 MMA.
+constexpr size_t pair_smem_bytes() {
+  // align slack + Q (two buffers x two tiles) + ring + barriers
+  return 1024 + (size_t)2 * 2 * BQ * 64 * 2 + (size_t)3 * 2 * BKV * 64 * 2 + 256;
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    prefill_pair_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
+                        const __grid_constant__ CUtensorMap tmq, Args a) {
+  constexpr int HD = 64, S = 3;
+  constexpr int kTileBytes = BKV * HD * 2;  // one of K or V (16 KB)
+  constexpr int kQBytes = BQ * HD * 2;      // one query tile (16 KB)
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* q_s = smem;                      // [2 buffers][2 tiles][128 x 64] K-major
+  uint8_t* ring = q_s + 4 * kQBytes;        // [S][K tile | V tile]
+  uint64_t* full = reinterpret_cast<uint64_t*>(ring + S * 2 * kTileBytes);
+  uint64_t* empty = full + S;
+  uint64_t* s_full = empty + S;     // [2] per warpgroup: its scores of a tile are in TMEM
+  uint64_t* s_free = s_full + 2;    // [2] per warpgroup: it has loaded them (128 arrivals)
+  uint64_t* p_full = s_free + 2;    // [2] per warpgroup: P written, output rescaled (128 arrivals)
+  uint64_t* pv_done = p_full + 2;   // [2] per warpgroup: its O += P V retired
+  uint64_t* q_full = pv_done + 2;   // [2] per Q buffer: the item's two Q tiles landed
+  uint64_t* q_empty = q_full + 2;   // [2] per Q buffer: the item's score MMAs retired
+  uint64_t* final_bar = q_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(final_bar + 1);
+  int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+  int* issued = abort_flag + 1;
+  int* issued_q = issued + 1;
+  volatile int* vabort = abort_flag;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (tid == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int k = 0; k < 2; ++k) {
+      mbar_init(&s_full[k], 1);
+      mbar_init(&s_free[k], BQ);
+      mbar_init(&p_full[k], BQ);
+      mbar_init(&pv_done[k], 1);
+      mbar_init(&q_full[k], 1);
+      mbar_init(&q_empty[k], 1);
+    }
+    mbar_init(final_bar, 1);
+    *abort_flag = 0;
+    *issued = 0;
+    *issued_q = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == kMmaWarp) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(tmem_slot)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int n_items = a.rows * a.kv_heads * ((a.n_qtiles + 1) / 2);
+
+  if (warp == kProducerWarp) {
+    // ------------------------------------------------------------ producer
+    const int bs = a.block_size, ppt = BKV / bs;
+    int g = 0, nq = 0;
+    bool run = true;
+    for (int e = blockIdx.x; run && e < n_items; e += gridDim.x) {
+      const PairItem it = decode_pair(a, e);
+      if (it.n_max == 0) continue;
+      if (lane == 0) {
+        const int qb = nq & 1;
+        if (!mbar_wait(&q_empty[qb], ((nq >> 1) & 1) ^ 1, vabort)) {
+          run = false;
+        } else {
+          mbar_expect_tx(&q_full[qb], 2 * kQBytes);
+          *issued_q = nq + 1;
+          for (int k = 0; k < 2; ++k) {
+            const int y = it.i * a.width + it.w0[k];
+            for (int gq = 0; gq < a.group; ++gq)
+              tma_load_2d(q_s + (qb * 2 + k) * kQBytes + gq * a.tpt * 128, &tmq, (it.hk * a.group + gq) * HD, y,
+                          &q_full[qb]);
+          }
+        }
+      }
+      run = __shfl_sync(0xffffffffu, run ? 1 : 0, 0) != 0;
+      if (!run) break;
+      ++nq;
+      auto page = [&](int j) -> int {
+        if (lane >= ppt || j >= it.n_max) return -1;
+        const int pi = j * ppt + lane;
+        if (pi >= a.nblocks[it.slot] || pi >= a.max_blocks || pi * bs >= it.kmax_all) return -1;
+        const int b = a.block_table[(int64_t)it.slot * a.max_blocks + pi];
+        return (b >= 0 && b < a.num_blocks) ? b : -1;
+      };
+      int cur = page(0);
+      for (int j = 0; j < it.n_max; ++j) {
+        const int nxt = page(j + 1);
+        const int s = g % S;
+        int stop = 0;
+        if (lane == 0) {
+          if (!mbar_wait(&empty[s], ((g / S) & 1) ^ 1, vabort)) {
+            stop = 1;
+          } else {
+            mbar_expect_tx(&full[s], 2 * kTileBytes);
+            *issued = g + 1;
+          }
+        }
+        stop = __shfl_sync(0xffffffffu, stop, 0);
+        if (stop) {
+          run = false;
+          break;
+        }
+        uint8_t* kst = ring + s * 2 * kTileBytes;
+        uint8_t* vst = kst + kTileBytes;
+        for (int p = 0; p < ppt; ++p) {
+          const int blk = __shfl_sync(0xffffffffu, cur, p);
+          if (lane == 0) {
+            const int y = blk >= 0 ? (blk * a.kv_heads + it.hk) * bs : a.oob_row;
+            tma_load_2d(kst + p * bs * 128, &tmk, 0, y, &full[s]);
+            tma_load_2d(vst + p * bs * 128, &tmv, 0, y, &full[s]);
+          }
+        }
+        cur = nxt;
+        ++g;
+      }
+    }
+  } else if (warp == kMmaWarp) {
+    // ------------------------------------------------------------ MMA issue
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = instr_desc(BKV, 0);
+      constexpr uint32_t idesc_o = instr_desc(HD, 1);
+      int g = 0, items = 0;
+      int gs[2] = {0, 0}, gp[2] = {0, 0};  // score / P V tiles issued per warpgroup
+      bool run = true;
+      for (int e = blockIdx.x; run && e < n_items; e += gridDim.x) {
+        const PairItem it = decode_pair(a, e);
+        if (it.n_max == 0) continue;
+        const int qb = items & 1;
+        if (!mbar_wait(&q_full[qb], (items >> 1) & 1, vabort)) break;
+        tc_fence_after();
+        int s_prev = 0;
+        for (int j = 0; run && j <= it.n_max; ++j) {
+          if (j < it.n_max) {
+            const int s = g % S;
+            if (!mbar_wait(&full[s], (g / S) & 1, vabort)) {
+              run = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t kb = su32(ring + s * 2 * kTileBytes);
+            for (int k = 0; k < 2; ++k) {
+              if (j >= it.n[k]) continue;
+              // the warpgroup has loaded its previous scores out of this buffer
+              if (gs[k] > 0 && !mbar_wait(&s_free[k], (gs[k] - 1) & 1, vabort)) {
+                run = false;
+                break;
+              }
+              tc_fence_after();
+              const uint32_t qa = su32(q_s + (qb * 2 + k) * kQBytes);
+#pragma unroll
+              for (int kk = 0; kk < HD / 16; ++kk)
+                mma_bf16(tmem + kColS + k * BKV, desc_kmajor(qa + kk * 32), desc_kmajor(kb + kk * 32), idesc_s,
+                         kk > 0);
+              mma_commit(&s_full[k]);
+              ++gs[k];
+            }
+            if (!run) break;
+            if (j + 1 == it.n_max) mma_commit(&q_empty[qb]);  // the item's last read of its Q tiles
+          }
+          if (j >= 1) {
+            const uint32_t vb = su32(ring + s_prev * 2 * kTileBytes + kTileBytes);
+            for (int k = 0; k < 2; ++k) {
+              if (j - 1 >= it.n[k]) continue;
+              if (!mbar_wait(&p_full[k], gp[k] & 1, vabort)) {
+                run = false;
+                break;
+              }
+              tc_fence_after();
+              // one head_dim half: the atom stride field is unused (8-row-group stride)
+#pragma unroll
+              for (int kk = 0; kk < BKV / 16; ++kk)
+                mma_bf16_ts(tmem + kColO + k * HD, tmem + kColP + k * (BKV / 2) + kk * 8,
+                            desc_mnmajor(vb + kk * 16 * 128, 1024u), idesc_o, (j > 1 || kk > 0) ? 1u : 0u);
+              mma_commit(&pv_done[k]);
+              ++gp[k];
+            }
+            if (!run) break;
+            mma_commit(&empty[s_prev]);
+          }
+          if (j < it.n_max) {
+            s_prev = g % S;
+            ++g;
+          }
+        }
+        ++items;
+      }
+      mma_commit(final_bar);
+    }
+  } else {
+    // ------------------------------------------------------------ softmax
+    const int k = warp >> 2, q4 = warp & 3;  // warpgroup k owns query tile k of the pair
+    const int r = 32 * q4 + lane;
+    const uint32_t lane_base = tmem + ((uint32_t)(32 * q4) << 16);
+    const uint32_t s_col = kColS + k * BKV, o_col = kColO + k * HD;
+    const int gq = r / a.tpt, wr = r % a.tpt;
+    const float sl2 = a.scale_log2;
+    int gk = 0;  // tiles this warpgroup has processed
+    bool run = true;
+    for (int e = blockIdx.x; run && e < n_items; e += gridDim.x) {
+      const PairItem it = decode_pair(a, e);
+      const int w = it.w0[k] + wr;
+      const bool row_ok = gq < a.group && w < it.w_end[k];
+      const int pos = it.base + w;
+      const bool valid = row_ok && pos < it.len;
+      const int h = it.hk * a.group + gq;
+      __nv_bfloat16* orow = a.out + ((int64_t)it.i * a.width + w) * a.out_tok_stride + (int64_t)h * HD;
+      const int n = it.n[k];
+      if (n == 0) {
+        if (row_ok) {
+#pragma unroll
+          for (int c = 0; c < HD / 8; ++c) *reinterpret_cast<uint4*>(orow + c * 8) = make_uint4(0, 0, 0, 0);
+        }
+        continue;
+      }
+      const int lim = row_ok ? min(pos + 1, it.kmax[k]) : it.kmax[k];
+      float m_used = -INFINITY, l = 0.f;
+      for (int j = 0; j < n; ++j) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&s_full[k], gk & 1, vabort))) {
+          run = false;
+          break;
+        }
+        tc_fence_after();
+        float sc[BKV];
+        {
+          uint32_t* u = reinterpret_cast<uint32_t*>(sc);
+#pragma unroll
+          for (int c = 0; c < BKV / 32; ++c) tmem_ld32(lane_base + s_col + c * 32, u + c * 32);
+          tmem_wait_ld();
+        }
+        // the scores are in registers: the MMA may write the next ones
+        tc_fence_before();
+        mbar_arrive(&s_free[k]);
+        const int key0 = j * BKV;
+        if (key0 + BKV > lim) {
+#pragma unroll
+          for (int c = 0; c < BKV; ++c) sc[c] = key0 + c < lim ? sc[c] : -INFINITY;
+        }
+        float m8[8];
+#pragma unroll
+        for (int x = 0; x < 8; ++x) m8[x] = sc[x];
+#pragma unroll
+        for (int c = 8; c < BKV; ++c) m8[c & 7] = fmaxf(m8[c & 7], sc[c]);
+        const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                               fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7]))) * sl2;
+        // the row's reference maximum moves only when it would grow by more
+        // than 8 (exponents stay <= 2^8); the output is rescaled then
+        float corr = 1.f;
+        bool rescale = false;
+        if (mx > m_used + 8.f) {
+          if (m_used != -INFINITY) {
+            corr = ex2(m_used - mx);
+            rescale = j > 0;
+          }
+          m_used = mx;
+        }
+        const float msub = m_used == -INFINITY ? 0.f : m_used;
+        float s8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int c = 0; c < BKV; ++c) {
+          sc[c] = ex2(fmaf(sc[c], sl2, -msub));
+          s8[c & 7] += sc[c];
+        }
+        l = l * corr + (((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7])));
+        // this warpgroup's previous P V has retired: its P buffer and output are free
+        if (gk > 0 && !__all_sync(0xffffffffu, mbar_wait(&pv_done[k], (gk - 1) & 1, vabort))) {
+          run = false;
+          break;
+        }
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll
+          for (int c = 0; c < HD / 32; ++c) {
+            uint32_t o[32];
+            tmem_ld32(lane_base + o_col + c * 32, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int x = 0; x < 32; ++x) o[x] = __float_as_uint(__uint_as_float(o[x]) * corr);
+            tmem_st32(lane_base + o_col + c * 32, o);
+          }
+          tmem_wait_st();
+        }
+#pragma unroll
+        for (int c0 = 0; c0 < BKV / 2; c0 += 32) {
+          // P as bf16 pairs into this warpgroup's TMEM columns (the PV MMA's A operand)
+          uint32_t pk[32];
+#pragma unroll
+          for (int c = 0; c < 32; ++c) pk[c] = pack_bf16(sc[2 * (c0 + c)], sc[2 * (c0 + c) + 1]);
+          tmem_st32(lane_base + kColP + k * (BKV / 2) + c0, pk);
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(&p_full[k]);
+        ++gk;
+      }
+      if (!run) break;
+      if (!__all_sync(0xffffffffu, mbar_wait(&pv_done[k], (gk - 1) & 1, vabort))) break;
+      tc_fence_after();
+      const float inv = valid && l > 0.f ? 1.f / l : 0.f;
+#pragma unroll
+      for (int c = 0; c < HD / 32; ++c) {
+        uint32_t o[32];
+        tmem_ld32(lane_base + o_col + c * 32, o);
+        tmem_wait_ld();
+        if (row_ok) {
+#pragma unroll
+          for (int x = 0; x < 32; x += 8) {
+            uint4 v;
+            v.x = pack_bf16(__uint_as_float(o[x + 0]) * inv, __uint_as_float(o[x + 1]) * inv);
+            v.y = pack_bf16(__uint_as_float(o[x + 2]) * inv, __uint_as_float(o[x + 3]) * inv);
+            v.z = pack_bf16(__uint_as_float(o[x + 4]) * inv, __uint_as_float(o[x + 5]) * inv);
+            v.w = pack_bf16(__uint_as_float(o[x + 6]) * inv, __uint_as_float(o[x + 7]) * inv);
+            *reinterpret_cast<uint4*>(orow + c * 32 + x) = v;
+          }
+        }
+      }
+      tc_fence_before();
+    }
+  }
+
+  __syncthreads();
+  if (*vabort) {
+    if (tid == 0) atomicOr(a.status, PSE_STATUS_TIMEOUT);
+    if (warp == kProducerWarp && lane == 0) {
+      const int n = *issued;
+      for (int t = n > S ? n - S : 0; t < n; ++t) mbar_drain(&full[t % S], (t / S) & 1);
+      const int nq = *issued_q;
+      for (int t = nq > 2 ? nq - 2 : 0; t < nq; ++t) mbar_drain(&q_full[t & 1], (t >> 1) & 1);
+    }
+  }
+  if (warp == kMmaWarp) {
+    if (lane == 0) mbar_drain(final_bar, 0);
+    __syncwarp();
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+  }
+}
+
+int launch_pair(const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mq, const Args& a, cudaStream_t s) {
+  constexpr size_t smem = pair_smem_bytes();
+  static_assert(smem <= 227 * 1024, "shared memory budget");
+  static const cudaError_t opt =
+      cudaFuncSetAttribute(prefill_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (opt != cudaSuccess) return (int)opt;
+  int sms = kNumSMs, dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const long long items = (long long)a.rows * a.kv_heads * ((a.n_qtiles + 1) / 2);
+  const int grid = items < sms ? (int)items : sms;
+  if (grid <= 0) return PSE_OK;
+  prefill_pair_kernel<<<grid, kThreads, smem, s>>>(mk, mv, mq, a);
+  PSE_LAUNCH_CHECK();
+  return PSE_OK;
+}
+
 }  // namespace pf
 
 namespace tc {
@@ -609,6 +1084,10 @@ int tensor_map(const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_
 // 128-key tile, 16-byte aligned query / output rows, GQA groups of 1..16 heads
 // dividing 128 (a group head's Q box of 128 / group tokens stays 1 KB aligned),
 // and at least 64 query rows per (row, KV head).
+// head_dim 64 runs the two-query-tile kernel unless switched off (parity tests
+// compare the two)
+bool g_prefill_pair = true;
+
 bool prefill_eligible(const pse_block_state& st, const pse_kv_layer& kv, const void* q, int64_t q_tok_stride,
                       const void* out, int64_t out_tok_stride, int q_heads, int width) {
   if (kv.dtype != PSE_BF16 || (kv.head_dim != 64 && kv.head_dim != 128)) return false;
@@ -663,7 +1142,8 @@ int prefill_attention(const pse_block_state& st, const pse_kv_layer& kv, const v
   CUtensorMap mq;
   rc = gemm::tensor_map(q, (int64_t)rows * width, (int64_t)q_heads * kv.head_dim, q_tok_stride, a.tpt, &mq);
   if (rc) return rc;
-  return kv.head_dim == 64 ? pf::launch<64>(mk, mv, mq, a, s) : pf::launch<128>(mk, mv, mq, a, s);
+  if (kv.head_dim == 64) return g_prefill_pair ? pf::launch_pair(mk, mv, mq, a, s) : pf::launch<64>(mk, mv, mq, a, s);
+  return pf::launch<128>(mk, mv, mq, a, s);
 }
 
 }  // namespace pse

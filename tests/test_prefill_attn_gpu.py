@@ -119,7 +119,17 @@ def test_prefill_attention_matches_previous_kernel(case):
     assert np.abs(new - old).max() < BF16_TOL
 
 
+@pytest.mark.parametrize("case", [c for c in CASES if c[4] == 64])
+def test_pair_and_single_tile_kernels_agree(case):
+    """head_dim 64 runs two query tiles per CTA by default; the one-tile kernel
+    (mode 2) must give the same rows, padding included."""
+    pair = _run(case, seed=11, ragged=True)
+    single = _run(case, seed=11, ragged=True, select=2)
+    assert np.abs(pair[0] - single[0]).max() < BF16_TOL
+    assert ((pair[0] == 0) == (single[0] == 0)).all()
+
+
 def test_prefill_select_rejects_unknown_mode():
     N = _N()
-    assert N.load().pse_attention_prefill_select(2) != 0
+    assert N.load().pse_attention_prefill_select(3) != 0
     assert N.load().pse_attention_prefill_select(-1) != 0
