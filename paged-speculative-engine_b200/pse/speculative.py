@@ -20,6 +20,7 @@ passing them back unchanged (as the scheduler does) costs no copy.
 """
 from __future__ import annotations
 
+import operator
 from dataclasses import dataclass
 
 import numpy as np
@@ -475,17 +476,17 @@ class StepRunner:
         stt = st_np.tolist()
         if not defer_bonus and tc.deferred_slots and not tc.deferred_slots.isdisjoint(stt):
             raise ValueError("request is in the deferred-bonus state: keep stepping it with defer_bonus=True")
-        for r, s in zip(request_ids, sd):
-            t = draft_next_logits[r]
-            v = dviews[s]
-            if t is not v and t.data_ptr() != v.data_ptr():
-                v.copy_(t.reshape(-1), non_blocking=True)
-        if not defer_bonus:
-            for r, s in zip(request_ids, stt):
-                t = target_next_logits[r]
-                v = tviews[s]
-                if t is not v and t.data_ptr() != v.data_ptr():
-                    v.copy_(t.reshape(-1), non_blocking=True)
+        # logits handed back unchanged (the previous step's views) need no copy
+        for given, views, slots in ((draft_next_logits, dviews, sd),
+                                    (None if defer_bonus else target_next_logits, tviews, stt)):
+            if given is None:
+                continue
+            vals = [given[r] for r in request_ids]
+            own = [views[x] for x in slots]
+            if not all(map(operator.is_, vals, own)):
+                for t, v in zip(vals, own):
+                    if t is not v and t.data_ptr() != v.data_ptr():
+                        v.copy_(t.reshape(-1), non_blocking=True)
         steps = self.request_steps
         key_np = steps_np = None
         if float(temperature) > 0 and uniforms is None and generator is None:
@@ -493,13 +494,12 @@ class StepRunner:
             steps_np = np.fromiter((steps.get(r, 0) for r in request_ids), np.int32, B)
         b, nacc_np = self._run(request_ids, sd_np, st_np, temperature, generator, uniforms, use_graph, defer_bonus,
                                key_np, steps_np)
-        hpn = b.host_pack_np
-        toks = hpn[:B * (k + 1)].reshape(B, k + 1).tolist()
+        toks = b.host_pack_np[:B * (k + 1)].reshape(B, k + 1).tolist()
         nacc = nacc_np.tolist()
         accepted = {r: toks[i][: nacc[i] + 1] for i, r in enumerate(request_ids)}
         n_acc = dict(zip(request_ids, nacc))
-        dn = {r: dviews[s] for r, s in zip(request_ids, sd)}
-        tn = dict.fromkeys(request_ids) if defer_bonus else {r: tviews[s] for r, s in zip(request_ids, stt)}
+        dn = dict(zip(request_ids, map(dviews.__getitem__, sd)))
+        tn = dict.fromkeys(request_ids) if defer_bonus else dict(zip(request_ids, map(tviews.__getitem__, stt)))
         for r in request_ids:
             steps[r] = steps.get(r, 0) + 1
         return BatchStepResult(accepted, n_acc, dn, tn)
