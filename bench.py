@@ -19,6 +19,7 @@ path (the oracle port, fp32) on a bounded sample.
 from __future__ import annotations
 
 import argparse
+import gc
 import json
 import math
 import os
@@ -135,14 +136,19 @@ def build_pair(workload, dtype, device, seed=0):
     return d.eval(), t.eval()
 
 
-def cache_for(model, workload, n_rows, dtype, device, extra_tokens):
+def cache_for(model, workload, n_rows, dtype, device, extra_tokens, prompts=None):
+    """A pool for n_rows requests of the workload: every row sized for the
+    longest prompt, or, given the prompts, for each prompt's own length."""
     import pse
     cfg = model.cfg
     kv = getattr(cfg, "n_kv_heads", cfg.n_heads)
     hd = cfg.d_model // cfg.n_heads
     bs = workload.block_size
     per_row = workload.prompt_hi + workload.max_new_tokens + extra_tokens
-    nb = n_rows * ((per_row + bs - 1) // bs) + 8
+    if prompts is None:
+        nb = n_rows * ((per_row + bs - 1) // bs) + 8
+    else:
+        nb = sum((len(p) + workload.max_new_tokens + extra_tokens + bs - 1) // bs for p in prompts) + 8
     return pse.PagedKVCache(cfg.n_layers, kv, hd, bs, nb, dtype=dtype, device=device, max_requests=n_rows,
                             max_blocks_per_request=(per_row + bs - 1) // bs)
 
@@ -584,8 +590,8 @@ def micro_scheduler(args, device):
     out = {}
     for run in ("warm", "timed"):
         reqs = [Request(f"{run}{i}", p, w.max_new_tokens) for i, p in enumerate(prompts)]
-        dc = cache_for(d, w, n, dtype, device, w.k + 2)
-        tc = cache_for(t, w, n, dtype, device, w.k + 2)
+        dc = cache_for(d, w, n, dtype, device, w.k + 2, prompts)
+        tc = cache_for(t, w, n, dtype, device, w.k + 2, prompts)
         torch.cuda.synchronize()
         t0 = time.perf_counter()
         if args.sched_mode == "plain":
@@ -599,7 +605,11 @@ def micro_scheduler(args, device):
         out[run] = (time.perf_counter() - t0, sum(len(r.output_ids) - len(p) for r, p in
                                                    zip(sorted(res, key=lambda r: int(r.request_id[len(run):])),
                                                        prompts)))
-        del dc, tc
+        # the caches hold their step runners (and those their graphs): free
+        # the warm-up run's pools before the timed run allocates its own
+        del dc, tc, res
+        gc.collect()
+        torch.cuda.empty_cache()
     secs, toks = out["timed"]
     cpu = None
     if not args.no_cpu_baseline and args.sched_mode == "spec":
