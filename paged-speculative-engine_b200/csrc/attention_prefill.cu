@@ -706,14 +706,22 @@ __device__ __forceinline__ PairItem decode_pair(const Args& a, int e) {
   return it;
 }
 
-// Warp roles as in the one-tile kernel: warps 0..3 and 4..7 are the two
-// softmax warpgroups, warp 8 TMA, warp 9 MMA.
+// Warps 0..15 are four softmax warpgroups: warpgroup 2k + h handles query tile
+// k's key columns 64h .. 64h + 63 (each thread 64 scores: no spills at the
+// register cap of 18 warps, four softmax warps per SMSP); warp 16 TMA, warp 17
+// MMA.
+constexpr int kPairThreads = 18 * 32;
+constexpr int kPairProducer = 16, kPairMma = 17;
+constexpr int kPairSoftmax = 256;  // softmax threads per query tile
+
 constexpr size_t pair_smem_bytes() {
-  // align slack + Q (two buffers x two tiles) + ring + barriers
-  return 1024 + (size_t)2 * 2 * BQ * 64 * 2 + (size_t)3 * 2 * BKV * 64 * 2 + 256;
+  // align slack + Q (two buffers x two tiles) + ring + barriers + the column
+  // halves' row exchange (2 tiles x 2 query tiles x 2 halves x 128 maxima,
+  // 2 query tiles x 2 halves x 128 sums)
+  return 1024 + (size_t)2 * 2 * BQ * 64 * 2 + (size_t)3 * 2 * BKV * 64 * 2 + 256 + (size_t)12 * BQ * 4;
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kPairThreads, 1)
     prefill_pair_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                         const __grid_constant__ CUtensorMap tmq, Args a) {
   constexpr int HD = 64, S = 3;
@@ -725,17 +733,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* ring = q_s + 4 * kQBytes;        // [S][K tile | V tile]
   uint64_t* full = reinterpret_cast<uint64_t*>(ring + S * 2 * kTileBytes);
   uint64_t* empty = full + S;
-  uint64_t* s_full = empty + S;     // [2] per warpgroup: its scores of a tile are in TMEM
-  uint64_t* s_free = s_full + 2;    // [2] per warpgroup: it has loaded them (128 arrivals)
-  uint64_t* p_full = s_free + 2;    // [2] per warpgroup: P written, output rescaled (128 arrivals)
-  uint64_t* pv_done = p_full + 2;   // [2] per warpgroup: its O += P V retired
+  uint64_t* s_full = empty + S;     // [2] per query tile: its scores of a tile are in TMEM
+  uint64_t* s_free = s_full + 2;    // [2] per query tile: they have been loaded (256 arrivals)
+  uint64_t* p_full = s_free + 2;    // [2] per query tile: P written, output rescaled (256 arrivals)
+  uint64_t* pv_done = p_full + 2;   // [2] per query tile: its O += P V retired
   uint64_t* q_full = pv_done + 2;   // [2] per Q buffer: the item's two Q tiles landed
   uint64_t* q_empty = q_full + 2;   // [2] per Q buffer: the item's score MMAs retired
   uint64_t* final_bar = q_empty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(final_bar + 1);
+  uint64_t* pair_bar = final_bar + 1;  // [2 query tiles][4 lane quarters]: column halves' exchange (64)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pair_bar + 8);
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
   int* issued = abort_flag + 1;
   int* issued_q = issued + 1;
+  float* xmax = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(full) + 256);  // [2][2][2][128]
+  float* xsum = xmax + 8 * BQ;                                                      // [2][2][128]
   volatile int* vabort = abort_flag;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -746,19 +757,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int k = 0; k < 2; ++k) {
       mbar_init(&s_full[k], 1);
-      mbar_init(&s_free[k], BQ);
-      mbar_init(&p_full[k], BQ);
+      mbar_init(&s_free[k], kPairSoftmax);
+      mbar_init(&p_full[k], kPairSoftmax);
       mbar_init(&pv_done[k], 1);
       mbar_init(&q_full[k], 1);
       mbar_init(&q_empty[k], 1);
     }
     mbar_init(final_bar, 1);
+    for (int x = 0; x < 8; ++x) mbar_init(&pair_bar[x], 64);
     *abort_flag = 0;
     *issued = 0;
     *issued_q = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == kMmaWarp) {
+  if (warp == kPairMma) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(tmem_slot)),
                  "r"(kTmemCols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
@@ -769,7 +781,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = *tmem_slot;
   const int n_items = a.rows * a.kv_heads * ((a.n_qtiles + 1) / 2);
 
-  if (warp == kProducerWarp) {
+  if (warp == kPairProducer) {
     // ------------------------------------------------------------ producer
     const int bs = a.block_size, ppt = BKV / bs;
     int g = 0, nq = 0;
@@ -834,7 +846,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ++g;
       }
     }
-  } else if (warp == kMmaWarp) {
+  } else if (warp == kPairMma) {
     // ------------------------------------------------------------ MMA issue
     if (lane == 0) {
       constexpr uint32_t idesc_s = instr_desc(BKV, 0);
@@ -908,13 +920,24 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ softmax
-    const int k = warp >> 2, q4 = warp & 3;  // warpgroup k owns query tile k of the pair
-    const int r = 32 * q4 + lane;
+    const int k = warp >> 3;            // query tile of the pair
+    const int half = (warp >> 2) & 1;   // key columns 64 * half .. + 63, output columns 32 * half .. + 31
+    const int q4 = warp & 3;
+    const int r = 32 * q4 + lane;       // tile row = TMEM lane
     const uint32_t lane_base = tmem + ((uint32_t)(32 * q4) << 16);
-    const uint32_t s_col = kColS + k * BKV, o_col = kColO + k * HD;
+    const uint32_t s_col = kColS + k * BKV + half * (BKV / 2), o_col = kColO + k * HD + half * (HD / 2);
+    const uint32_t p_col = kColP + k * (BKV / 2) + half * (BKV / 4);
     const int gq = r / a.tpt, wr = r % a.tpt;
     const float sl2 = a.scale_log2;
-    int gk = 0;  // tiles this warpgroup has processed
+    constexpr int kCols = BKV / 2, kOCols = HD / 2;
+    uint64_t* const xbar = &pair_bar[k * 4 + q4];
+    int nx = 0;  // exchanges with the other column half so far (its barrier phase)
+    auto exchange = [&]() -> bool {  // after this thread's arrive: wait for the partner's
+      const bool ok = mbar_wait(xbar, nx & 1, vabort);
+      ++nx;
+      return __all_sync(0xffffffffu, ok);
+    };
+    int gk = 0;  // tiles of this query tile processed
     bool run = true;
     for (int e = blockIdx.x; run && e < n_items; e += gridDim.x) {
       const PairItem it = decode_pair(a, e);
@@ -923,12 +946,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int pos = it.base + w;
       const bool valid = row_ok && pos < it.len;
       const int h = it.hk * a.group + gq;
-      __nv_bfloat16* orow = a.out + ((int64_t)it.i * a.width + w) * a.out_tok_stride + (int64_t)h * HD;
+      __nv_bfloat16* orow = a.out + ((int64_t)it.i * a.width + w) * a.out_tok_stride + (int64_t)h * HD + half * kOCols;
       const int n = it.n[k];
       if (n == 0) {
         if (row_ok) {
 #pragma unroll
-          for (int c = 0; c < HD / 8; ++c) *reinterpret_cast<uint4*>(orow + c * 8) = make_uint4(0, 0, 0, 0);
+          for (int c = 0; c < kOCols / 8; ++c) *reinterpret_cast<uint4*>(orow + c * 8) = make_uint4(0, 0, 0, 0);
         }
         continue;
       }
@@ -940,30 +963,38 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         tc_fence_after();
-        float sc[BKV];
+        float sc[kCols];
         {
           uint32_t* u = reinterpret_cast<uint32_t*>(sc);
 #pragma unroll
-          for (int c = 0; c < BKV / 32; ++c) tmem_ld32(lane_base + s_col + c * 32, u + c * 32);
+          for (int c = 0; c < kCols / 32; ++c) tmem_ld32(lane_base + s_col + c * 32, u + c * 32);
           tmem_wait_ld();
         }
         // the scores are in registers: the MMA may write the next ones
         tc_fence_before();
         mbar_arrive(&s_free[k]);
-        const int key0 = j * BKV;
-        if (key0 + BKV > lim) {
+        const int key0 = j * BKV + half * kCols;
+        if (key0 + kCols > lim) {
 #pragma unroll
-          for (int c = 0; c < BKV; ++c) sc[c] = key0 + c < lim ? sc[c] : -INFINITY;
+          for (int c = 0; c < kCols; ++c) sc[c] = key0 + c < lim ? sc[c] : -INFINITY;
         }
-        float m8[8];
+        float m4[4];
 #pragma unroll
-        for (int x = 0; x < 8; ++x) m8[x] = sc[x];
+        for (int x = 0; x < 4; ++x) m4[x] = sc[x];
 #pragma unroll
-        for (int c = 8; c < BKV; ++c) m8[c & 7] = fmaxf(m8[c & 7], sc[c]);
-        const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
-                               fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7]))) * sl2;
+        for (int c = 4; c < kCols; ++c) m4[c & 3] = fmaxf(m4[c & 3], sc[c]);
+        const float pm = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+        float* xm = xmax + ((gk & 1) * 4 + k * 2) * BQ;
+        xm[half * BQ + r] = pm;
+        mbar_arrive(xbar);
+        if (!exchange()) {
+          run = false;
+          break;
+        }
+        const float mx = fmaxf(pm, xm[(half ^ 1) * BQ + r]) * sl2;
         // the row's reference maximum moves only when it would grow by more
-        // than 8 (exponents stay <= 2^8); the output is rescaled then
+        // than 8 (exponents stay <= 2^8); the output is rescaled then.  Both
+        // column halves see the same maximum, so they decide alike.
         float corr = 1.f;
         bool rescale = false;
         if (mx > m_used + 8.f) {
@@ -974,38 +1005,33 @@ __global__ void __launch_bounds__(kThreads, 1)
           m_used = mx;
         }
         const float msub = m_used == -INFINITY ? 0.f : m_used;
-        float s8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        float s4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int c = 0; c < BKV; ++c) {
+        for (int c = 0; c < kCols; ++c) {
           sc[c] = ex2(fmaf(sc[c], sl2, -msub));
-          s8[c & 7] += sc[c];
+          s4[c & 3] += sc[c];
         }
-        l = l * corr + (((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7])));
-        // this warpgroup's previous P V has retired: its P buffer and output are free
+        l = l * corr + ((s4[0] + s4[1]) + (s4[2] + s4[3]));
+        // this query tile's previous P V has retired: its P and output are free
         if (gk > 0 && !__all_sync(0xffffffffu, mbar_wait(&pv_done[k], (gk - 1) & 1, vabort))) {
           run = false;
           break;
         }
         tc_fence_after();
-        if (__any_sync(0xffffffffu, rescale)) {
+        {
+          // this half's 64 keys of P as bf16 pairs into TMEM (the PV MMA's A operand)
+          uint32_t pk[kCols / 2];
 #pragma unroll
-          for (int c = 0; c < HD / 32; ++c) {
-            uint32_t o[32];
-            tmem_ld32(lane_base + o_col + c * 32, o);
-            tmem_wait_ld();
-#pragma unroll
-            for (int x = 0; x < 32; ++x) o[x] = __float_as_uint(__uint_as_float(o[x]) * corr);
-            tmem_st32(lane_base + o_col + c * 32, o);
-          }
-          tmem_wait_st();
+          for (int c = 0; c < kCols / 2; ++c) pk[c] = pack_bf16(sc[2 * c], sc[2 * c + 1]);
+          tmem_st32(lane_base + p_col, pk);
         }
+        if (__any_sync(0xffffffffu, rescale)) {
+          uint32_t o[32];
+          tmem_ld32(lane_base + o_col, o);
+          tmem_wait_ld();
 #pragma unroll
-        for (int c0 = 0; c0 < BKV / 2; c0 += 32) {
-          // P as bf16 pairs into this warpgroup's TMEM columns (the PV MMA's A operand)
-          uint32_t pk[32];
-#pragma unroll
-          for (int c = 0; c < 32; ++c) pk[c] = pack_bf16(sc[2 * (c0 + c)], sc[2 * (c0 + c) + 1]);
-          tmem_st32(lane_base + kColP + k * (BKV / 2) + c0, pk);
+          for (int x = 0; x < 32; ++x) o[x] = __float_as_uint(__uint_as_float(o[x]) * corr);
+          tmem_st32(lane_base + o_col, o);
         }
         tmem_wait_st();
         tc_fence_before();
@@ -1013,24 +1039,27 @@ __global__ void __launch_bounds__(kThreads, 1)
         ++gk;
       }
       if (!run) break;
+      // the item's output: O / l once the last P V has retired; the row's sum
+      // is the two halves' partial sums (same reference maximum)
+      xsum[(k * 2 + half) * BQ + r] = l;
+      mbar_arrive(xbar);
+      if (!exchange()) break;
+      const float L = l + xsum[(k * 2 + (half ^ 1)) * BQ + r];
       if (!__all_sync(0xffffffffu, mbar_wait(&pv_done[k], (gk - 1) & 1, vabort))) break;
       tc_fence_after();
-      const float inv = valid && l > 0.f ? 1.f / l : 0.f;
+      const float inv = valid && L > 0.f ? 1.f / L : 0.f;
+      uint32_t o[32];
+      tmem_ld32(lane_base + o_col, o);
+      tmem_wait_ld();
+      if (row_ok) {
 #pragma unroll
-      for (int c = 0; c < HD / 32; ++c) {
-        uint32_t o[32];
-        tmem_ld32(lane_base + o_col + c * 32, o);
-        tmem_wait_ld();
-        if (row_ok) {
-#pragma unroll
-          for (int x = 0; x < 32; x += 8) {
-            uint4 v;
-            v.x = pack_bf16(__uint_as_float(o[x + 0]) * inv, __uint_as_float(o[x + 1]) * inv);
-            v.y = pack_bf16(__uint_as_float(o[x + 2]) * inv, __uint_as_float(o[x + 3]) * inv);
-            v.z = pack_bf16(__uint_as_float(o[x + 4]) * inv, __uint_as_float(o[x + 5]) * inv);
-            v.w = pack_bf16(__uint_as_float(o[x + 6]) * inv, __uint_as_float(o[x + 7]) * inv);
-            *reinterpret_cast<uint4*>(orow + c * 32 + x) = v;
-          }
+        for (int x = 0; x < 32; x += 8) {
+          uint4 v;
+          v.x = pack_bf16(__uint_as_float(o[x + 0]) * inv, __uint_as_float(o[x + 1]) * inv);
+          v.y = pack_bf16(__uint_as_float(o[x + 2]) * inv, __uint_as_float(o[x + 3]) * inv);
+          v.z = pack_bf16(__uint_as_float(o[x + 4]) * inv, __uint_as_float(o[x + 5]) * inv);
+          v.w = pack_bf16(__uint_as_float(o[x + 6]) * inv, __uint_as_float(o[x + 7]) * inv);
+          *reinterpret_cast<uint4*>(orow + x) = v;
         }
       }
       tc_fence_before();
@@ -1040,14 +1069,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   if (*vabort) {
     if (tid == 0) atomicOr(a.status, PSE_STATUS_TIMEOUT);
-    if (warp == kProducerWarp && lane == 0) {
+    if (warp == kPairProducer && lane == 0) {
       const int n = *issued;
       for (int t = n > S ? n - S : 0; t < n; ++t) mbar_drain(&full[t % S], (t / S) & 1);
       const int nq = *issued_q;
       for (int t = nq > 2 ? nq - 2 : 0; t < nq; ++t) mbar_drain(&q_full[t & 1], (t >> 1) & 1);
     }
   }
-  if (warp == kMmaWarp) {
+  if (warp == kPairMma) {
     if (lane == 0) mbar_drain(final_bar, 0);
     __syncwarp();
     tc_fence_after();
@@ -1066,7 +1095,7 @@ int launch_pair(const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap&
   const long long items = (long long)a.rows * a.kv_heads * ((a.n_qtiles + 1) / 2);
   const int grid = items < sms ? (int)items : sms;
   if (grid <= 0) return PSE_OK;
-  prefill_pair_kernel<<<grid, kThreads, smem, s>>>(mk, mv, mq, a);
+  prefill_pair_kernel<<<grid, kPairThreads, smem, s>>>(mk, mv, mq, a);
   PSE_LAUNCH_CHECK();
   return PSE_OK;
 }
