@@ -320,6 +320,7 @@ class StepRunner:
         self.tpending = None  # per target slot: token not yet appended (deferred-bonus mode)
         self.commit: CommitArena | None = None  # the scheduler's device output arena
         self._slots_key, self._slots_ids, self._slots_np = None, None, None
+        self._ws_sizes: dict = {}  # (rows, draft / target context bound) -> split-KV workspace bytes
 
     # ---------------------------------------------------------------- device program
     def _ctx_bound(self, cache, dm) -> int:
@@ -460,7 +461,8 @@ class StepRunner:
         B = len(request_ids)
         if B == 0:
             return BatchStepResult({}, {}, {}, {})
-        if len(set(request_ids)) != B:
+        # (the previous step's list, unchanged, is known to be unique)
+        if self._slots_ids != request_ids and len(set(request_ids)) != B:
             raise ValueError("request_ids must be unique")
         dc, tc = self.dcache, self.tcache
         # slot arrays: reused while the request list and the slot assignment are unchanged
@@ -579,14 +581,16 @@ class StepRunner:
             # size every buffer the program touches before the graph key is taken
             self.sc_d.ensure(2 * B)
             self.sc_t.ensure(B * (k + 1))
-            dmd, dmt = self.dm_d, self.dm_t
-            self.sc_d.ensure_ws(max(
-                N.size_call("pse_paged_attention_workspace", B, 1, dmd.q_heads, dmd.kv_heads, dmd.head_dim, mcd),
-                N.size_call("pse_paged_attention_workspace", B, 2, dmd.q_heads, dmd.kv_heads, dmd.head_dim, mcd)))
-            self.sc_t.ensure_ws(max(
-                N.size_call("pse_paged_attention_workspace", B, k + 1, dmt.q_heads, dmt.kv_heads, dmt.head_dim, mct),
-                N.size_call("pse_paged_attention_workspace", B, k, dmt.q_heads, dmt.kv_heads, dmt.head_dim, mct),
-                N.size_call("pse_paged_attention_workspace", B, 1, dmt.q_heads, dmt.kv_heads, dmt.head_dim, mct)))
+            ws = self._ws_sizes.get((B, mcd, mct))
+            if ws is None:
+                dmd, dmt = self.dm_d, self.dm_t
+                ws = self._ws_sizes[(B, mcd, mct)] = (
+                    max(N.size_call("pse_paged_attention_workspace", B, w, dmd.q_heads, dmd.kv_heads, dmd.head_dim,
+                                    mcd) for w in (1, 2)),
+                    max(N.size_call("pse_paged_attention_workspace", B, w, dmt.q_heads, dmt.kv_heads, dmt.head_dim,
+                                    mct) for w in (k + 1, k, 1)))
+            self.sc_d.ensure_ws(ws[0])
+            self.sc_t.ensure_ws(ws[1])
         key = (B, T, philox, defer_bonus, dc.generation, tc.generation, self.sc_d.generation, self.sc_t.generation,
                None if self.tpending is None else self.tpending.data_ptr(),
                None if commit is None else (id(commit), commit.generation))
