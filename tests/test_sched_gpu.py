@@ -158,3 +158,38 @@ def test_on_step_with_device_bookkeeping_is_refused():
     d, t = _pair()
     with pytest.raises(ValueError):
         _run(d, t, [pse.Request("a", [1, 2], 3)], 2, 2, 0.0, device_bookkeeping=True, on_step=lambda i, r: None)
+
+
+def _state(cache):
+    return ({r: cache.block_table(r) for r in cache._slot}, dict(cache._lengths), cache.allocator.free_list())
+
+
+def test_device_bookkeeping_raises_like_host_loop_when_the_pool_runs_dry():
+    """A pool too small for the run: both loops raise MemoryError at the same
+    step and leave both caches (tables, lengths, free lists) in the same state."""
+    import pse
+    d, t = _pair()
+    rng = np.random.default_rng(9)
+    prompts = [rng.integers(0, 64, size=12).tolist() for _ in range(4)]
+    states = []
+    for dev in (True, False):
+        reqs = [pse.Request(f"m{i}", p, 40) for i, p in enumerate(prompts)]
+        dc = pse.PagedKVCache(2, 2, 16, 8, 14)
+        tc = pse.PagedKVCache(3, 4, 16, 8, 14)
+        with pytest.raises(MemoryError):
+            pse.run_continuous_speculative_batches(d, t, reqs, dc, tc, 4, k=3, temperature=0.0,
+                                                   device_bookkeeping=dev)
+        states.append((_state(dc), _state(tc)))
+    assert states[0] == states[1]
+
+
+def test_device_bookkeeping_rejects_duplicate_ids_like_host_loop():
+    import pse
+    d, t = _pair()
+    for dev in (True, False):
+        reqs = [pse.Request("dup", [1, 2, 3], 4), pse.Request("dup", [4, 5], 4)]
+        dc = pse.PagedKVCache(2, 2, 16, 8, 64)
+        tc = pse.PagedKVCache(3, 4, 16, 8, 64)
+        with pytest.raises(ValueError):
+            pse.run_continuous_speculative_batches(d, t, reqs, dc, tc, 4, k=2, temperature=0.0,
+                                                   device_bookkeeping=dev)
