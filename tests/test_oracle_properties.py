@@ -1,0 +1,211 @@
+"""Properties of the CPU oracle itself, beyond the golden vectors: the
+reference's own property tests (tests/test_paged_cache_properties.py:34-100,
+tests/test_scheduler_properties.py:49-81) run against the oracle, the
+device-allocator restatement (``oracle.alloc.BlockState``) against the
+sequential cache under random op sequences, the greedy accept rule, the
+scheduler's per-row commit, and Philox4x32-10 against the published
+known-answer vectors.  CPU only."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+from hypothesis import HealthCheck, given, settings
+from hypothesis import strategies as st
+
+from oracle import alloc
+from oracle.accept import accept_row
+from oracle.generate import generate_cached
+from oracle.model import ModelConfig, TinyGPT
+from oracle.paged_cache import PagedKVCache
+from oracle.philox import philox4x32_10
+from oracle.scheduler import Request, commit_rows, run_continuous_speculative_batches
+
+
+# Random123's kat_vectors for philox4x32_10: (counter, key) -> output words.
+PHILOX_KAT = [
+    ((0, 0, 0, 0), (0, 0), (0x6627E8D5, 0xE169C58D, 0xBC57AC4C, 0x9B00DBD8)),
+    ((0xFFFFFFFF,) * 4, (0xFFFFFFFF,) * 2, (0x408F276D, 0x41C83B0E, 0xA20BC7C6, 0x6D5451FD)),
+    ((0x243F6A88, 0x85A308D3, 0x13198A2E, 0x03707344), (0xA4093822, 0x299F31D0),
+     (0xD16CFE09, 0x94FDCCEB, 0x5001E420, 0x24126EA1)),
+]
+
+
+def test_philox_known_answers():
+    for ctr, key, want in PHILOX_KAT:
+        got = philox4x32_10(np.array(ctr, dtype=np.uint32), np.array(key, dtype=np.uint32))
+        assert [int(x) for x in got] == list(want)
+    # vectorised form: the same vectors stacked give the same words
+    ctrs = np.array([c for c, _, _ in PHILOX_KAT], dtype=np.uint32)
+    keys = np.array([k for _, k, _ in PHILOX_KAT], dtype=np.uint32)
+    assert philox4x32_10(ctrs, keys).tolist() == [list(w) for _, _, w in PHILOX_KAT]
+
+
+NUM_BLOCKS = 16
+RIDS = ("a", "b", "c")
+OP = st.one_of(
+    st.tuples(st.just("append"), st.sampled_from(RIDS), st.integers(1, 9)),
+    st.tuples(st.just("truncate"), st.sampled_from(RIDS), st.integers(0, 40)),
+    st.tuples(st.just("free"), st.sampled_from(RIDS), st.just(0)),
+)
+
+
+@settings(max_examples=150, deadline=None, suppress_health_check=[HealthCheck.too_slow])
+@given(ops=st.lists(OP, min_size=1, max_size=40), block_size=st.integers(1, 5), seed=st.integers(0, 2**16))
+def test_block_state_tracks_sequential_cache(ops, block_size, seed):
+    """The reference's cache property (block conservation after every op,
+    content fidelity through gather) on the oracle cache, with the batched
+    prefix-scan restatement driven alongside: same tables, lengths and free
+    list after every op, exhaustion included (the reference's test discards
+    exhausted draws; here both sides must agree on the state they leave)."""
+    g = torch.Generator().manual_seed(seed)
+    cache = PagedKVCache(1, 2, 3, block_size, NUM_BLOCKS)
+    bs = alloc.BlockState(NUM_BLOCKS, block_size, num_slots=len(RIDS), max_blocks=NUM_BLOCKS + 10)
+    slot = {r: i for i, r in enumerate(RIDS)}
+    shadow: dict[str, list[torch.Tensor]] = {}
+    for r in RIDS:
+        cache.create_request(r)
+        shadow[r] = []
+    for kind, r, n in ops:
+        if kind == "append":
+            k = torch.randn(2, n, 3, generator=g)
+            try:
+                cache.append(r, [k], [k + 1])
+            except MemoryError:
+                bs.status = 0
+                bs.reserve([slot[r]], n)
+                assert bs.status & alloc.OOM
+                # the reference keeps the blocks the failed append got; the
+                # row's length (and so what gather returns) is unchanged
+                bs.status = 0
+            else:
+                bs.reserve([slot[r]], n)
+                assert bs.status == 0
+                shadow[r].extend(k.unbind(1))
+        elif kind == "truncate":
+            m = min(n, cache.length(r))
+            cache.truncate(r, m)
+            bs.truncate([slot[r]], [m])
+            del shadow[r][m:]
+        else:
+            cache.free_request(r)
+            cache.create_request(r)
+            bs.release([slot[r]])
+            shadow[r] = []
+        assert bs.status == 0
+        used = sum(cache.num_blocks_in_use(x) for x in RIDS)
+        assert cache.allocator.num_free + used == NUM_BLOCKS
+        assert bs.free_list() == cache.allocator.free_list()
+        for x in RIDS:
+            assert bs.row_table(slot[x]) == cache.block_table(x)
+            assert int(bs.seq_len[slot[x]]) == cache.length(x)
+    lens = [cache.length(x) for x in RIDS]
+    if max(lens) == 0:
+        return
+    (kk,), (vv,), mask, _ = cache.gather(list(RIDS))
+    for i, x in enumerate(RIDS):
+        assert mask[i].tolist() == [j < lens[i] for j in range(max(lens))]
+        if lens[i]:
+            want = torch.stack(shadow[x], 1)
+            assert torch.equal(kk[i, :, : lens[i]], want)
+            assert torch.equal(vv[i, :, : lens[i]], want + 1)
+        assert not kk[i, :, lens[i]:].any()
+
+
+def test_block_state_reports_errors_instead_of_raising():
+    """The reference raises ValueError on truncate past the length
+    (engine/paged_cache.py:140-154) and on a double free (:50-56); the
+    restatement records them in its status word, which the device mirrors."""
+    bs = alloc.BlockState(8, 2, num_slots=2, max_blocks=8)
+    bs.reserve([0], 3)
+    bs.truncate([0], [5])
+    assert bs.status & alloc.TRUNCATE_BEYOND_LENGTH
+    assert int(bs.seq_len[0]) == 3 and bs.row_table(0) == [7, 6]
+    bs.status = 0
+    bs._push([[0]])  # block 0 is still free
+    assert bs.status & alloc.DOUBLE_FREE
+    bs = alloc.BlockState(4, 2, num_slots=1, max_blocks=2)
+    bs.reserve([0], 5)
+    assert bs.status & alloc.TABLE_OVERFLOW and bs.free_list() == [0, 1, 2, 3]
+    cache = PagedKVCache(1, 1, 1, 2, 8)
+    cache.create_request("a")
+    cache.append("a", [torch.ones(1, 3, 1)], [torch.ones(1, 3, 1)])
+    with pytest.raises(ValueError):
+        cache.truncate("a", 5)
+    with pytest.raises(ValueError):
+        cache.allocator.free(0)
+    with pytest.raises(MemoryError):
+        cache.append("a", [torch.ones(1, 20, 1)], [torch.ones(1, 20, 1)])
+
+
+REQ = st.tuples(st.lists(st.integers(1, 31), min_size=1, max_size=5), st.integers(1, 8))
+
+
+@settings(max_examples=40, deadline=None, suppress_health_check=[HealthCheck.too_slow])
+@given(seed=st.integers(0, 1000), spec=st.lists(REQ, min_size=1, max_size=5, unique_by=lambda r: tuple(r[0])),
+       max_batch_size=st.integers(1, 4), k=st.integers(1, 5), block_size=st.integers(1, 5))
+def test_oracle_scheduler_matches_solo_generation(seed, spec, max_batch_size, k, block_size):
+    """The reference's main conformance property on the oracle: every request
+    through the continuous speculative scheduler at T = 0 equals its solo
+    ``generate_cached``, and both caches get every block back."""
+    torch.manual_seed(seed)
+    cfg = ModelConfig(vocab_size=32, d_model=12, n_layers=2, n_heads=2, d_ff=24, max_seq_len=256)
+    d, t = TinyGPT(cfg).eval(), TinyGPT(cfg).eval()
+    reqs = [Request(f"r{i}", p, m) for i, (p, m) in enumerate(spec)]
+    ceiling = sum(len(r.prompt_ids) + r.max_new_tokens + k + 1 for r in reqs)
+    nb = (ceiling // block_size + 1) * len(reqs) + 4
+    hd = cfg.d_model // cfg.n_heads
+    dc = PagedKVCache(cfg.n_layers, cfg.n_heads, hd, block_size, nb)
+    tc = PagedKVCache(cfg.n_layers, cfg.n_heads, hd, block_size, nb)
+    res = run_continuous_speculative_batches(d, t, reqs, dc, tc, max_batch_size, k=k, temperature=0.0)
+    by = {r.request_id: r.output_ids for r in res}
+    assert sorted(by) == sorted(r.request_id for r in reqs)
+    for r in reqs:
+        assert by[r.request_id] == generate_cached(t, torch.tensor([r.prompt_ids]), r.max_new_tokens)
+    assert dc.allocator.num_free == nb and tc.allocator.num_free == nb
+
+
+@settings(max_examples=300, deadline=None)
+@given(seed=st.integers(0, 2**31 - 1), k=st.integers(1, 6), vocab=st.integers(2, 9))
+def test_greedy_accept_is_longest_agreeing_prefix(seed, k, vocab):
+    """engine/speculative.py:146-155: at T = 0 the step keeps the drafts up to
+    the first one that differs from the target's argmax, then emits the
+    target's argmax there (or the bonus argmax when all k agree)."""
+    rng = np.random.default_rng(seed)
+    target = rng.standard_normal((k + 1, vocab)).astype(np.float32)
+    best = target.argmax(-1)
+    drafts = np.where(rng.random(k) < 0.7, best[:k], rng.integers(0, vocab, size=k))
+    tokens, n = accept_row(target, None, drafts, None, k, 0.0)
+    assert len(tokens) == n + 1
+    assert tokens[:n] == drafts[:n].tolist() == best[:n].tolist()
+    assert tokens[n] == best[n]
+    if n < k:
+        assert drafts[n] != best[n]
+
+
+@settings(max_examples=200, deadline=None)
+@given(seed=st.integers(0, 2**31 - 1), n_req=st.integers(1, 12), k=st.integers(1, 5))
+def test_commit_rows_counts_and_trims(seed, n_req, k):
+    """engine/scheduler.py:107-126 restated on row arrays: a request finishes
+    at the first step where its count reaches max_new and leaves exactly
+    max_new tokens; an unfinished one holds every token it accepted."""
+    rng = np.random.default_rng(seed)
+    max_new = rng.integers(0, 15, size=n_req).tolist()
+    generated = [0] * n_req
+    outputs: list[list[int]] = [[] for _ in range(n_req)]
+    stream: list[list[int]] = [[] for _ in range(n_req)]
+    live = list(range(n_req))
+    while live:
+        ords = [int(o) for o in rng.permutation(live)[: int(rng.integers(1, len(live) + 1))]]
+        tokens = rng.integers(0, 1000, size=(len(ords), k + 1))
+        n_acc = rng.integers(0, k + 1, size=len(ords))
+        before = list(generated)
+        fin = commit_rows(tokens.tolist(), n_acc.tolist(), ords, generated, max_new, outputs)
+        assert fin == sorted(fin)
+        for i, o in enumerate(ords):
+            stream[o].extend(tokens[i, : n_acc[i] + 1].tolist())
+            assert generated[o] == before[o] + n_acc[i] + 1
+            done = generated[o] >= max_new[o]
+            assert (i in fin) == done
+            assert outputs[o] == (stream[o][: max_new[o]] if done else stream[o])
+        live = [o for o in live if generated[o] < max_new[o]]
