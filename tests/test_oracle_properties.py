@@ -3,8 +3,9 @@ reference's own property tests (tests/test_paged_cache_properties.py:34-100,
 tests/test_scheduler_properties.py:49-81) run against the oracle, the
 device-allocator restatement (``oracle.alloc.BlockState``) against the
 sequential cache under random op sequences, the greedy accept rule, the
-scheduler's per-row commit, and Philox4x32-10 against the published
-known-answer vectors.  CPU only."""
+scheduler's per-row commit, the paged-attention oracle against the model's
+masked attention, and Philox4x32-10 against the published known-answer
+vectors.  CPU only."""
 from __future__ import annotations
 
 import numpy as np
@@ -209,3 +210,42 @@ def test_commit_rows_counts_and_trims(seed, n_req, k):
             assert (i in fin) == done
             assert outputs[o] == (stream[o][: max_new[o]] if done else stream[o])
         live = [o for o in live if generated[o] < max_new[o]]
+
+
+@pytest.mark.parametrize("rows,width,hq,hk,hd,bs,seed", [
+    (3, 1, 4, 4, 8, 4, 0),     # width-1 draft/bonus calls, MHA
+    (4, 6, 6, 2, 8, 3, 1),     # verify width k + 1, GQA 3, block size not a power of two
+    (2, 17, 8, 1, 4, 16, 2),   # prompt-shaped call, one KV head for all query heads
+    (5, 4, 2, 2, 16, 1, 3),    # block size 1
+])
+def test_paged_attention_oracle_equals_model_attention(rows, width, hq, hk, hd, bs, seed):
+    """The check of the paged-attention kernels (oracle.attention, float64 on
+    the block layout) against the model's own masked attention over the
+    reference cache's padded gather (engine/model.py:99-116 with the padding
+    mask of engine/batched_forward.py:44), on ragged rows whose blocks come
+    from one shared pool in allocation order."""
+    from oracle.attention import paged_attention
+    from oracle.model import _masked_attention
+    g = torch.Generator().manual_seed(seed)
+    base = torch.randint(0, 3 * bs + 5, (rows,), generator=g)
+    ctx = base + width
+    nb = int(sum((int(c) + bs - 1) // bs for c in ctx)) + 2
+    cache = PagedKVCache(1, hk, hd, bs, nb, dtype=torch.float64)
+    rids = [f"r{i}" for i in range(rows)]
+    for r in rids:
+        cache.create_request(r)
+    # interleaved appends so each row's blocks are scattered through the pool
+    done = [0] * rows
+    while any(done[i] < int(ctx[i]) for i in range(rows)):
+        for i, r in enumerate(rids):
+            n = min(int(torch.randint(1, 4, (1,), generator=g)), int(ctx[i]) - done[i])
+            if n > 0:
+                kv = torch.randn(2, hk, n, hd, generator=g, dtype=torch.float64)
+                cache.append(r, [kv[0]], [kv[1]])
+                done[i] += n
+    q = torch.randn(rows, hq, width, hd, generator=g, dtype=torch.float64)
+    (k,), (v,), mask, _ = cache.gather(rids)
+    want = _masked_attention(q, k, v, width, base, mask, None)  # [R, Hq, W, hd]
+    got = paged_attention(q.permute(0, 2, 1, 3).numpy(), cache._k_pool[0].numpy(), cache._v_pool[0].numpy(),
+                          [cache.block_table(r) for r in rids], base.tolist())
+    np.testing.assert_allclose(got, want.permute(0, 2, 1, 3).numpy(), rtol=0, atol=1e-12)
