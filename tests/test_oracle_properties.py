@@ -4,8 +4,9 @@ tests/test_scheduler_properties.py:49-81) run against the oracle, the
 device-allocator restatement (``oracle.alloc.BlockState``) against the
 sequential cache under random op sequences, the greedy accept rule, the
 scheduler's per-row commit, the paged-attention oracle against the model's
-masked attention, and Philox4x32-10 against the published known-answer
-vectors.  CPU only."""
+masked attention, the Llama-style restatement (RoPE, cached against
+recomputed decoding, the reference scheduler over GQA caches), and
+Philox4x32-10 against the published known-answer vectors.  CPU only."""
 from __future__ import annotations
 
 import numpy as np
@@ -249,3 +250,61 @@ def test_paged_attention_oracle_equals_model_attention(rows, width, hq, hk, hd, 
     got = paged_attention(q.permute(0, 2, 1, 3).numpy(), cache._k_pool[0].numpy(), cache._v_pool[0].numpy(),
                           [cache.block_table(r) for r in rids], base.tolist())
     np.testing.assert_allclose(got, want.permute(0, 2, 1, 3).numpy(), rtol=0, atol=1e-12)
+
+
+def test_rope_keeps_norms_and_depends_on_relative_position():
+    """The Llama-style restatement's rotary embedding: each rotation keeps the
+    vector's length, and a query-key dot product depends only on the distance
+    between their positions (shifting both leaves it unchanged)."""
+    from oracle.model import rope_rotate
+    g = torch.Generator().manual_seed(4)
+    q = torch.randn(1, 3, 1, 64, generator=g)
+    k = torch.randn(1, 3, 1, 64, generator=g)
+    for m, n, shift in ((0, 0, 7), (5, 2, 100), (300, 17, 4000), (1, 1000, 123)):
+        qm = rope_rotate(q, torch.tensor([[m]]), 10000.0)
+        kn = rope_rotate(k, torch.tensor([[n]]), 10000.0)
+        qs = rope_rotate(q, torch.tensor([[m + shift]]), 10000.0)
+        ks = rope_rotate(k, torch.tensor([[n + shift]]), 10000.0)
+        torch.testing.assert_close(qm.norm(dim=-1), q.norm(dim=-1), rtol=1e-5, atol=1e-5)
+        torch.testing.assert_close((qm * kn).sum(-1), (qs * ks).sum(-1), rtol=1e-4, atol=1e-4)
+    assert torch.equal(rope_rotate(q, torch.tensor([[0]]), 10000.0), q)
+
+
+def _llama_pair(seed):
+    from oracle.model import LlamaConfig, TinyLlama
+    torch.manual_seed(seed)
+    cfg = LlamaConfig(vocab_size=48, d_model=32, n_layers=2, n_heads=4, n_kv_heads=2, d_ff=64, max_seq_len=256)
+    return TinyLlama(cfg).eval(), TinyLlama(cfg).eval(), cfg
+
+
+@pytest.mark.parametrize("seed", [0, 1, 2])
+def test_llama_cached_generation_equals_full_recompute(seed):
+    """The Llama-style model follows the reference model's forward contract
+    (past_kv, position_offset; engine/model.py:158-206): greedy decoding over
+    its cache equals decoding that recomputes the whole sequence each token
+    (engine/generate.py:12-38), so RoPE positions and the GQA cache agree."""
+    from oracle.generate import generate_naive
+    _, t, _ = _llama_pair(seed)
+    rng = np.random.default_rng(seed)
+    for plen in (1, 5, 13):
+        prompt = torch.tensor([rng.integers(0, 48, size=plen).tolist()])
+        assert generate_cached(t, prompt, 12) == generate_naive(t, prompt, 12)
+
+
+@pytest.mark.parametrize("seed,k,block_size", [(0, 3, 4), (1, 1, 1), (2, 5, 3)])
+def test_llama_pair_through_the_reference_scheduler(seed, k, block_size):
+    """The reference scheduler drives the Llama-style pair unchanged over
+    caches of n_kv_heads heads: every request equals its solo greedy decode."""
+    d, t, cfg = _llama_pair(seed)
+    rng = np.random.default_rng(10 + seed)
+    reqs = [Request(f"q{i}", rng.integers(0, 48, size=int(rng.integers(1, 9))).tolist(), int(rng.integers(1, 10)))
+            for i in range(5)]
+    hd = cfg.d_model // cfg.n_heads
+    nb = 4 * sum(len(r.prompt_ids) + r.max_new_tokens + k + 1 for r in reqs) // block_size + 8
+    dc = PagedKVCache(cfg.n_layers, cfg.n_kv_heads, hd, block_size, nb)
+    tc = PagedKVCache(cfg.n_layers, cfg.n_kv_heads, hd, block_size, nb)
+    res = run_continuous_speculative_batches(d, t, reqs, dc, tc, 3, k=k, temperature=0.0)
+    by = {r.request_id: r.output_ids for r in res}
+    for r in reqs:
+        assert by[r.request_id] == generate_cached(t, torch.tensor([r.prompt_ids]), r.max_new_tokens)
+    assert dc.allocator.num_free == nb and tc.allocator.num_free == nb
