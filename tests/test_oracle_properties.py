@@ -308,3 +308,37 @@ def test_llama_pair_through_the_reference_scheduler(seed, k, block_size):
     for r in reqs:
         assert by[r.request_id] == generate_cached(t, torch.tensor([r.prompt_ids]), r.max_new_tokens)
     assert dc.allocator.num_free == nb and tc.allocator.num_free == nb
+
+
+@pytest.mark.parametrize("case", [
+    dict(seed=0, k=3, T=1.0, same=False),   # independent draft
+    dict(seed=1, k=1, T=0.7, same=False),
+    dict(seed=2, k=4, T=1.3, same=True),    # draft = target: every draft is accepted
+])
+def test_sampled_accept_preserves_the_target_distribution(case):
+    """The reference's distribution test (tests/test_distribution_preserving.py:
+    73-92: 4000 trials, vocab 12, chi-squared p > 0.01 on the first output
+    token against softmax(target / T)) on the explicit-uniform accept rule the
+    kernels implement: draft token 0 drawn from the draft distribution with
+    u[0], then accept / residual / bonus with u[k..2k]."""
+    from scipy.stats import chisquare
+    from oracle.sampling import sample_with_uniform
+    rng = np.random.default_rng(case["seed"])
+    k, T, V, trials = case["k"], case["T"], 12, 4000
+    target = (rng.standard_normal((k + 1, V)) * 1.5).astype(np.float32)
+    draft = target[:k].copy() if case["same"] else (rng.standard_normal((k, V)) * 1.5).astype(np.float32)
+    counts = np.zeros(V)
+    accepted_first = 0
+    for _ in range(trials):
+        u = rng.random(2 * k + 1)
+        drafts = [sample_with_uniform(draft[j], T, u[j]) for j in range(k)]
+        tokens, n = accept_row(target, draft, drafts, u, k, T)
+        counts[tokens[0]] += 1
+        accepted_first += n > 0
+    p = np.exp((target[0].astype(np.float64) - target[0].max()) / T)
+    p /= p.sum()
+    keep = p * trials >= 5  # the reference renormalises over the cells with enough expected mass
+    exp_counts = p[keep] / p[keep].sum() * counts[keep].sum()
+    assert chisquare(counts[keep], exp_counts).pvalue > 0.01
+    if case["same"]:
+        assert accepted_first == trials
