@@ -3,7 +3,8 @@ reference's own property tests (tests/test_paged_cache_properties.py:34-100,
 tests/test_scheduler_properties.py:49-81) run against the oracle, the
 device-allocator restatement (``oracle.alloc.BlockState``) against the
 sequential cache under random op sequences, the greedy accept rule, the
-scheduler's per-row commit, the paged-attention oracle against the model's
+scheduler's per-row commit, the reference's distribution test on the
+explicit-uniform accept rule, the paged-attention oracle against the model's
 masked attention, the Llama-style restatement (RoPE, cached against
 recomputed decoding, the reference scheduler over GQA caches), and
 Philox4x32-10 against the published known-answer vectors.  CPU only."""
