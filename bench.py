@@ -191,11 +191,10 @@ def run_pse(args, rank, world, device):
     k, T = w.k, w.temperature
 
     def api_step(defer):
+        nonlocal dn, tn
         res = pse.batched_speculative_step(d, t, rids, dc, tc, dn, tn, k, T, defer_bonus=defer)
-        for r in rids:
-            dn[r] = res.draft_next_logits[r]
-            tn[r] = res.target_next_logits[r]
-        return sum(len(v) for v in res.accepted_tokens.values())
+        dn, tn = res.draft_next_logits, res.target_next_logits  # what the next step takes back
+        return sum(map(len, res.accepted_tokens.values()))
 
     runner = runner_for(d, t, dc, tc, k)
 

@@ -494,14 +494,21 @@ class StepRunner:
         if float(temperature) > 0 and uniforms is None and generator is None:
             key_np = np.array([_fnv1a(r) for r in request_ids], dtype=np.uint32).view(np.int32)
             steps_np = np.fromiter((steps.get(r, 0) for r in request_ids), np.int32, B)
+        views = []
+
+        def while_device_runs():
+            # the next-logits dicts depend only on the slots: build them during the step
+            views.append(dict(zip(request_ids, map(dviews.__getitem__, sd))))
+            views.append(dict.fromkeys(request_ids) if defer_bonus
+                         else dict(zip(request_ids, map(tviews.__getitem__, stt))))
+
         b, nacc_np = self._run(request_ids, sd_np, st_np, temperature, generator, uniforms, use_graph, defer_bonus,
-                               key_np, steps_np)
+                               key_np, steps_np, while_device_runs=while_device_runs)
         toks = b.host_pack_np[:B * (k + 1)].reshape(B, k + 1).tolist()
         nacc = nacc_np.tolist()
         accepted = {r: toks[i][: nacc[i] + 1] for i, r in enumerate(request_ids)}
         n_acc = dict(zip(request_ids, nacc))
-        dn = dict(zip(request_ids, map(dviews.__getitem__, sd)))
-        tn = dict.fromkeys(request_ids) if defer_bonus else dict(zip(request_ids, map(tviews.__getitem__, stt)))
+        dn, tn = views
         for r in request_ids:
             steps[r] = steps.get(r, 0) + 1
         return BatchStepResult(accepted, n_acc, dn, tn)
@@ -524,10 +531,13 @@ class StepRunner:
         return nacc_np, b.host_pack_np[at + 1:at + 1 + nfin].copy()
 
     def _run(self, request_ids, sd_np, st_np, temperature, generator, uniforms, use_graph, defer_bonus,
-             req_key_np=None, steps_np=None, ords_np=None, commit: CommitArena | None = None):
+             req_key_np=None, steps_np=None, ords_np=None, commit: CommitArena | None = None,
+             while_device_runs=None):
         """Launch one step (replaying its graph when captured), copy its result
         to the host, raise a latched device error, update the host length
-        mirrors.  Returns the step's buffers and n_acc as int64."""
+        mirrors.  ``while_device_runs`` (optional) is called after the launch,
+        before waiting for the device.  Returns the step's buffers and n_acc as
+        int64."""
         k, V = self.k, self.V
         B = len(request_ids)
         dc, tc = self.dcache, self.tcache
@@ -617,6 +627,8 @@ class StepRunner:
             b.host_pack.copy_(b.pack, non_blocking=True)
         else:  # the tokens stay on the device
             b.host_pack[nt:].copy_(b.pack[nt:], non_blocking=True)
+        if while_device_runs is not None:
+            while_device_runs()
         torch.cuda.current_stream().synchronize()
         hpn = b.host_pack_np
         status_d, status_t = int(hpn[nt + B]), int(hpn[nt + B + 1])
