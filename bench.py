@@ -307,6 +307,12 @@ def run_pse(args, rank, world, device):
     step_bytes = (w_t + head["ctx_mean"][1] * kv_bytes_per_token(t)
                   + k * (w_d + head["ctx_mean"][0] * kv_bytes_per_token(d)))
 
+    # host <-> device bytes of one API step, counted from the buffers it copies:
+    # the whole per-row input buffer in, the whole packed result out
+    sb = runner.bufs[B]
+    h2d = sb.host_in.numel() * sb.host_in.element_size()
+    d2h = sb.host_pack.numel() * sb.host_pack.element_size()
+
     from pse.dist import reduce_stats
     out = {}
     for name, m in (("ref", ref), ("head", head)):
@@ -315,7 +321,7 @@ def run_pse(args, rank, world, device):
         out[name] = dict(committed=c_, ms=s_ * 1000.0, e2e_tokens=e_, e2e_ms=es_ * 1000.0)
     return dict(ref=out["ref"], head=out["head"], attn_ms=attn_ms, attn_bytes=attn_bytes, attn_width=width,
                 prefill_s=prefill_s, prefill_tokens=prefill_tokens, clocks=head["clocks"], B=B, k=k, kernels_per_step=head["kernels"],
-                dtype=str(dtype), h2d=6 * B * 4, d2h=(B * (k + 1) + B + 2) * 4, step_bytes=step_bytes,
+                dtype=str(dtype), h2d=h2d, d2h=d2h, step_bytes=step_bytes,
                 tokens_per_step_mean=head["committed"] / args.steps / max(world, 1),
                 deferred=not args.reference_structure)
 
