@@ -207,13 +207,16 @@ def run_pse(args, rank, world, device):
         return int(c._blocks.seq_len[slots.long()].sum().item())
 
     def measure(defer):
-        """W warm-up steps through the API (the first runs eagerly and counts its
-        kernels, the second captures the step's CUDA graph), K timed graph
+        """W warm-up steps through the API (the first runs eagerly -- for the
+        deferred-bonus structure it also moves every row into that state, one
+        truncate per row, once -- and the second captures the step's CUDA
+        graph, counting each of the step's kernels once), K timed graph
         replays (inputs resident), then K timed steps through the public API."""
+        api_step(defer)
         before = sum(N.launches.values())
         api_step(defer)
         kernels = sum(N.launches.values()) - before
-        for _ in range(max(args.warmup, 3) - 1):
+        for _ in range(max(args.warmup, 3) - 2):
             api_step(defer)
         if args.profile_step:
             torch.cuda.synchronize()
