@@ -33,6 +33,23 @@ def test_library_builds_and_exports_every_declared_symbol():
     assert set(_native.exported_symbols()) == set(declared)
 
 
+def test_ctypes_prototypes_match_the_header():
+    """Every prototype in the ctypes table takes as many arguments as the
+    header's declaration (a drifted binding would pass misread arguments)."""
+    from pse import _native
+    with open(os.path.join(ROOT, "include", "pse.h")) as f:
+        text = re.sub(r"/\*.*?\*/", "", f.read(), flags=re.S)
+    decls = dict(re.findall(r"(?:int|size_t)\s+(pse_\w+)\s*\(([^)]*)\)\s*;", text))
+    assert len(decls) == len(_declared())
+    checked = 0
+    for name, (argtypes, _) in _native._PROTOS.items():
+        params = decls[name].strip()
+        n = 0 if params in ("", "void") else params.count(",") + 1
+        assert len(argtypes) == n, name
+        checked += 1
+    assert checked >= 20
+
+
 def test_engine_refuses_to_run_without_cuda():
     import torch
     if torch.cuda.is_available():
