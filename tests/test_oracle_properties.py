@@ -5,7 +5,8 @@ device-allocator restatement (``oracle.alloc.BlockState``) against the
 sequential cache under random op sequences, the greedy accept rule, the
 scheduler's per-row commit, the reference's distribution test on the
 explicit-uniform accept rule, the paged-attention oracle against the model's
-masked attention, the Llama-style restatement (RoPE, cached against
+masked attention, the batched forward over ragged rows against each row's
+own forward, the Llama-style restatement (RoPE, cached against
 recomputed decoding, the reference scheduler over GQA caches), and
 Philox4x32-10 against the published known-answer vectors.  CPU only."""
 from __future__ import annotations
@@ -343,3 +344,30 @@ def test_sampled_accept_preserves_the_target_distribution(case):
     assert chisquare(counts[keep], exp_counts).pvalue > 0.01
     if case["same"]:
         assert accepted_first == trials
+
+
+@pytest.mark.parametrize("seed,width,block_size", [(0, 1, 4), (1, 3, 2), (2, 5, 16)])
+def test_batched_forward_over_ragged_rows_equals_each_rows_own_forward(seed, width, block_size):
+    """engine/batched_forward.py:27-72 restated: one padded forward over rows
+    of different lengths (gathered from the paged cache, per-row positions)
+    gives each row the logits of its own forward over its whole sequence, and
+    appends each row's new K/V to its own blocks."""
+    from oracle.batched_forward import batched_forward_append
+    torch.manual_seed(seed)
+    cfg = ModelConfig(vocab_size=40, d_model=16, n_layers=2, n_heads=2, d_ff=32, max_seq_len=128)
+    model = TinyGPT(cfg).eval()
+    rng = np.random.default_rng(seed)
+    prompts = [rng.integers(0, 40, size=int(n)).tolist() for n in (3, 11, 1, 7)]
+    cache = PagedKVCache(cfg.n_layers, cfg.n_heads, cfg.d_model // cfg.n_heads, block_size, 64)
+    rids = [f"r{i}" for i in range(len(prompts))]
+    for r, p in zip(rids, prompts):  # each prompt prefilled on its own (a batch of one row)
+        cache.create_request(r)
+        batched_forward_append(model, cache, [r], torch.tensor([p]))
+    new = torch.from_numpy(rng.integers(0, 40, size=(len(rids), width)))
+    got = batched_forward_append(model, cache, rids, new)
+    with torch.no_grad():
+        for i, p in enumerate(prompts):
+            full = torch.tensor([p + new[i].tolist()])
+            want = model(full)[0][0, len(p):]
+            torch.testing.assert_close(got[i], want, rtol=1e-5, atol=1e-5)
+            assert cache.length(rids[i]) == len(p) + width
