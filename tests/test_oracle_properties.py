@@ -371,3 +371,27 @@ def test_batched_forward_over_ragged_rows_equals_each_rows_own_forward(seed, wid
             want = model(full)[0][0, len(p):]
             torch.testing.assert_close(got[i], want, rtol=1e-5, atol=1e-5)
             assert cache.length(rids[i]) == len(p) + width
+
+
+@settings(max_examples=300, deadline=None)
+@given(seed=st.integers(0, 2**31 - 1), vocab=st.integers(1, 40), temp=st.sampled_from([0.3, 1.0, 2.5]))
+def test_inverse_cdf_is_monotone_and_skips_zero_weights(seed, vocab, temp):
+    """The explicit-uniform draw the sampling kernels implement: the token is a
+    non-decreasing function of u, never a zero-weight entry, and agrees with a
+    float64 cumulative-sum search away from bucket edges."""
+    from oracle.sampling import inverse_cdf, weights
+    rng = np.random.default_rng(seed)
+    logits = (rng.standard_normal(vocab) * 4).astype(np.float32)
+    logits[rng.random(vocab) < 0.2] = -np.inf  # masked-out entries have zero weight
+    if np.isinf(logits).all():
+        logits[0] = 0.0
+    w, z = weights(logits, temp)
+    assert w.dtype == np.float32 and z > 0
+    us = np.sort(rng.random(64))
+    toks = [inverse_cdf(w, float(z), float(u)) for u in us]
+    assert toks == sorted(toks)
+    assert all(w[t] > 0 for t in toks)
+    cdf = np.cumsum(w.astype(np.float64)) / float(z)
+    for u, t in zip(us, toks):
+        if np.min(np.abs(cdf - u)) > 1e-9:
+            assert t == int(np.searchsorted(cdf, u, side="right"))
