@@ -242,6 +242,8 @@ def run_pse(args, rank, world, device):
         ms = e0.elapsed_time(e1)
         ctx1 = (sum_ctx(dc, b.slots_d), sum_ctx(tc, b.slots_t))
         committed = int(nacc_hist.sum().item()) + args.steps * B
+        # rows of the timed steps by number of drafts accepted (0..k)
+        acc_hist = np.bincount(nacc_hist.cpu().numpy().ravel().clip(0, k), minlength=k + 1).tolist()
         for c in (dc, tc):  # host mirrors of the lengths after the replays
             c._resync_lengths()
         barrier()
@@ -251,7 +253,8 @@ def run_pse(args, rank, world, device):
         f1.record()
         barrier()
         return dict(ms=ms, committed=committed, e2e_ms=f0.elapsed_time(f1), e2e_tokens=e2e_tokens,
-                    kernels=kernels, ctx_mean=((ctx0[0] + ctx1[0]) / 2, (ctx0[1] + ctx1[1]) / 2))
+                    kernels=kernels, ctx_mean=((ctx0[0] + ctx1[0]) / 2, (ctx0[1] + ctx1[1]) / 2),
+                    acc_hist=acc_hist)
 
     if args.profile_step:
         return measure(not args.reference_structure)
@@ -326,7 +329,7 @@ def run_pse(args, rank, world, device):
                 prefill_s=prefill_s, prefill_tokens=prefill_tokens, clocks=head["clocks"], B=B, k=k, kernels_per_step=head["kernels"],
                 dtype=str(dtype), h2d=h2d, d2h=d2h, step_bytes=step_bytes,
                 tokens_per_step_mean=head["committed"] / args.steps / max(world, 1),
-                deferred=not args.reference_structure)
+                deferred=not args.reference_structure, acc_hist=head["acc_hist"])
 
 
 def cpu_reference(args, sample_rows, sample_steps, threads, warmup=0):
@@ -924,6 +927,8 @@ def main():
                                                   "kind": "port", "sample": cpu["sample"]},
         "clocks": r["clocks"],
         "gpu_launches": r["kernels_per_step"] * args.steps,
+        "acceptance": {"rows_by_drafts_accepted": r["acc_hist"], "k": r["k"],
+                       "note": "rank 0's rows over the timed steps, index = drafts accepted (0..k)"},
         "prefill": {"requests": r["B"], "prompt_tokens": r["prefill_tokens"], "seconds": r["prefill_s"],
                     "tokens_per_s": r["prefill_tokens"] / r["prefill_s"], "mode": "batched (prefill_requests)"},
     }
