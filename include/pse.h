@@ -164,9 +164,12 @@ size_t pse_paged_attention_workspace(int32_t rows, int32_t width, int32_t q_head
  * PSE_NOALLOC_SCRATCH_BYTES compiled into the library, resident on every GPU
  * that loads it until the process exits.  Calls whose scratch need
  * (pse_paged_attention_workspace) exceeds that return PSE_ESCRATCH without
- * launching.  The first call on each device looks up the array's device
- * address (cudaGetSymbolAddress) with that device current; make that first
- * call before any stream capture.  All calls share the array and it keeps the
+ * launching (wide prompt-shaped calls, which take the prefill kernel and use
+ * no split-KV scratch, are never refused for size).  The first call on each
+ * device looks up the array's device address (cudaGetSymbolAddress) with that
+ * device current and keeps it for the life of the process; make that first
+ * call before any stream capture, and do not keep using the library across a
+ * device reset (cudaDeviceReset), after which the kept address is stale.  All calls share the array and it keeps the
  * last call's contents (nothing in it needs to start at zero): calls that
  * overlap on the GPU race, so issue them on one stream or otherwise ordered.
  * No counterpart in the reference. */

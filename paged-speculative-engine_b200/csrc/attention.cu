@@ -571,6 +571,11 @@ extern "C" int pse_paged_attention_noalloc(pse_block_state st, pse_kv_layer kv, 
     return PSE_EINVAL;
   if (kv.kv_heads <= 0 || q_heads <= 0 || q_heads % kv.kv_heads != 0) return PSE_EINVAL;
   if (kv.head_dim <= 0 || kv.head_dim > 256 || max_ctx <= 0 || st.block_size <= 0) return PSE_EINVAL;
+  cudaStream_t s = (cudaStream_t)stream;
+  // wide (prompt) calls use no split-KV scratch: route them before the size check
+  if (use_prefill(st, kv, q, q_tok_stride, out, out_tok_stride, q_heads, width))
+    return prefill_attention(st, kv, q, q_tok_stride, out, out_tok_stride, slots, base_len, rows, width, q_heads,
+                             scale, nullptr, s);
   const size_t need = pse_paged_attention_workspace(rows, width, q_heads, kv.kv_heads, kv.head_dim, max_ctx);
   if (need > kNoallocScratchBytes) return PSE_ESCRATCH;
   Plan p = make_plan(rows, width, q_heads, kv.kv_heads, kv.head_dim, max_ctx);
@@ -602,11 +607,7 @@ extern "C" int pse_paged_attention_noalloc(pse_block_state st, pse_kv_layer kv, 
   // call; every (split, row, head) slot after it is written before the combine
   // reads it, so stale contents from an earlier call never leak in.
   a.ws = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(scratch) + kWsHeader);
-  cudaStream_t s = (cudaStream_t)stream;
-  if (use_prefill(st, kv, q, q_tok_stride, out, out_tok_stride, q_heads, width))
-    return prefill_attention(st, kv, q, q_tok_stride, out, out_tok_stride, slots, base_len, rows, width, q_heads,
-                             scale, nullptr, s);
-  if (tc_eligible(st, kv, q_heads, width)) {
+  if (tc_eligible(st, kv, q_heads, width) && !g_force_generic) {
     rc = tc_attention(st, kv, q, q_tok_stride, out, out_tok_stride, slots, base_len, rows, width, q_heads, scale,
                       p.split_tokens, p.n_splits, a.ws, reinterpret_cast<int*>(scratch), nullptr,
                       /*self_reset=*/false, s);

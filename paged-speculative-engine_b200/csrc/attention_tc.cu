@@ -26,10 +26,8 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
-#include <mutex>
-#include <unordered_map>
-
 #include "common.cuh"
+#include "tmap_cache.h"
 
 namespace pse {
 namespace tc {
@@ -595,46 +593,13 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? PSE_TC_MINB64 : PSE_TC_MI
 }
 
 // ---------------------------------------------------------------- host side
-PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
-std::mutex g_mu;
-std::unordered_map<uint64_t, CUtensorMap>* g_maps = nullptr;
-
-int encoder() {
-  if (g_encode) return 0;
-  cudaDriverEntryPointQueryResult q;
-  void* fn = nullptr;
-  cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
-  if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn) return e != cudaSuccess ? (int)e : PSE_EINVAL;
-  g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
-  return 0;
-}
+TmapCache g_maps;
 
 // 2-D view of one layer's pool: rows = num_blocks * kv_heads * block_size,
 // columns = head_dim; box = [block_size rows x 64 columns], 128-byte swizzle.
 int tensor_map(const void* pool, int num_blocks, int kv_heads, int bs, int hd, CUtensorMap* out) {
-  const uint64_t key = reinterpret_cast<uint64_t>(pool) ^ ((uint64_t)num_blocks << 40) ^ ((uint64_t)bs << 32) ^
-                       ((uint64_t)hd << 24) ^ ((uint64_t)kv_heads << 48);
-  std::lock_guard<std::mutex> lk(g_mu);
-  if (!g_maps) g_maps = new std::unordered_map<uint64_t, CUtensorMap>();
-  auto it = g_maps->find(key);
-  if (it != g_maps->end()) {
-    *out = it->second;
-    return 0;
-  }
-  int rc = encoder();
-  if (rc) return rc;
-  CUtensorMap m;
-  const cuuint64_t dims[2] = {(cuuint64_t)hd, (cuuint64_t)num_blocks * kv_heads * bs};
-  const cuuint64_t strides[1] = {(cuuint64_t)hd * 2};
-  const cuuint32_t box[2] = {64, (cuuint32_t)bs};
-  const cuuint32_t estr[2] = {1, 1};
-  CUresult r = g_encode(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(pool), dims, strides, box, estr,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return PSE_EINVAL;
-  (*g_maps)[key] = m;
-  *out = m;
-  return 0;
+  return g_maps.get(pool, (uint64_t)hd, (uint64_t)num_blocks * kv_heads * bs, (uint64_t)hd * 2, 64u, (uint32_t)bs,
+                    PSE_EINVAL, out);
 }
 
 template <int HD>

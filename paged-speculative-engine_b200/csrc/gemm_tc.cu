@@ -17,10 +17,8 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
-#include <mutex>
-#include <unordered_map>
-
 #include "common.cuh"
+#include "tmap_cache.h"
 
 namespace pse {
 namespace gemm {
@@ -253,50 +251,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
 }
 
 // ---------------------------------------------------------------- host side
-PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
-std::mutex g_mu;
-std::unordered_map<uint64_t, CUtensorMap>* g_maps = nullptr;
-
-int encoder() {
-  if (g_encode) return 0;
-  cudaDriverEntryPointQueryResult q;
-  void* fn = nullptr;
-  cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
-  if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn) return e != cudaSuccess ? (int)e : PSE_EINVAL;
-  g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
-  return 0;
-}
+TmapCache g_maps;
 
 // [rows x cols] bf16 row-major with leading dimension ld (elements); box
 // [box_rows x 64 columns], 128-byte swizzle, out-of-range reads as zero.
 int tensor_map(const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows, CUtensorMap* out) {
-  uint64_t key = reinterpret_cast<uint64_t>(ptr);
-  key = key * 1000003ull ^ (uint64_t)rows;
-  key = key * 1000003ull ^ (uint64_t)cols;
-  key = key * 1000003ull ^ (uint64_t)ld;
-  key = key * 1000003ull ^ (uint64_t)box_rows;
-  std::lock_guard<std::mutex> lk(g_mu);
-  if (!g_maps) g_maps = new std::unordered_map<uint64_t, CUtensorMap>();
-  auto it = g_maps->find(key);
-  if (it != g_maps->end()) {
-    *out = it->second;
-    return 0;
-  }
-  int rc = encoder();
-  if (rc) return rc;
-  CUtensorMap m;
-  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-  const cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
-  const cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
-  const cuuint32_t estr[2] = {1, 1};
-  CUresult r = g_encode(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return PSE_EINVAL;
-  if (g_maps->size() > 4096) g_maps->clear();
-  (*g_maps)[key] = m;
-  *out = m;
-  return 0;
+  return g_maps.get(ptr, (uint64_t)cols, (uint64_t)rows, (uint64_t)ld * 2, (uint32_t)BK, (uint32_t)box_rows, PSE_EINVAL,
+                    out);
 }
 
 template <int BN>

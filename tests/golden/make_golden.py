@@ -5,7 +5,7 @@ The reference is only importable where its source tree is present; the
 fixtures it produces are committed so the tests can check the oracle and the
 CUDA path without it.  Run from the repository root:
 
-    python tests/golden/make_golden.py /root/reference
+    python tests/golden/make_golden.py <reference checkout>
 
 Fixtures:
 
@@ -189,4 +189,6 @@ def main(ref_root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: make_golden.py <path to the reference checkout (its engine/ package)>")
+    main(sys.argv[1])

@@ -57,3 +57,18 @@ def test_engine_refuses_to_run_without_cuda():
     import pse
     with pytest.raises(RuntimeError):
         pse.PagedKVCache(1, 1, 2, 4, 8)
+
+
+def test_tensor_map_cache_compares_the_full_descriptor_key(tmp_path):
+    """Two pools whose (pointer, sizes) fold onto one 64-bit value still get
+    distinct descriptor-cache keys: a hit needs every field equal."""
+    cuda_inc = "/usr/local/cuda/include"
+    if not os.path.isdir(cuda_inc):
+        pytest.skip("CUDA headers not found")
+    exe = str(tmp_path / "tmap_key_check")
+    src = os.path.join(ROOT, "tests", "native", "tmap_key_check.cpp")
+    csrc = os.path.join(ROOT, "paged-speculative-engine_b200", "csrc")
+    subprocess.run(["g++", "-std=c++17", "-O1", f"-I{csrc}", f"-I{cuda_inc}", src, "-o", exe], check=True)
+    out = subprocess.run([exe], capture_output=True, text=True)
+    assert out.returncode == 0, out.stdout + out.stderr
+    assert out.stdout.strip() == "OK"

@@ -89,3 +89,33 @@ def test_noalloc_refuses_scratch_beyond_its_array():
                                          slots.data_ptr(), base_d.data_ptr(), rows, width, hq, 0.125, max_ctx,
                                          N.stream_ptr())
     assert rc == N.PSE_ESCRATCH
+
+
+def test_noalloc_prompt_shaped_call_is_not_refused_for_size():
+    """A wide (prompt-shaped) call runs the prefill kernel, which uses no
+    split-KV scratch: it is served even when the split-KV formula's figure for
+    the same shape exceeds the array, and returns what the workspace-taking
+    entry point returns, on two calls in a row."""
+    rows, width, hq, hk, hd, bs = 1, 256, 32, 32, 128, 16
+    N, c, slots, base_d, _ = _setup(rows, width, hq, hk, hd, bs, 600, torch.bfloat16, seed=7)
+    c._blocks.seq_len[:rows] = base_d + width  # the prompt's tokens lie inside the row
+    max_ctx = 1024
+    need = N.size_call("pse_paged_attention_workspace", rows, width, hq, hk, hd, max_ctx)
+    assert need > N.NOALLOC_SCRATCH_BYTES
+    ws = torch.zeros(need, dtype=torch.uint8, device="cuda")
+    g = torch.Generator().manual_seed(9)
+    st = N.stream_ptr()
+    for call in range(2):
+        q = torch.randn(rows * width, hq * hd, generator=g).to(torch.bfloat16).cuda()
+        want = torch.empty_like(q)
+        got = torch.full_like(q, float("nan"))
+        N.call("pse_paged_attention", c.state, c.layer(0), q.data_ptr(), hq * hd, want.data_ptr(), hq * hd,
+               slots.data_ptr(), base_d.data_ptr(), rows, width, hq, 1.0 / math.sqrt(hd), max_ctx,
+               None, ws.data_ptr(), ws.numel(), st)
+        N.call("pse_paged_attention_noalloc", c.state, c.layer(0), q.data_ptr(), hq * hd, got.data_ptr(), hq * hd,
+               slots.data_ptr(), base_d.data_ptr(), rows, width, hq, 1.0 / math.sqrt(hd), max_ctx, st)
+        torch.cuda.synchronize()
+        assert torch.isfinite(got).all(), call
+        assert want.float().abs().max().item() > 0, call  # the rows' keys were really read
+        assert (got.float() - want.float()).abs().max().item() < BF16_TOL, call
+    assert int(c._blocks.status.item()) == 0
