@@ -189,11 +189,20 @@ def run_pse(args, rank, world, device):
     prefill_s = time.perf_counter() - t0
     prefill_tokens = sum(len(p) for p in prompts)
     k, T = w.k, w.temperature
+    # committed tokens of the first rows, over every step of the run (checked against the oracle afterwards)
+    n_chk = min(2, B)
+    chk_tokens = {r: [] for r in rids[:n_chk]}
 
-    def api_step(defer):
+    def api_step(reference_structure):
         nonlocal dn, tn
-        res = pse.batched_speculative_step(d, t, rids, dc, tc, dn, tn, k, T, defer_bonus=defer)
+        if reference_structure:
+            res = pse.batched_speculative_step(d, t, rids, dc, tc, dn, tn, k, T, defer_bonus=False)
+        else:
+            # exactly the reference scheduler's call (engine/scheduler.py:102-105)
+            res = pse.batched_speculative_step(d, t, rids, dc, tc, dn, tn, k, T)
         dn, tn = res.draft_next_logits, res.target_next_logits  # what the next step takes back
+        for r in chk_tokens:
+            chk_tokens[r].extend(res.accepted_tokens[r])
         return sum(map(len, res.accepted_tokens.values()))
 
     runner = runner_for(d, t, dc, tc, k)
@@ -206,28 +215,33 @@ def run_pse(args, rank, world, device):
     def sum_ctx(c, slots):
         return int(c._blocks.seq_len[slots.long()].sum().item())
 
-    def measure(defer):
-        """W warm-up steps through the API (the first runs eagerly -- for the
-        deferred-bonus structure it also moves every row into that state, one
-        truncate per row, once -- and the second captures the step's CUDA
-        graph, counting each of the step's kernels once), K timed graph
-        replays (inputs resident), then K timed steps through the public API."""
-        api_step(defer)
+    def measure(reference_structure):
+        """W >= 3 warm-up steps through the API (eager runs, then the CUDA-graph
+        capture of the steady-state step; each of that step's kernels is
+        counted once, in its eager run), K timed graph replays (inputs
+        resident), then K timed steps through the public API.  The default
+        structure's first step runs from rows just prefilled (width-k verify,
+        bonus deferred); from the second on every row is pending (width-k+1
+        verify from the pending position)."""
+        api_step(reference_structure)
         before = sum(N.launches.values())
-        api_step(defer)
+        api_step(reference_structure)
         kernels = sum(N.launches.values()) - before
         for _ in range(max(args.warmup, 3) - 2):
-            api_step(defer)
+            api_step(reference_structure)
         if args.profile_step:
             torch.cuda.synchronize()
             torch.cuda.nvtx.range_push("pse_step")
-            pse.batched_speculative_step(d, t, rids, dc, tc, dn, tn, k, T, use_graph=False, defer_bonus=defer)
+            pse.batched_speculative_step(d, t, rids, dc, tc, dn, tn, k, T, use_graph=False,
+                                         defer_bonus=False if reference_structure else None)
             torch.cuda.synchronize()
             torch.cuda.nvtx.range_pop()
             return None
-        graph = [g for key, g in runner.graphs.items() if key[0] == B and key[3] == defer][0]
+        steady = (False, False) if reference_structure else (True, True)  # (rows pending in, bonus deferred out)
+        graph = [g for key, g in runner.graphs.items() if key[0] == B and key[3:5] == steady][0]
         b = runner.bufs[B]
         nacc_hist = torch.zeros(args.steps, B, dtype=torch.int32, device=device)
+        tok_hist = torch.zeros(args.steps, n_chk, k + 1, dtype=torch.int32, device=device)
         ctx0 = (sum_ctx(dc, b.slots_d), sum_ctx(tc, b.slots_t))
         barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -236,10 +250,15 @@ def run_pse(args, rank, world, device):
         for s in range(args.steps):
             graph.replay()
             nacc_hist[s].copy_(b.n_acc)
+            tok_hist[s].copy_(b.tokens[:n_chk])
         e1.record()
         barrier()
         clk.mark()
         ms = e0.elapsed_time(e1)
+        th, nh = tok_hist.cpu().numpy(), nacc_hist[:, :n_chk].cpu().numpy()
+        for s in range(args.steps):
+            for i, r in enumerate(rids[:n_chk]):
+                chk_tokens[r].extend(th[s, i, :nh[s, i] + 1].tolist())
         ctx1 = (sum_ctx(dc, b.slots_d), sum_ctx(tc, b.slots_t))
         committed = int(nacc_hist.sum().item()) + args.steps * B
         # rows of the timed steps by number of drafts accepted (0..k)
@@ -249,7 +268,7 @@ def run_pse(args, rank, world, device):
         barrier()
         f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         f0.record()
-        e2e_tokens = sum(api_step(defer) for _ in range(args.steps))
+        e2e_tokens = sum(api_step(reference_structure) for _ in range(args.steps))
         f1.record()
         barrier()
         return dict(ms=ms, committed=committed, e2e_ms=f0.elapsed_time(f1), e2e_tokens=e2e_tokens,
@@ -257,12 +276,12 @@ def run_pse(args, rank, world, device):
                     acc_hist=acc_hist)
 
     if args.profile_step:
-        return measure(not args.reference_structure)
+        return measure(args.reference_structure)
     # clocks are sampled from before the first warm-up to the end of the last timed region;
     # the summary keeps the samples taken inside the timed regions
     with ClockSampler(device.index or 0) as clk:
-        ref = measure(False)  # the reference's step structure: 2 target + k+1 draft calls
-        head = ref if args.reference_structure else measure(True)  # 1 target call of width k+1 + k+1 draft calls
+        ref = measure(True)  # the reference's step structure: 2 target + k+1 draft calls
+        head = ref if args.reference_structure else measure(False)  # 1 target call of width k+1 + k+1 draft calls
     head["clocks"] = clk.summary()
     b = runner.bufs[B]
     width = k if args.reference_structure else k + 1
@@ -329,14 +348,57 @@ def run_pse(args, rank, world, device):
                 prefill_s=prefill_s, prefill_tokens=prefill_tokens, clocks=head["clocks"], B=B, k=k, kernels_per_step=head["kernels"],
                 dtype=str(dtype), h2d=h2d, d2h=d2h, step_bytes=step_bytes,
                 tokens_per_step_mean=head["committed"] / args.steps / max(world, 1),
-                deferred=not args.reference_structure, acc_hist=head["acc_hist"])
+                deferred=not args.reference_structure, acc_hist=head["acc_hist"],
+                check_rows=[(prompts[i], chk_tokens[rids[i]]) for i in range(n_chk)])
+
+
+def token_check(args, rows, threads):
+    """Greedy parity of committed tokens from the timed run: for each checked
+    row, one teacher-forced forward of the oracle (fp32 CPU model on the same
+    weights rounded to bf16) over prompt + everything the row committed; each
+    committed token must be the oracle's argmax given the same prefix or lie
+    within the bf16 logit tolerance of it (the oracle of engine/generate.py:
+    24-38 takes the argmax)."""
+    from oracle.model import LlamaConfig, ModelConfig, TinyGPT, TinyLlama
+    from pse import workload as wl
+    w = wl.WORKLOADS[args.workload]
+    if w.temperature > 0 or not rows:
+        return None
+    torch.set_num_threads(threads)
+    pr = w.pair
+    torch.manual_seed(0)
+    if pr.kind == "gpt":
+        TinyGPT(ModelConfig(vocab_size=pr.vocab, **pr.draft))  # same RNG stream as the engine's pair
+        t = TinyGPT(ModelConfig(vocab_size=pr.vocab, **pr.target)).eval()
+    else:
+        TinyLlama(LlamaConfig(vocab_size=pr.vocab, **pr.draft))
+        t = TinyLlama(LlamaConfig(vocab_size=pr.vocab, **pr.target)).eval()
+    with torch.no_grad():
+        for p in t.parameters():
+            p.copy_(p.to(torch.bfloat16).float())
+    n_tok, n_div, worst = 0, 0, 0.0
+    for prompt, gen in rows:
+        with torch.no_grad():
+            ol = t(torch.tensor([list(prompt) + gen[:-1]]))[0][0][len(prompt) - 1:]
+        g = torch.tensor(gen)
+        gap = ol.max(dim=-1).values - ol.gather(1, g.view(-1, 1)).view(-1)
+        n_tok += len(gen)
+        n_div += int((ol.argmax(dim=-1) != g).sum())
+        worst = max(worst, float(gap.max()))
+    return {"rows": len(rows), "tokens": n_tok, "not_oracle_argmax": n_div, "max_logit_gap": worst,
+            "tolerance": 2e-2, "ok": worst < 2e-2}
 
 
 def cpu_reference(args, sample_rows, sample_steps, threads, warmup=0):
     """The reference's CPU path (the oracle port of engine/*.py, fp32) on a
-    bounded sample of the same workload: prefill and ``warmup`` steps are
-    untimed, then ``sample_steps`` batched speculative steps over
-    ``sample_rows`` rows."""
+    sample of the same workload: ``sample_steps`` batched speculative steps
+    over the workload's first ``sample_rows`` rows after ``warmup`` untimed
+    ones.  Rows start at their prompts' lengths.  Where the prompts hold more
+    than ``CPU_PREFILL_TOKENS`` tokens in all, the per-request CPU prefill
+    (minutes at 256 rows) is replaced by appending seeded N(0,1) K/V of each
+    prompt's length and seeded next-token logits: a step's work depends on
+    the rows' lengths, not on the cached values, and with random-init models
+    the committed tokens per row are ~1 per step either way."""
     from oracle.model import LlamaConfig, ModelConfig, TinyGPT, TinyLlama
     from oracle.paged_cache import PagedKVCache
     from oracle.speculative import batched_speculative_step, prefill_request
@@ -352,20 +414,36 @@ def cpu_reference(args, sample_rows, sample_steps, threads, warmup=0):
     else:
         d = TinyLlama(LlamaConfig(vocab_size=pr.vocab, **pr.draft)).eval()
         t = TinyLlama(LlamaConfig(vocab_size=pr.vocab, **pr.target)).eval()
+    prompts = wl.prompts(w, seed=0, n=sample_rows)
+    steps_total = warmup + sample_steps
 
     def mk(m):
         c = m.cfg
         kv = getattr(c, "n_kv_heads", c.n_heads)
-        per = w.prompt_hi + w.max_new_tokens + w.k + 2
-        return PagedKVCache(c.n_layers, kv, c.d_model // c.n_heads, w.block_size,
-                            sample_rows * ((per + w.block_size - 1) // w.block_size) + 8)
+        nb = sum((len(p) + (w.k + 1) * (steps_total + 1) + w.block_size - 1) // w.block_size for p in prompts) + 8
+        return PagedKVCache(c.n_layers, kv, c.d_model // c.n_heads, w.block_size, nb)
 
     dc, tc = mk(d), mk(t)
-    prompts = wl.prompts(w, seed=0, n=sample_rows)
     rids = [f"c{i}" for i in range(sample_rows)]
     dn, tn = {}, {}
-    for r, p in zip(rids, prompts):
-        dn[r], tn[r] = prefill_request(d, t, dc, tc, r, p)
+    synthetic = sum(len(p) for p in prompts) > CPU_PREFILL_TOKENS
+    if not synthetic:
+        for r, p in zip(rids, prompts):
+            dn[r], tn[r] = prefill_request(d, t, dc, tc, r, p)
+    else:
+        g = torch.Generator().manual_seed(0)
+        longest = max(len(p) for p in prompts)
+        for m, c, nxt in ((d, dc, dn), (t, tc, tn)):
+            cfg = m.cfg
+            kv, hd = getattr(cfg, "n_kv_heads", cfg.n_heads), cfg.d_model // cfg.n_heads
+            src_k = torch.randn(cfg.n_layers, kv, longest, hd, generator=g)
+            src_v = torch.randn(cfg.n_layers, kv, longest, hd, generator=g)
+            for r, p in zip(rids, prompts):
+                c.create_request(r)
+                n = len(p)
+                c.append(r, [src_k[l, :, :n] for l in range(cfg.n_layers)],
+                         [src_v[l, :, :n] for l in range(cfg.n_layers)])
+                nxt[r] = torch.randn(pr.vocab, generator=g)
     for _ in range(warmup):
         res = batched_speculative_step(d, t, rids, dc, tc, dn, tn, w.k, w.temperature)
         dn, tn = res.draft_next_logits, res.target_next_logits
@@ -376,9 +454,15 @@ def cpu_reference(args, sample_rows, sample_steps, threads, warmup=0):
         tok += sum(len(v) for v in res.accepted_tokens.values())
         dn, tn = res.draft_next_logits, res.target_next_logits
     dt = time.perf_counter() - t0
+    start = ("rows start from seeded random K/V and next logits of their prompts' lengths (the per-request CPU "
+             "prefill is not run)" if synthetic else "prefill untimed")
     return dict(value=tok / dt, tokens=tok, seconds=dt, cores=threads,
-                sample=f"{sample_rows} of {w.max_batch_size} rows x {sample_steps} steps of the {w.name} "
-                       f"workload (prompts from the same seed), fp32 oracle port, prefill untimed")
+                sample=f"{sample_rows} of {w.max_batch_size} rows x {sample_steps} batched steps of the {w.name} "
+                       f"workload (its first {sample_rows} prompts, after {warmup} untimed steps), fp32 oracle "
+                       f"port of the reference's step, {threads} threads; {start}")
+
+
+CPU_PREFILL_TOKENS = 16384  # above this many prompt tokens the CPU sample starts from synthetic K/V
 
 
 # ncu dram__bytes_read.sum + dram__bytes_write.sum over the algorithmic bytes of
@@ -403,7 +487,7 @@ ATTN_SHAPES = {
 }
 
 
-def micro_attention(args, device):
+def micro_attention(args, device, emit=True):
     """Verify-attention kernel microbenchmark: one layer's pools, block tables a
     random permutation of a shared pool, Q/K/V ~ N(0,1), bf16.  Bytes are the
     algorithmic K/V bytes (sum of contexts x kv_heads x head_dim x 2 x 2 B) plus
@@ -475,16 +559,19 @@ def micro_attention(args, device):
     keys = int(sum(int(b) * width + width * (width + 1) // 2 for b in (ctx - width)))
     tflops = 4 * hq * hd * keys / (ms / 1000) / 1e12
     N.call("pse_attention_prefill_select", 0)
-    print(json.dumps({"metric": "paged attention HBM GB/s", "shape": args.attn_shape, "value": gbs, "unit": "GB/s",
+    res = {"metric": "paged attention HBM GB/s", "shape": args.attn_shape, "value": gbs, "unit": "GB/s",
                       "frac_of_peak": gbs / peak, "peak": peak, "peak_kind": kind, "us_per_launch": ms * 1000,
                       "tflops": tflops, "tflops_frac_of_bf16_peak": tflops / _tensor_peak()[0],
                       "prefill_kernel": args.prefill_kernel,
                       "algorithmic_bytes": alg, "rows": rows, "width": width, "q_heads": hq, "kv_heads": hk,
                       "head_dim": hd, "block_size": bs, "ctx_mean": float(ctx.mean()), "pages": args.attn_pages,
-                      "pool_bytes": 2 * c.k_pool.numel() * 2, "clocks": clk.summary()}), flush=True)
+                      "pool_bytes": 2 * c.k_pool.numel() * 2, "clocks": clk.summary()}
+    if emit:
+        print(json.dumps(res), flush=True)
+    return res
 
 
-def micro_accept(args, device):
+def micro_accept(args, device, emit=True):
     """Accept / resample microbenchmark: fp32 target logits [R, k+1, V] and
     draft logits [R, k, V] ~ N(0, 3^2), V = 128256, R = 1024, k = 8, drafts drawn
     from the draft distributions with explicit uniforms.  Bytes counted are the
@@ -529,14 +616,17 @@ def micro_accept(args, device):
     need = rows_read * V * 4
     formula = (2 * k + 1) * R * V * 4
     peak, kind = _peaks()
-    print(json.dumps({"metric": "accept/resample HBM GB/s", "value": need / (ms / 1000) / 1e9, "unit": "GB/s",
+    res = {"metric": "accept/resample HBM GB/s", "value": need / (ms / 1000) / 1e9, "unit": "GB/s",
                       "frac_of_peak": need / (ms / 1000) / 1e9 / peak, "peak": peak, "peak_kind": kind,
                       "us_per_launch": ms * 1000, "bytes_needed": need, "bytes_formula_2k+1": formula,
                       "formula_GBps": formula / (ms / 1000) / 1e9, "rows": R, "k": k, "vocab": V, "temperature": T,
                       "mean_accepted": n.float().mean().item(),
                       "kernel": ["streaming CTA per row", "CTA per row (scalar)", "cluster per row"][args.accept_kernel]
-                      if T > 0 else "CTA per row (argmax)"}), flush=True)
+                      if T > 0 else "CTA per row (argmax)"}
     N.load().pse_accept_select(0)
+    if emit:
+        print(json.dumps(res), flush=True)
+    return res
 
 
 def micro_prefill(args, device):
@@ -610,7 +700,7 @@ def micro_scheduler(args, device):
         else:
             res = pse.run_continuous_speculative_batches(d, t, reqs, dc, tc, w.max_batch_size, k=w.k,
                                                          temperature=w.temperature,
-                                                         defer_bonus=not args.reference_structure,
+                                                         defer_bonus=False if args.reference_structure else None,
                                                          device_bookkeeping=not args.sched_host_loop)
         torch.cuda.synchronize()
         out[run] = (time.perf_counter() - t0, sum(len(r.output_ids) - len(p) for r, p in
@@ -652,7 +742,7 @@ def micro_scheduler(args, device):
                "sample": f"the whole {w.name} workload ({n} requests), fp32 oracle port"}
     print(json.dumps({"metric": "committed tokens/s (scheduler, whole workload)", "workload": w.name, "k": w.k,
                       "temperature": w.temperature, "requests": n, "max_batch_size": w.max_batch_size,
-                      "step": "reference structure" if args.reference_structure else "deferred bonus",
+                      "step": "reference structure" if args.reference_structure else "default (bonus deferred)",
                       "bookkeeping": "host" if args.sched_host_loop else "device",
                       "mode": {"spec": "speculative, independent draft", "self": "speculative, draft = target",
                                "plain": "plain continuous batching, no speculation"}[args.sched_mode],
@@ -722,7 +812,7 @@ def micro_gemm(args, device):
     print(json.dumps({"metric": "projection GEMMs", "rows": rows}), flush=True)
 
 
-def micro_churn(args, device):
+def micro_churn(args, device, emit=True):
     """Truncate churn: 1024 rows of block 16 with lengths U[512, 32768]; each
     step reserves 8 tokens (verify), truncates every row to base + U{0..8}
     and reserves 1 more (bonus), as one step of the engine commits.  1000
@@ -768,10 +858,45 @@ def micro_churn(args, device):
     status = int(c._blocks.status.item())
     expect = init + (acc.sum(0) + steps).to(torch.int32)
     ok = bool(torch.equal(c._blocks.seq_len[:R], expect)) and status == 0
-    print(json.dumps({"metric": "truncate churn us/step", "value": ms * 1000 / steps, "unit": "us/step",
+    res = {"metric": "truncate churn us/step", "value": ms * 1000 / steps, "unit": "us/step",
                       "higher_is_better": False, "rows": R, "block_size": bs, "steps": steps,
                       "host_syncs_per_step": 0, "launches_per_step": 3, "lengths_ok": ok, "status": status,
-                      "free_blocks_end": int(c._blocks.free_top.item())}), flush=True)
+                      "free_blocks_end": int(c._blocks.free_top.item())}
+    if emit:
+        print(json.dumps(res), flush=True)
+    return res
+
+
+def kernel_configs(args, device):
+    """The kernel microbenchmark configurations, timed after the step on the
+    same GPU (each allocates its own buffers): 5a verify attention (1024 rows,
+    contexts U[512, 32768], GQA 32/8, head_dim 128, block 16; ~70 GB of K/V),
+    5b accept / resample (1024 rows x 8 drafts, vocab 128256, T = 1 and
+    T = 0), 5c truncate churn (1024 rows, 1000 steps).  Summaries only."""
+    import copy
+    gc.collect()
+    torch.cuda.empty_cache()
+    out = {}
+    a = copy.copy(args)
+    a.rows, a.steps, a.warmup = None, 10, 3
+    a.attn_shape, a.prefill_kernel, a.attn_pages = "verify-5a", "tc", "permuted"
+    r = micro_attention(a, device, emit=False)
+    out["5a_verify_attention"] = {k: r[k] for k in ("value", "unit", "frac_of_peak", "peak_kind", "us_per_launch",
+                                                    "algorithmic_bytes", "rows", "ctx_mean")}
+    gc.collect()
+    torch.cuda.empty_cache()
+    for T in (1.0, 0.0):
+        a.temperature, a.accept_kernel = T, 0
+        r = micro_accept(a, device, emit=False)
+        out[f"5b_accept_T{T:g}"] = {k: r[k] for k in ("value", "unit", "frac_of_peak", "us_per_launch",
+                                                     "bytes_needed", "formula_GBps", "mean_accepted", "kernel")}
+        gc.collect()
+        torch.cuda.empty_cache()
+    a.steps = 1000
+    r = micro_churn(a, device, emit=False)
+    out["5c_truncate_churn"] = {k: r[k] for k in ("value", "unit", "host_syncs_per_step", "lengths_ok", "rows",
+                                                  "steps")}
+    return out
 
 
 def config_block(args, w, B, world):
@@ -802,9 +927,16 @@ def main():
                          "on the device")
     ap.add_argument("--step-temperature", type=float, default=None,
                     help="sampling temperature of the step (default: the workload's)")
-    ap.add_argument("--cpu-rows", type=int, default=4)
-    ap.add_argument("--cpu-steps", type=int, default=10)
+    ap.add_argument("--cpu-rows", type=int, default=8,
+                    help="rows of the CPU sample: the reference's CPU step is fastest per token at 4-8 rows "
+                         "(padding to the longest row and the O(rows x longest) gather grow faster than the rows)")
+    ap.add_argument("--cpu-steps", type=int, default=4)
+    ap.add_argument("--cpu-ladder", default=None,
+                    help="comma-separated row counts: time the CPU path at each (1 warm-up + --cpu-steps steps) "
+                         "and print one JSON line per count, then exit")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-kernel-configs", action="store_true",
+                    help="skip the 5a / 5b / 5c kernel configurations after the step (they run at N=1 only)")
     ap.add_argument("--micro", choices=["attn", "accept", "churn", "prefill", "scheduler", "gemm"], default=None,
                     help="kernel microbenchmark instead of the step")
     ap.add_argument("--temperature", type=float, default=1.0, help="--micro accept: temperature")
@@ -812,7 +944,7 @@ def main():
                     help="--micro accept at T > 0: 0 streaming CTA per row, 1 scalar CTA per row, 2 cluster per row")
     ap.add_argument("--reference-structure", action="store_true",
                     help="headline the reference's step structure (2 target calls per step) instead of the "
-                         "deferred-bonus step (the target's bonus call folded into the next verify)")
+                         "default step (the target's bonus call deferred into the next verify)")
     ap.add_argument("--attn-shape", default="gpt2-verify", choices=sorted(ATTN_SHAPES))
     ap.add_argument("--prefill-kernel", default="tc", choices=["tc", "off", "single"],
                     help="wide attention calls (prefill) on the tcgen05 kernels, on the mma.sync kernel, or on the "
@@ -835,6 +967,15 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     metric = "committed tokens/s"
+
+    if args.cpu_ladder:
+        threads = os.cpu_count() or 1
+        for rows in [int(x) for x in args.cpu_ladder.split(",")]:
+            r = cpu_reference(args, rows, args.cpu_steps, threads, warmup=1)
+            print(json.dumps({"metric": "CPU reference-path committed tokens/s by batch rows", "workload": w.name,
+                              "rows": rows, "value": r["value"], "unit": "tokens/s", "seconds": r["seconds"],
+                              "cores": r["cores"], "sample": r["sample"]}), flush=True)
+        return
 
     if args.impl == "reference":
         if rank != 0:
@@ -884,6 +1025,10 @@ def main():
     if r is None:
         return
     peak, peak_kind = _peaks()
+    kernel_cfgs = None
+    if world == 1 and not args.no_kernel_configs:
+        kernel_cfgs = kernel_configs(args, device)
+    check = token_check(args, r["check_rows"], os.cpu_count() or 1) if rank == 0 else None
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_reference(args, args.cpu_rows, args.cpu_steps, os.cpu_count() or 1)
@@ -904,8 +1049,10 @@ def main():
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16" if "bfloat16" in r["dtype"] else "f32",
         "data": "synthetic prompts (seeded), random-init weights (seed 0)",
         "config": config_block(args, w, r["B"], world),
-        "step": ("deferred bonus: 1 target call of width k+1 + k+1 draft calls per step; token streams identical "
-                 "to the reference structure" if r["deferred"] else
+        "step": ("default step (target bonus call deferred into the next verify): 1 target call of width k+1 + "
+                 "k+1 draft calls per step; tokens, block tables, lengths and free lists identical to the "
+                 "reference structure; e2e driven by the reference scheduler's unchanged call "
+                 "(returned logits handed back)" if r["deferred"] else
                  "reference structure: 2 target + k+1 draft calls per step"),
         "e2e": {"value": hd_["e2e_tokens"] / (hd_["e2e_ms"] / 1000.0), "unit": "tokens/s",
                 "h2d_bytes_per_step": r["h2d"], "d2h_bytes_per_step": r["d2h"]},
@@ -927,6 +1074,8 @@ def main():
                                                   "kind": "port", "sample": cpu["sample"]},
         "clocks": r["clocks"],
         "gpu_launches": r["kernels_per_step"] * args.steps,
+        "token_check": check,
+        "kernel_configs": kernel_cfgs,
         "acceptance": {"rows_by_drafts_accepted": r["acc_hist"], "k": r["k"],
                        "note": "rank 0's rows over the timed steps, index = drafts accepted (0..k)"},
         "prefill": {"requests": r["B"], "prompt_tokens": r["prefill_tokens"], "seconds": r["prefill_s"],

@@ -22,6 +22,7 @@ def batched_forward_append(model, cache, request_ids, new_input_ids: torch.Tenso
     if len(set(request_ids)) != len(request_ids):
         raise ValueError("request_ids must be unique")
     dm = device_model(model, cache.dtype, cache.device)
+    cache._flush_ids(request_ids)  # a deferred target call owed to these rows runs first
     B, W = int(new_input_ids.shape[0]), int(new_input_ids.shape[1])
     ids_host = new_input_ids.reshape(-1)
     if ids_host.device.type == "cpu":

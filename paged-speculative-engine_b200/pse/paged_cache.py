@@ -17,6 +17,13 @@ Request ids map to slots on the host.  Lengths are mirrored on the host
 exactly (every length change is known there without a device read);
 ``num_blocks_in_use`` and ``allocator.num_free`` read the device.
 
+A target cache driven by the speculative step can hold *pending* slots: the
+row's last position (the step's final token) is reserved and counted, as the
+reference's bonus append leaves it, but its K/V is written by the next step's
+verify.  Tables, lengths and the free list are exact meanwhile; calls that
+read or extend a row's K/V (``append``, ``truncate``, ``gather``,
+``batched_forward_append``) first run the deferred target call for it.
+
 Errors keep the reference's exception types: ``MemoryError`` on exhaustion,
 ``ValueError`` on a duplicate request, a truncate beyond the length or a
 double free.  Device-detected errors (exhaustion inside a batched forward) are
@@ -177,10 +184,14 @@ class PagedKVCache:
         self.slot_version = 0  # bumped whenever a request id gets or loses a slot
         self.generation = 0  # bumped whenever device buffers move (captured graphs must be rebuilt)
         self._layer_structs = [self._layer_struct(l) for l in range(n_layers)]
-        # last token id appended to each slot by a forward (the deferred-bonus
-        # step re-runs it), and the slots whose last token is pending
+        # last token id of each slot (for a pending slot: the token whose
+        # position is reserved and counted but whose K/V the next step's
+        # verify writes), the pending slots, the call that completes them
+        # (set by the speculative step) and per-slot occupancy serials
         self.last_token = torch.zeros(self._blocks.num_slots, dtype=torch.int32, device=self.device)
-        self.deferred_slots: set[int] = set()
+        self.pending_slots: set[int] = set()
+        self._flusher = None
+        self._serial = np.zeros(self._blocks.num_slots, dtype=np.int64)
 
     # ------------------------------------------------------------------ internals
     def _layer_struct(self, layer: int) -> N.KVLayer:
@@ -234,6 +245,9 @@ class PagedKVCache:
         lens = np.zeros(num_slots, dtype=np.int64)
         lens[: old.num_slots] = self._len_np
         self._len_np = lens
+        ser = np.zeros(num_slots, dtype=np.int64)
+        ser[: old.num_slots] = self._serial
+        self._serial = ser
         self.generation += 1
 
     def ensure_capacity(self, request_ids, extra_tokens: int) -> None:
@@ -284,6 +298,24 @@ class PagedKVCache:
     def note_append(self, request_ids, width: int) -> None:
         self._len_np[self.slots_np(request_ids)] += width
 
+    def slot_serial(self, slot: int) -> int:
+        """Occupancy serial of ``slot`` (changes whenever a request takes or leaves it)."""
+        return int(self._serial[slot])
+
+    def flush_pending(self, slots=None) -> None:
+        """Complete pending slots (all of them, or those of ``slots`` that are
+        pending): run the target call the speculative step deferred, which
+        writes the pending token's K/V and that slot's next-token logits."""
+        if not self.pending_slots:
+            return
+        todo = sorted(self.pending_slots if slots is None else self.pending_slots.intersection(slots))
+        if todo:
+            self._flusher(self, todo)
+
+    def _flush_ids(self, request_ids) -> None:
+        if self.pending_slots:
+            self.flush_pending([self._slot[r] for r in request_ids if r in self._slot])
+
     def note_last_tokens(self, slots: torch.Tensor, ids: torch.Tensor, rows: int, width: int) -> None:
         """Record the last token id each row appended (device op, stream-ordered)."""
         self.last_token.index_copy_(0, slots.long(), ids.view(rows, width)[:, width - 1].to(torch.int32))
@@ -295,10 +327,11 @@ class PagedKVCache:
             raise ValueError(f"request {request_id} already exists in this cache")
         if not self._free_slots:
             self._grow(self._blocks.num_slots * 2, self._blocks.max_blocks)
-        self._slot[request_id] = self._free_slots.pop()
-        self._len_np[self._slot[request_id]] = 0
+        s = self._slot[request_id] = self._free_slots.pop()
+        self._len_np[s] = 0
+        self._serial[s] += 1
         self.slot_version += 1
-        self.deferred_slots.discard(self._slot[request_id])
+        self.pending_slots.discard(s)
 
     def length(self, request_id: str) -> int:
         return int(self._len_np[self._slot[request_id]])
@@ -313,6 +346,7 @@ class PagedKVCache:
 
     def append(self, request_id: str, new_k, new_v) -> None:
         """engine/paged_cache.py:104-138: new_k / new_v are per-layer [n_heads, n, head_dim]."""
+        self._flush_ids([request_id])
         n = int(new_k[0].shape[1])
         self.ensure_capacity([request_id], n)
         slots = torch.tensor([self._slot[request_id]], dtype=torch.int32, device=self.device)
@@ -329,6 +363,7 @@ class PagedKVCache:
 
     def truncate(self, request_id: str, new_length: int) -> None:
         """engine/paged_cache.py:140-154."""
+        self._flush_ids([request_id])
         old = self.length(request_id)
         if new_length > old:
             raise ValueError(f"truncate({new_length}) > current length {old}")
@@ -341,8 +376,9 @@ class PagedKVCache:
         """engine/paged_cache.py:156-160."""
         s = self._slot.pop(request_id)
         self._len_np[s] = 0
+        self._serial[s] += 1
         self.slot_version += 1
-        self.deferred_slots.discard(s)
+        self.pending_slots.discard(s)
         slots = torch.tensor([s], dtype=torch.int32).to(self.device, non_blocking=True)
         N.call("pse_kv_release", self.state, slots.data_ptr(), 1, N.stream_ptr())
         self._free_slots.append(s)
@@ -353,8 +389,9 @@ class PagedKVCache:
             return
         slots = [self._slot.pop(r) for r in request_ids]
         self._len_np[slots] = 0
+        self._serial[slots] += 1
         self.slot_version += 1
-        self.deferred_slots.difference_update(slots)
+        self.pending_slots.difference_update(slots)
         t = torch.tensor(slots, dtype=torch.int32).to(self.device, non_blocking=True)
         N.call("pse_kv_release", self.state, t.data_ptr(), len(slots), N.stream_ptr())
         self._free_slots.extend(slots)
@@ -362,6 +399,7 @@ class PagedKVCache:
     def gather(self, request_ids):
         """engine/paged_cache.py:162-198: padded per-layer [B, H, max_len, hd]
         K and V, the [B, max_len] padding mask and the [B] lengths (device tensors)."""
+        self._flush_ids(request_ids)
         lengths = torch.tensor([self.length(r) for r in request_ids], dtype=torch.long)
         max_len = int(lengths.max().item()) if len(lengths) else 0
         batch = len(request_ids)

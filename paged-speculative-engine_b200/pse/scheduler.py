@@ -60,12 +60,12 @@ class _Active:
 @torch.no_grad()
 def run_continuous_speculative_batches(draft_model, target_model, requests, draft_cache, target_cache,
                                        max_batch_size, k=4, temperature=0.0, generator=None, *,
-                                       uniform_fn=None, on_step=None, use_graph=None, defer_bonus=False,
+                                       uniform_fn=None, on_step=None, use_graph=None, defer_bonus=None,
                                        device_bookkeeping=None):
     """engine/scheduler.py:61-128.  ``uniform_fn(request_ids, steps, n)`` (optional)
     supplies explicit uniforms per step; ``on_step(ids, result)`` observes steps;
-    ``defer_bonus`` folds the target's bonus call into the next verify (see
-    ``batched_speculative_step``); ``device_bookkeeping`` (default: whenever
+    ``defer_bonus`` (default: on) defers the target's bonus call into the next
+    verify (see ``batched_speculative_step``; False runs it in every step); ``device_bookkeeping`` (default: whenever
     ``on_step`` is not given) keeps the per-row token lists and finish tests
     on the device, False runs them on the host as the reference does."""
     requests = list(requests)

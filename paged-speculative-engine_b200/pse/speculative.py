@@ -17,6 +17,15 @@ from the device Philox stream keyed by (seed, request id, request step).
 ``draft_next_logits`` / ``target_next_logits`` in the result are views of
 per-request device buffers that the next step of the same request overwrites;
 passing them back unchanged (as the scheduler does) costs no copy.
+
+By default the target's width-1 bonus call is deferred: the final token's
+position is reserved where the reference's bonus append puts it (block
+tables, lengths and free lists stay the reference's), and the next step's
+verify runs at width k+1 from that position, its column 0 giving the logits
+the bonus call would have returned.  The step then costs one target pass
+instead of two.  The returned ``target_next_logits`` are ``PendingLogits``
+(pse/pending.py): handing them back is free, reading them runs the deferred
+call first.  ``defer_bonus=False`` runs the bonus call inside the step.
 """
 from __future__ import annotations
 
@@ -29,6 +38,7 @@ import torch
 from . import _native as N
 from .device_model import device_model
 from .engine import Scratch, forward, lm_head, scratch_for
+from .pending import pending_view
 
 DEFAULT_SEED = 0x5EED5EED
 USE_GRAPHS = True  # replay steps from CUDA graphs (from the second step of a batch size on)
@@ -73,6 +83,52 @@ def next_logits_views(cache, vocab: int) -> list:
         cached = (buf, list(buf.unbind(0)))
         cache._next_views = cached
     return cached[1]
+
+
+def pending_views(cache, vocab: int, slots: np.ndarray) -> list:
+    """One ``PendingLogits`` per slot over ``next_logits_buffer`` (see
+    ``next_logits_views``), bound to the slot's current occupant: entries of
+    ``slots`` whose occupant changed since they were made are remade."""
+    buf = next_logits_buffer(cache, vocab)
+    cached = getattr(cache, "_pending_views", None)
+    if cached is None or cached[0] is not buf or len(cached[2]) != buf.shape[0]:
+        rows = next_logits_views(cache, vocab)
+        ser = cache._serial[: buf.shape[0]].copy()
+        cached = (buf, ser, [pending_view(rows[s], cache, s) for s in range(buf.shape[0])])
+        cache._pending_views = cached
+        return cached[2]
+    _, ser, views = cached
+    stale = slots[cache._serial[slots] != ser[slots]]
+    if len(stale):
+        rows = next_logits_views(cache, vocab)
+        for s in stale.tolist():
+            views[s] = pending_view(rows[s], cache, s)
+            ser[s] = cache._serial[s]
+    return views
+
+
+@torch.no_grad()
+def _flush_pending(cache, slots) -> None:
+    """The target call a deferred step left owing for ``slots`` (pending slots
+    of ``cache``): one width-1 forward over each row's final token at its
+    reserved position (nothing allocated), writing its K/V and the slot's
+    next-token logits -- the reference's bonus call (engine/speculative.py:
+    170-175), run late."""
+    dm = cache._pending_dm
+    st_np = np.asarray(slots, dtype=np.int32)
+    B = len(st_np)
+    lens = cache.lengths_np(st_np)
+    dev = cache.device
+    slots_t = torch.from_numpy(st_np).to(dev)
+    base = torch.from_numpy((lens - 1).astype(np.int32)).to(dev)
+    ids = cache.last_token.index_select(0, slots_t.long())
+    buf = next_logits_buffer(cache, dm.vocab)
+    logits = torch.empty(B, dm.vocab, dtype=torch.float32, device=dev)
+    forward(dm, cache, slots_t, ids, B, 1, base, int(lens.max()), logits, scratch=scratch_for(dm), reserve=False)
+    N.call("pse_scatter_rows", logits.data_ptr(), dm.vocab, slots_t.data_ptr(), B, dm.vocab, buf.data_ptr(), dm.vocab,
+           buf.shape[0], N.stream_ptr())
+    cache.pending_slots.difference_update(st_np.tolist())
+    cache.check_status("deferred target call")
 
 
 def _check_ids(ids, vocab: int) -> None:
@@ -251,8 +307,9 @@ class _StepBuffers:
         self.n_acc = torch.empty(B, **i32)
         self.final = torch.empty(B, **i32)
         self.u = torch.zeros(B, 2 * k + 1, dtype=torch.float64, device=device)
-        self.vids = None    # deferred-bonus mode: verify ids [B, k+1] and logits [B*(k+1), V]
+        self.vids = None    # verify from pending rows: ids [B, k+1], logits [B*(k+1), V], first positions [B]
         self.vlog2 = None
+        self.basem1 = torch.empty(B, **i32)
         self.nacc1 = torch.empty(B, **i32)
         # the step's result, copied to pinned host memory in one transfer:
         # [tokens B*(k+1) | n_acc B | status_d | status_t | finished count | finished rows B]
@@ -317,7 +374,6 @@ class StepRunner:
         self.use_graphs = USE_GRAPHS
         self.sc_d = Scratch(dm_d)
         self.sc_t = Scratch(dm_t)
-        self.tpending = None  # per target slot: token not yet appended (deferred-bonus mode)
         self.commit: CommitArena | None = None  # the scheduler's device output arena
         self._slots_key, self._slots_ids, self._slots_np = None, None, None
         self._ws_sizes: dict = {}  # (rows, draft / target context bound) -> split-KV workspace bytes
@@ -330,7 +386,10 @@ class StepRunner:
         return bound
 
     def _program(self, b: _StepBuffers, T: float, philox: bool, max_ctx_d: int, max_ctx_t: int,
-                 defer: bool = False, commit: CommitArena | None = None) -> None:
+                 in_pending: bool = False, out_defer: bool = False, commit: CommitArena | None = None) -> None:
+        """One step on the device.  ``in_pending``: every row's last target
+        position is pending (reserved, K/V unwritten); ``out_defer``: leave the
+        rows pending instead of running the target's bonus call."""
         k, V, B = self.k, self.V, b.B
         st = N.stream_ptr()
         dnext = next_logits_buffer(self.dcache, V)
@@ -356,21 +415,25 @@ class StepRunner:
                 # the last round's position is still allocated here, so the draft's
                 # block tables and free list follow the reference's sequence exactly
                 N.call("pse_kv_reserve", self.dcache.state, b.slots_d.data_ptr(), B, 1, b.base[j].data_ptr(), st)
-        if not defer:
+        if not in_pending:
             # verify: one width-k target call (engine/speculative.py:115-117)
             forward(self.dm_t, self.tcache, b.slots_t, b.drafts.view(-1), B, k, b.base[k], max_ctx_t, b.vlog,
                     scratch=self.sc_t, row_order=b.order_t)
             t0, t0_stride, t0_index = tnext.data_ptr(), V, b.slots_t.data_ptr()
             ver, v_row = b.vlog.data_ptr(), k * V
         else:
-            # verify of width k+1: the previous step's final token (never appended
-            # to the target) followed by the k drafts; column 0 predicts what the
-            # reference's bonus call would have returned as target_next.
-            slots_t = b.slots_t.long()
-            b.vids[:, 0] = self.tpending.index_select(0, slots_t)
+            # every row's last position holds the previous step's final token,
+            # reserved and counted but not yet computed.  The k draft positions
+            # are reserved as the reference's width-k verify appends them, then
+            # one width-(k+1) call runs from the pending position over
+            # [final, d_1..d_k] without allocating; its column 0 gives what the
+            # reference's bonus call returned as target_next.
+            N.call("pse_kv_reserve", self.tcache.state, b.slots_t.data_ptr(), B, k, b.base[k].data_ptr(), st)
+            torch.sub(b.base[k], 1, out=b.basem1)
+            b.vids[:, 0] = self.tcache.last_token.index_select(0, b.slots_t.long())
             b.vids[:, 1:] = b.drafts
-            forward(self.dm_t, self.tcache, b.slots_t, b.vids.view(-1), B, k + 1, b.base[k], max_ctx_t, b.vlog2,
-                    scratch=self.sc_t, row_order=b.order_t)
+            forward(self.dm_t, self.tcache, b.slots_t, b.vids.view(-1), B, k + 1, b.basem1, max_ctx_t, b.vlog2,
+                    scratch=self.sc_t, row_order=b.order_t, reserve=False)
             t0, t0_stride, t0_index = b.vlog2.data_ptr(), (k + 1) * V, None
             ver, v_row = b.vlog2.data_ptr() + 4 * V, (k + 1) * V
         # accept / reject / resample (engine/speculative.py:119-157)
@@ -387,16 +450,10 @@ class StepRunner:
         # commit (engine/speculative.py:159-164)
         N.call("pse_kv_truncate", self.dcache.state, b.slots_d.data_ptr(), B, None, b.base[0].data_ptr(),
                b.n_acc.data_ptr(), st)
-        torch.add(b.n_acc, 1, out=b.nacc1)
-        if not defer:
-            N.call("pse_kv_truncate", self.tcache.state, b.slots_t.data_ptr(), B, None, b.base[k].data_ptr(),
-                   b.n_acc.data_ptr(), st)
-        else:
-            N.call("pse_kv_truncate", self.tcache.state, b.slots_t.data_ptr(), B, None, b.base[k].data_ptr(),
-                   b.nacc1.data_ptr(), st)
-            self.tpending.index_copy_(0, slots_t, b.final)
-        # bonus forwards (engine/speculative.py:166-177); the target's is folded
-        # into the next verify in deferred mode.  The draft's is one width-2
+        N.call("pse_kv_truncate", self.tcache.state, b.slots_t.data_ptr(), B, None, b.base[k].data_ptr(),
+               b.n_acc.data_ptr(), st)
+        # bonus forwards (engine/speculative.py:166-177); the target's is
+        # deferred to the next verify when out_defer.  The draft's is one width-2
         # call: [x_{k-1}, final] when every draft was accepted (the last round's
         # token was never computed), else [final, final] whose second position
         # lies past the row's length (its K/V lands in a block the row holds
@@ -417,46 +474,26 @@ class StepRunner:
         lm_head(self.dm_d, b.hsel, b.blog)
         N.call("pse_scatter_rows", b.blog.data_ptr(), V, b.slots_d.data_ptr(), B, V, dnext.data_ptr(), V,
                dnext.shape[0], st)
-        if not defer:
+        if not out_defer:
             forward(self.dm_t, self.tcache, b.slots_t, b.final, B, 1, b.base[k + 2], max_ctx_t, b.blog,
                     scratch=self.sc_t, row_order=b.order_t)
             N.call("pse_scatter_rows", b.blog.data_ptr(), V, b.slots_t.data_ptr(), B, V, tnext.data_ptr(), V,
                    tnext.shape[0], st)
+        else:
+            # the reference's bonus append without its forward: the final
+            # token's position is reserved in the same order (same blocks)
+            N.call("pse_kv_reserve", self.tcache.state, b.slots_t.data_ptr(), B, 1, b.base[k + 2].data_ptr(), st)
         self.dcache.last_token.index_copy_(0, b.slots_d.long(), b.final)
-        if not defer:
-            self.tcache.last_token.index_copy_(0, b.slots_t.long(), b.final)
+        self.tcache.last_token.index_copy_(0, b.slots_t.long(), b.final)
         nt = B * (k + 1)
         b.pack[:nt].copy_(b.tokens.view(-1))
         b.pack[nt:nt + B].copy_(b.n_acc)
         b.pack[nt + B:nt + B + 1].copy_(self.dcache.status_tensor())
         b.pack[nt + B + 1:nt + B + 2].copy_(self.tcache.status_tensor())
 
-    def _enter_deferred(self, request_ids, slots_t) -> None:
-        """Move rows into the deferred-bonus state: the target forgets its last
-        token (truncate by one) and keeps it as the row's pending token, to be
-        re-run as column 0 of the next verify."""
-        tc = self.tcache
-        if self.tpending is None or self.tpending.shape[0] < tc.state.num_slots:
-            old = self.tpending
-            self.tpending = torch.zeros(tc.state.num_slots, dtype=torch.int32, device=self.device)
-            if old is not None:
-                self.tpending[: old.shape[0]] = old
-        if len(tc.deferred_slots) >= len(slots_t) and tc.deferred_slots.issuperset(slots_t):
-            return
-        new = [(r, s) for r, s in zip(request_ids, slots_t) if s not in tc.deferred_slots]
-        if not new:
-            return
-        idx = torch.tensor([s for _, s in new], dtype=torch.long).to(self.device)
-        self.tpending.index_copy_(0, idx, tc.last_token.index_select(0, idx))
-        for r, s in new:
-            if tc.length(r) < 1:
-                raise ValueError(f"request {r} has no token to defer")
-            tc.truncate(r, tc.length(r) - 1)
-            tc.deferred_slots.add(s)
-
     # ---------------------------------------------------------------- host side
     def step(self, request_ids, draft_next_logits, target_next_logits, temperature, generator=None,
-             uniforms=None, use_graph=None, defer_bonus: bool = False) -> BatchStepResult:
+             uniforms=None, use_graph=None, defer_bonus=None) -> BatchStepResult:
         k, V = self.k, self.V
         B = len(request_ids)
         if B == 0:
@@ -474,20 +511,26 @@ class StepRunner:
             self._slots_key, self._slots_ids, self._slots_np = skey, list(request_ids), (sd_np, st_np)
         dviews = next_logits_views(dc, V)
         tviews = next_logits_views(tc, V)
+        pviews = pending_views(tc, V, st_np)
         sd = sd_np.tolist()
         stt = st_np.tolist()
-        if not defer_bonus and tc.deferred_slots and not tc.deferred_slots.isdisjoint(stt):
-            raise ValueError("request is in the deferred-bonus state: keep stepping it with defer_bonus=True")
         # logits handed back unchanged (the previous step's views) need no copy
-        for given, views, slots in ((draft_next_logits, dviews, sd),
-                                    (None if defer_bonus else target_next_logits, tviews, stt)):
-            if given is None:
-                continue
-            vals = [given[r] for r in request_ids]
-            own = [views[x] for x in slots]
-            if not all(map(operator.is_, vals, own)):
-                for t, v in zip(vals, own):
-                    if t is not v and t.data_ptr() != v.data_ptr():
+        vals = [draft_next_logits[r] for r in request_ids]
+        own = [dviews[x] for x in sd]
+        if not all(map(operator.is_, vals, own)):
+            for t, v in zip(vals, own):
+                if t is not v and t.data_ptr() != v.data_ptr():
+                    v.copy_(t.reshape(-1), non_blocking=True)
+        vals = [target_next_logits[r] for r in request_ids]
+        if not all(map(operator.is_, vals, map(pviews.__getitem__, stt))):
+            foreign = [(t, x) for t, x in zip(vals, stt) if t is not pviews[x] and t is not tviews[x]]
+            if foreign:
+                # rows given other logits: a pending row's deferred call runs first
+                # (it writes the row's K/V), then the given values replace its logits
+                tc.flush_pending([x for _, x in foreign])
+                for t, x in foreign:
+                    v = tviews[x]
+                    if t.data_ptr() != v.data_ptr():
                         v.copy_(t.reshape(-1), non_blocking=True)
         steps = self.request_steps
         key_np = steps_np = None
@@ -499,8 +542,7 @@ class StepRunner:
         def while_device_runs():
             # the next-logits dicts depend only on the slots: build them during the step
             views.append(dict(zip(request_ids, map(dviews.__getitem__, sd))))
-            views.append(dict.fromkeys(request_ids) if defer_bonus
-                         else dict(zip(request_ids, map(tviews.__getitem__, stt))))
+            views.append(dict(zip(request_ids, map((tviews if defer_bonus is False else pviews).__getitem__, stt))))
 
         b, nacc_np = self._run(request_ids, sd_np, st_np, temperature, generator, uniforms, use_graph, defer_bonus,
                                key_np, steps_np, while_device_runs=while_device_runs)
@@ -514,7 +556,7 @@ class StepRunner:
         return BatchStepResult(accepted, n_acc, dn, tn)
 
     def step_rows(self, request_ids, sd_np, st_np, ords_np, commit: CommitArena, temperature, generator=None,
-                  uniforms=None, use_graph=None, defer_bonus: bool = False, req_key_np=None, steps_np=None):
+                  uniforms=None, use_graph=None, defer_bonus=None, req_key_np=None, steps_np=None):
         """The scheduler's form of ``step``: rows come as slot arrays, each
         request's next logits are already in its slot's row (as prefill and
         every step leave them), the accepted tokens stay on the device in
@@ -541,8 +583,18 @@ class StepRunner:
         k, V = self.k, self.V
         B = len(request_ids)
         dc, tc = self.dcache, self.tcache
-        if not defer_bonus and tc.deferred_slots and not tc.deferred_slots.isdisjoint(st_np.tolist()):
-            raise ValueError("request is in the deferred-bonus state: keep stepping it with defer_bonus=True")
+        out_defer = defer_bonus is not False
+        # rows whose target call is still owed: the fast program needs all of
+        # them pending; a mixed batch (rows just admitted, or given other
+        # logits) or an eager step first completes the pending ones
+        in_pending = False
+        if tc.pending_slots:
+            stl = st_np.tolist()
+            n_p = sum(map(tc.pending_slots.__contains__, stl))
+            if n_p == B and out_defer:
+                in_pending = True
+            elif n_p:
+                tc.flush_pending(stl)
         len_d = dc.lengths_np(sd_np)
         len_t = tc.lengths_np(st_np)
         for dm, c, lens in ((self.dm_d, dc, len_d), (self.dm_t, tc, len_t)):
@@ -553,14 +605,9 @@ class StepRunner:
         b = self.bufs.get(B)
         if b is None:
             b = self.bufs[B] = _StepBuffers(B, k, V, self.device, self.dm_d.d_model, self.dm_d.dtype)
-        if defer_bonus and b.vids is None:
+        if in_pending and b.vids is None:
             b.vids = torch.empty(B, k + 1, dtype=torch.int32, device=self.device)
             b.vlog2 = torch.empty(B * (k + 1), V, dtype=torch.float32, device=self.device)
-        if defer_bonus:
-            n_before = len(tc.deferred_slots)
-            self._enter_deferred(request_ids, st_np.tolist())
-            if len(tc.deferred_slots) != n_before:  # rows entered the deferred state: lengths moved
-                len_t = tc.lengths_np(st_np)
         T = float(temperature)
         philox = False
         hin = b.host_in
@@ -601,27 +648,26 @@ class StepRunner:
                                     mct) for w in (k + 1, k, 1)))
             self.sc_d.ensure_ws(ws[0])
             self.sc_t.ensure_ws(ws[1])
-        key = (B, T, philox, defer_bonus, dc.generation, tc.generation, self.sc_d.generation, self.sc_t.generation,
-               None if self.tpending is None else self.tpending.data_ptr(),
-               None if commit is None else (id(commit), commit.generation))
+        key = (B, T, philox, in_pending, out_defer, dc.generation, tc.generation, self.sc_d.generation,
+               self.sc_t.generation, None if commit is None else (id(commit), commit.generation))
         if graphs and key in self.graphs:
             self.graphs[key].replay()
         elif graphs and key in self.warm:
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g):
-                self._program(b, T, philox, mcd, mct, defer_bonus, commit)
+                self._program(b, T, philox, mcd, mct, in_pending, out_defer, commit)
             self.graphs[key] = g
             g.replay()
         else:
             if graphs:
                 # eager steps use the same context bound so the captured
                 # program's buffers (split-KV workspace) are already sized
-                self._program(b, T, philox, mcd, mct, defer_bonus, commit)
+                self._program(b, T, philox, mcd, mct, in_pending, out_defer, commit)
                 self.warm.add(key)
             else:
                 ld = int(len_d.max()) + k + 1
                 lt = int(len_t.max()) + k + 1
-                self._program(b, T, philox, ld, lt + 1, defer_bonus, commit)
+                self._program(b, T, philox, ld, lt + 1, in_pending, out_defer, commit)
         nt = B * (k + 1)
         if commit is None:
             b.host_pack.copy_(b.pack, non_blocking=True)
@@ -639,6 +685,10 @@ class StepRunner:
         nacc_np = hpn[nt:nt + B].astype(np.int64)
         dc.note_lengths_slots(sd_np, len_d + nacc_np + 1)
         tc.note_lengths_slots(st_np, len_t + nacc_np + 1)
+        if out_defer:
+            tc.pending_slots.update(st_np.tolist())
+            tc._pending_dm = self.dm_t
+            tc._flusher = _flush_pending
         return b, nacc_np
 
 
@@ -656,16 +706,17 @@ def runner_for(draft_model, target_model, draft_cache, target_cache, k: int) -> 
 @torch.no_grad()
 def batched_speculative_step(draft_model, target_model, request_ids, draft_cache, target_cache,
                              draft_next_logits, target_next_logits, k, temperature, generator=None, *,
-                             uniforms=None, use_graph=None, defer_bonus=False) -> BatchStepResult:
+                             uniforms=None, use_graph=None, defer_bonus=None) -> BatchStepResult:
     """engine/speculative.py:76-177 on the device.
 
-    ``defer_bonus=True`` folds the target's width-1 bonus call into the next
-    step's verify, which then runs at width k+1 (the final token, then the k
-    drafts): one target pass per step instead of two, same accepted tokens.
-    In that mode ``target_next_logits`` in the result are ``None`` (the values
-    are computed, as column 0 of the next verify, but never materialised),
-    ``target_cache.length()`` is one less than the reference's (the final token
-    is pending), and the request must keep being stepped in this mode."""
+    By default (``defer_bonus`` None or True) the target's width-1 bonus call
+    is deferred into the next step's verify, which runs at width k+1 (the
+    final token, then the k drafts): one target pass per step instead of two,
+    same accepted tokens, same block tables, lengths and free lists.  The
+    result's ``target_next_logits`` are then ``PendingLogits``: passing them
+    back unchanged is free, reading them runs the deferred call first.
+    ``defer_bonus=False`` runs the bonus call inside the step (the reference's
+    structure; the logits are plain views)."""
     runner = runner_for(draft_model, target_model, draft_cache, target_cache, k)
     return runner.step(list(request_ids), draft_next_logits, target_next_logits, temperature, generator,
                        uniforms, use_graph, defer_bonus)

@@ -92,3 +92,57 @@ def test_device_philox_stream_first_token_distribution():
                                             k=3, temperature=1.0, use_graph=False)
         samples.append(step.accepted_tokens[f"r{trial}"][0])
     assert _pvalue(samples, _true(t, prompt)) > ALPHA
+
+
+@pytest.mark.parametrize("k", [2, 8])
+def test_sampled_workload_first_tokens_match_target_distributions(k):
+    """The T = 1 configuration's 64 requests (TinyGPT pair, vocab 256, prompts
+    U[8,64]) share every step; over independent trials (device Philox stream,
+    one seed per trial) each request's first output token must follow the
+    target's softmax after its own prompt.  Per request, a chi-squared test
+    (the reference's method; bins whose expected count is below 5 pooled);
+    the 64 p-values must pass a Bonferroni bound (min p > 0.01 / 64) and
+    Fisher's combined test (p > 0.01)."""
+    import numpy as np
+    from scipy.stats import chi2
+
+    import pse
+    import pse.speculative as S
+    from pse import workload as wl
+    w = wl.WORKLOADS["tiny-sampled"]
+    torch.manual_seed(0)
+    d = TinyGPT(ModelConfig(vocab_size=w.pair.vocab, **w.pair.draft)).eval()
+    t = TinyGPT(ModelConfig(vocab_size=w.pair.vocab, **w.pair.target)).eval()
+    prompts = wl.prompts(w, seed=0)
+    n, trials, V = len(prompts), 1500, w.pair.vocab
+    pd, pt = w.pair.draft, w.pair.target
+    nb = sum((len(p) + 2 * k + 2 + w.block_size - 1) // w.block_size for p in prompts) + 8
+    dc = pse.PagedKVCache(pd["n_layers"], pd["n_heads"], pd["d_model"] // pd["n_heads"], w.block_size, nb,
+                          max_requests=n)
+    tc = pse.PagedKVCache(pt["n_layers"], pt["n_heads"], pt["d_model"] // pt["n_heads"], w.block_size, nb,
+                          max_requests=n)
+    counts = np.zeros((n, V), dtype=np.int64)
+    for trial in range(trials):
+        ids = [f"t{trial}_{i}" for i in range(n)]
+        out = pse.prefill_requests(d, t, dc, tc, ids, prompts)
+        S.runner_for(d, t, dc, tc, k).seed = 5000 + trial
+        res = pse.batched_speculative_step(d, t, ids, dc, tc, {r: out[r][0] for r in ids},
+                                           {r: out[r][1] for r in ids}, k, 1.0)
+        for i, r in enumerate(ids):
+            counts[i, res.accepted_tokens[r][0]] += 1
+        dc.free_requests(ids)
+        tc.free_requests(ids)
+    pvals = []
+    for i, p in enumerate(prompts):
+        probs = _true(t, p).double().numpy()
+        exp = probs * trials
+        small = exp < 5
+        obs_b = np.append(counts[i][~small], counts[i][small].sum())
+        exp_b = np.append(exp[~small], exp[small].sum())
+        keep = exp_b > 0
+        obs_b, exp_b = obs_b[keep], exp_b[keep] / exp_b[keep].sum() * trials
+        pvals.append(chisquare(obs_b, exp_b)[1])
+    pvals = np.array(pvals)
+    fisher = chi2.sf(-2 * np.log(np.maximum(pvals, 1e-300)).sum(), 2 * n)
+    assert pvals.min() > ALPHA / n, sorted(pvals)[:5]
+    assert fisher > ALPHA, fisher

@@ -44,7 +44,12 @@ def _state(cache):
 
 
 @pytest.mark.parametrize("graphs", [False, True])
-def test_tiny_workload_reproduces_reference_trace(graphs):
+@pytest.mark.parametrize("defer", [None, False])
+def test_tiny_workload_reproduces_reference_trace(graphs, defer):
+    """Both step structures: the default (target bonus call deferred into the
+    next verify, its position reserved where the reference appends it) and
+    the reference's own (bonus call inside the step) leave the same tables,
+    lengths and free lists after every step."""
     import pse
     g = _load("tiny_greedy.json")
     tiny, d, t = _tiny()
@@ -56,7 +61,8 @@ def test_tiny_workload_reproduces_reference_trace(graphs):
 
     reqs = [pse.Request(r, p, tiny.max_new_tokens) for r, p in zip(g["request_ids"], g["prompts"])]
     res = pse.run_continuous_speculative_batches(d, t, reqs, dc, tc, tiny.max_batch_size, k=tiny.k,
-                                                 temperature=0.0, on_step=on_step, use_graph=graphs)
+                                                 temperature=0.0, on_step=on_step, use_graph=graphs,
+                                                 defer_bonus=defer)
     assert {r.request_id: r.output_ids for r in res} == g["outputs"]
     assert len(trace) == len(g["steps"])
     for n, (got, ref) in enumerate(zip(trace, g["steps"])):
@@ -69,26 +75,7 @@ def test_tiny_workload_reproduces_reference_trace(graphs):
         assert tfree == ref["target"]["free"], n
     assert dc.allocator.free_list() == g["final_free"]["draft"]
     assert tc.allocator.free_list() == g["final_free"]["target"]
-
-
-@pytest.mark.parametrize("graphs", [False, True])
-def test_tiny_workload_deferred_bonus_same_outputs(graphs):
-    """Folding the target's bonus call into the next verify (width k+1) changes
-    no token: every request's output and every step's accepted tokens equal
-    the reference's."""
-    import pse
-    g = _load("tiny_greedy.json")
-    tiny, d, t = _tiny()
-    dc, tc = _caches(tiny, g["num_blocks"])
-    steps = []
-    reqs = [pse.Request(r, p, tiny.max_new_tokens) for r, p in zip(g["request_ids"], g["prompts"])]
-    res = pse.run_continuous_speculative_batches(
-        d, t, reqs, dc, tc, tiny.max_batch_size, k=tiny.k, temperature=0.0, use_graph=graphs, defer_bonus=True,
-        on_step=lambda ids, r: steps.append(dict(r.accepted_tokens)))
-    assert {r.request_id: r.output_ids for r in res} == g["outputs"]
-    assert steps == [s["accepted"] for s in g["steps"]]
-    assert dc.allocator.num_free == g["num_blocks"] and tc.allocator.num_free == g["num_blocks"]
-    assert not tc.deferred_slots
+    assert not tc.pending_slots
 
 
 def test_prompt_logits_match_reference_fp32():

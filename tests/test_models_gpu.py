@@ -149,3 +149,41 @@ def test_deferred_bonus_property_matches_solo_greedy():
         for q in reqs:
             assert by[q.request_id] == generate_cached(t, torch.tensor([q.prompt_ids]), q.max_new_tokens), (trial, q)
         assert dc.allocator.num_free == nb and tc.allocator.num_free == nb
+
+
+@pytest.mark.parametrize("k", [2, 4, 8])
+def test_sampled_workload_matches_oracle_draw_for_draw(k):
+    """The T = 1 configuration itself (TinyGPT pair fp32, 64 requests, prompts
+    U[8,64], 128 new tokens, block 16, all 64 rows in every step) at k = 2, 4,
+    8: with the same explicit Philox uniforms, every step's accepted tokens
+    (hence accepted_len) equal the oracle's."""
+    import pse
+    from pse import workload as wl
+    w = wl.WORKLOADS["tiny-sampled"]
+    torch.manual_seed(0)
+    d = TinyGPT(ModelConfig(vocab_size=w.pair.vocab, **w.pair.draft)).eval()
+    t = TinyGPT(ModelConfig(vocab_size=w.pair.vocab, **w.pair.target)).eval()
+    prompts = wl.prompts(w, seed=0)
+    seed = 77 + k
+
+    def uniform_fn(ids, steps, n):
+        return step_uniforms(seed, [request_key(r) for r in ids], steps, n)
+
+    nb = sum((len(p) + w.max_new_tokens + 2 * k + 2 + w.block_size - 1) // w.block_size for p in prompts) + 8
+    pd, pt = w.pair.draft, w.pair.target
+    oracle_steps, device_steps = [], []
+    ores = OS.run_continuous_speculative_batches(
+        d, t, [OS.Request(f"r{i}", p, w.max_new_tokens) for i, p in enumerate(prompts)],
+        OracleCache(pd["n_layers"], pd["n_heads"], pd["d_model"] // pd["n_heads"], w.block_size, nb),
+        OracleCache(pt["n_layers"], pt["n_heads"], pt["d_model"] // pt["n_heads"], w.block_size, nb),
+        w.max_batch_size, k=k, temperature=1.0, uniform_fn=uniform_fn,
+        on_step=lambda ids, r: oracle_steps.append([r.num_draft_accepted[x] for x in ids]))
+    dc = pse.PagedKVCache(pd["n_layers"], pd["n_heads"], pd["d_model"] // pd["n_heads"], w.block_size, nb)
+    tc = pse.PagedKVCache(pt["n_layers"], pt["n_heads"], pt["d_model"] // pt["n_heads"], w.block_size, nb)
+    pres = pse.run_continuous_speculative_batches(
+        d, t, [pse.Request(f"r{i}", p, w.max_new_tokens) for i, p in enumerate(prompts)], dc, tc,
+        w.max_batch_size, k=k, temperature=1.0, uniform_fn=uniform_fn, device_bookkeeping=False,
+        on_step=lambda ids, r: device_steps.append([r.num_draft_accepted[x] for x in ids]))
+    assert device_steps == oracle_steps  # accepted_len of every row at every step
+    assert {r.request_id: r.output_ids for r in pres} == {r.request_id: r.output_ids for r in ores}
+    assert max(max(s) for s in device_steps) >= 2  # multi-draft accepts happened

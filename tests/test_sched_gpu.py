@@ -147,9 +147,8 @@ def test_device_bookkeeping_reproduces_golden_outputs():
         res = pse.run_continuous_speculative_batches(d, t, reqs, dc, tc, tiny.max_batch_size, k=tiny.k,
                                                      temperature=0.0, defer_bonus=defer)
         assert {r.request_id: r.output_ids for r in res} == g["outputs"]
-        if not defer:
-            assert dc.allocator.free_list() == g["final_free"]["draft"]
-            assert tc.allocator.free_list() == g["final_free"]["target"]
+        assert dc.allocator.free_list() == g["final_free"]["draft"]
+        assert tc.allocator.free_list() == g["final_free"]["target"]
         assert dc.allocator.num_free == g["num_blocks"] and tc.allocator.num_free == g["num_blocks"]
 
 
