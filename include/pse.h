@@ -185,6 +185,19 @@ int pse_paged_attention_noalloc(pse_block_state st, pse_kv_layer kv, const void 
  * two); no counterpart in the reference. */
 int pse_attention_force_generic(int32_t on);
 
+/* on != 0 (the default): the per-token kernels of the forward (embedding,
+ * residual add + norm, bf16 epilogues, K/V append) and the projection GEMM
+ * launch with programmatic dependent launch, so each may start while the
+ * kernel before it finishes and waits for it before touching memory; 0
+ * launches them plainly.  Process-wide; no counterpart in the reference. */
+int pse_launch_overlap(int32_t on);
+
+/* on != 0 (the default): pse_gemm_bf16 runs wide problems on two-SM tiles
+ * (a cluster of two CTAs, tcgen05.mma.cta_group::2, 256 x 256 outputs) and
+ * the rest on single-CTA tiles; 0: single-CTA tiles always (tests compare
+ * the two).  No counterpart in the reference. */
+int pse_gemm_pair_tiles(int32_t on);
+
 /* Wide calls (at least 64 query rows per row and KV head: prompt prefill, a
  * wide batched append) with bf16 pools, head_dim 64/128, block_size 16..128
  * dividing 128 and 16-byte aligned q / out rows run a tcgen05 kernel (scores

@@ -107,6 +107,40 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int* tmp, int* total)
 
 __host__ __device__ __forceinline__ int ceil_div(int a, int b) { return (a + b - 1) / b; }
 
+// ---------------------------------------------------------------- programmatic dependent launch
+// A kernel launched with launch_pdl may start while the kernel before it on
+// the stream is still running: everything before pdl_wait() overlaps that
+// kernel's tail, so a kernel must call pdl_wait() before it reads or writes
+// any memory an earlier kernel touches (all of them call it first thing).
+// pdl_trigger() lets the next kernel launch once every CTA of this one has
+// issued it (or exited).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;"); }
+
+// Whether the small per-token kernels launch with programmatic dependent
+// launch (pse_launch_overlap); on by default.
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                              Args... args) {
+  if (!pdl_enabled()) {
+    kern<<<grid, block, smem, s>>>(args...);
+    return cudaGetLastError();
+  }
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
 __device__ __forceinline__ int blocks_for(int n_tokens, int block_size) {
   return n_tokens == 0 ? 0 : (n_tokens - 1) / block_size + 1;
 }

@@ -224,9 +224,11 @@ __global__ void append_kernel(pse_block_state st, T* __restrict__ k_pool, T* __r
                               int head_dim, const T* __restrict__ k_src, const T* __restrict__ v_src,
                               int64_t tok_stride, int64_t head_stride, const int32_t* __restrict__ slots,
                               const int32_t* __restrict__ base_len, int rows, int width) {
+  // new K/V may come from the kernel just before (this launch may overlap it)
+  pdl_wait();
   // the attention kernel that follows may launch now (it waits for this
   // kernel's writes before it copies any page)
-  asm volatile("griddepcontrol.launch_dependents;");
+  pdl_trigger();
   const int vecs = head_dim / VEC;
   const int per_tok = kv_heads * vecs;
   const int n_tok = rows * width;
@@ -296,6 +298,8 @@ inline int grid_for(int64_t work, int threads) {
   return g < 1 ? 1 : (int)g;
 }
 
+bool g_pdl = true;
+
 bool state_ok(const pse_block_state& st) {
   return st.block_table && st.seq_len && st.nblocks && st.free_stack && st.free_top && st.block_free && st.status &&
          st.num_blocks >= 0 && st.block_size > 0 && st.max_blocks > 0 && st.num_slots > 0;
@@ -315,9 +319,10 @@ int launch_append(const pse_block_state& st, const pse_kv_layer& kv, const void*
   if (vec_ok) {
     const int per_tok = kv.kv_heads * (kv.head_dim / V16);
     const int threads = per_tok >= 256 ? 256 : ((per_tok + 31) / 32) * 32;
-    append_kernel<T, V16><<<grid, threads, 0, s>>>(st, (T*)kv.k_pool, (T*)kv.v_pool, kv.kv_heads, kv.head_dim,
-                                                   (const T*)k_src, (const T*)v_src, tok_stride, head_stride, slots,
-                                                   base_len, rows, width);
+    cudaError_t e = launch_pdl(append_kernel<T, V16>, dim3(grid), dim3(threads), 0, s, st, (T*)kv.k_pool,
+                               (T*)kv.v_pool, (int)kv.kv_heads, (int)kv.head_dim, (const T*)k_src, (const T*)v_src,
+                               tok_stride, head_stride, slots, base_len, rows, width);
+    if (e != cudaSuccess) return (int)e;
   } else {
     const int per_tok = kv.kv_heads * kv.head_dim;
     const int threads = per_tok >= 256 ? 256 : ((per_tok + 31) / 32) * 32;
@@ -426,5 +431,14 @@ extern "C" int pse_kv_gather(pse_block_state st, pse_kv_layer kv, const int32_t*
   else
     return PSE_EINVAL;
   PSE_LAUNCH_CHECK();
+  return PSE_OK;
+}
+
+namespace pse {
+bool pdl_enabled() { return g_pdl; }
+}  // namespace pse
+
+extern "C" int pse_launch_overlap(int32_t on) {
+  g_pdl = on != 0;
   return PSE_OK;
 }

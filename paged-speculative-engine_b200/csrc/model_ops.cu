@@ -12,6 +12,8 @@ namespace {
 // host rejects them before launch; the device only stays in bounds).
 __global__ void embed_kernel(const int32_t* ids, const int32_t* base_len, int width, const void* tok_emb,
                              const void* pos_emb, int d, int dtype, float* x, int vocab, int n_pos) {
+  pdl_wait();
+  pdl_trigger();
   const int t = blockIdx.x;
   const int i = t / width, w = t % width;
   const int64_t tok = ids[t];
@@ -167,6 +169,8 @@ __global__ void __launch_bounds__(1024) add_norm_bf16x8_kernel(float* __restrict
                                                                float eps, int rms, __nv_bfloat16* __restrict__ out,
                                                                int64_t ldo) {
   __shared__ float sh[32];
+  pdl_wait();
+  pdl_trigger();
   const int row = blockIdx.x;
   const int c = threadIdx.x * 8;
   const bool on = c < d;
@@ -274,6 +278,8 @@ __global__ void epilogue_kernel(int op, void* y, int64_t ldy, const void* bias, 
 template <typename I>
 __global__ void epilogue_bf16x8_kernel(int op, __nv_bfloat16* y, int64_t ldy, const __nv_bfloat16* bias,
                                        __nv_bfloat16* y2, int64_t ldy2, int n_rows, int n) {
+  pdl_wait();
+  pdl_trigger();
   const int vecs = n / 8;
   const I total = (I)n_rows * vecs;
   for (I e = blockIdx.x * (I)blockDim.x + threadIdx.x; e < total; e += (I)gridDim.x * blockDim.x) {
@@ -363,9 +369,9 @@ extern "C" int pse_embed(const int32_t* ids, const int32_t* base_len, int32_t ro
   if (rows < 0 || width < 0 || d <= 0 || vocab <= 0) return PSE_EINVAL;
   if (rows == 0 || width == 0) return PSE_OK;
   if (!ids || !tok_emb || !x || (pos_emb && !base_len)) return PSE_EINVAL;
-  embed_kernel<<<rows * width, 128, 0, (cudaStream_t)stream>>>(ids, base_len, width, tok_emb, pos_emb, d, emb_dtype, x,
-                                                               vocab, n_pos);
-  PSE_LAUNCH_CHECK();
+  cudaError_t e = launch_pdl(embed_kernel, dim3((unsigned)(rows * width)), dim3(128), 0, (cudaStream_t)stream, ids,
+                             base_len, width, tok_emb, pos_emb, d, emb_dtype, x, vocab, n_pos);
+  if (e != cudaSuccess) return (int)e;
   return PSE_OK;
 }
 
@@ -400,11 +406,11 @@ extern "C" int pse_add_norm(float* x, int64_t ldx, const void* y, int64_t ldy, c
   if (dt == PSE_BF16 && d % 8 == 0 && ldx % 4 == 0 && ldy % 8 == 0 && ldo % 8 == 0 && al16(x) && al16(y) &&
       al16(bias) && al16(gamma) && al16(beta) && al16(out)) {
     const int threads = ((d / 8 + 31) / 32) * 32;  // d <= 4096: at most 512
-    add_norm_bf16x8_kernel<<<n_rows, threads, 0, s>>>(x, ldx, (const __nv_bfloat16*)y, ldy,
-                                                      (const __nv_bfloat16*)bias, (const __nv_bfloat16*)gamma,
-                                                      (const __nv_bfloat16*)beta, d, eps, rms, (__nv_bfloat16*)out,
-                                                      ldo);
-    PSE_LAUNCH_CHECK();
+    cudaError_t e = launch_pdl(add_norm_bf16x8_kernel, dim3((unsigned)n_rows), dim3(threads), 0, s, x, ldx,
+                               (const __nv_bfloat16*)y, ldy, (const __nv_bfloat16*)bias,
+                               (const __nv_bfloat16*)gamma, (const __nv_bfloat16*)beta, d, eps, rms,
+                               (__nv_bfloat16*)out, ldo);
+    if (e != cudaSuccess) return (int)e;
     return PSE_OK;
   }
   if (d <= 256)
@@ -430,13 +436,13 @@ extern "C" int pse_epilogue(int32_t op, void* y, int64_t ldy, const void* bias, 
   cudaStream_t s = (cudaStream_t)stream;
   if (vec) {
     const int64_t work = (int64_t)n_rows * (n / 8);
-    if (work < kIdx32)
-      epilogue_bf16x8_kernel<int><<<grid_for(work, 256), 256, 0, s>>>(
-          op, (__nv_bfloat16*)y, ldy, (const __nv_bfloat16*)bias, (__nv_bfloat16*)y2, ldy2, n_rows, n);
-    else
-      epilogue_bf16x8_kernel<int64_t><<<grid_for(work, 256), 256, 0, s>>>(
-          op, (__nv_bfloat16*)y, ldy, (const __nv_bfloat16*)bias, (__nv_bfloat16*)y2, ldy2, n_rows, n);
-    PSE_LAUNCH_CHECK();
+    const dim3 grid(grid_for(work, 256)), block(256);
+    cudaError_t e = work < kIdx32
+                        ? launch_pdl(epilogue_bf16x8_kernel<int>, grid, block, 0, s, (int)op, (__nv_bfloat16*)y, ldy,
+                                     (const __nv_bfloat16*)bias, (__nv_bfloat16*)y2, ldy2, (int)n_rows, (int)n)
+                        : launch_pdl(epilogue_bf16x8_kernel<int64_t>, grid, block, 0, s, (int)op, (__nv_bfloat16*)y,
+                                     ldy, (const __nv_bfloat16*)bias, (__nv_bfloat16*)y2, ldy2, (int)n_rows, (int)n);
+    if (e != cudaSuccess) return (int)e;
     return PSE_OK;
   }
   const int64_t work = (int64_t)n_rows * n;

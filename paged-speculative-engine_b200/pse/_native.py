@@ -73,6 +73,8 @@ _PROTOS = {
     "pse_scatter_rows": ([c_p, c_i64, c_p, c_i32, c_i32, c_p, c_i64, c_i32, c_p], 1),
     "pse_attention_force_generic": ([c_i32], 0),
     "pse_accept_select": ([c_i32], 0),
+    "pse_launch_overlap": ([c_i32], 0),
+    "pse_gemm_pair_tiles": ([c_i32], 0),
     "pse_attention_prefill_select": ([c_i32], 0),
     "pse_gemm_bf16": ([c_p, c_i64, c_p, c_i64, c_p, c_p, c_i64, c_i32, c_i32, c_i32, c_i32, c_i32, c_p, c_p], 1),
     "pse_paged_attention_noalloc": ([BlockState, KVLayer, c_p, c_i64, c_p, c_i64, c_p, c_p, c_i32, c_i32, c_i32,

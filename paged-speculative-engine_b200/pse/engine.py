@@ -76,12 +76,13 @@ def scratch_for(dm: DeviceModel) -> Scratch:
 
 
 USE_TC_GEMM = False  # bf16 projections on the tcgen05 GEMM (pse_gemm_bf16); off until it beats cuBLAS on these shapes
+TC_GEMM_MAX_ROWS = 1 << 30  # with USE_TC_GEMM: only GEMMs of at most this many rows
 
 
 def _tc_ok(a: torch.Tensor, w: torch.Tensor, out: torch.Tensor) -> bool:
     """pse_gemm_bf16 takes bf16 operands, k in whole 64-element slabs, row
     pitches in 16-byte units and 16-byte aligned bases."""
-    if not USE_TC_GEMM or a.dtype != torch.bfloat16 or w.dtype != torch.bfloat16:
+    if not USE_TC_GEMM or a.dtype != torch.bfloat16 or w.dtype != torch.bfloat16 or a.shape[0] > TC_GEMM_MAX_ROWS:
         return False
     k = a.shape[1]
     esz = out.element_size()
