@@ -763,9 +763,9 @@ GEMM_SHAPES = {
 
 def micro_gemm(args, device):
     """The step's projection GEMMs, cuBLAS (torch, bias fused, GELU as a
-    separate pass) against pse_gemm_bf16 (tcgen05, bias and GELU fused): device
-    us per call (50 calls captured in a CUDA graph, replayed 4 times, CUDA
-    events) and TFLOP/s."""
+    separate pass) against pse_gemm_bf16 (tcgen05, bias and GELU fused; as
+    dispatched, and with single-CTA tiles only): device us per call (50 calls
+    captured in a CUDA graph, replayed 4 times, CUDA events) and TFLOP/s."""
     import pse._native as N
     rows = []
     g = torch.Generator(device=device).manual_seed(0)
@@ -789,8 +789,14 @@ def micro_gemm(args, device):
             N.call("pse_gemm_bf16", a.data_ptr(), K, w.data_ptr(), K, None if b is None else b.data_ptr(),
                    c.data_ptr(), Nn, M, Nn, K, 1 if gelu else 0, 1 if f32 else 0, None, N.stream_ptr())
 
+        def ours_1cta():
+            lib = N.load()
+            lib.pse_gemm_pair_tiles(0)
+            ours()
+            lib.pse_gemm_pair_tiles(1)
+
         res = {}
-        for label, fn in (("cublas", cublas), ("tcgen05", ours)):
+        for label, fn in (("cublas", cublas), ("tcgen05", ours), ("tcgen05_1cta", ours_1cta)):
             for _ in range(5):
                 fn()
             torch.cuda.synchronize()

@@ -38,7 +38,7 @@ namespace pse {
 namespace gemm {
 
 constexpr int BM = 128, BK = 64;
-constexpr int kEpiWarps = 4;
+constexpr int kEpiWarps = 8;  // two per TMEM lane quarter, each draining half of the tile's columns
 constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr uint32_t kSpinLimit = 1u << 24;
 
@@ -116,22 +116,6 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
                : "memory");
 }
 
-// 32 consecutive accumulator columns of this thread's TMEM lane.
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
-  uint32_t r[32];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
-        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
-        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-}
-
 __device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.f + erff(x * 0.70710678118654752440f)); }
 
 struct Args {
@@ -144,6 +128,112 @@ struct Args {
   int out_f32;  // 1: fp32 C, 0: bf16 C
   int32_t* status;
 };
+
+// Issue a 32-column accumulator load of this thread's TMEM lane; the values
+// may be used only after tmem_ld_wait on the same registers.
+__device__ __forceinline__ void tmem_ld32_issue(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+// Wait for this thread's accumulator loads; the registers are in-out operands
+// so no use of them is scheduled before the wait.
+__device__ __forceinline__ void tmem_ld_wait(uint32_t (&r)[32]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
+                 "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]),
+                 "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+               :
+               : "memory");
+}
+
+// Epilogue of one 32-column chunk of one accumulator row (bias, GELU, store).
+__device__ __forceinline__ void store_chunk(const Args& a, int row, int col, float* v) {
+  if (row >= a.M || col >= a.N) return;
+  const bool full_chunk = col + 32 <= a.N;
+  if (a.bias) {
+    if (full_chunk) {
+      const uint4* bp = reinterpret_cast<const uint4*>(a.bias + col);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint4 w = __ldg(bp + j);
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __bfloat1622float2(h[e]);
+          v[8 * j + 2 * e] += f.x;
+          v[8 * j + 2 * e + 1] += f.y;
+        }
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] += col + j < a.N ? __bfloat162float(a.bias[col + j]) : 0.f;
+    }
+  }
+  if (a.act == 1) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = gelu_erf(v[j]);
+  }
+  if (a.out_f32) {
+    float* cr = reinterpret_cast<float*>(a.c) + (int64_t)row * a.ldc + col;
+    if (full_chunk) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(cr + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (col + j < a.N) cr[j] = v[j];
+    }
+  } else {
+    __nv_bfloat16* cr = reinterpret_cast<__nv_bfloat16*>(a.c) + (int64_t)row * a.ldc + col;
+    if (full_chunk) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 8) {
+        uint4 w;
+        __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&w);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(v[j + 2 * e], v[j + 2 * e + 1]);
+        *reinterpret_cast<uint4*>(cr + j) = w;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (col + j < a.N) cr[j] = __float2bfloat16_rn(v[j]);
+    }
+  }
+}
+
+// Drain `ncols` (a multiple of 32) accumulator columns of this thread's TMEM
+// lane starting at `taddr`, output row `row`, output columns from `col0`: the
+// load of the next 32 columns is in flight while the current ones are stored.
+__device__ __forceinline__ void drain_cols(const Args& a, uint32_t taddr, int row, int col0, int ncols) {
+  uint32_t r0[32], r1[32];
+  float v[32];
+  tmem_ld32_issue(taddr, r0);
+  tmem_ld_wait(r0);
+#pragma unroll 1
+  for (int c = 0; c < ncols; c += 64) {
+    const bool more1 = c + 32 < ncols, more2 = c + 64 < ncols;
+    if (more1) tmem_ld32_issue(taddr + c + 32, r1);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r0[j]);
+    store_chunk(a, row, col0 + c, v);
+    if (!more1) break;
+    tmem_ld_wait(r1);
+    if (more2) tmem_ld32_issue(taddr + c + 64, r0);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r1[j]);
+    store_chunk(a, row, col0 + c + 32, v);
+    if (more2) tmem_ld_wait(r0);
+  }
+}
 
 template <int BN>
 __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a,
@@ -261,65 +351,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
       }
       const int m0 = (t % a.tiles_m) * BM, n0 = (t / a.tiles_m) * BN;
       const int row = m0 + 32 * q + lane;
-      const uint32_t tbase = tmem + ((uint32_t)(32 * q) << 16) + buf * BN;
-#pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 32) {
-        float v[32];
-        tmem_ld32(tbase + c0, v);
-        const int col = n0 + c0;
-        if (row >= a.M || col >= a.N) continue;
-        const bool full_chunk = col + 32 <= a.N;
-        if (a.bias) {
-          if (full_chunk) {
-            const uint4* bp = reinterpret_cast<const uint4*>(a.bias + col);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const uint4 w = __ldg(bp + j);
-              const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w);
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const float2 f = __bfloat1622float2(h[e]);
-                v[8 * j + 2 * e] += f.x;
-                v[8 * j + 2 * e + 1] += f.y;
-              }
-            }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] += col + j < a.N ? __bfloat162float(a.bias[col + j]) : 0.f;
-          }
-        }
-        if (a.act == 1) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = gelu_erf(v[j]);
-        }
-        if (a.out_f32) {
-          float* cr = reinterpret_cast<float*>(a.c) + (int64_t)row * a.ldc + col;
-          if (full_chunk) {
-#pragma unroll
-            for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(cr + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (col + j < a.N) cr[j] = v[j];
-          }
-        } else {
-          __nv_bfloat16* cr = reinterpret_cast<__nv_bfloat16*>(a.c) + (int64_t)row * a.ldc + col;
-          if (full_chunk) {
-#pragma unroll
-            for (int j = 0; j < 32; j += 8) {
-              uint4 w;
-              __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&w);
-#pragma unroll
-              for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(v[j + 2 * e], v[j + 2 * e + 1]);
-              *reinterpret_cast<uint4*>(cr + j) = w;
-            }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (col + j < a.N) cr[j] = __float2bfloat16_rn(v[j]);
-          }
-        }
-      }
+      const int half = (warp - 2) / 4;  // which half of the tile's columns this warp drains
+      const uint32_t tbase = tmem + ((uint32_t)(32 * q) << 16) + buf * BN + half * (BN / 2);
+      drain_cols(a, tbase, row, n0 + half * (BN / 2), BN / 2);
       // this accumulator may take the tile after next
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       __syncwarp();
@@ -399,62 +433,6 @@ __host__ __device__ constexpr uint32_t instr_desc_pair(int bn) {
 }
 
 __host__ __device__ constexpr int pair_stages(int bn) { return bn == 256 ? 6 : 8; }
-
-// Epilogue of one 32-column chunk of one accumulator row (bias, GELU, store).
-__device__ __forceinline__ void store_chunk(const Args& a, int row, int col, float* v) {
-  if (row >= a.M || col >= a.N) return;
-  const bool full_chunk = col + 32 <= a.N;
-  if (a.bias) {
-    if (full_chunk) {
-      const uint4* bp = reinterpret_cast<const uint4*>(a.bias + col);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const uint4 w = __ldg(bp + j);
-        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 f = __bfloat1622float2(h[e]);
-          v[8 * j + 2 * e] += f.x;
-          v[8 * j + 2 * e + 1] += f.y;
-        }
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] += col + j < a.N ? __bfloat162float(a.bias[col + j]) : 0.f;
-    }
-  }
-  if (a.act == 1) {
-#pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = gelu_erf(v[j]);
-  }
-  if (a.out_f32) {
-    float* cr = reinterpret_cast<float*>(a.c) + (int64_t)row * a.ldc + col;
-    if (full_chunk) {
-#pragma unroll
-      for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(cr + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-    } else {
-#pragma unroll
-      for (int j = 0; j < 32; ++j)
-        if (col + j < a.N) cr[j] = v[j];
-    }
-  } else {
-    __nv_bfloat16* cr = reinterpret_cast<__nv_bfloat16*>(a.c) + (int64_t)row * a.ldc + col;
-    if (full_chunk) {
-#pragma unroll
-      for (int j = 0; j < 32; j += 8) {
-        uint4 w;
-        __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&w);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(v[j + 2 * e], v[j + 2 * e + 1]);
-        *reinterpret_cast<uint4*>(cr + j) = w;
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 32; ++j)
-        if (col + j < a.N) cr[j] = __float2bfloat16_rn(v[j]);
-    }
-  }
-}
 
 template <int BN>
 __global__ void __launch_bounds__(kThreads, 1) gemm_pair_kernel(const __grid_constant__ CUtensorMap tma_a,
@@ -582,13 +560,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_pair_kernel(const __grid_con
       const int m0 = (t % a.tiles_m) * (2 * BM) + (int)rank * BM;
       const int n0 = (t / a.tiles_m) * BN;
       const int row = m0 + 32 * q + lane;
-      const uint32_t tbase = tmem + ((uint32_t)(32 * q) << 16) + buf * BN;
-#pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 32) {
-        float v[32];
-        tmem_ld32(tbase + c0, v);
-        store_chunk(a, row, n0 + c0, v);
-      }
+      const int half = (warp - 2) / 4;
+      const uint32_t tbase = tmem + ((uint32_t)(32 * q) << 16) + buf * BN + half * (BN / 2);
+      drain_cols(a, tbase, row, n0 + half * (BN / 2), BN / 2);
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       __syncwarp();
       if (lane == 0) mbar_arrive_remote(peer_addr(&acc_empty[buf], 0));
