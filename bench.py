@@ -770,6 +770,8 @@ def micro_gemm(args, device):
     rows = []
     g = torch.Generator(device=device).manual_seed(0)
     for name, (M, K, Nn, bias, gelu, f32) in GEMM_SHAPES.items():
+        if args.gemm_only and name != args.gemm_only:
+            continue
         a = torch.randn(M, K, device=device, generator=g).to(torch.bfloat16)
         w = (torch.randn(Nn, K, device=device, generator=g) * 0.05).to(torch.bfloat16)
         b = torch.randn(Nn, device=device, generator=g).to(torch.bfloat16) if bias else None
@@ -795,6 +797,12 @@ def micro_gemm(args, device):
             ours()
             lib.pse_gemm_pair_tiles(1)
 
+        if args.gemm_only:  # plain launches of the tcgen05 kernel only (a short program for ncu)
+            for _ in range(max(args.steps, 1)):
+                ours()
+            torch.cuda.synchronize()
+            rows.append({"gemm": name, "M": M, "K": K, "N": Nn, "launches": max(args.steps, 1)})
+            continue
         res = {}
         for label, fn in (("cublas", cublas), ("tcgen05", ours), ("tcgen05_1cta", ours_1cta)):
             for _ in range(5):
@@ -952,6 +960,9 @@ def main():
                     help="headline the reference's step structure (2 target calls per step) instead of the "
                          "default step (the target's bonus call deferred into the next verify)")
     ap.add_argument("--attn-shape", default="gpt2-verify", choices=sorted(ATTN_SHAPES))
+    ap.add_argument("--gemm-only", default=None, choices=sorted(GEMM_SHAPES),
+                    help="--micro gemm: launch only this shape's tcgen05 GEMM, --steps times, without graphs or "
+                         "timing (a short program for ncu)")
     ap.add_argument("--prefill-kernel", default="tc", choices=["tc", "off", "single"],
                     help="wide attention calls (prefill) on the tcgen05 kernels, on the mma.sync kernel, or on the "
                          "one-query-tile tcgen05 kernel at every head_dim")
@@ -1002,6 +1013,9 @@ def main():
 
     if world > 1:
         import datetime
+        # NCCL's communicator lines (ranks, devices, transports) stay in the log
+        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
         torch.cuda.set_device(local)
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                              device_id=torch.device("cuda", local))
