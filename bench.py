@@ -175,9 +175,9 @@ def run_pse(args, rank, world, device):
     # committing up to k+1 tokens, plus the roofline launch's k+1 reserved tokens
     n_steps = 2 * (max(args.warmup, 3) + 2 * args.steps)
     extra = (w.k + 1) * (n_steps + 1) + w.k + 2
-    dc = cache_for(d, w, B, dtype, device, extra)
-    tc = cache_for(t, w, B, dtype, device, extra)
     prompts = [r.prompt_ids for r in mine]
+    dc = cache_for(d, w, B, dtype, device, extra, prompts)
+    tc = cache_for(t, w, B, dtype, device, extra, prompts)
     rids = [r.request_id for r in mine]
     dn, tn = {}, {}
     torch.cuda.synchronize()
@@ -913,6 +913,33 @@ def kernel_configs(args, device):
     return out
 
 
+def llama_step(args, device, peak):
+    """The Llama-style configuration's step on this GPU (512 rows of its
+    workload, bf16, k=4, block 32): the same measurement as the headline on a
+    second workload, summarised."""
+    import copy
+    gc.collect()
+    torch.cuda.empty_cache()
+    a = copy.copy(args)
+    a.workload, a.rows, a.steps, a.warmup = "llama-1b", 512, 10, 3
+    a.reference_structure = False
+    r = run_pse(a, 0, 1, device)
+    hd_, rf_ = r["head"], r["ref"]
+    value = hd_["committed"] / (hd_["ms"] / 1000.0)
+    achieved = r["attn_bytes"] / (r["attn_ms"] / 1000.0) / 1e9
+    roof = (hd_["committed"] / a.steps) / (r["step_bytes"] / (peak * 1e9))
+    out = {"workload": "llama-1b: 512 rows (prompts lognormal median 2048, clipped to [128, 8192]), k=4, block 32, "
+                       "greedy, bf16", "value": value, "unit": "tokens/s", "ms_per_step": hd_["ms"] / a.steps,
+           "e2e": hd_["e2e_tokens"] / (hd_["e2e_ms"] / 1000.0),
+           "reference_structure": rf_["committed"] / (rf_["ms"] / 1000.0),
+           "verify_attention_frac": achieved / peak, "step_roofline_frac": value / roof,
+           "prefill_tokens_per_s": r["prefill_tokens"] / r["prefill_s"], "clocks": r["clocks"]}
+    del r
+    gc.collect()
+    torch.cuda.empty_cache()
+    return out
+
+
 def config_block(args, w, B, world):
     dist = (f"lognormal(median {w.lognormal_median:g}, sigma {w.lognormal_sigma:g}) clipped to "
             f"[{w.prompt_lo},{w.prompt_hi}]" if w.lognormal_sigma > 0 else f"U[{w.prompt_lo},{w.prompt_hi}]")
@@ -1013,9 +1040,11 @@ def main():
 
     if world > 1:
         import datetime
-        # NCCL's communicator lines (ranks, devices, transports) stay in the log
-        os.environ.setdefault("NCCL_DEBUG", "INFO")
-        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+        # NCCL's communicator lines (ranks, devices, transports) go to the log
+        # (the image's default level, VERSION, prints only the version)
+        if os.environ.get("NCCL_DEBUG", "VERSION").upper() in ("", "VERSION", "WARN"):
+            os.environ["NCCL_DEBUG"] = "INFO"
+            os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
         torch.cuda.set_device(local)
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                              device_id=torch.device("cuda", local))
@@ -1048,6 +1077,8 @@ def main():
     kernel_cfgs = None
     if world == 1 and not args.no_kernel_configs:
         kernel_cfgs = kernel_configs(args, device)
+        if args.workload == "gpt2-small":
+            kernel_cfgs["4_llama_1b_step"] = llama_step(args, device, peak)
     check = token_check(args, r["check_rows"], os.cpu_count() or 1) if rank == 0 else None
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
