@@ -621,7 +621,8 @@ def micro_accept(args, device, emit=True):
                       "us_per_launch": ms * 1000, "bytes_needed": need, "bytes_formula_2k+1": formula,
                       "formula_GBps": formula / (ms / 1000) / 1e9, "rows": R, "k": k, "vocab": V, "temperature": T,
                       "mean_accepted": n.float().mean().item(),
-                      "kernel": ["streaming CTA per row", "CTA per row (scalar)", "cluster per row"][args.accept_kernel]
+                      "kernel": ["cluster-split streaming", "CTA per row (scalar)", "cluster per row (on chip)",
+                                 "streaming CTA per row"][args.accept_kernel]
                       if T > 0 else "CTA per row (argmax)"}
     N.load().pse_accept_select(0)
     if emit:
@@ -981,8 +982,9 @@ def main():
     ap.add_argument("--micro", choices=["attn", "accept", "churn", "prefill", "scheduler", "gemm"], default=None,
                     help="kernel microbenchmark instead of the step")
     ap.add_argument("--temperature", type=float, default=1.0, help="--micro accept: temperature")
-    ap.add_argument("--accept-kernel", type=int, default=0, choices=[0, 1, 2],
-                    help="--micro accept at T > 0: 0 streaming CTA per row, 1 scalar CTA per row, 2 cluster per row")
+    ap.add_argument("--accept-kernel", type=int, default=0, choices=[0, 1, 2, 3],
+                    help="--micro accept at T > 0: 0 cluster-split streaming (default), 1 scalar CTA per row, "
+                         "2 cluster per row holding the row on chip, 3 streaming CTA per row")
     ap.add_argument("--reference-structure", action="store_true",
                     help="headline the reference's step structure (2 target calls per step) instead of the "
                          "default step (the target's bonus call deferred into the next verify)")

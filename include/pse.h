@@ -251,13 +251,15 @@ int pse_spec_accept(const float *target0, int64_t t0_stride, const int32_t *t0_i
                     int32_t k, int32_t vocab, float temperature, int32_t *tokens,
                     int32_t *n_accepted, int32_t *final_token, void *stream);
 
-/* Which kernel pse_spec_accept runs at T > 0: 0 the default (L2-resident
- * streaming CTA per row), 1 the CTA-per-row scalar kernel, 2 one thread-block
- * cluster of ceil(vocab / 16384) CTAs per row with the row held on chip
- * (vocab <= 131072).  All three give the same tokens; parity tests compare
- * them.  Draft sampling (pse_sample_tokens) at T > 0 likewise runs a streaming
- * CTA per row for 0 and the scalar kernel otherwise.  No counterpart in the
- * reference. */
+/* Which kernel pse_spec_accept runs at T > 0: 0 the default (one cluster of
+ * min(8, ceil(vocab / 8192)) CTAs per row, several clusters per SM, the row
+ * streamed from HBM once and re-read from L2), 1 the CTA-per-row scalar
+ * kernel, 2 one thread-block cluster of ceil(vocab / 16384) CTAs per row with
+ * the row held on chip (vocab <= 131072), 3 one streaming CTA per row.  All
+ * four give the same tokens; parity tests compare them.  Draft sampling
+ * (pse_sample_tokens) at T > 0 runs a streaming CTA per row for 0 and 3 and
+ * the scalar kernel otherwise.  Other values: PSE_EINVAL.  No counterpart in
+ * the reference. */
 int pse_accept_select(int32_t kernel);
 
 /* ------------------------------------------------------------------------ */

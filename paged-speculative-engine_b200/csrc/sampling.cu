@@ -24,9 +24,10 @@ namespace {
 constexpr int kSampleThreads = 512;
 
 // Which accept kernel runs at T > 0 (tests compare the forms): 0 the default
-// (streaming), 1 the CTA-per-row scalar kernel, 2 the cluster kernel.  Draft
-// sampling at T > 0 uses the streaming kernel when this is 0, the scalar
-// kernel otherwise.
+// (cluster-split streaming), 1 the CTA-per-row scalar kernel, 2 the cluster
+// kernel holding the row on chip, 3 the CTA-per-row streaming kernel.  Draft
+// sampling at T > 0 uses the streaming sampler when this is 0 or 3, the
+// scalar kernel otherwise.
 int g_accept_kernel = 0;
 constexpr int kWarpsPerBlock = kSampleThreads / 32;
 
@@ -1181,6 +1182,357 @@ __global__ void __launch_bounds__(kStThreads, 1) accept_stream_kernel(AcceptArgs
   }
 }
 
+// ---------------------------------------------------------------- accept / resample, T > 0, cluster-split streaming
+//
+// A cluster of C CTAs (C = min(8, ceil(V / 8192))) owns one request row at a
+// time and several clusters share each SM (256-thread CTAs), so the
+// reductions and barriers of one cluster overlap the loads of another.  CTA r
+// of a cluster owns the vocabulary chunk [r * chunk, (r + 1) * chunk), cut
+// into 8 warp segments of `seg` entries (a multiple of 128); a warp reads its
+// segment as 128-entry rows, lane l taking entries 4l..4l+3 with one 16-byte
+// load, four rows' loads issued before their arithmetic.  Per position:
+//   1. maxima of s = l / T over the target (P) and draft (Q) logits: the only
+//      read from HBM (ld.global.cg, cached in L2 only);
+//   2. fp64 segment sums of w = expf(s - m) for P and Q (re-read from L2);
+//      every thread reads the drafted token's two logits itself (one
+//      broadcast load per warp) for the accept test;
+//   3. after a rejection, fp64 segment sums of the residual (re-read again);
+//   4. inverse CDF: every warp finds the crossing segment from the segment
+//      sums (none: the last segment holding a nonzero entry, scanned with no
+//      threshold); that segment's warp re-reads and scans it, remembering
+//      its last nonzero entry for the no-crossing case.
+// The clusters in flight are capped so that their rows (2 x V x 4 bytes each)
+// stay within kSpL2Budget of L2: every re-read hits L2 (ncu: DRAM reads 1.11x
+// the needed bytes at vocab 128256).  The kernel is issue-bound: ~15
+// instructions per logit per pass (expf, the fp64 conversion and sum).
+//
+// Every warp stores its segment's partial into the mailbox of every CTA of
+// the cluster (DSMEM) before one cluster barrier; each warp then reduces the
+// mailbox with the same fixed tree, so all CTAs hold bit-identical totals,
+// take identical decisions and keep their barriers matched.  Mailboxes
+// alternate between two slots: a slot is rewritten two reductions later,
+// after every CTA has passed the barrier that follows its reads of it.
+//
+// Sums: a lane adds its entries in index order; lanes combine by butterfly;
+// segment sums combine in lane-major order (2 segments per lane).
+
+constexpr int kSpThreads = 256;
+constexpr int kSpWarps = kSpThreads / 32;
+constexpr int kSpMaxC = 8;                     // portable cluster size
+constexpr int kSpSegs = kSpMaxC * kSpWarps;    // warp segments per row, at most
+constexpr int kSpG = kSpSegs / 32;             // segments per lane in the descent
+constexpr int kSpBatch = 4;                    // 128-entry rows loaded before their arithmetic
+constexpr size_t kSpL2Budget = 96u << 20;      // bytes of logits rows in flight
+
+struct SpMail {
+  float mx[2][kSpSegs];    // maxima of s_p, s_q per segment
+  double sum[3][kSpSegs];  // sums of w_p, w_q, residual per segment
+};
+
+__device__ __forceinline__ float4 neg_inf4() { return make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY); }
+
+template <int C>
+__global__ void __launch_bounds__(kSpThreads, 4) accept_split_kernel(AcceptArgs a, int rows, int seg) {
+  __shared__ SpMail box[2];
+  constexpr int n_seg = C * kSpWarps;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int rank = (int)cluster_ctarank();
+  const int n_cl = (int)cluster_count_x();
+  const int k = a.k, V = a.V;
+  const float T = a.T;
+  const int g = rank * kSpWarps + warp;  // this warp's segment
+  const int e0 = g * seg + lane * 4;     // this lane's first entry
+  const int n_c = seg >> 7;              // 128-entry rows per segment
+  int ph = 0;
+
+  for (int i = (int)cluster_id_x(); i < rows; i += n_cl) {
+    const double* u = a.u + (int64_t)i * a.u_stride;
+    const int32_t* drafted = a.drafts + (int64_t)i * k;
+    int32_t* toks = a.tokens + (int64_t)i * (k + 1);
+    for (int j = 0; j <= k; ++j) {
+      const bool bonus = j == k;  // every draft accepted: sample target[k]
+      const float* P = target_row(a, i, j);
+      const float* Q = bonus ? P : draft_row(a, i, j);
+      // ---- 1. maxima of s = l / T
+      float mp = -INFINITY, mq = -INFINITY;
+#pragma unroll 4
+      for (int c = 0; c < n_c; ++c) {
+        const int e = e0 + c * 128;
+        if (e < V) {
+          const float4 sp = scale_s(ld_l2(P + e), T);
+          mp = fmaxf(mp, fmaxf(fmaxf(sp.x, sp.y), fmaxf(sp.z, sp.w)));
+          if (!bonus) {
+            const float4 sq = scale_s(ld_l2(Q + e), T);
+            mq = fmaxf(mq, fmaxf(fmaxf(sq.x, sq.y), fmaxf(sq.z, sq.w)));
+          }
+        }
+      }
+      mp = warp_max(mp);
+      mq = warp_max(mq);
+      if (lane < C) {
+        const uint32_t b = peer_addr(&box[ph], lane);
+        st_peer(b + (uint32_t)offsetof(SpMail, mx[0][0]) + 4u * g, mp);
+        st_peer(b + (uint32_t)offsetof(SpMail, mx[1][0]) + 4u * g, mq);
+      }
+      cluster_sync_all();
+      {
+        const SpMail& m = box[ph];
+        float x0 = -INFINITY, y0 = -INFINITY;
+#pragma unroll
+        for (int jj = 0; jj < kSpG; ++jj) {
+          const int sg = kSpG * lane + jj;
+          if (sg < n_seg) {
+            x0 = fmaxf(x0, m.mx[0][sg]);
+            y0 = fmaxf(y0, m.mx[1][sg]);
+          }
+        }
+        mp = warp_max(x0);
+        mq = warp_max(y0);
+      }
+      ph ^= 1;
+      // ---- 2. weights: segment sums; the drafted token's logits
+      const int x = bonus ? -1 : drafted[j];
+      const bool x_ok = x >= 0 && x < V;
+      float lpx = 0.f, lqx = 0.f;
+      if (x_ok) {
+        lpx = __ldcg(P + x);
+        lqx = __ldcg(Q + x);
+      }
+      double sp = 0.0, sq = 0.0;
+      for (int c0 = 0; c0 < n_c; c0 += kSpBatch) {
+        float4 lp4[kSpBatch], lq4[kSpBatch];
+#pragma unroll
+        for (int b = 0; b < kSpBatch; ++b) {
+          const int e = e0 + (c0 + b) * 128;
+          const bool ok = c0 + b < n_c && e < V;  // -inf pads weigh 0
+          lp4[b] = ok ? ld_l2(P + e) : neg_inf4();
+          lq4[b] = ok && !bonus ? ld_l2(Q + e) : neg_inf4();
+        }
+#pragma unroll
+        for (int b = 0; b < kSpBatch; ++b) {
+          const float4 wp = weights4(lp4[b], T, mp);
+          sp += (double)wp.x;
+          sp += (double)wp.y;
+          sp += (double)wp.z;
+          sp += (double)wp.w;
+          if (!bonus) {
+            const float4 wq = weights4(lq4[b], T, mq);
+            sq += (double)wq.x;
+            sq += (double)wq.y;
+            sq += (double)wq.z;
+            sq += (double)wq.w;
+          }
+        }
+      }
+      sp = warp_sum_d(sp);
+      sq = warp_sum_d(sq);
+      if (lane < C) {
+        const uint32_t b = peer_addr(&box[ph], lane);
+        st_peer(b + (uint32_t)offsetof(SpMail, sum[0][0]) + 8u * g, sp);
+        st_peer(b + (uint32_t)offsetof(SpMail, sum[1][0]) + 8u * g, sq);
+      }
+      cluster_sync_all();
+      double segv[kSpG];  // segment sums of the distribution the draw descends
+      double Zp = 0.0, Zq = 0.0;
+      {
+        const SpMail& m = box[ph];
+#pragma unroll
+        for (int jj = 0; jj < kSpG; ++jj) {
+          const int sg = kSpG * lane + jj;
+          segv[jj] = sg < n_seg ? m.sum[0][sg] : 0.0;
+          Zp += segv[jj];
+          Zq += sg < n_seg ? m.sum[1][sg] : 0.0;
+        }
+      }
+      ph ^= 1;
+      Zp = warp_sum_d(Zp);
+      Zq = warp_sum_d(Zq);
+      int n_acc = k;
+      bool use_resid = false;
+      double invp = 0.0, invq = 0.0, R = 0.0;
+      if (!bonus) {
+        // engine/speculative.py:133-142
+        double prob = 0.0;
+        if (x_ok) {
+          const double wpx = (double)expf((T != 1.0f ? lpx / T : lpx) - mp);
+          const double wqx = (double)expf((T != 1.0f ? lqx / T : lqx) - mq);
+          if (wqx > 0.0) {
+            const double ratio = __ddiv_rn(__dmul_rn(wpx, Zq), __dmul_rn(wqx, Zp));
+            prob = ratio < 1.0 ? ratio : 1.0;
+          }
+        }
+        if (u[k + j] < prob) {
+          if (rank == 0 && threadIdx.x == 0) toks[j] = x;
+          continue;
+        }
+        // engine/speculative.py:43-50: residual max(0, p - q), or p if it is empty
+        n_acc = j;
+        invp = 1.0 / Zp;
+        invq = 1.0 / Zq;
+        // ---- 3. residual segment sums
+        double sr = 0.0;
+        for (int c0 = 0; c0 < n_c; c0 += kSpBatch) {
+          float4 lp4[kSpBatch], lq4[kSpBatch];
+#pragma unroll
+          for (int b = 0; b < kSpBatch; ++b) {
+            const int e = e0 + (c0 + b) * 128;
+            const bool ok = c0 + b < n_c && e < V;
+            lp4[b] = ok ? ld_l2(P + e) : neg_inf4();
+            lq4[b] = ok ? ld_l2(Q + e) : neg_inf4();
+          }
+#pragma unroll
+          for (int b = 0; b < kSpBatch; ++b) {
+            const float4 wp = weights4(lp4[b], T, mp);
+            const float4 wq = weights4(lq4[b], T, mq);
+            sr += resid(wp.x, wq.x, invp, invq);
+            sr += resid(wp.y, wq.y, invp, invq);
+            sr += resid(wp.z, wq.z, invp, invq);
+            sr += resid(wp.w, wq.w, invp, invq);
+          }
+        }
+        sr = warp_sum_d(sr);
+        if (lane < C) {
+          const uint32_t b = peer_addr(&box[ph], lane);
+          st_peer(b + (uint32_t)offsetof(SpMail, sum[2][0]) + 8u * g, sr);
+        }
+        cluster_sync_all();
+        double segr[kSpG];
+        {
+          const SpMail& m = box[ph];
+#pragma unroll
+          for (int jj = 0; jj < kSpG; ++jj) {
+            const int sg = kSpG * lane + jj;
+            segr[jj] = sg < n_seg ? m.sum[2][sg] : 0.0;
+            R += segr[jj];
+          }
+        }
+        ph ^= 1;
+        R = warp_sum_d(R);
+        if (R > 0.0) {
+          use_resid = true;
+#pragma unroll
+          for (int jj = 0; jj < kSpG; ++jj) segv[jj] = segr[jj];
+        }
+      }
+      // ---- 4. inverse CDF: segment -> 128-entry row -> entry
+      double t = u[2 * k] * (use_resid ? R : Zp);
+      double run = 0.0;
+      int g_scan = group_cross<kSpG>(segv, t, run);
+      if (g_scan < 0) {
+        // rounding left no crossing: the last entry of nonzero weight, found
+        // in the last segment whose sum is nonzero (sums of nonnegative terms)
+        int ls = -1;
+#pragma unroll
+        for (int jj = 0; jj < kSpG; ++jj)
+          if (segv[jj] > 0.0) ls = kSpG * lane + jj;
+        g_scan = warp_max_i(ls);
+        t = INFINITY;
+      }
+      if (g == (g_scan >= 0 ? g_scan : 0)) {  // one warp of the cluster finishes the row
+        int found = -1, last_nz = -1;
+        if (g_scan >= 0) {
+          for (int c = 0; c < n_c && found < 0; ++c) {
+            const int e = e0 + c * 128;
+            double v0 = 0.0, v1 = 0.0, v2 = 0.0, v3 = 0.0;
+            if (e < V) {
+              const float4 wp = weights4(ld_l2(P + e), T, mp);
+              if (use_resid) {
+                const float4 wq = weights4(ld_l2(Q + e), T, mq);
+                v0 = resid(wp.x, wq.x, invp, invq);
+                v1 = resid(wp.y, wq.y, invp, invq);
+                v2 = resid(wp.z, wq.z, invp, invq);
+                v3 = resid(wp.w, wq.w, invp, invq);
+              } else {
+                v0 = wp.x;
+                v1 = wp.y;
+                v2 = wp.z;
+                v3 = wp.w;
+              }
+            }
+            const double incl = warp_inclusive_scan_d(((v0 + v1) + v2) + v3);
+            const double ex = __shfl_up_sync(0xffffffffu, incl, 1);
+            double acc = run + (lane == 0 ? 0.0 : ex);
+            int f = -1, lz = -1;
+            acc += v0;
+            if (v0 > 0.0) {
+              lz = e;
+              if (acc > t) f = e;
+            }
+            acc += v1;
+            if (v1 > 0.0) {
+              lz = e + 1;
+              if (f < 0 && acc > t) f = e + 1;
+            }
+            acc += v2;
+            if (v2 > 0.0) {
+              lz = e + 2;
+              if (f < 0 && acc > t) f = e + 2;
+            }
+            acc += v3;
+            if (v3 > 0.0) {
+              lz = e + 3;
+              if (f < 0 && acc > t) f = e + 3;
+            }
+            const unsigned hit = __ballot_sync(0xffffffffu, f >= 0);
+            if (hit) found = __shfl_sync(0xffffffffu, f, __ffs(hit) - 1);
+            last_nz = max(last_nz, warp_max_i(lz));
+            run += __shfl_sync(0xffffffffu, incl, 31);
+          }
+        }
+        // no crossing inside the hit segment (rounding): its last nonzero entry
+        const int fin = found >= 0 ? found : (last_nz >= 0 ? last_nz : 0);
+        if (lane == 0) {
+          toks[n_acc] = fin;
+          for (int jj = n_acc + 1; jj <= k; ++jj) toks[jj] = -1;
+          a.n_accepted[i] = n_acc;
+          a.final_token[i] = fin;
+        }
+      }
+      break;  // the row is finished (rejection or bonus)
+    }
+  }
+  // no CTA leaves while a peer may still store into its mailbox
+  cluster_sync_all();
+}
+
+template <int C>
+int launch_accept_split(const AcceptArgs& a, int rows, int seg, cudaStream_t stream) {
+  static int max_clusters[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -1;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = C;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(kSpThreads, 1, 1);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (max_clusters[dev] == 0) {
+    int sms = kNumSMs;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cfg.gridDim = dim3((unsigned)(C * (sms / C)), 1, 1);
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, accept_split_kernel<C>, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      return -1;
+    }
+    max_clusters[dev] = n;
+  }
+  // rows in flight: every resident cluster, capped so their logits rows stay in L2
+  int n_cl = max_clusters[dev];
+  const int64_t row_bytes = (int64_t)a.V * 8;  // target + draft row
+  const int64_t cap = (int64_t)kSpL2Budget / row_bytes;
+  if (n_cl > cap) n_cl = cap < 1 ? 1 : (int)cap;
+  if (n_cl > rows) n_cl = rows;
+  cfg.gridDim = dim3((unsigned)(C * n_cl), 1, 1);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, accept_split_kernel<C>, a, rows, seg);
+  return e == cudaSuccess ? 0 : (int)e;
+}
+
 // ---------------------------------------------------------------- draft sampling, T > 0, one CTA per row
 //
 // The streaming kernel's layout for one logits row: the max pass, one exp /
@@ -1345,7 +1697,7 @@ extern "C" int pse_sample_tokens(const float* logits, int64_t row_stride, const 
   if (rows < 0 || vocab <= 0) return PSE_EINVAL;
   if (rows == 0) return PSE_OK;
   if (!logits || !out || (temperature > 0.f && !u)) return PSE_EINVAL;
-  if (temperature > 0.f && g_accept_kernel == 0 && vocab % 4 == 0 && row_stride % 4 == 0 &&
+  if (temperature > 0.f && (g_accept_kernel == 0 || g_accept_kernel == 3) && vocab % 4 == 0 && row_stride % 4 == 0 &&
       (reinterpret_cast<uintptr_t>(logits) & 15) == 0) {
     const int seg = ((vocab + kStWarps - 1) / kStWarps + 127) & ~127;
     sample_stream_kernel<<<rows, kStThreads, 0, (cudaStream_t)stream>>>(logits, row_stride, index, rows, vocab,
@@ -1362,7 +1714,7 @@ extern "C" int pse_sample_tokens(const float* logits, int64_t row_stride, const 
 }
 
 extern "C" int pse_accept_select(int32_t kernel) {
-  if (kernel < 0 || kernel > 2) return PSE_EINVAL;
+  if (kernel < 0 || kernel > 3) return PSE_EINVAL;
   g_accept_kernel = kernel;
   return PSE_OK;
 }
@@ -1381,6 +1733,28 @@ extern "C" int pse_spec_accept(const float* target0, int64_t t0_stride, const in
                dr_row, dr_pos, drafts, u, u_stride, k, vocab, temperature, tokens, n_accepted, final_token};
   const bool vec = temperature > 0.f && vec_accept_ok(a);
   if (vec && g_accept_kernel == 0) {
+    // one cluster of C CTAs per row, several clusters per SM
+    int C = (vocab + 8191) / 8192;
+    if (C > kSpMaxC) C = kSpMaxC;
+    const int unit = kSpWarps * 128;
+    const int chunk = ((vocab + C - 1) / C + unit - 1) / unit * unit;
+    const int seg = chunk / kSpWarps;
+    int rc = -1;
+    switch (C) {
+      case 1: rc = launch_accept_split<1>(a, rows, seg, (cudaStream_t)stream); break;
+      case 2: rc = launch_accept_split<2>(a, rows, seg, (cudaStream_t)stream); break;
+      case 3: rc = launch_accept_split<3>(a, rows, seg, (cudaStream_t)stream); break;
+      case 4: rc = launch_accept_split<4>(a, rows, seg, (cudaStream_t)stream); break;
+      case 5: rc = launch_accept_split<5>(a, rows, seg, (cudaStream_t)stream); break;
+      case 6: rc = launch_accept_split<6>(a, rows, seg, (cudaStream_t)stream); break;
+      case 7: rc = launch_accept_split<7>(a, rows, seg, (cudaStream_t)stream); break;
+      default: rc = launch_accept_split<8>(a, rows, seg, (cudaStream_t)stream); break;
+    }
+    if (rc > 0) return rc;
+    if (rc == 0) return PSE_OK;
+    // rc < 0: no cluster of this size fits on the device; the streaming kernel below handles it
+  }
+  if (vec && (g_accept_kernel == 0 || g_accept_kernel == 3)) {
     const int seg = ((vocab + kStWarps - 1) / kStWarps + 127) & ~127;
     int sms = kNumSMs, dev = 0;
     if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);

@@ -120,6 +120,7 @@ def test_sampling_and_model_ops_reject_bad_arguments():
     assert lib.pse_rope(h.data_ptr(), 8, 2, 1, 1, 1, 7, keys.data_ptr(), 10000.0, 1, None) == EINVAL  # odd dim
     assert lib.pse_embed(keys.data_ptr(), keys.data_ptr(), 2, 1, h.data_ptr(), None, 0, 1, 8, 0,
                          x.data_ptr(), None) == EINVAL                                 # d = 0
-    assert lib.pse_accept_select(3) == EINVAL and lib.pse_accept_select(0) == 0
+    assert lib.pse_accept_select(4) == EINVAL and lib.pse_accept_select(-1) == EINVAL
+    assert lib.pse_accept_select(0) == 0
     torch.cuda.synchronize()
     assert not out.any() and not x.any()

@@ -344,14 +344,14 @@ def test_accept_resample_matches_oracle(k, vocab, temp, agree):
     (20, 3, 200000, 1.0, 0.97),   # beyond the cluster kernel's reach (it falls back to the scalar kernel)
 ])
 def test_accept_kernels_match_oracle(rows, k, vocab, temp, agree):
-    """T > 0 has three kernels (L2-resident streaming CTA per row, the default;
-    CTA-per-row scalar; one thread-block cluster per row).  Each must give the
-    oracle's tokens exactly."""
+    """T > 0 has four kernels (cluster-split streaming, the default; CTA-per-row
+    scalar; one thread-block cluster per row holding the row on chip; streaming
+    CTA per row).  Each must give the oracle's tokens exactly."""
     N = _N()
     tgt, drf, u, drafts = _accept_inputs(rows, k, vocab, temp, seed=rows + k + vocab, agree=agree)
     outs = []
     try:
-        for kern in (0, 1, 2):
+        for kern in (0, 1, 2, 3):
             N.load().pse_accept_select(kern)
             outs.append(_run_accept(N, tgt, drf, u, drafts, temp))
     finally:
