@@ -751,6 +751,80 @@ def micro_scheduler(args, device):
                       "cpu_baseline": cpu}), flush=True)
 
 
+def micro_prefix(args, device):
+    """Prefix caching on a shared-system-prompt workload: the gpt2-small pair,
+    N requests (default 256), each prompt a common system prompt
+    (--prefix-len tokens, default 512) plus its own suffix of U[16, 128]
+    tokens, 64 new tokens, greedy, the whole workload through
+    run_continuous_speculative_batches with the prefix index off and on (each
+    after an untimed run of the same workload).  Reports committed tokens/s,
+    the prompt tokens computed, the index hit rate, and whether both runs gave
+    identical outputs."""
+    import pse
+    from pse import workload as wl
+    from pse.scheduler import Request
+    w = wl.WORKLOADS["gpt2-small"]
+    n = args.rows or 256
+    rng = np.random.default_rng(0)
+    system = rng.integers(0, w.pair.vocab, size=args.prefix_len).tolist()
+    prompts = [system + rng.integers(0, w.pair.vocab, size=int(rng.integers(16, 129))).tolist() for _ in range(n)]
+    max_new = 64
+    d, t = build_pair(w, torch.bfloat16, device)
+    res_by_mode, lines = {}, {}
+    for prefix in (False, True):
+        for run in ("warm", "timed"):
+            reqs = [Request(f"{run}{i}", p, max_new) for i, p in enumerate(prompts)]
+            caches = []
+            for m in (d, t):
+                cfg = m.cfg
+                bs = w.block_size
+                nb = sum((len(p) + max_new + w.k + 2 + bs - 1) // bs for p in prompts) + 8
+                caches.append(pse.PagedKVCache(cfg.n_layers, cfg.n_heads, cfg.d_model // cfg.n_heads, bs, nb,
+                                               dtype=torch.bfloat16, device=device, max_requests=n,
+                                               prefix_cache=prefix))
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            res = pse.run_continuous_speculative_batches(d, t, reqs, caches[0], caches[1], n, k=w.k)
+            torch.cuda.synchronize()
+            secs = time.perf_counter() - t0
+            if run == "timed":
+                by = {r.request_id[len(run):]: r.output_ids for r in res}
+                res_by_mode[prefix] = by
+                toks = sum(len(by[str(i)]) - len(p) for i, p in enumerate(prompts))
+                st = caches[1].prefix.stats() if prefix else None
+                computed = sum(len(p) for p in prompts) - (st["hit_tokens"] if st else 0)
+                lines[prefix] = {"value": toks / secs, "unit": "tokens/s", "seconds": secs,
+                                 "prompt_tokens": sum(len(p) for p in prompts), "prompt_tokens_computed": computed,
+                                 "target_index": st}
+            del caches, res
+            gc.collect()
+            torch.cuda.empty_cache()
+        # the admission alone: all prompts prefilled in one batched call (after a warm one)
+        for run in ("warm", "timed"):
+            caches = []
+            for m in (d, t):
+                cfg = m.cfg
+                nb = sum((len(p) + w.block_size - 1) // w.block_size for p in prompts) + 8
+                caches.append(pse.PagedKVCache(cfg.n_layers, cfg.n_heads, cfg.d_model // cfg.n_heads, w.block_size,
+                                               nb, dtype=torch.bfloat16, device=device, max_requests=n,
+                                               prefix_cache=prefix))
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            pse.prefill_requests(d, t, caches[0], caches[1], [f"p{i}" for i in range(n)], prompts)
+            torch.cuda.synchronize()
+            lines[prefix]["prefill_seconds"] = time.perf_counter() - t0
+            del caches
+            gc.collect()
+            torch.cuda.empty_cache()
+    same = res_by_mode[False] == res_by_mode[True]
+    print(json.dumps({"metric": "committed tokens/s (scheduler, shared system prompt)", "workload":
+                      f"gpt2-small pair, {n} requests: {args.prefix_len}-token system prompt + U[16,128] suffix, "
+                      f"{max_new} new, k={w.k}, greedy, bf16", "prefix_cache_off": lines[False],
+                      "prefix_cache_on": lines[True], "speedup": lines[True]["value"] / lines[False]["value"],
+                      "prefill_speedup": lines[False]["prefill_seconds"] / lines[True]["prefill_seconds"],
+                      "outputs_identical": same}), flush=True)
+
+
 GEMM_SHAPES = {
     # name: (M, K, N, bias, gelu, fp32 out) -- the gpt2-small step's projections
     "t.qkv": (1536, 768, 2304, True, False, False), "t.out": (1536, 768, 768, True, False, False),
@@ -979,9 +1053,11 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-kernel-configs", action="store_true",
                     help="skip the 5a / 5b / 5c kernel configurations after the step (they run at N=1 only)")
-    ap.add_argument("--micro", choices=["attn", "accept", "churn", "prefill", "scheduler", "gemm"], default=None,
+    ap.add_argument("--micro", choices=["attn", "accept", "churn", "prefill", "scheduler", "gemm", "prefix"],
+                    default=None,
                     help="kernel microbenchmark instead of the step")
     ap.add_argument("--temperature", type=float, default=1.0, help="--micro accept: temperature")
+    ap.add_argument("--prefix-len", type=int, default=512, help="--micro prefix: system prompt tokens")
     ap.add_argument("--accept-kernel", type=int, default=0, choices=[0, 1, 2, 3],
                     help="--micro accept at T > 0: 0 cluster-split streaming (default), 1 scalar CTA per row, "
                          "2 cluster per row holding the row on chip, 3 streaming CTA per row")
@@ -1068,6 +1144,9 @@ def main():
         return
     if args.micro == "scheduler":
         micro_scheduler(args, device)
+        return
+    if args.micro == "prefix":
+        micro_prefix(args, device)
         return
     if args.micro == "gemm":
         micro_gemm(args, device)

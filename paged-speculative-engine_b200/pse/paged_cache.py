@@ -38,6 +38,7 @@ import numpy as np
 import torch
 
 from . import _native as N
+from .prefix_cache import PrefixIndex
 
 
 def _blocks_for(n: int, bs: int) -> int:
@@ -157,13 +158,16 @@ class PagedKVCache:
 
     Extra keyword arguments (all optional): ``dtype`` (pool dtype, float32 by
     default like the reference; bfloat16 for the bf16 engine), ``device``,
-    ``max_requests`` (initial slot count; grows on demand) and
-    ``max_blocks_per_request`` (block-table width; grows on demand).
+    ``max_requests`` (initial slot count; grows on demand),
+    ``max_blocks_per_request`` (block-table width; grows on demand) and
+    ``prefix_cache`` (share the blocks of common prompt prefixes between
+    requests: see ``pse.prefix_cache``; off by default, which keeps the
+    reference's allocation order bit for bit).
     """
 
     def __init__(self, n_layers: int, n_heads: int, head_dim: int, block_size: int, num_blocks: int, *,
                  dtype: torch.dtype = torch.float32, device=None, max_requests: int = 64,
-                 max_blocks_per_request: int | None = None) -> None:
+                 max_blocks_per_request: int | None = None, prefix_cache: bool = False) -> None:
         N.load()
         self.n_layers, self.n_heads, self.head_dim = n_layers, n_heads, head_dim
         self.block_size, self.num_blocks = block_size, num_blocks
@@ -192,6 +196,7 @@ class PagedKVCache:
         self.pending_slots: set[int] = set()
         self._flusher = None
         self._serial = np.zeros(self._blocks.num_slots, dtype=np.int64)
+        self.prefix = PrefixIndex(self) if prefix_cache else None
 
     # ------------------------------------------------------------------ internals
     def _layer_struct(self, layer: int) -> N.KVLayer:
@@ -367,10 +372,16 @@ class PagedKVCache:
         old = self.length(request_id)
         if new_length > old:
             raise ValueError(f"truncate({new_length}) > current length {old}")
-        slots = torch.tensor([self._slot[request_id]], dtype=torch.int32).to(self.device, non_blocking=True)
-        lens = torch.tensor([new_length], dtype=torch.int32).to(self.device, non_blocking=True)
+        s = self._slot[request_id]
+        shared = self.prefix.shared_tokens(s) if self.prefix is not None else 0
+        slots = torch.tensor([s], dtype=torch.int32).to(self.device, non_blocking=True)
+        lens = torch.tensor([max(new_length, shared)], dtype=torch.int32).to(self.device, non_blocking=True)
         N.call("pse_kv_truncate", self.state, slots.data_ptr(), 1, lens.data_ptr(), None, None, N.stream_ptr())
-        self._len_np[self._slot[request_id]] = new_length
+        self._len_np[s] = max(new_length, shared)
+        if new_length < shared:
+            # below the shared prefix: the row's own blocks are gone; the shared
+            # ones past the new length leave its table, a partly kept one is copied
+            self.prefix.truncate_shared(s, new_length)
 
     def free_request(self, request_id: str) -> None:
         """engine/paged_cache.py:156-160."""
@@ -379,6 +390,8 @@ class PagedKVCache:
         self._serial[s] += 1
         self.slot_version += 1
         self.pending_slots.discard(s)
+        if self.prefix is not None:
+            self.prefix.release_rows([s])
         slots = torch.tensor([s], dtype=torch.int32).to(self.device, non_blocking=True)
         N.call("pse_kv_release", self.state, slots.data_ptr(), 1, N.stream_ptr())
         self._free_slots.append(s)
@@ -392,6 +405,8 @@ class PagedKVCache:
         self._serial[slots] += 1
         self.slot_version += 1
         self.pending_slots.difference_update(slots)
+        if self.prefix is not None:
+            self.prefix.release_rows(slots)
         t = torch.tensor(slots, dtype=torch.int32).to(self.device, non_blocking=True)
         N.call("pse_kv_release", self.state, t.data_ptr(), len(slots), N.stream_ptr())
         self._free_slots.extend(slots)

@@ -147,6 +147,11 @@ def _check_positions(dm, cache, request_ids, extra: int) -> int:
 def prefill_request(draft_model, target_model, draft_cache, target_cache, request_id, prompt_ids):
     """engine/speculative.py:53-73: seed both caches with the prompt and
     return the two next-token logits rows (device views)."""
+    if draft_cache.prefix is not None or target_cache.prefix is not None:
+        out = _prefill_prefix([(draft_model, draft_cache), (target_model, target_cache)], [request_id],
+                              [list(prompt_ids)])
+        if out is not None:
+            return out[0][0], out[1][0]
     draft_cache.create_request(request_id)
     target_cache.create_request(request_id)
     prompt_ids = list(prompt_ids)
@@ -173,7 +178,8 @@ def prefill_request(draft_model, target_model, draft_cache, target_cache, reques
 
 def _batch_prefill_safe(pairs, request_ids, prompts) -> bool:
     """True when prefilling these requests one by one could not raise part-way
-    (so one batched pass leaves exactly the same state)."""
+    (so one batched pass leaves exactly the same state).  Idle blocks of a
+    prefix index count as free (they are evicted on demand)."""
     if len(set(request_ids)) != len(request_ids):
         return False
     for dm, cache in pairs:
@@ -187,9 +193,89 @@ def _batch_prefill_safe(pairs, request_ids, prompts) -> bool:
             if dm.pos_emb is not None and len(p) > dm.max_seq_len:
                 return False
             need += (len(p) + bs - 1) // bs
-        if need > cache.allocator.num_free:
+        idle = len(cache.prefix.idle) if cache.prefix is not None else 0
+        if need > cache.allocator.num_free + idle:
             return False
     return True
+
+
+def _prefill_prefix(models_caches, request_ids, prompts, max_tokens_per_call: int = 32768):
+    """``prefill_many`` for caches with a prefix index (``pse.prefix_cache``):
+    each prompt's longest indexed prefix of full blocks (leaving at least its
+    last token) is mapped into the head of its block table and only the rest
+    is computed, at positions from the end of the shared prefix; the prompt's
+    full blocks are then indexed.  Inside one call the first prompt of every
+    distinct first block is prefilled before the others, so they find its
+    blocks.  Caches without an index take every prompt whole.  Returns what
+    ``prefill_many`` returns (None, having changed nothing, when one-by-one
+    prefills could raise part-way)."""
+    ids = list(request_ids)
+    prompts = [list(p) for p in prompts]
+    pairs = [(device_model(m, c.dtype, c.device), c) for m, c in models_caches]
+    if not ids or not _batch_prefill_safe(pairs, ids, prompts):
+        return None
+    for r in ids:
+        for _, cache in pairs:
+            cache.create_request(r)
+    n = len(ids)
+    P_all = np.array([len(p) for p in prompts], dtype=np.int64)
+    st = N.stream_ptr()
+    for dm, cache in pairs:
+        dev, bs, idx = cache.device, cache.block_size, cache.prefix
+        cache.ensure_capacity_len(int(P_all.max()))
+        buf = next_logits_buffer(cache, dm.vocab)
+        sc = scratch_for(dm)
+        for wave in (idx.waves(prompts) if idx is not None else [list(range(n))]):
+            wids = [ids[i] for i in wave]
+            wprom = [prompts[i] for i in wave]
+            m = len(wave)
+            slots_np = np.fromiter((cache.slot(r) for r in wids), np.int32, m)
+            hits = [idx.lookup(p) for p in wprom] if idx is not None else [[] for _ in wave]
+            shared = np.array([len(h) * bs for h in hits], dtype=np.int64)
+            P = P_all[wave]
+            widths = P - shared
+            if idx is not None:
+                need = int(sum((int(q) + bs - 1) // bs - len(h) for q, h in zip(P, hits)))
+                idx.make_room(need, keep=[b for h in hits for b in h])
+                idx.attach(slots_np.tolist(), hits)
+            slots = torch.from_numpy(slots_np).to(dev)
+            wd = torch.from_numpy(widths.astype(np.int32)).to(dev)
+            base = torch.empty(m, dtype=torch.int32, device=dev)
+            N.call("pse_kv_reserve_rows", cache.state, slots.data_ptr(), m, wd.data_ptr(), base.data_ptr(), st)
+            order = np.argsort(-widths, kind="stable")  # groups of similar suffix length, longest first
+            i0 = 0
+            while i0 < m:
+                W = int(widths[order[i0]])
+                grp = order[i0:i0 + max(1, max_tokens_per_call // W)]
+                i0 += len(grp)
+                g = len(grp)
+                ids_pad = np.zeros((g, W), dtype=np.int32)
+                for j, q in enumerate(grp):
+                    ids_pad[j, : widths[q]] = wprom[q][shared[q]:]
+                gids = torch.from_numpy(ids_pad).to(dev)
+                gslots = torch.from_numpy(slots_np[grp]).to(dev)
+                gbase = torch.from_numpy(shared[grp].astype(np.int32)).to(dev)
+                forward(dm, cache, gslots, gids.view(-1), g, W, gbase, int(shared[grp].max()) + W, None, scratch=sc,
+                        reserve=False)
+                last = torch.from_numpy(np.arange(g, dtype=np.int64) * W + widths[grp] - 1).to(dev)
+                hsel = torch.index_select(sc.h[: g * W], 0, last)
+                logits = torch.empty(g, dm.vocab, dtype=torch.float32, device=dev)
+                lm_head(dm, hsel, logits)
+                N.call("pse_scatter_rows", logits.data_ptr(), dm.vocab, gslots.data_ptr(), g, dm.vocab,
+                       buf.data_ptr(), dm.vocab, buf.shape[0], st)
+                last_tok = torch.from_numpy(np.array([wprom[q][-1] for q in grp], dtype=np.int32)).to(dev)
+                cache.last_token.index_copy_(0, gslots.long(), last_tok)
+            cache.note_lengths(wids, P.tolist())
+            if idx is not None:
+                cache.check_status("prefill")  # the blocks are indexed only once they hold their K/V
+                idx.register(slots_np.tolist(), wprom)
+    for _, cache in pairs:
+        cache.check_status("prefill")
+    out = []
+    for dm, cache in pairs:
+        views = next_logits_views(cache, dm.vocab)
+        out.append([views[cache.slot(r)] for r in ids])
+    return out
 
 
 @torch.no_grad()
@@ -210,6 +296,8 @@ def prefill_many(models_caches, request_ids, prompts, max_tokens_per_call: int =
     prompts = [list(p) for p in prompts]
     if len(ids) != len(prompts):
         raise ValueError("one prompt per request id")
+    if any(c.prefix is not None for _, c in models_caches):
+        return _prefill_prefix(models_caches, ids, prompts, max_tokens_per_call)
     pairs = [(device_model(m, c.dtype, c.device), c) for m, c in models_caches]
     if len(ids) <= 1 or not _batch_prefill_safe(pairs, ids, prompts):
         return None
@@ -584,6 +672,10 @@ class StepRunner:
         B = len(request_ids)
         dc, tc = self.dcache, self.tcache
         out_defer = defer_bonus is not False
+        for c in (dc, tc):
+            if c.prefix is not None and c.prefix.idle:
+                # idle prefix blocks give way to the step's worst-case growth (k + 2 tokens per row)
+                c.prefix.make_room(B * ((k + 2 + c.block_size - 1) // c.block_size + 1))
         # rows whose target call is still owed: the fast program needs all of
         # them pending; a mixed batch (rows just admitted, or given other
         # logits) or an eager step first completes the pending ones
