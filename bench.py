@@ -171,6 +171,8 @@ def run_pse(args, rank, world, device):
     mine = shard_requests(allreq, world, rank)
     B = len(mine)
     d, t = build_pair(w, dtype, device)
+    if getattr(args, "self_draft", False):
+        d = t  # draft == target: every draft accepted at T = 0 (the reference benchmark's ceiling)
     # room for every step the run takes (two structures x (warm-up + K replays + K API steps)), each
     # committing up to k+1 tokens, plus the roofline launch's k+1 reserved tokens
     n_steps = 2 * (max(args.warmup, 3) + 2 * args.steps)
@@ -1015,6 +1017,30 @@ def llama_step(args, device, peak):
     return out
 
 
+def self_draft_step(args, device):
+    """The headline workload's step with draft = target (the reference
+    benchmark's ceiling configuration): every draft is accepted, so the timed
+    steps commit k+1 tokens per row and exercise multi-token commits, multi-block
+    truncation and the all-accepted bonus path that the independent random draft
+    almost never reaches.  Summarised."""
+    import copy
+    gc.collect()
+    torch.cuda.empty_cache()
+    a = copy.copy(args)
+    a.steps, a.warmup, a.self_draft, a.reference_structure = 10, 3, True, False
+    r = run_pse(a, 0, 1, device)
+    hd_, rf_ = r["head"], r["ref"]
+    out = {"workload": f"{args.workload}, draft = target", "value": hd_["committed"] / (hd_["ms"] / 1000.0),
+           "unit": "tokens/s", "ms_per_step": hd_["ms"] / a.steps,
+           "e2e": hd_["e2e_tokens"] / (hd_["e2e_ms"] / 1000.0),
+           "reference_structure": rf_["committed"] / (rf_["ms"] / 1000.0),
+           "acceptance": {"rows_by_drafts_accepted": r["acc_hist"], "k": r["k"]}}
+    del r
+    gc.collect()
+    torch.cuda.empty_cache()
+    return out
+
+
 def config_block(args, w, B, world):
     dist = (f"lognormal(median {w.lognormal_median:g}, sigma {w.lognormal_sigma:g}) clipped to "
             f"[{w.prompt_lo},{w.prompt_hi}]" if w.lognormal_sigma > 0 else f"U[{w.prompt_lo},{w.prompt_hi}]")
@@ -1160,6 +1186,7 @@ def main():
         kernel_cfgs = kernel_configs(args, device)
         if args.workload == "gpt2-small":
             kernel_cfgs["4_llama_1b_step"] = llama_step(args, device, peak)
+        kernel_cfgs["self_draft_step"] = self_draft_step(args, device)
     check = token_check(args, r["check_rows"], os.cpu_count() or 1) if rank == 0 else None
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
