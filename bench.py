@@ -674,7 +674,7 @@ def micro_prefill(args, device):
                       "identical_tables_and_free_lists": same}), flush=True)
 
 
-def micro_scheduler(args, device):
+def micro_scheduler(args, device, emit=True):
     """The whole workload through run_continuous_speculative_batches (FIFO
     admission up to the batch size, batched prefill, steps until every request
     has max_new_tokens, as the reference's own benchmark drives it): committed
@@ -743,14 +743,17 @@ def micro_scheduler(args, device):
         ctoks = sum(len(r.output_ids) for r in ores) - sum(len(p) for p in prompts)
         cpu = {"value": ctoks / csecs, "unit": "tokens/s", "cores": os.cpu_count() or 1, "kind": "port",
                "sample": f"the whole {w.name} workload ({n} requests), fp32 oracle port"}
-    print(json.dumps({"metric": "committed tokens/s (scheduler, whole workload)", "workload": w.name, "k": w.k,
-                      "temperature": w.temperature, "requests": n, "max_batch_size": w.max_batch_size,
-                      "step": "reference structure" if args.reference_structure else "default (bonus deferred)",
-                      "bookkeeping": "host" if args.sched_host_loop else "device",
-                      "mode": {"spec": "speculative, independent draft", "self": "speculative, draft = target",
-                               "plain": "plain continuous batching, no speculation"}[args.sched_mode],
-                      "generated_tokens": toks, "seconds": secs, "value": toks / secs, "unit": "tokens/s",
-                      "cpu_baseline": cpu}), flush=True)
+    res = {"metric": "committed tokens/s (scheduler, whole workload)", "workload": w.name, "k": w.k,
+           "temperature": w.temperature, "requests": n, "max_batch_size": w.max_batch_size,
+           "step": "reference structure" if args.reference_structure else "default (bonus deferred)",
+           "bookkeeping": "host" if args.sched_host_loop else "device",
+           "mode": {"spec": "speculative, independent draft", "self": "speculative, draft = target",
+                    "plain": "plain continuous batching, no speculation"}[args.sched_mode],
+           "generated_tokens": toks, "seconds": secs, "value": toks / secs, "unit": "tokens/s",
+           "cpu_baseline": cpu}
+    if emit:
+        print(json.dumps(res), flush=True)
+    return res
 
 
 def micro_prefix(args, device):
@@ -987,6 +990,18 @@ def kernel_configs(args, device):
     r = micro_churn(a, device, emit=False)
     out["5c_truncate_churn"] = {k: r[k] for k in ("value", "unit", "host_syncs_per_step", "lengths_ok", "rows",
                                                   "steps")}
+    gc.collect()
+    torch.cuda.empty_cache()
+    if args.workload == "gpt2-small":
+        # every decode position, not only the early steps the replays time: the whole workload
+        # (256 requests x 256 new tokens, batched prefill included) through the scheduler
+        a.workload, a.rows, a.sched_mode, a.reference_structure = "gpt2-small", None, "spec", False
+        a.sched_host_loop, a.no_cpu_baseline = False, True
+        r = micro_scheduler(a, device, emit=False)
+        out["3_whole_workload"] = {k: r[k] for k in ("value", "unit", "seconds", "generated_tokens", "requests",
+                                                     "step", "bookkeeping")}
+        gc.collect()
+        torch.cuda.empty_cache()
     return out
 
 

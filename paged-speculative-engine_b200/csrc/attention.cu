@@ -328,6 +328,12 @@ struct Plan {
   int rmax, maxd, n_qtiles, n_splits, split_tokens;
 };
 
+// Work items the split plan aims for per SM: a call with fewer (row, KV head,
+// query tile) items than this splits each row's keys into more items.
+#ifndef PSE_ATTN_ITEMS_PER_SM
+#define PSE_ATTN_ITEMS_PER_SM 4
+#endif
+
 // The KV split count depends only on the call's shape (not on which kernel
 // runs it), so the workspace query and both kernels agree.
 Plan make_plan(int rows, int width, int q_heads, int kv_heads, int head_dim, int max_ctx) {
@@ -337,7 +343,7 @@ Plan make_plan(int rows, int width, int q_heads, int kv_heads, int head_dim, int
   p.maxd = head_dim <= 32 ? 1 : head_dim <= 64 ? 2 : head_dim <= 128 ? 4 : 8;
   p.n_qtiles = ceil_div(n_qrows, p.rmax);
   const long base_ctas = (long)rows * kv_heads * ceil_div(n_qrows, 16);
-  const int target = 4 * kNumSMs;
+  const int target = PSE_ATTN_ITEMS_PER_SM * kNumSMs;
   int splits = base_ctas >= target ? 1 : (int)((target + base_ctas - 1) / base_ctas);
   const int max_useful = ceil_div(max_ctx > 0 ? max_ctx : 1, 256);
   if (splits > max_useful) splits = max_useful;

@@ -75,14 +75,19 @@ def scratch_for(dm: DeviceModel) -> Scratch:
     return s
 
 
-USE_TC_GEMM = False  # bf16 projections on the tcgen05 GEMM (pse_gemm_bf16); off until it beats cuBLAS on these shapes
+# bf16 projections on the tcgen05 GEMM (pse_gemm_bf16): False (cuBLAS), True
+# (every projection), or "gelu" (only the MLP up-projections, whose GELU the
+# GEMM applies in its epilogue instead of a separate kernel after cuBLAS)
+USE_TC_GEMM = False
 TC_GEMM_MAX_ROWS = 1 << 30  # with USE_TC_GEMM: only GEMMs of at most this many rows
 
 
-def _tc_ok(a: torch.Tensor, w: torch.Tensor, out: torch.Tensor) -> bool:
+def _tc_ok(a: torch.Tensor, w: torch.Tensor, out: torch.Tensor, gelu: bool = False) -> bool:
     """pse_gemm_bf16 takes bf16 operands, k in whole 64-element slabs, row
     pitches in 16-byte units and 16-byte aligned bases."""
-    if not USE_TC_GEMM or a.dtype != torch.bfloat16 or w.dtype != torch.bfloat16 or a.shape[0] > TC_GEMM_MAX_ROWS:
+    if not USE_TC_GEMM or (USE_TC_GEMM == "gelu" and not gelu):
+        return False
+    if a.dtype != torch.bfloat16 or w.dtype != torch.bfloat16 or a.shape[0] > TC_GEMM_MAX_ROWS:
         return False
     k = a.shape[1]
     esz = out.element_size()
@@ -95,7 +100,7 @@ def _mm(a: torch.Tensor, w: torch.Tensor, out: torch.Tensor, bias: torch.Tensor 
         gelu: bool = False) -> bool:
     """out = a @ w^T (+ bias).  With ``gelu`` the tensor-core path also applies
     GELU; returns whether it did (the cuBLAS fallback never does)."""
-    if _tc_ok(a, w, out):
+    if _tc_ok(a, w, out, gelu):
         N.call("pse_gemm_bf16", a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0), N.ptr(bias), out.data_ptr(),
                out.stride(0), a.shape[0], w.shape[0], a.shape[1], 1 if gelu else 0,
                1 if out.dtype == torch.float32 else 0, None, N.stream_ptr())
