@@ -251,6 +251,34 @@ int pse_spec_accept(const float *target0, int64_t t0_stride, const int32_t *t0_i
                     int32_t k, int32_t vocab, float temperature, int32_t *tokens,
                     int32_t *n_accepted, int32_t *final_token, void *stream);
 
+/* Tree speculation: accept / reject / resample over a token tree of
+ * `branches` (b <= 8) first-level candidates, each followed by a draft chain:
+ * node (j, d), j < b, d < k, is branch j's token at depth d (chain[(i*b + j)*k
+ * + d]).  The reference has no counterpart (its README lists tree-based
+ * speculation as future work); b = 1 is exactly pse_spec_accept's rule.
+ * Target logits at the root: p_root + (pr_index ? pr_index[i] : i) * pr_stride;
+ * after node (j, d): verify + (i*b + j)*v_row + d*v_pos.  Draft logits at the
+ * root: q_root (+ qr_index / qr_stride); after node (j, d), d < k-1:
+ * dchain + d*dc_depth + (i*b + j)*dc_row (draft logits unused at T <= 0).
+ * T <= 0: the first branch whose candidate is the target's argmax, then the
+ * greedy rule along it.  T > 0: recursive rejection over the b candidates
+ * (drawn iid from the draft's root distribution): candidate j is tested
+ * against the normalised residual of the rounds before it, so the first token
+ * keeps the target's distribution; then the linear rule along the accepted
+ * branch.  Uniforms u[i*u_stride + ...]: d*b + j drew node (j, d), b*k + j
+ * tests candidate j, b*k + b + d - 1 tests depth d >= 1, b*k + b + k - 1 is
+ * the final draw.  Writes tokens[i*(k+1) + 0..n] (accepted nodes, then the
+ * corrected / bonus token), n_accepted[i], branch[i] (0 when no candidate was
+ * accepted) and final_token[i].  One CTA per row. */
+int pse_tree_accept(const float *p_root, int64_t pr_stride, const int32_t *pr_index,
+                    const float *q_root, int64_t qr_stride, const int32_t *qr_index,
+                    const float *verify, int64_t v_row, int64_t v_pos,
+                    const float *dchain, int64_t dc_depth, int64_t dc_row,
+                    const int32_t *chain, const double *u, int64_t u_stride, int32_t rows,
+                    int32_t branches, int32_t k, int32_t vocab, float temperature,
+                    int32_t *tokens, int32_t *n_accepted, int32_t *branch,
+                    int32_t *final_token, void *stream);
+
 /* Which kernel pse_spec_accept runs at T > 0: 0 the default (one cluster of
  * min(8, ceil(vocab / 8192)) CTAs per row, several clusters per SM, the row
  * streamed from HBM once and re-read from L2), 1 the CTA-per-row scalar

@@ -27,6 +27,8 @@ Modules (each function cites the reference file:line it restates):
 * ``attention``       paged attention over a block pool (engine/model.py:99-116
                       applied to engine/paged_cache.py's layout).
 * ``philox``          Philox4x32-10 counter-based generator (Salmon et al. 2011).
+* ``tree``            tree speculation (b candidate branches per step; the
+                      reference's README future work), b = 1 being the linear step.
 
 Parity pin: ``tests/golden/`` holds vectors produced by running the reference
 itself (script ``tests/golden/make_golden.py``); ``tests/test_oracle_golden.py``

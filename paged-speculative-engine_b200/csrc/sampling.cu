@@ -1663,6 +1663,229 @@ __global__ void __launch_bounds__(kStThreads, 1) sample_stream_kernel(const floa
   }
 }
 
+// ---------------------------------------------------------------- tree speculation: accept / resample
+//
+// One CTA per request row over a token tree of b branches x k depths (node
+// (j, d) is branch j's token at depth d).  T = 0: the first branch whose
+// candidate is the target's argmax, then the greedy linear rule along it.
+// T > 0: recursive rejection over the b candidates at depth 0 (round i tests
+// candidate i against P_{i-1}, the previous rounds' normalised residual
+// max(0, P - Q) / R), then the linear rule (accept_kernel above) along the
+// accepted branch.  Uniform layout per row: u[d*b + j] drew node (j, d),
+// u[b*k + i] tests candidate i, u[b*k + b + d - 1] tests depth d >= 1,
+// u[b*k + b + k - 1] is the final draw.  Arithmetic as stated in the header
+// of this file, plus: P_0 = w_p * (1/Z_p), Q = w_q * (1/Z_q), r = max(0, P - Q),
+// P_next = r * (1/R) -- each product and difference rounded on its own.
+
+constexpr int kTreeMaxB = 8;
+
+struct TreeArgs {
+  const float* p_root;
+  int64_t pr_stride;
+  const int32_t* pr_index;
+  const float* q_root;
+  int64_t qr_stride;
+  const int32_t* qr_index;
+  const float* verify;  // node (i, j, d): verify + (i*b + j) * v_row + d * v_pos
+  int64_t v_row, v_pos;
+  const float* dchain;  // draft after node (i, j, d), d < k-1: dchain + d * dc_depth + (i*b + j) * dc_row
+  int64_t dc_depth, dc_row;
+  const int32_t* chain;  // [rows][b][k]
+  const double* u;
+  int64_t u_stride;
+  int b, k, V;
+  float T;
+  int32_t* tokens;  // [rows][k+1]
+  int32_t* n_accepted;
+  int32_t* branch;
+  int32_t* final_token;
+};
+
+// P_rounds(e): the target's root distribution after `rounds` residual rounds
+// (invR[s] == 0 marks a round whose residual was empty: P unchanged).
+struct TreeChainP {
+  const float* p;
+  const float* q;
+  float T, mp, mq;
+  double invp, invq;
+  const double* invR;
+  int rounds;
+  __device__ __forceinline__ double Q(int e) const { return __dmul_rn((double)expf(q[e] / T - mq), invq); }
+  __device__ __forceinline__ double P(int e) const {
+    double P = __dmul_rn((double)expf(p[e] / T - mp), invp);
+    if (rounds == 0) return P;
+    const double qe = Q(e);
+    for (int s = 0; s < rounds; ++s) {
+      if (invR[s] > 0.0) {
+        const double d = __dsub_rn(P, qe);
+        P = __dmul_rn(d > 0.0 ? d : 0.0, invR[s]);
+      }
+    }
+    return P;
+  }
+};
+
+// r_{rounds+1}(e) = max(0, P_rounds(e) - Q(e)): the residual of the next round.
+struct TreeResidual {
+  TreeChainP c;
+  __device__ double operator()(int e) const {
+    const double d = __dsub_rn(c.P(e), c.Q(e));
+    return d > 0.0 ? d : 0.0;
+  }
+};
+
+__device__ __forceinline__ const float* tree_node_target(const TreeArgs& a, int i, int j, int d) {
+  return a.verify + ((int64_t)i * a.b + j) * a.v_row + (int64_t)d * a.v_pos;
+}
+__device__ __forceinline__ const float* tree_node_draft(const TreeArgs& a, int i, int j, int d) {
+  return a.dchain + (int64_t)d * a.dc_depth + ((int64_t)i * a.b + j) * a.dc_row;
+}
+
+__global__ void __launch_bounds__(kSampleThreads) tree_accept_kernel(TreeArgs a) {
+  __shared__ Scratch sh;
+  const int i = blockIdx.x;
+  const int b = a.b, k = a.k, V = a.V;
+  const float T = a.T;
+  const int32_t* chain = a.chain + (int64_t)i * b * k;
+  int32_t* toks = a.tokens + (int64_t)i * (k + 1);
+  const float* pr = a.p_root + (int64_t)(a.pr_index ? a.pr_index[i] : i) * a.pr_stride;
+  const float* qr = a.q_root + (int64_t)(a.qr_index ? a.qr_index[i] : i) * a.qr_stride;
+  int n_acc = 0, fin = -1, jb = 0;
+
+  if (T <= 0.f) {
+    const int y0 = block_argmax(pr, V, sh);
+    jb = -1;
+    for (int j = 0; j < b; ++j)
+      if (chain[j * k] == y0) {
+        jb = j;
+        break;
+      }
+    if (jb < 0) {
+      jb = 0;
+      fin = y0;
+    } else {
+      if (threadIdx.x == 0) toks[0] = y0;
+      n_acc = k;
+      for (int d = 1; d <= k; ++d) {
+        const int y = block_argmax(tree_node_target(a, i, jb, d - 1), V, sh);
+        if (d == k) {
+          fin = y;
+          break;
+        }
+        if (threadIdx.x == 0) toks[d] = y;
+        if (chain[jb * k + d] != y) {
+          n_acc = d;
+          fin = y;
+          break;
+        }
+      }
+    }
+  } else {
+    const double* u = a.u + (int64_t)i * a.u_stride;
+    const int base = b * k;
+    const double u_fin = u[base + b + k - 1];
+    const Stats sp = row_stats(pr, V, T, sh);
+    const Stats sq = row_stats(qr, V, T, sh);
+    double invR[kTreeMaxB];
+    TreeChainP cp{pr, qr, T, sp.m, sq.m, 1.0 / sp.z, 1.0 / sq.z, invR, 0};
+    double last_R = 0.0;
+    int last_round = -1;
+    jb = -1;
+    for (int r = 0; r < b; ++r) {
+      // round r + 1: candidate r against P_r (engine/speculative.py:133-142 for r = 0)
+      const int x = chain[r * k];
+      const bool x_ok = x >= 0 && x < V;
+      double prob = 0.0;
+      if (x_ok) {
+        if (r == 0) {
+          const double wpx = (double)expf(pr[x] / T - sp.m), wqx = (double)expf(qr[x] / T - sq.m);
+          if (wqx > 0.0) {
+            const double ratio = __ddiv_rn(__dmul_rn(wpx, sq.z), __dmul_rn(wqx, sp.z));
+            prob = ratio < 1.0 ? ratio : 1.0;
+          }
+        } else {
+          cp.rounds = r;
+          const double qx = cp.Q(x);
+          if (qx > 0.0) {
+            const double ratio = __ddiv_rn(cp.P(x), qx);
+            prob = ratio < 1.0 ? ratio : 1.0;
+          }
+        }
+      }
+      if (u[base + r] < prob) {
+        jb = r;
+        break;
+      }
+      cp.rounds = r;
+      const TreeResidual rw{cp};
+      double R = 0.0;
+      for (int e = threadIdx.x; e < V; e += blockDim.x) R += rw(e);
+      R = block_sum_d(R, sh);
+      invR[r] = R > 0.0 ? 1.0 / R : 0.0;
+      if (R > 0.0) {
+        last_R = R;
+        last_round = r;
+      }
+    }
+    if (jb < 0) {
+      // every candidate rejected: the last non-empty residual, else p
+      jb = 0;
+      n_acc = 0;
+      if (last_round >= 0) {
+        cp.rounds = last_round;
+        fin = block_icdf(TreeResidual{cp}, V, u_fin * last_R, sh);
+      } else {
+        fin = block_icdf(SoftmaxWeight{pr, T, sp.m}, V, u_fin * sp.z, sh);
+      }
+    } else {
+      if (threadIdx.x == 0) toks[0] = chain[jb * k];
+      n_acc = k;
+      for (int d = 1; d < k; ++d) {
+        // engine/speculative.py:133-142 along the accepted branch
+        const float* p = tree_node_target(a, i, jb, d - 1);
+        const float* q = tree_node_draft(a, i, jb, d - 1);
+        const int x = chain[jb * k + d];
+        const bool x_ok = x >= 0 && x < V;
+        const Stats s1 = row_stats(p, V, T, sh);
+        const Stats s2 = row_stats(q, V, T, sh);
+        const double wpx = x_ok ? (double)expf(p[x] / T - s1.m) : 0.0;
+        const double wqx = x_ok ? (double)expf(q[x] / T - s2.m) : 0.0;
+        double prob = 0.0;
+        if (wqx > 0.0) {
+          const double ratio = __ddiv_rn(__dmul_rn(wpx, s2.z), __dmul_rn(wqx, s1.z));
+          prob = ratio < 1.0 ? ratio : 1.0;
+        }
+        if (u[base + b + d - 1] < prob) {
+          if (threadIdx.x == 0) toks[d] = x;
+          continue;
+        }
+        // engine/speculative.py:43-50
+        const ResidualWeight rw{p, q, T, s1.m, s2.m, 1.0 / s1.z, 1.0 / s2.z};
+        double R = 0.0;
+        for (int e = threadIdx.x; e < V; e += blockDim.x) R += rw(e);
+        R = block_sum_d(R, sh);
+        fin = R <= 0.0 ? block_icdf(SoftmaxWeight{p, T, s1.m}, V, u_fin * s1.z, sh)
+                       : block_icdf(rw, V, u_fin * R, sh);
+        n_acc = d;
+        break;
+      }
+      if (fin < 0) {
+        // every depth accepted: the bonus from the target after node (jb, k-1)
+        const float* p = tree_node_target(a, i, jb, k - 1);
+        const Stats s1 = row_stats(p, V, T, sh);
+        fin = block_icdf(SoftmaxWeight{p, T, s1.m}, V, u_fin * s1.z, sh);
+      }
+    }
+  }
+  if (threadIdx.x == 0) {
+    toks[n_acc] = fin;
+    for (int j = n_acc + 1; j <= k; ++j) toks[j] = -1;
+    a.n_accepted[i] = n_acc;
+    a.branch[i] = jb;
+    a.final_token[i] = fin;
+  }
+}
+
 // The vector kernels read 16-byte vectors: every logits row must start on a
 // 16-byte boundary (base pointers aligned, strides and vocab multiples of 4).
 bool vec_accept_ok(const AcceptArgs& a) {
@@ -1785,6 +2008,23 @@ extern "C" int pse_spec_accept(const float* target0, int64_t t0_stride, const in
     // rc < 0: no cluster of this size fits on the device; the CTA-per-row kernel below handles it
   }
   accept_kernel<<<rows, kSampleThreads, 0, (cudaStream_t)stream>>>(a);
+  PSE_LAUNCH_CHECK();
+  return PSE_OK;
+}
+
+extern "C" int pse_tree_accept(const float* p_root, int64_t pr_stride, const int32_t* pr_index, const float* q_root,
+                               int64_t qr_stride, const int32_t* qr_index, const float* verify, int64_t v_row,
+                               int64_t v_pos, const float* dchain, int64_t dc_depth, int64_t dc_row,
+                               const int32_t* chain, const double* u, int64_t u_stride, int32_t rows, int32_t branches,
+                               int32_t k, int32_t vocab, float temperature, int32_t* tokens, int32_t* n_accepted,
+                               int32_t* branch, int32_t* final_token, void* stream) {
+  if (rows < 0 || k < 1 || vocab <= 0 || branches < 1 || branches > kTreeMaxB || branches > vocab) return PSE_EINVAL;
+  if (rows == 0) return PSE_OK;
+  if (!p_root || !verify || !chain || !tokens || !n_accepted || !branch || !final_token) return PSE_EINVAL;
+  if (temperature > 0.f && (!u || !q_root || (k > 1 && !dchain))) return PSE_EINVAL;
+  TreeArgs a{p_root, pr_stride, pr_index, q_root, qr_stride, qr_index, verify, v_row, v_pos, dchain, dc_depth, dc_row,
+             chain, u, u_stride, branches, k, vocab, temperature, tokens, n_accepted, branch, final_token};
+  tree_accept_kernel<<<rows, kSampleThreads, 0, (cudaStream_t)stream>>>(a);
   PSE_LAUNCH_CHECK();
   return PSE_OK;
 }

@@ -14,10 +14,12 @@ from .paged_cache import BlockAllocator, PagedKVCache
 from .scheduler import Request, RequestResult, run_continuous_speculative_batches
 from .plain import run_plain_continuous_batches
 from .speculative import BatchStepResult, batched_speculative_step, prefill_request, prefill_requests
+from .tree import batched_tree_speculative_step, speculative_generate_tree
 
 __all__ = [
     "BatchStepResult", "BlockAllocator", "LlamaConfig", "ModelConfig", "PagedKVCache", "Request",
     "RequestResult", "TinyGPT", "TinyLlama", "batched_forward_append", "batched_speculative_step",
+    "batched_tree_speculative_step", "speculative_generate_tree",
     "prefill_request", "prefill_requests", "run_continuous_speculative_batches", "run_plain_continuous_batches",
     "speculative_generate_batched",
 ]

@@ -64,6 +64,8 @@ _PROTOS = {
     "pse_sample_tokens": ([c_p, c_i64, c_p, c_i32, c_i32, c_f32, c_p, c_i64, c_i32, c_p, c_i64, c_p, c_i64, c_p], 1),
     "pse_spec_accept": ([c_p, c_i64, c_p, c_p, c_i64, c_i64, c_p, c_i64, c_p, c_p, c_i64, c_i64, c_p, c_p, c_i64,
                          c_i32, c_i32, c_i32, c_f32, c_p, c_p, c_p, c_p], 1),
+    "pse_tree_accept": ([c_p, c_i64, c_p, c_p, c_i64, c_p, c_p, c_i64, c_i64, c_p, c_i64, c_i64, c_p, c_p, c_i64,
+                         c_i32, c_i32, c_i32, c_i32, c_f32, c_p, c_p, c_p, c_p, c_p], 1),
     "pse_embed": ([c_p, c_p, c_i32, c_i32, c_p, c_p, c_i32, c_i32, c_i32, c_i32, c_p, c_p], 1),
     "pse_norm": ([c_p, c_i64, c_p, c_p, c_i32, c_i32, c_i32, c_f32, c_i32, c_p, c_i64, c_i32, c_p], 1),
     "pse_add_norm": ([c_p, c_i64, c_p, c_i64, c_p, c_i32, c_p, c_p, c_i32, c_i32, c_i32, c_f32, c_i32, c_p, c_i64,

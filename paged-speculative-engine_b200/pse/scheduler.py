@@ -26,6 +26,7 @@ import numpy as np
 import torch
 
 from .speculative import _fnv1a, batched_speculative_step, prefill_requests, runner_for, CommitArena
+from .tree import batched_tree_speculative_step, tree_uniform_count
 
 
 @dataclass
@@ -61,16 +62,22 @@ class _Active:
 def run_continuous_speculative_batches(draft_model, target_model, requests, draft_cache, target_cache,
                                        max_batch_size, k=4, temperature=0.0, generator=None, *,
                                        uniform_fn=None, on_step=None, use_graph=None, defer_bonus=None,
-                                       device_bookkeeping=None):
+                                       device_bookkeeping=None, tree_branches=None):
     """engine/scheduler.py:61-128.  ``uniform_fn(request_ids, steps, n)`` (optional)
     supplies explicit uniforms per step; ``on_step(ids, result)`` observes steps;
     ``defer_bonus`` (default: on) defers the target's bonus call into the next
     verify (see ``batched_speculative_step``; False runs it in every step); ``device_bookkeeping`` (default: whenever
     ``on_step`` is not given) keeps the per-row token lists and finish tests
-    on the device, False runs them on the host as the reference does."""
+    on the device, False runs them on the host as the reference does.
+    ``tree_branches`` (optional) runs token-tree steps of that many branches
+    (``pse.tree``; the per-row bookkeeping then runs on the host)."""
     requests = list(requests)
     if device_bookkeeping and on_step is not None:
         raise ValueError("on_step needs every step's result on the host: device_bookkeeping must be off")
+    if tree_branches is not None:
+        if device_bookkeeping:
+            raise ValueError("token-tree steps keep the per-row bookkeeping on the host")
+        device_bookkeeping = False
     if (device_bookkeeping is None or device_bookkeeping) and on_step is None and \
             all(isinstance(q.max_new_tokens, Integral) and q.max_new_tokens >= 0 for q in requests):
         return _run_device_bookkeeping(draft_model, target_model, requests, draft_cache, target_cache,
@@ -105,12 +112,19 @@ def run_continuous_speculative_batches(draft_model, target_model, requests, draf
         ids = list(active.keys())
         u = None
         if uniform_fn is not None and temperature > 0:
-            u = uniform_fn(ids, [steps_taken[r] for r in ids], 2 * k + 1)
-        step = batched_speculative_step(
-            draft_model, target_model, ids, draft_cache, target_cache,
-            {r: active[r].draft_next_logits for r in ids}, {r: active[r].target_next_logits for r in ids},
-            k, temperature, generator, uniforms=u, use_graph=use_graph, defer_bonus=defer_bonus,
-        )
+            n_u = 2 * k + 1 if tree_branches is None else tree_uniform_count(k, tree_branches)
+            u = uniform_fn(ids, [steps_taken[r] for r in ids], n_u)
+        if tree_branches is not None:
+            step = batched_tree_speculative_step(
+                draft_model, target_model, ids, draft_cache, target_cache,
+                {r: active[r].draft_next_logits for r in ids}, {r: active[r].target_next_logits for r in ids},
+                k, tree_branches, temperature, generator, uniforms=u)
+        else:
+            step = batched_speculative_step(
+                draft_model, target_model, ids, draft_cache, target_cache,
+                {r: active[r].draft_next_logits for r in ids}, {r: active[r].target_next_logits for r in ids},
+                k, temperature, generator, uniforms=u, use_graph=use_graph, defer_bonus=defer_bonus,
+            )
         if on_step is not None:
             on_step(ids, step)
         finished = []
