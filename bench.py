@@ -830,6 +830,62 @@ def micro_prefix(args, device):
                       "outputs_identical": same}), flush=True)
 
 
+def micro_tree(args, device):
+    """Token-tree speculation against the linear chain on the gpt2-small pair,
+    bf16, greedy, 256 requests x 64 new tokens through the scheduler (host
+    bookkeeping for both, so only the step differs).  Random-init weights make
+    an independent draft agree with the target almost never, so the draft
+    here is the target with Gaussian noise of --tree-noise x each weight's
+    standard deviation added: it agrees often but not always, the regime
+    where a second candidate pays.  Reports committed tokens/s and tokens per
+    step for k=4 with 1 (linear), 2 and 4 branches, and whether every run
+    produced the same outputs (greedy: they must)."""
+    import pse
+    from pse import workload as wl
+    from pse.scheduler import Request
+    w = wl.WORKLOADS["gpt2-small"]
+    n = args.rows or 256
+    prompts = wl.prompts(w, seed=0, n=n)
+    max_new, k = 64, 4
+    _, t = build_pair(w, torch.bfloat16, device)
+    torch.manual_seed(1)
+    d = type(t)(t.cfg).eval()
+    with torch.no_grad():
+        for pd, pt in zip(d.parameters(), t.parameters()):
+            pd.copy_(pt + args.tree_noise * pt.float().std() * torch.randn_like(pt))
+    outs, lines = {}, {}
+    for b in (1, 2, 4):
+        for run in ("warm", "timed"):
+            reqs = [Request(f"{run}{i}", p, max_new) for i, p in enumerate(prompts)]
+            dc = cache_for(d, w, n, torch.bfloat16, device, 2 * (k + 2) * b, prompts)
+            tc = cache_for(t, w, n, torch.bfloat16, device, 2 * (k + 2) * b, prompts)
+            steps = [0]
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            if b == 1:
+                res = pse.run_continuous_speculative_batches(d, t, reqs, dc, tc, n, k=k, defer_bonus=False,
+                                                             device_bookkeeping=False,
+                                                             on_step=lambda ids, r: steps.__setitem__(0, steps[0] + 1))
+            else:
+                res = pse.run_continuous_speculative_batches(d, t, reqs, dc, tc, n, k=k, tree_branches=b,
+                                                             on_step=lambda ids, r: steps.__setitem__(0, steps[0] + 1))
+            torch.cuda.synchronize()
+            secs = time.perf_counter() - t0
+            if run == "timed":
+                by = {r.request_id[len(run):]: r.output_ids for r in res}
+                toks = sum(len(by[str(i)]) - len(p) for i, p in enumerate(prompts))
+                outs[b] = by
+                lines[b] = {"value": toks / secs, "unit": "tokens/s", "seconds": secs, "steps": steps[0],
+                            "tokens_per_row_step": toks / max(1, steps[0]) / n}
+            del dc, tc, res
+            gc.collect()
+            torch.cuda.empty_cache()
+    print(json.dumps({"metric": "committed tokens/s (scheduler, token-tree speculation)", "workload":
+                      f"gpt2-small pair, {n} requests x {max_new} new, k={k}, greedy, bf16, draft = target + "
+                      f"{args.tree_noise:g} sd noise", "linear": lines[1], "branches_2": lines[2],
+                      "branches_4": lines[4], "outputs_identical": outs[1] == outs[2] == outs[4]}), flush=True)
+
+
 GEMM_SHAPES = {
     # name: (M, K, N, bias, gelu, fp32 out) -- the gpt2-small step's projections
     "t.qkv": (1536, 768, 2304, True, False, False), "t.out": (1536, 768, 768, True, False, False),
@@ -1094,11 +1150,13 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-kernel-configs", action="store_true",
                     help="skip the 5a / 5b / 5c kernel configurations after the step (they run at N=1 only)")
-    ap.add_argument("--micro", choices=["attn", "accept", "churn", "prefill", "scheduler", "gemm", "prefix"],
+    ap.add_argument("--micro", choices=["attn", "accept", "churn", "prefill", "scheduler", "gemm", "prefix", "tree"],
                     default=None,
                     help="kernel microbenchmark instead of the step")
     ap.add_argument("--temperature", type=float, default=1.0, help="--micro accept: temperature")
     ap.add_argument("--prefix-len", type=int, default=512, help="--micro prefix: system prompt tokens")
+    ap.add_argument("--tree-noise", type=float, default=0.1,
+                    help="--micro tree: draft = target + this many weight standard deviations of noise")
     ap.add_argument("--accept-kernel", type=int, default=0, choices=[0, 1, 2, 3],
                     help="--micro accept at T > 0: 0 cluster-split streaming (default), 1 scalar CTA per row, "
                          "2 cluster per row holding the row on chip, 3 streaming CTA per row")
@@ -1188,6 +1246,9 @@ def main():
         return
     if args.micro == "prefix":
         micro_prefix(args, device)
+        return
+    if args.micro == "tree":
+        micro_tree(args, device)
         return
     if args.micro == "gemm":
         micro_gemm(args, device)
