@@ -838,8 +838,8 @@ def micro_tree(args, device):
     here is the target with Gaussian noise of --tree-noise x each weight's
     standard deviation added: it agrees often but not always, the regime
     where a second candidate pays.  Reports committed tokens/s and tokens per
-    step for k=4 with 1 (linear), 2 and 4 branches, and whether every run
-    produced the same outputs (greedy: they must)."""
+    step for k=4 with 1 (linear), 2 and 4 branches, and how many requests'
+    outputs equal the linear run's."""
     import pse
     from pse import workload as wl
     from pse.scheduler import Request
@@ -883,7 +883,12 @@ def micro_tree(args, device):
     print(json.dumps({"metric": "committed tokens/s (scheduler, token-tree speculation)", "workload":
                       f"gpt2-small pair, {n} requests x {max_new} new, k={k}, greedy, bf16, draft = target + "
                       f"{args.tree_noise:g} sd noise", "linear": lines[1], "branches_2": lines[2],
-                      "branches_4": lines[4], "outputs_identical": outs[1] == outs[2] == outs[4]}), flush=True)
+                      "branches_4": lines[4],
+                      "requests_identical_to_linear": {f"branches_{b}": sum(outs[b][r] == outs[1][r] for r in outs[1])
+                                                       for b in (2, 4)},
+                      "note": "bf16: the verify call's width differs between the forms (k vs b*k nodes), so a "
+                              "near-tie argmax can differ; fp32 parity is exact (tests/test_tree_gpu.py)"}),
+          flush=True)
 
 
 GEMM_SHAPES = {

@@ -156,6 +156,30 @@ int pse_paged_attention(pse_block_state st, pse_kv_layer kv, const void *q, int6
 size_t pse_paged_attention_workspace(int32_t rows, int32_t width, int32_t q_heads, int32_t kv_heads,
                                      int32_t head_dim, int32_t max_ctx);
 
+/* pse_paged_attention for a token-tree call (no counterpart in the reference:
+ * its README lists tree-based speculation as future work).  The call's tokens
+ * are tree nodes of `tree_branches` (b) branches in depth-major order, from
+ * depth tree_depth0 (d0): query w is node n = d0*b + w, branch n % b at depth
+ * n / b, at position L + n of its row (L = base_len[i] - d0*b, the row's
+ * length at the tree's root); it attends to positions 0..L-1 and to its own
+ * branch's nodes at depths up to its own.  Everything else as
+ * pse_paged_attention (same workspace rules); prompt-sized calls do not take
+ * the prefill kernel.  tree_branches < 1: PSE_EINVAL. */
+int pse_paged_attention_tree(pse_block_state st, pse_kv_layer kv, const void *q, int64_t q_tok_stride,
+                             void *out, int64_t out_tok_stride, const int32_t *slots,
+                             const int32_t *base_len, int32_t rows, int32_t width, int32_t q_heads,
+                             float scale, int32_t max_ctx, const int32_t *row_order, void *workspace,
+                             size_t workspace_bytes, int32_t tree_branches, int32_t tree_depth0,
+                             void *stream);
+
+/* Token-tree commit for one layer: row i keeps n[i] of the tokens its tree
+ * calls appended -- the token at position base_len[i] + src[i*max_n + m] moves
+ * to position base_len[i] + m, m < n[i] (src increasing, src[m] >= m).  The
+ * caller then truncates the row to base_len[i] + n[i].  No counterpart in the
+ * reference. */
+int pse_kv_compact(pse_block_state st, pse_kv_layer kv, const int32_t *slots, const int32_t *base_len,
+                   const int32_t *src, const int32_t *n, int32_t rows, int32_t max_n, void *stream);
+
 /* pse_paged_attention without a workspace argument, for hosts that cannot
  * allocate device memory where they call this library (a runtime in another
  * language that binds only this C ABI and has no CUDA allocator, or a process
@@ -257,9 +281,9 @@ int pse_spec_accept(const float *target0, int64_t t0_stride, const int32_t *t0_i
  * + d]).  The reference has no counterpart (its README lists tree-based
  * speculation as future work); b = 1 is exactly pse_spec_accept's rule.
  * Target logits at the root: p_root + (pr_index ? pr_index[i] : i) * pr_stride;
- * after node (j, d): verify + (i*b + j)*v_row + d*v_pos.  Draft logits at the
- * root: q_root (+ qr_index / qr_stride); after node (j, d), d < k-1:
- * dchain + d*dc_depth + (i*b + j)*dc_row (draft logits unused at T <= 0).
+ * after node (j, d): verify + i*v_req + j*v_branch + d*v_depth.  Draft logits
+ * at the root: q_root (+ qr_index / qr_stride); after node (j, d), d < k-1:
+ * dchain + i*dc_req + j*dc_branch + d*dc_depth (draft logits unused at T <= 0).
  * T <= 0: the first branch whose candidate is the target's argmax, then the
  * greedy rule along it.  T > 0: recursive rejection over the b candidates
  * (drawn iid from the draft's root distribution): candidate j is tested
@@ -272,8 +296,8 @@ int pse_spec_accept(const float *target0, int64_t t0_stride, const int32_t *t0_i
  * accepted) and final_token[i].  One CTA per row. */
 int pse_tree_accept(const float *p_root, int64_t pr_stride, const int32_t *pr_index,
                     const float *q_root, int64_t qr_stride, const int32_t *qr_index,
-                    const float *verify, int64_t v_row, int64_t v_pos,
-                    const float *dchain, int64_t dc_depth, int64_t dc_row,
+                    const float *verify, int64_t v_req, int64_t v_branch, int64_t v_depth,
+                    const float *dchain, int64_t dc_req, int64_t dc_branch, int64_t dc_depth,
                     const int32_t *chain, const double *u, int64_t u_stride, int32_t rows,
                     int32_t branches, int32_t k, int32_t vocab, float temperature,
                     int32_t *tokens, int32_t *n_accepted, int32_t *branch,
@@ -301,6 +325,12 @@ int pse_accept_select(int32_t kernel);
 int pse_embed(const int32_t *ids, const int32_t *base_len, int32_t rows, int32_t width,
               const void *tok_emb, const void *pos_emb, int32_t d, int32_t emb_dtype, int32_t vocab,
               int32_t n_pos, float *x, void *stream);
+
+/* pse_embed with the position of every token given (positions[i*width + w]),
+ * for calls whose tokens are not consecutive positions (token-tree nodes). */
+int pse_embed_pos(const int32_t *ids, const int32_t *positions, int32_t rows, int32_t width,
+                  const void *tok_emb, const void *pos_emb, int32_t d, int32_t emb_dtype, int32_t vocab,
+                  int32_t n_pos, float *x, void *stream);
 
 /* LayerNorm (engine/model.py:124-126, eps 1e-5, biased variance) or RMSNorm
  * (rms != 0, beta ignored) of fp32 rows into out (out_dtype). */
@@ -339,6 +369,10 @@ int pse_gemm_bf16(const void *a, int64_t lda, const void *w, int64_t ldw, const 
  * (q heads at column 0, k heads after them), position base_len[i] + w. */
 int pse_rope(void *qkv, int64_t ld, int32_t rows, int32_t width, int32_t q_heads, int32_t kv_heads,
              int32_t head_dim, const int32_t *base_len, float theta, int32_t dtype, void *stream);
+
+/* pse_rope with the position of every token given (positions[i*width + w]). */
+int pse_rope_pos(void *qkv, int64_t ld, int32_t rows, int32_t width, int32_t q_heads, int32_t kv_heads,
+                 int32_t head_dim, const int32_t *positions, float theta, int32_t dtype, void *stream);
 
 /* Scatter rows: dst[index[i] * ld_dst + :n] = src[i * ld_src + :n] (fp32),
  * for index[i] in [0, n_dst_rows). */

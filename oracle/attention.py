@@ -21,8 +21,24 @@ def gather_row(pool: np.ndarray, table, n_tokens: int) -> np.ndarray:
     return blocks.transpose(1, 0, 2, 3).reshape(pool.shape[1], nblk * bs, pool.shape[3])[:, :n_tokens]
 
 
-def paged_attention(q, k_pool, v_pool, tables, base_len, scale=None):
-    """q [R, W, Hq, hd] -> out [R, W, Hq, hd] (float64)."""
+def visible(base: int, width: int, ctx: int, tree=None) -> np.ndarray:
+    """[W, ctx] keys each query of a call sees.  Causal by default; ``tree=(b,
+    d0)``: the call's tokens are token-tree nodes in depth-major order from
+    depth d0 (query w is node n = d0*b + w at position L + n, L = base - d0*b),
+    each seeing the keys below L and its own branch (n % b) at depths <= n // b
+    (tree speculation: no reference counterpart)."""
+    keys = np.arange(ctx)[None, :]
+    if tree is None:
+        return keys <= (base + np.arange(width))[:, None]
+    b, d0 = tree
+    n = d0 * b + np.arange(width)[:, None]
+    L = base - d0 * b
+    m = keys - L
+    return (keys < L) | ((m >= 0) & (m % b == n % b) & (m // b <= n // b))
+
+
+def paged_attention(q, k_pool, v_pool, tables, base_len, scale=None, tree=None):
+    """q [R, W, Hq, hd] -> out [R, W, Hq, hd] (float64); ``tree`` as in ``visible``."""
     q = np.asarray(q, dtype=np.float64)
     rows, width, n_q, hd = q.shape
     n_kv = k_pool.shape[1]
@@ -36,8 +52,7 @@ def paged_attention(q, k_pool, v_pool, tables, base_len, scale=None):
         k = np.repeat(k, group, axis=0)  # [Hq, ctx, hd]
         v = np.repeat(v, group, axis=0)
         s = np.einsum("whd,htd->wht", q[i], k) * scale  # [W, Hq, ctx]
-        pos = int(base_len[i]) + np.arange(width)
-        allowed = np.arange(ctx)[None, :] <= pos[:, None]  # [W, ctx]
+        allowed = visible(int(base_len[i]), width, ctx, tree)  # [W, ctx]
         s = np.where(allowed[:, None, :], s, -np.inf)
         s = s - s.max(axis=-1, keepdims=True)
         p = np.exp(s)

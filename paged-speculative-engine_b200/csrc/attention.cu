@@ -42,6 +42,7 @@ struct AttnArgs {
   float scale;
   int split_tokens, n_splits, n_qtiles;
   float* ws;  // [n_splits][rows*width][q_heads][head_dim + 2]
+  int tree_b, tree_d0;  // token-tree call (key_vis in common.cuh); tree_b == 0: causal
 };
 
 template <typename T>
@@ -111,9 +112,9 @@ __global__ void __launch_bounds__(kThreads) paged_attn_kernel(AttnArgs a) {
   const int k_hi = min(k_lo + a.split_tokens, kmax);
   const int row_nblocks = a.nblocks[slot];
 
-  int qpos[RMAX];
+  KeyVis vis[RMAX];
 #pragma unroll
-  for (int r = 0; r < RMAX; ++r) qpos[r] = r < nr ? base + (r0 + r) / group : -1;
+  for (int r = 0; r < RMAX; ++r) vis[r] = r < nr ? key_vis(base, (r0 + r) / group, a.tree_b, a.tree_d0) : kNoKeys;
 
   float m[RMAX], l[RMAX], o[RMAX][MAXD];
 #pragma unroll
@@ -199,7 +200,7 @@ __global__ void __launch_bounds__(kThreads) paged_attn_kernel(AttnArgs a) {
     float p[RMAX], corr[RMAX];
 #pragma unroll
     for (int r = 0; r < RMAX; ++r) {
-      const bool ok = tok < k_hi && tok <= qpos[r];
+      const bool ok = tok < k_hi && key_visible(vis[r], tok, a.tree_b);
       const float sv = ok ? s[r] : -INFINITY;
       const float cmax = warp_max(sv);
       const float m_new = fmaxf(m[r], cmax);
@@ -411,7 +412,7 @@ bool tc_eligible(const pse_block_state& st, const pse_kv_layer& kv, int q_heads,
 int tc_attention(const pse_block_state& st, const pse_kv_layer& kv, const void* q, int64_t q_tok_stride, void* out,
                  int64_t out_tok_stride, const int32_t* slots, const int32_t* base_len, int rows, int width,
                  int q_heads, float scale, int split_tokens, int n_splits, void* ws, int* counter,
-                 const int32_t* row_order, bool self_reset, cudaStream_t s);
+                 const int32_t* row_order, bool self_reset, int tree_b, int tree_d0, cudaStream_t s);
 
 extern bool g_prefill_pair;
 bool prefill_eligible(const pse_block_state& st, const pse_kv_layer& kv, const void* q, int64_t q_tok_stride,
@@ -461,11 +462,12 @@ extern "C" size_t pse_paged_attention_workspace(int32_t rows, int32_t width, int
   return kWsHeader + (size_t)p.n_splits * rows * width * q_heads * (head_dim + 2) * sizeof(float);
 }
 
-extern "C" int pse_paged_attention(pse_block_state st, pse_kv_layer kv, const void* q, int64_t q_tok_stride, void* out,
-                                   int64_t out_tok_stride, const int32_t* slots, const int32_t* base_len, int32_t rows,
-                                   int32_t width, int32_t q_heads, float scale, int32_t max_ctx,
-                                   const int32_t* row_order, void* workspace, size_t workspace_bytes, void* stream) {
-  if (rows < 0 || width < 0) return PSE_EINVAL;
+namespace {
+int paged_attention(const pse_block_state& st, const pse_kv_layer& kv, const void* q, int64_t q_tok_stride, void* out,
+                    int64_t out_tok_stride, const int32_t* slots, const int32_t* base_len, int32_t rows, int32_t width,
+                    int32_t q_heads, float scale, int32_t max_ctx, const int32_t* row_order, void* workspace,
+                    size_t workspace_bytes, int tree_b, int tree_d0, void* stream) {
+  if (rows < 0 || width < 0 || tree_b < 0 || tree_d0 < 0) return PSE_EINVAL;
   if (rows == 0 || width == 0) return PSE_OK;
   if (!q || !out || !slots || !base_len || !kv.k_pool || !kv.v_pool || !st.block_table || !st.nblocks)
     return PSE_EINVAL;
@@ -500,14 +502,17 @@ extern "C" int pse_paged_attention(pse_block_state st, pse_kv_layer kv, const vo
   a.n_splits = p.n_splits;
   a.n_qtiles = p.n_qtiles;
   a.ws = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(workspace) + kWsHeader);
+  a.tree_b = tree_b;
+  a.tree_d0 = tree_d0;
   cudaStream_t s = (cudaStream_t)stream;
-  if (use_prefill(st, kv, q, q_tok_stride, out, out_tok_stride, q_heads, width))
+  // the prompt kernel is causal only: token-tree calls (narrow) never take it
+  if (tree_b == 0 && use_prefill(st, kv, q, q_tok_stride, out, out_tok_stride, q_heads, width))
     return prefill_attention(st, kv, q, q_tok_stride, out, out_tok_stride, slots, base_len, rows, width, q_heads,
                              scale, row_order, s);
   if (tc_eligible(st, kv, q_heads, width) && !g_force_generic) {
     int rc = tc_attention(st, kv, q, q_tok_stride, out, out_tok_stride, slots, base_len, rows, width, q_heads, scale,
                           p.split_tokens, p.n_splits, a.ws, reinterpret_cast<int*>(workspace), row_order,
-                          /*self_reset=*/true, s);
+                          /*self_reset=*/true, tree_b, tree_d0, s);
     if (rc) return rc;
     if (p.n_splits > 1) {
       const int64_t items = (int64_t)rows * width * q_heads;
@@ -520,6 +525,26 @@ extern "C" int pse_paged_attention(pse_block_state st, pse_kv_layer kv, const vo
   if (kv.dtype == PSE_BF16) return launch_d<__nv_bfloat16>(a, p, s);
   if (kv.dtype == PSE_F32) return launch_d<float>(a, p, s);
   return PSE_EINVAL;
+}
+}  // namespace
+
+extern "C" int pse_paged_attention(pse_block_state st, pse_kv_layer kv, const void* q, int64_t q_tok_stride, void* out,
+                                   int64_t out_tok_stride, const int32_t* slots, const int32_t* base_len, int32_t rows,
+                                   int32_t width, int32_t q_heads, float scale, int32_t max_ctx,
+                                   const int32_t* row_order, void* workspace, size_t workspace_bytes, void* stream) {
+  return paged_attention(st, kv, q, q_tok_stride, out, out_tok_stride, slots, base_len, rows, width, q_heads, scale,
+                         max_ctx, row_order, workspace, workspace_bytes, 0, 0, stream);
+}
+
+extern "C" int pse_paged_attention_tree(pse_block_state st, pse_kv_layer kv, const void* q, int64_t q_tok_stride,
+                                        void* out, int64_t out_tok_stride, const int32_t* slots,
+                                        const int32_t* base_len, int32_t rows, int32_t width, int32_t q_heads,
+                                        float scale, int32_t max_ctx, const int32_t* row_order, void* workspace,
+                                        size_t workspace_bytes, int32_t tree_branches, int32_t tree_depth0,
+                                        void* stream) {
+  if (tree_branches < 1) return PSE_EINVAL;
+  return paged_attention(st, kv, q, q_tok_stride, out, out_tok_stride, slots, base_len, rows, width, q_heads, scale,
+                         max_ctx, row_order, workspace, workspace_bytes, tree_branches, tree_depth0, stream);
 }
 
 // ---------------------------------------------------------------------------
@@ -613,10 +638,12 @@ extern "C" int pse_paged_attention_noalloc(pse_block_state st, pse_kv_layer kv, 
   // call; every (split, row, head) slot after it is written before the combine
   // reads it, so stale contents from an earlier call never leak in.
   a.ws = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(scratch) + kWsHeader);
+  a.tree_b = 0;
+  a.tree_d0 = 0;
   if (tc_eligible(st, kv, q_heads, width) && !g_force_generic) {
     rc = tc_attention(st, kv, q, q_tok_stride, out, out_tok_stride, slots, base_len, rows, width, q_heads, scale,
                       p.split_tokens, p.n_splits, a.ws, reinterpret_cast<int*>(scratch), nullptr,
-                      /*self_reset=*/false, s);
+                      /*self_reset=*/false, 0, 0, s);
     if (rc) return rc;
     if (p.n_splits > 1) {
       const int64_t items = (int64_t)rows * width * q_heads;

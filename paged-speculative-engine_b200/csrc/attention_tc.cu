@@ -83,6 +83,7 @@ struct Args {
   int* counter; // work counter (zeroed before the launch)
   const int32_t* row_order;  // rows in the order items are handed out (nullable: 0..rows-1)
   int self_reset;            // the last CTA zeroes counter[0..1] (counter[1] counts CTAs done)
+  int tree_b, tree_d0;       // token-tree call (key_vis in common.cuh); tree_b == 0: causal
 };
 
 __device__ __forceinline__ uint32_t su32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -196,7 +197,9 @@ __device__ __forceinline__ Item decode_item(const Args& a, int e) {
 
 constexpr int kFirst = 1, kLast = 2, kEmpty = 4, kEnd = 8;
 
-template <int HD, int MT>
+// TREE: a token-tree call (the key_vis rule); the causal instantiation
+// compiles without any of it.
+template <int HD, int MT, bool TREE>
 __global__ void __launch_bounds__(kThreads, HD == 64 ? PSE_TC_MINB64 : PSE_TC_MINB128) attn_tc_kernel(const __grid_constant__ CUtensorMap tmk,
                                                           const __grid_constant__ CUtensorMap tmv, Args a) {
   extern __shared__ uint8_t smem_raw[];
@@ -385,7 +388,8 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? PSE_TC_MINB64 : PSE_TC_MI
     }
     float o[HD / 8][4];
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
-    int qpos0 = -1, qpos1 = -1, qpos_min = -1;
+    KeyVis vis0 = kNoKeys, vis1 = kNoKeys;
+    int qpos_min = -1;
     Item it{};
     for (int t = 0;; ++t) {
       const int s = t % kStages;
@@ -418,12 +422,13 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? PSE_TC_MINB64 : PSE_TC_MI
         m0 = m1 = -INFINITY;
         l0 = l1 = 0.f;
         const int ra = mt * 16 + gid, rb = ra + 8;
-        qpos0 = ra < it.nr ? it.base + (it.r0 + ra) / group : -1;
-        qpos1 = rb < it.nr ? it.base + (it.r0 + rb) / group : -1;
-        // smallest causal limit over this m-tile's valid rows: tokens at or
+        const int tb = TREE ? a.tree_b : 0;
+        vis0 = ra < it.nr ? key_vis(it.base, (it.r0 + ra) / group, tb, a.tree_d0) : kNoKeys;
+        vis1 = rb < it.nr ? key_vis(it.base, (it.r0 + rb) / group, tb, a.tree_d0) : kNoKeys;
+        // smallest visibility limit over this m-tile's valid rows: tokens at or
         // below it are visible to every row of the tile
         const int nr_mt = min(16, it.nr - mt * 16);
-        qpos_min = nr_mt > 0 ? it.base + (it.r0 + mt * 16) / group : -1;
+        qpos_min = nr_mt > 0 ? key_vis(it.base, (it.r0 + mt * 16) / group, tb, a.tree_d0).lim : -1;
       }
       if (!(flags & kEmpty)) {
         const int tt = desc_tile[s];
@@ -459,8 +464,9 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? PSE_TC_MINB64 : PSE_TC_MI
               for (int c = 0; c < 2; ++c) {
                 const int tok = tok_abs + n * 8 + 2 * tid4 + c;
                 const bool live = tok < it.k_hi;
-                sc[n][c] = (live && tok <= qpos0) ? sc[n][c] * a.scale_log2 : -INFINITY;
-                sc[n][2 + c] = (live && tok <= qpos1) ? sc[n][2 + c] * a.scale_log2 : -INFINITY;
+                const int tb = TREE ? a.tree_b : 0;
+                sc[n][c] = (live && key_visible(vis0, tok, tb)) ? sc[n][c] * a.scale_log2 : -INFINITY;
+                sc[n][2 + c] = (live && key_visible(vis1, tok, tb)) ? sc[n][2 + c] * a.scale_log2 : -INFINITY;
                 mx0 = fmaxf(mx0, sc[n][c]);
                 mx1 = fmaxf(mx1, sc[n][2 + c]);
               }
@@ -610,9 +616,9 @@ constexpr size_t smem_bytes(int mt) {
 
 // Persistent launch: as many CTAs as fit on the GPU at once (never more than
 // work items); each pulls items from the work counter until it runs dry.
-template <int HD, int MT>
+template <int HD, int MT, bool TREE>
 int launch(const CUtensorMap& mk, const CUtensorMap& mv, const Args& a, cudaStream_t s) {
-  auto kern = attn_tc_kernel<HD, MT>;
+  auto kern = attn_tc_kernel<HD, MT, TREE>;
   constexpr size_t smem = smem_bytes<HD>(MT);
   static_assert(smem <= 227 * 1024, "shared memory budget");
   static const cudaError_t opt = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -668,7 +674,7 @@ bool tc_eligible(const pse_block_state& st, const pse_kv_layer& kv, int q_heads,
 int tc_attention(const pse_block_state& st, const pse_kv_layer& kv, const void* q, int64_t q_tok_stride, void* out,
                  int64_t out_tok_stride, const int32_t* slots, const int32_t* base_len, int rows, int width,
                  int q_heads, float scale, int split_tokens, int n_splits, void* ws, int* counter,
-                 const int32_t* row_order, bool self_reset, cudaStream_t s) {
+                 const int32_t* row_order, bool self_reset, int tree_b, int tree_d0, cudaStream_t s) {
   const int n_qrows = (q_heads / kv.kv_heads) * width;
   const int MT = n_qrows <= 16 ? 1 : 2;
   tc::Args a;
@@ -700,14 +706,21 @@ int tc_attention(const pse_block_state& st, const pse_kv_layer& kv, const void* 
   a.counter = counter;
   a.self_reset = self_reset ? 1 : 0;
   a.row_order = row_order;
+  a.tree_b = tree_b;
+  a.tree_d0 = tree_d0;
   if (!counter) return PSE_EINVAL;
   CUtensorMap mk, mv;
   int rc = tc::tensor_map(kv.k_pool, st.num_blocks, kv.kv_heads, st.block_size, kv.head_dim, &mk);
   if (rc) return rc;
   rc = tc::tensor_map(kv.v_pool, st.num_blocks, kv.kv_heads, st.block_size, kv.head_dim, &mv);
   if (rc) return rc;
-  if (kv.head_dim == 64) return MT == 1 ? tc::launch<64, 1>(mk, mv, a, s) : tc::launch<64, 2>(mk, mv, a, s);
-  return MT == 1 ? tc::launch<128, 1>(mk, mv, a, s) : tc::launch<128, 2>(mk, mv, a, s);
+  if (tree_b > 0) {
+    if (kv.head_dim == 64)
+      return MT == 1 ? tc::launch<64, 1, true>(mk, mv, a, s) : tc::launch<64, 2, true>(mk, mv, a, s);
+    return MT == 1 ? tc::launch<128, 1, true>(mk, mv, a, s) : tc::launch<128, 2, true>(mk, mv, a, s);
+  }
+  if (kv.head_dim == 64) return MT == 1 ? tc::launch<64, 1, false>(mk, mv, a, s) : tc::launch<64, 2, false>(mk, mv, a, s);
+  return MT == 1 ? tc::launch<128, 1, false>(mk, mv, a, s) : tc::launch<128, 2, false>(mk, mv, a, s);
 }
 
 }  // namespace pse

@@ -145,4 +145,31 @@ __device__ __forceinline__ int blocks_for(int n_tokens, int block_size) {
   return n_tokens == 0 ? 0 : (n_tokens - 1) / block_size + 1;
 }
 
+// ---------------------------------------------------------------- which keys a query sees
+// Query w of a row whose call starts at cache position `base`.  tree_b == 0:
+// causal, keys <= base + w.  tree_b = b > 0 (a token-tree call): the call's
+// tokens are tree nodes in depth-major order from depth tree_d0 -- node
+// n = tree_d0 * b + w sits at position L + n (L = base - tree_d0 * b, the
+// row's length at the tree's root), is branch n % b at depth n / b, and sees
+// the keys below L plus its own branch's nodes at depths up to its own.
+struct KeyVis {
+  int lim;  // every key <= lim is visible (-1: none)
+  int L, br, dep;
+};
+
+__device__ __forceinline__ KeyVis key_vis(int base, int w, int tree_b, int tree_d0) {
+  if (tree_b <= 0) return KeyVis{base + w, 0, 0, -1};
+  const int n = tree_d0 * tree_b + w, L = base - tree_d0 * tree_b;
+  return KeyVis{L - 1, L, n % tree_b, n / tree_b};
+}
+
+__device__ __forceinline__ bool key_visible(const KeyVis& v, int tok, int tree_b) {
+  if (tok <= v.lim) return true;
+  if (tree_b <= 0 || tok < v.L) return false;
+  const int m = tok - v.L;
+  return m % tree_b == v.br && m / tree_b <= v.dep;
+}
+
+constexpr KeyVis kNoKeys{-1, 0, 0, -1};
+
 }  // namespace pse

@@ -413,6 +413,67 @@ extern "C" int pse_kv_append(pse_block_state st, pse_kv_layer kv, const void* k_
   return PSE_EINVAL;
 }
 
+// Token-tree commit: row i keeps n[i] of the tokens its tree calls appended,
+// the token at position base_len[i] + src[i*max_n + m] moving to position
+// base_len[i] + m (m < n[i]; src increasing with src[m] >= m, so no source is
+// overwritten before it is read: each thread walks m in order over its own
+// (head, element) slice).
+template <typename T>
+__global__ void compact_kernel(pse_block_state st, T* __restrict__ k_pool, T* __restrict__ v_pool, int kv_heads,
+                               int head_dim, const int32_t* slots, const int32_t* base_len, const int32_t* src,
+                               const int32_t* n, int max_n) {
+  const int i = blockIdx.x;
+  const int slot = slots[i];
+  if (slot < 0 || slot >= st.num_slots) {
+    if (threadIdx.x == 0) atomicOr(st.status, PSE_STATUS_BAD_BLOCK);
+    return;
+  }
+  const int L = base_len[i], cnt = min(n[i], max_n), len = st.seq_len[slot], nb = st.nblocks[slot];
+  const int bs = st.block_size;
+  const int32_t* row = st.block_table + (int64_t)slot * st.max_blocks;
+  bool bad = false;
+  for (int e = threadIdx.x; e < kv_heads * head_dim; e += blockDim.x) {
+    const int h = e / head_dim, d = e % head_dim;
+    for (int m = 0; m < cnt; ++m) {
+      const int from = L + src[(int64_t)i * max_n + m], to = L + m;
+      if (from == to) continue;
+      if (to < 0 || from < to || from >= len || from / bs >= nb) {
+        bad = true;
+        break;
+      }
+      const int bf = row[from / bs], bt = row[to / bs];
+      if (bf < 0 || bf >= st.num_blocks || bt < 0 || bt >= st.num_blocks) {
+        bad = true;
+        break;
+      }
+      const int64_t of = (((int64_t)bf * kv_heads + h) * bs + from % bs) * head_dim + d;
+      const int64_t ot = (((int64_t)bt * kv_heads + h) * bs + to % bs) * head_dim + d;
+      k_pool[ot] = k_pool[of];
+      v_pool[ot] = v_pool[of];
+    }
+  }
+  if (bad) atomicOr(st.status, PSE_STATUS_BAD_BLOCK);
+}
+
+extern "C" int pse_kv_compact(pse_block_state st, pse_kv_layer kv, const int32_t* slots, const int32_t* base_len,
+                              const int32_t* src, const int32_t* n, int32_t rows, int32_t max_n, void* stream) {
+  if (!state_ok(st) || !kv.k_pool || !kv.v_pool || kv.kv_heads <= 0 || kv.head_dim <= 0 || rows < 0 || max_n < 0)
+    return PSE_EINVAL;
+  if (rows == 0 || max_n == 0) return PSE_OK;
+  if (!slots || !base_len || !src || !n) return PSE_EINVAL;
+  cudaStream_t s = (cudaStream_t)stream;
+  if (kv.dtype == PSE_BF16)
+    compact_kernel<__nv_bfloat16><<<rows, 256, 0, s>>>(st, (__nv_bfloat16*)kv.k_pool, (__nv_bfloat16*)kv.v_pool,
+                                                        kv.kv_heads, kv.head_dim, slots, base_len, src, n, max_n);
+  else if (kv.dtype == PSE_F32)
+    compact_kernel<float><<<rows, 256, 0, s>>>(st, (float*)kv.k_pool, (float*)kv.v_pool, kv.kv_heads, kv.head_dim,
+                                               slots, base_len, src, n, max_n);
+  else
+    return PSE_EINVAL;
+  PSE_LAUNCH_CHECK();
+  return PSE_OK;
+}
+
 extern "C" int pse_kv_gather(pse_block_state st, pse_kv_layer kv, const int32_t* slots, int32_t rows, int32_t max_len,
                              void* k_out, void* v_out, void* stream) {
   if (!state_ok(st) || rows < 0 || max_len < 0) return PSE_EINVAL;

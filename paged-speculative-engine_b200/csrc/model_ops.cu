@@ -10,14 +10,15 @@ namespace {
 // x[t] = tok_emb[ids[t]] + pos_emb[base_len[t / width] + t % width]
 // Ids outside [0, vocab) and positions outside [0, n_pos) read nothing (the
 // host rejects them before launch; the device only stays in bounds).
-__global__ void embed_kernel(const int32_t* ids, const int32_t* base_len, int width, const void* tok_emb,
-                             const void* pos_emb, int d, int dtype, float* x, int vocab, int n_pos) {
+__global__ void embed_kernel(const int32_t* ids, const int32_t* base_len, const int32_t* positions, int width,
+                             const void* tok_emb, const void* pos_emb, int d, int dtype, float* x, int vocab,
+                             int n_pos) {
   pdl_wait();
   pdl_trigger();
   const int t = blockIdx.x;
   const int i = t / width, w = t % width;
   const int64_t tok = ids[t];
-  const int64_t pos = base_len ? (int64_t)base_len[i] + w : 0;
+  const int64_t pos = positions ? (int64_t)positions[t] : base_len ? (int64_t)base_len[i] + w : 0;
   const bool tok_ok = tok >= 0 && tok < vocab;
   const bool pos_ok = pos_emb != nullptr && pos >= 0 && pos < n_pos;
   for (int c = threadIdx.x; c < d; c += blockDim.x) {
@@ -317,14 +318,14 @@ __global__ void epilogue_bf16x8_kernel(int op, __nv_bfloat16* y, int64_t ldy, co
 // Rotate-half RoPE on the q heads and k heads of a fused qkv row.
 template <typename I>
 __global__ void rope_kernel(void* qkv, int64_t ld, int width, int q_heads, int kv_heads, int hd,
-                            const int32_t* base_len, float theta, int dtype, I total) {
+                            const int32_t* base_len, const int32_t* positions, float theta, int dtype, I total) {
   const int half = hd / 2;
   for (I e = blockIdx.x * (I)blockDim.x + threadIdx.x; e < total; e += (I)gridDim.x * blockDim.x) {
     const int p = (int)(e % half);
     I r = e / half;
     const int h = (int)(r % (q_heads + kv_heads));
     const int64_t t = r / (q_heads + kv_heads);
-    const int64_t pos = (int64_t)base_len[t / width] + t % width;
+    const int64_t pos = positions ? (int64_t)positions[t] : (int64_t)base_len[t / width] + t % width;
     const double inv_freq = pow((double)theta, -2.0 * p / hd);
     double sn, cs;
     sincos((double)pos * inv_freq, &sn, &cs);
@@ -370,7 +371,20 @@ extern "C" int pse_embed(const int32_t* ids, const int32_t* base_len, int32_t ro
   if (rows == 0 || width == 0) return PSE_OK;
   if (!ids || !tok_emb || !x || (pos_emb && !base_len)) return PSE_EINVAL;
   cudaError_t e = launch_pdl(embed_kernel, dim3((unsigned)(rows * width)), dim3(128), 0, (cudaStream_t)stream, ids,
-                             base_len, width, tok_emb, pos_emb, d, emb_dtype, x, vocab, n_pos);
+                             base_len, (const int32_t*)nullptr, width, tok_emb, pos_emb, d, emb_dtype, x, vocab, n_pos);
+  if (e != cudaSuccess) return (int)e;
+  return PSE_OK;
+}
+
+extern "C" int pse_embed_pos(const int32_t* ids, const int32_t* positions, int32_t rows, int32_t width,
+                             const void* tok_emb, const void* pos_emb, int32_t d, int32_t emb_dtype, int32_t vocab,
+                             int32_t n_pos, float* x, void* stream) {
+  if (rows < 0 || width < 0 || d <= 0 || vocab <= 0) return PSE_EINVAL;
+  if (rows == 0 || width == 0) return PSE_OK;
+  if (!ids || !tok_emb || !x || (pos_emb && !positions)) return PSE_EINVAL;
+  cudaError_t e = launch_pdl(embed_kernel, dim3((unsigned)(rows * width)), dim3(128), 0, (cudaStream_t)stream, ids,
+                             (const int32_t*)nullptr, positions, width, tok_emb, pos_emb, d, emb_dtype, x, vocab,
+                             n_pos);
   if (e != cudaSuccess) return (int)e;
   return PSE_OK;
 }
@@ -455,22 +469,36 @@ extern "C" int pse_epilogue(int32_t op, void* y, int64_t ldy, const void* bias, 
   return PSE_OK;
 }
 
-extern "C" int pse_rope(void* qkv, int64_t ld, int32_t rows, int32_t width, int32_t q_heads, int32_t kv_heads,
-                        int32_t head_dim, const int32_t* base_len, float theta, int32_t dtype, void* stream) {
+namespace {
+int rope(void* qkv, int64_t ld, int32_t rows, int32_t width, int32_t q_heads, int32_t kv_heads, int32_t head_dim,
+         const int32_t* base_len, const int32_t* positions, float theta, int32_t dtype, void* stream) {
   if (rows < 0 || width < 0 || head_dim <= 0 || head_dim % 2) return PSE_EINVAL;
   if (rows == 0 || width == 0) return PSE_OK;
-  if (!qkv || !base_len) return PSE_EINVAL;
+  if (!qkv || (!base_len && !positions)) return PSE_EINVAL;
   const int64_t total = (int64_t)rows * width * (q_heads + kv_heads) * (head_dim / 2);
   if (total < kIdx32)
     rope_kernel<int><<<grid_for(total, 256), 256, 0, (cudaStream_t)stream>>>(qkv, ld, width, q_heads, kv_heads,
-                                                                           head_dim, base_len, theta, dtype,
-                                                                           (int)total);
+                                                                           head_dim, base_len, positions, theta,
+                                                                           dtype, (int)total);
   else
     rope_kernel<int64_t><<<grid_for(total, 256), 256, 0, (cudaStream_t)stream>>>(qkv, ld, width, q_heads, kv_heads,
-                                                                               head_dim, base_len, theta, dtype,
-                                                                               total);
+                                                                               head_dim, base_len, positions, theta,
+                                                                               dtype, total);
   PSE_LAUNCH_CHECK();
   return PSE_OK;
+}
+}  // namespace
+
+extern "C" int pse_rope(void* qkv, int64_t ld, int32_t rows, int32_t width, int32_t q_heads, int32_t kv_heads,
+                        int32_t head_dim, const int32_t* base_len, float theta, int32_t dtype, void* stream) {
+  if (!base_len) return PSE_EINVAL;
+  return rope(qkv, ld, rows, width, q_heads, kv_heads, head_dim, base_len, nullptr, theta, dtype, stream);
+}
+
+extern "C" int pse_rope_pos(void* qkv, int64_t ld, int32_t rows, int32_t width, int32_t q_heads, int32_t kv_heads,
+                            int32_t head_dim, const int32_t* positions, float theta, int32_t dtype, void* stream) {
+  if (!positions) return PSE_EINVAL;
+  return rope(qkv, ld, rows, width, q_heads, kv_heads, head_dim, nullptr, positions, theta, dtype, stream);
 }
 
 extern "C" int pse_scatter_rows(const float* src, int64_t ld_src, const int32_t* index, int32_t rows, int32_t n,

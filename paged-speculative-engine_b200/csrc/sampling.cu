@@ -1686,10 +1686,10 @@ struct TreeArgs {
   const float* q_root;
   int64_t qr_stride;
   const int32_t* qr_index;
-  const float* verify;  // node (i, j, d): verify + (i*b + j) * v_row + d * v_pos
-  int64_t v_row, v_pos;
-  const float* dchain;  // draft after node (i, j, d), d < k-1: dchain + d * dc_depth + (i*b + j) * dc_row
-  int64_t dc_depth, dc_row;
+  const float* verify;  // target after node (i, j, d): verify + i * v_req + j * v_branch + d * v_depth
+  int64_t v_req, v_branch, v_depth;
+  const float* dchain;  // draft after node (i, j, d), d < k-1: dchain + i * dc_req + j * dc_branch + d * dc_depth
+  int64_t dc_req, dc_branch, dc_depth;
   const int32_t* chain;  // [rows][b][k]
   const double* u;
   int64_t u_stride;
@@ -1735,10 +1735,10 @@ struct TreeResidual {
 };
 
 __device__ __forceinline__ const float* tree_node_target(const TreeArgs& a, int i, int j, int d) {
-  return a.verify + ((int64_t)i * a.b + j) * a.v_row + (int64_t)d * a.v_pos;
+  return a.verify + (int64_t)i * a.v_req + (int64_t)j * a.v_branch + (int64_t)d * a.v_depth;
 }
 __device__ __forceinline__ const float* tree_node_draft(const TreeArgs& a, int i, int j, int d) {
-  return a.dchain + (int64_t)d * a.dc_depth + ((int64_t)i * a.b + j) * a.dc_row;
+  return a.dchain + (int64_t)i * a.dc_req + (int64_t)j * a.dc_branch + (int64_t)d * a.dc_depth;
 }
 
 __global__ void __launch_bounds__(kSampleThreads) tree_accept_kernel(TreeArgs a) {
@@ -2013,17 +2013,19 @@ extern "C" int pse_spec_accept(const float* target0, int64_t t0_stride, const in
 }
 
 extern "C" int pse_tree_accept(const float* p_root, int64_t pr_stride, const int32_t* pr_index, const float* q_root,
-                               int64_t qr_stride, const int32_t* qr_index, const float* verify, int64_t v_row,
-                               int64_t v_pos, const float* dchain, int64_t dc_depth, int64_t dc_row,
-                               const int32_t* chain, const double* u, int64_t u_stride, int32_t rows, int32_t branches,
-                               int32_t k, int32_t vocab, float temperature, int32_t* tokens, int32_t* n_accepted,
-                               int32_t* branch, int32_t* final_token, void* stream) {
+                               int64_t qr_stride, const int32_t* qr_index, const float* verify, int64_t v_req,
+                               int64_t v_branch, int64_t v_depth, const float* dchain, int64_t dc_req,
+                               int64_t dc_branch, int64_t dc_depth, const int32_t* chain, const double* u,
+                               int64_t u_stride, int32_t rows, int32_t branches, int32_t k, int32_t vocab,
+                               float temperature, int32_t* tokens, int32_t* n_accepted, int32_t* branch,
+                               int32_t* final_token, void* stream) {
   if (rows < 0 || k < 1 || vocab <= 0 || branches < 1 || branches > kTreeMaxB || branches > vocab) return PSE_EINVAL;
   if (rows == 0) return PSE_OK;
   if (!p_root || !verify || !chain || !tokens || !n_accepted || !branch || !final_token) return PSE_EINVAL;
   if (temperature > 0.f && (!u || !q_root || (k > 1 && !dchain))) return PSE_EINVAL;
-  TreeArgs a{p_root, pr_stride, pr_index, q_root, qr_stride, qr_index, verify, v_row, v_pos, dchain, dc_depth, dc_row,
-             chain, u, u_stride, branches, k, vocab, temperature, tokens, n_accepted, branch, final_token};
+  TreeArgs a{p_root,  pr_stride, pr_index, q_root,   qr_stride, qr_index, verify, v_req,  v_branch,
+             v_depth, dchain,    dc_req,   dc_branch, dc_depth,  chain,    u,      u_stride, branches,
+             k,       vocab,     temperature, tokens, n_accepted, branch, final_token};
   tree_accept_kernel<<<rows, kSampleThreads, 0, (cudaStream_t)stream>>>(a);
   PSE_LAUNCH_CHECK();
   return PSE_OK;

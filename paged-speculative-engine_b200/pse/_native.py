@@ -64,8 +64,13 @@ _PROTOS = {
     "pse_sample_tokens": ([c_p, c_i64, c_p, c_i32, c_i32, c_f32, c_p, c_i64, c_i32, c_p, c_i64, c_p, c_i64, c_p], 1),
     "pse_spec_accept": ([c_p, c_i64, c_p, c_p, c_i64, c_i64, c_p, c_i64, c_p, c_p, c_i64, c_i64, c_p, c_p, c_i64,
                          c_i32, c_i32, c_i32, c_f32, c_p, c_p, c_p, c_p], 1),
-    "pse_tree_accept": ([c_p, c_i64, c_p, c_p, c_i64, c_p, c_p, c_i64, c_i64, c_p, c_i64, c_i64, c_p, c_p, c_i64,
-                         c_i32, c_i32, c_i32, c_i32, c_f32, c_p, c_p, c_p, c_p, c_p], 1),
+    "pse_tree_accept": ([c_p, c_i64, c_p, c_p, c_i64, c_p, c_p, c_i64, c_i64, c_i64, c_p, c_i64, c_i64, c_i64, c_p,
+                         c_p, c_i64, c_i32, c_i32, c_i32, c_i32, c_f32, c_p, c_p, c_p, c_p, c_p], 1),
+    "pse_paged_attention_tree": ([BlockState, KVLayer, c_p, c_i64, c_p, c_i64, c_p, c_p, c_i32, c_i32, c_i32,
+                                  c_f32, c_i32, c_p, c_p, c_sz, c_i32, c_i32, c_p], 1),
+    "pse_embed_pos": ([c_p, c_p, c_i32, c_i32, c_p, c_p, c_i32, c_i32, c_i32, c_i32, c_p, c_p], 1),
+    "pse_rope_pos": ([c_p, c_i64, c_i32, c_i32, c_i32, c_i32, c_i32, c_p, c_f32, c_i32, c_p], 1),
+    "pse_kv_compact": ([BlockState, KVLayer, c_p, c_p, c_p, c_p, c_i32, c_i32, c_p], 1),
     "pse_embed": ([c_p, c_p, c_i32, c_i32, c_p, c_p, c_i32, c_i32, c_i32, c_i32, c_p, c_p], 1),
     "pse_norm": ([c_p, c_i64, c_p, c_p, c_i32, c_i32, c_i32, c_f32, c_i32, c_p, c_i64, c_i32, c_p], 1),
     "pse_add_norm": ([c_p, c_i64, c_p, c_i64, c_p, c_i32, c_p, c_p, c_i32, c_i32, c_i32, c_f32, c_i32, c_p, c_i64,

@@ -124,14 +124,19 @@ def lm_head(dm: DeviceModel, h: torch.Tensor, out: torch.Tensor) -> None:
 
 def forward(dm: DeviceModel, cache, slots: torch.Tensor, ids: torch.Tensor, rows: int, width: int,
             base_len: torch.Tensor, max_ctx: int, logits_out: torch.Tensor | None, last_only: bool = False,
-            scratch: Scratch | None = None, row_order: torch.Tensor | None = None, reserve: bool = True) -> None:
+            scratch: Scratch | None = None, row_order: torch.Tensor | None = None, reserve: bool = True,
+            tree: tuple | None = None) -> None:
     """One paged forward.  ``slots`` int32 [rows]; ``ids`` int32 [rows*width];
     ``base_len`` int32 [rows] receives the rows' lengths before the call;
     ``max_ctx`` >= every row's length after it.  ``logits_out`` fp32
     [rows*width, V] (or [rows, V] with ``last_only``) or None.  With
     ``reserve=False`` nothing is allocated: ``base_len`` gives each row's first
     position, and K/V of positions in blocks the row does not hold are dropped.
-    The final normed hidden rows stay in the scratch's ``h``."""
+    ``tree=(b, d0)``: the call's tokens are token-tree nodes of b branches in
+    depth-major order from depth d0 (``pse_paged_attention_tree``): node
+    positions are the row's root length plus the node's depth, and each node
+    attends to the root context and its own branch.  The final normed hidden
+    rows stay in the scratch's ``h``."""
     T = rows * width
     sc = scratch or scratch_for(dm)
     sc.ensure(T)
@@ -144,9 +149,18 @@ def forward(dm: DeviceModel, cache, slots: torch.Tensor, ids: torch.Tensor, rows
         N.call("pse_kv_reserve", state, slots.data_ptr(), rows, width, base_len.data_ptr(), st)
     x, h, qkv, attn, tmp, up, act = (sc.x[:T], sc.h[:T], sc.qkv[:T], sc.attn[:T], sc.tmp[:T], sc.up[:T],
                                       sc.act[:T])
-    N.call("pse_embed", ids.data_ptr(), base_len.data_ptr(), rows, width, dm.tok_emb.data_ptr(),
-           None if dm.pos_emb is None else dm.pos_emb.data_ptr(), d, dt, dm.vocab,
-           0 if dm.pos_emb is None else dm.pos_emb.shape[0], x.data_ptr(), st)
+    pos = None
+    if tree is not None:
+        tb, td0 = tree
+        off = (td0 * tb + torch.arange(width, device=base_len.device)) // tb - td0 * tb
+        pos = (base_len.view(-1, 1).long() + off.view(1, -1)).to(torch.int32).reshape(-1)
+        N.call("pse_embed_pos", ids.data_ptr(), pos.data_ptr(), rows, width, dm.tok_emb.data_ptr(),
+               None if dm.pos_emb is None else dm.pos_emb.data_ptr(), d, dt, dm.vocab,
+               0 if dm.pos_emb is None else dm.pos_emb.shape[0], x.data_ptr(), st)
+    else:
+        N.call("pse_embed", ids.data_ptr(), base_len.data_ptr(), rows, width, dm.tok_emb.data_ptr(),
+               None if dm.pos_emb is None else dm.pos_emb.data_ptr(), d, dt, dm.vocab,
+               0 if dm.pos_emb is None else dm.pos_emb.shape[0], x.data_ptr(), st)
     ws_bytes = N.size_call("pse_paged_attention_workspace", rows, width, dm.q_heads, dm.kv_heads, hd, max_ctx)
     sc.ensure_ws(ws_bytes)
     scale = 1.0 / math.sqrt(hd)
@@ -157,16 +171,24 @@ def forward(dm: DeviceModel, cache, slots: torch.Tensor, ids: torch.Tensor, rows
     n_layers = len(dm.layers)
     for li, L in enumerate(dm.layers):
         _mm(h, L.qkv_w, qkv, L.qkv_b)
-        if dm.kind == "llama":
+        if dm.kind == "llama" and pos is not None:
+            N.call("pse_rope_pos", qkv.data_ptr(), qkv.stride(0), rows, width, dm.q_heads, dm.kv_heads, hd,
+                   pos.data_ptr(), dm.rope_theta, dt, st)
+        elif dm.kind == "llama":
             N.call("pse_rope", qkv.data_ptr(), qkv.stride(0), rows, width, dm.q_heads, dm.kv_heads, hd,
                    base_len.data_ptr(), dm.rope_theta, dt, st)
         kvl = cache.layer(li)
         N.call("pse_kv_append", state, kvl, qkv.data_ptr() + nq * qkv.element_size(),
                qkv.data_ptr() + (nq + nk) * qkv.element_size(), qkv.stride(0), hd, slots.data_ptr(),
                base_len.data_ptr(), rows, width, st)
-        N.call("pse_paged_attention", state, kvl, qkv.data_ptr(), qkv.stride(0), attn.data_ptr(), attn.stride(0),
-               slots.data_ptr(), base_len.data_ptr(), rows, width, dm.q_heads, scale, max_ctx,
-               N.ptr(row_order), sc.ws.data_ptr(), sc.ws.numel(), st)
+        if tree is not None:
+            N.call("pse_paged_attention_tree", state, kvl, qkv.data_ptr(), qkv.stride(0), attn.data_ptr(),
+                   attn.stride(0), slots.data_ptr(), base_len.data_ptr(), rows, width, dm.q_heads, scale, max_ctx,
+                   N.ptr(row_order), sc.ws.data_ptr(), sc.ws.numel(), tree[0], tree[1], st)
+        else:
+            N.call("pse_paged_attention", state, kvl, qkv.data_ptr(), qkv.stride(0), attn.data_ptr(),
+                   attn.stride(0), slots.data_ptr(), base_len.data_ptr(), rows, width, dm.q_heads, scale, max_ctx,
+                   N.ptr(row_order), sc.ws.data_ptr(), sc.ws.numel(), st)
         _mm(attn, L.out_w, tmp, L.out_b)
         # x += attn-out (bias already added by the GEMM); h = norm2(x)
         N.call("pse_add_norm", x.data_ptr(), d, tmp.data_ptr(), d, None, dt, L.norm2_w.data_ptr(),

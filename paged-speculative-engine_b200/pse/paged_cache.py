@@ -411,110 +411,6 @@ class PagedKVCache:
         N.call("pse_kv_release", self.state, t.data_ptr(), len(slots), N.stream_ptr())
         self._free_slots.extend(slots)
 
-    # ------------------------------------------------------------------ token-tree forks
-    def fork_rows(self, request_ids, branches: int):
-        """Temporary rows for a token-tree step (``pse.tree``): per request,
-        ``branches - 1`` forks whose block tables start with the request's
-        full blocks (shared, never written: every tree node lies past them) and
-        hold a copy of its last partial block.  Returns the slot array [B,
-        branches] (column 0: the requests' own rows) and the fork ids, request
-        by request."""
-        ids = list(request_ids)
-        B, b = len(ids), int(branches)
-        own = self.slots_np(ids)
-        if b == 1:
-            return own.reshape(B, 1), []
-        if self.prefix is not None:
-            raise ValueError("token-tree steps do not combine with prefix caching")
-        need = B * (b - 1)
-        if len(self._free_slots) < need:
-            self._grow(max(self._blocks.num_slots * 2, self._blocks.num_slots + need), self._blocks.max_blocks)
-        fork_ids = [f"{r}\x00fork{j}" for r in ids for j in range(1, b)]
-        for f in fork_ids:
-            self.create_request(f)
-        forks = self.slots_np(fork_ids)
-        bs = self.block_size
-        L = self._len_np[own]
-        full = L // bs
-        dev = self.device
-        blocks = self._blocks
-        src = torch.from_numpy(np.repeat(own, b - 1).astype(np.int64)).to(dev)
-        dst = torch.from_numpy(forks.astype(np.int64)).to(dev)
-        full_r = torch.from_numpy(np.repeat(full, b - 1).astype(np.int32)).to(dev)
-        width = int(full.max()) if B else 0
-        if width:
-            cols = torch.arange(width, device=dev)
-            head = blocks.block_table[src.view(-1, 1), cols.view(1, -1)]
-            head = torch.where(cols.view(1, -1) < full_r.view(-1, 1), head, torch.full_like(head, -1))
-            blocks.block_table[dst.view(-1, 1), cols.view(1, -1)] = head
-        blocks.nblocks[dst] = full_r
-        blocks.seq_len[dst] = full_r * bs
-        # the partial last block: one block of the fork's own, holding a copy
-        part = np.repeat(L - full * bs, b - 1).astype(np.int32)
-        base = torch.empty(need, dtype=torch.int32, device=dev)
-        dst32 = dst.to(torch.int32)  # kept referenced until the launch is queued
-        part_d = torch.from_numpy(part).to(dev)
-        N.call("pse_kv_reserve_rows", self.state, dst32.data_ptr(), need, part_d.data_ptr(), base.data_ptr(),
-               N.stream_ptr())
-        self.check_status("fork")
-        sel = np.nonzero(part > 0)[0]
-        if len(sel):
-            s_src = src[torch.from_numpy(sel).to(dev)]
-            s_dst = dst[torch.from_numpy(sel).to(dev)]
-            col = full_r[torch.from_numpy(sel).to(dev)].long()
-            old = blocks.block_table[s_src, col].long()
-            new = blocks.block_table[s_dst, col].long()
-            for pool in (self.k_pool, self.v_pool):
-                pool[:, new] = pool[:, old]
-        self._len_np[forks] = np.repeat(L, b - 1)
-        self._fork_shared = dict(zip(forks.tolist(), np.repeat(full, b - 1).tolist()))
-        slots = np.concatenate([own.reshape(B, 1), forks.reshape(B, b - 1)], axis=1)
-        return slots, fork_ids
-
-    def resolve_forks(self, request_ids, fork_ids, branch) -> None:
-        """End a token-tree step: request i keeps branch ``branch[i]``.  A fork
-        that won becomes the request's row (its slot takes the request's id);
-        the request's old row and the losing forks are released, their shared
-        head first moved out of their tables so only their own blocks return
-        to the free list."""
-        ids = list(request_ids)
-        if not fork_ids:
-            return
-        b = len(fork_ids) // len(ids) + 1
-        shared = self._fork_shared
-        out, shift = [], []
-        for i, r in enumerate(ids):
-            own = self._slot[r]
-            w = int(branch[i])
-            for j in range(1, b):
-                f = fork_ids[i * (b - 1) + j - 1]
-                s = self._slot.pop(f)
-                n = shared.pop(s)
-                if j == w:
-                    self._slot[r] = s
-                    out.append(own)
-                    self._serial[s] += 1
-                else:
-                    out.append(s)
-                shift.append(n)
-        self.slot_version += 1
-        dev = self.device
-        blocks = self._blocks
-        t = torch.from_numpy(np.asarray(out, dtype=np.int64)).to(dev)
-        n = torch.from_numpy(np.asarray(shift, dtype=np.int64)).to(dev)
-        mb = blocks.max_blocks
-        idx = torch.arange(mb, device=dev).view(1, -1) + n.view(-1, 1)
-        rows = blocks.block_table[t]
-        moved = torch.gather(rows, 1, idx.clamp(max=mb - 1))
-        blocks.block_table[t] = torch.where(idx < mb, moved, torch.full_like(moved, -1))
-        blocks.nblocks[t] -= n.to(torch.int32)
-        self._len_np[out] = 0
-        self._serial[out] += 1
-        self.pending_slots.difference_update(out)
-        t32 = t.to(torch.int32)
-        N.call("pse_kv_release", self.state, t32.data_ptr(), len(out), N.stream_ptr())
-        self._free_slots.extend(out)
-
     def gather(self, request_ids):
         """engine/paged_cache.py:162-198: padded per-layer [B, H, max_len, hd]
         K and V, the [B, max_len] padding mask and the [B] lengths (device tensors)."""

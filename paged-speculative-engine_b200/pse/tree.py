@@ -7,26 +7,22 @@ continuations per step, not a single linear chain of k tokens") as future work
 (README.md:210-214) and has no code for it; its linear step
 (engine/speculative.py:76-177, ``pse.batched_speculative_step``) is the
 one-branch case.  The rule (candidates, recursive rejection at depth 0, the
-linear rule along the accepted branch, uniform layout) is stated in the
-header of include/pse.h at ``pse_tree_accept``.
+linear rule along the accepted branch, uniform layout) is stated in
+include/pse.h at ``pse_tree_accept``.
 
-Layout: each branch runs as a row of its own.  Before the step every request
-gets ``branches - 1`` forks (``PagedKVCache.fork_rows``): block tables that
-start with the request's full blocks -- shared, never written -- plus a copy
-of its last partial block.  The draft extends every branch row by one token
-per call (k calls of width 1 over B x branches rows), the target verifies
-every branch row at width k in one call, and the accept kernel picks, per
-request, the branch it keeps and the tokens it commits.  The kept branch row
-is truncated to the accepted length and becomes the request's row
-(``PagedKVCache.resolve_forks``); the other rows return their own blocks.
-Then the reference's bonus call (width 1 on both models, the final token)
-writes the final token's K/V and the next-token logits, as in the linear
-step's reference structure.  Each branch row's attention reads the shared
-context pages itself (the rows of one request are handed out together, so
-the second read of a page tends to find it in L2).
+Layout: a request's tree lives in its own row.  The nodes are appended after
+the row's root length L in depth-major order (node (j, d) at position
+L + d*b + j): the draft extends all b branches with one call of width b per
+depth, the target verifies all b*k nodes in one call of width b*k, and every
+node attends to the root context and its own branch only
+(``pse_paged_attention_tree``; its position for the embeddings / RoPE is
+L + d), so the context's K/V is read once per request, not once per branch.
+After acceptance ``pse_kv_compact`` moves the kept branch's accepted nodes to
+positions L, L+1, ... and the row is truncated to them; then the reference's
+bonus call (width 1 on both models, the final token) writes the final token's
+K/V and the next-token logits, as in the linear step's reference structure.
 
-Steps run eagerly (no CUDA graph).  Caches with ``prefix_cache=True`` are not
-supported here.
+Steps run eagerly (no CUDA graph).
 """
 from __future__ import annotations
 
@@ -94,8 +90,7 @@ def batched_tree_speculative_step(draft_model, target_model, request_ids, draft_
     p_root = torch.stack([target_next_logits[r].reshape(-1) for r in ids]).float().contiguous()
     q_root = torch.stack([draft_next_logits[r].reshape(-1) for r in ids]).float().contiguous()
     for dm, c in ((dm_d, dc), (dm_t, tc)):
-        _check_positions(dm, c, ids, k + 1)
-        c.ensure_capacity(ids, k + 1)
+        _check_positions(dm, c, ids, k + 1)  # node positions stop at L + k - 1, the bonus at L + k
     u = None
     if T > 0:
         if uniforms is not None:
@@ -112,14 +107,14 @@ def batched_tree_speculative_step(draft_model, target_model, request_ids, draft_
                 steps[r] = steps.get(r, 0) + 1
     L_d = dc.lengths_np(dc.slots_np(ids)).copy()
     L_t = tc.lengths_np(tc.slots_np(ids)).copy()
-    sd_all, fork_d = dc.fork_rows(ids, b)
-    st_all, fork_t = tc.fork_rows(ids, b)
+    for c in (dc, tc):
+        c.ensure_capacity(ids, b * k + 1)
     R = B * b
-    sd = torch.from_numpy(sd_all.reshape(-1).astype(np.int32)).to(dev)
-    stt = torch.from_numpy(st_all.reshape(-1).astype(np.int32)).to(dev)
+    sd = dc.slots_tensor(ids)
+    stt = tc.slots_tensor(ids)
     sc = _scratch(tc, dm_d, dm_t)
 
-    # ---- candidates (node (j, 0)) and draft chains, branch rows row-major (request, branch)
+    # ---- candidates (node (j, 0)) and draft chains: chain[i, j, d] is node (j, d) of request i
     chain = torch.empty(B, b, k, dtype=torch.int32, device=dev)
     if T <= 0:
         chain[:, :, 0] = torch.topk(q_root, b, dim=-1, sorted=True).indices.to(torch.int32)
@@ -129,36 +124,43 @@ def batched_tree_speculative_step(draft_model, target_model, request_ids, draft_
                    chain.data_ptr() + 4 * j * k, b * k, None, 0, st)
     dchain = torch.empty(max(k - 1, 1), R, V, dtype=torch.float32, device=dev)
     ids_d = torch.empty(R, dtype=torch.int32, device=dev)
-    base = torch.empty(R, dtype=torch.int32, device=dev)
-    max_d = int(L_d.max()) + k + 1
+    base = torch.empty(B, dtype=torch.int32, device=dev)
     for d in range(k):
+        # depth d of every branch: one call of width b (logits row i*b + j)
         ids_d.copy_(chain[:, :, d].reshape(-1))
-        forward(dm_d, dc, sd, ids_d, R, 1, base, max_d, dchain[d] if d < k - 1 else None, scratch=sc.sc_d)
+        forward(dm_d, dc, sd, ids_d, B, b, base, int(L_d.max()) + (d + 1) * b,
+                dchain[d] if d < k - 1 else None, scratch=sc.sc_d, tree=(b, d))
         if d < k - 1:
             ud = None if u is None else u[:, (d + 1) * b:(d + 2) * b].reshape(-1).contiguous()
             N.call("pse_sample_tokens", dchain[d].data_ptr(), V, None, R, V, T, N.ptr(ud), 1, 0,
                    chain.data_ptr() + 4 * (d + 1), k, None, 0, st)
-    # ---- verify every branch row at width k
-    vlog = torch.empty(R * k, V, dtype=torch.float32, device=dev)
-    forward(dm_t, tc, stt, chain.view(-1), R, k, base, int(L_t.max()) + k + 1, vlog, scratch=sc.sc_t)
+    # ---- verify all b*k nodes (depth-major) in one call
+    nodes = chain.permute(0, 2, 1).reshape(-1).contiguous()
+    vlog = torch.empty(B * b * k, V, dtype=torch.float32, device=dev)
+    forward(dm_t, tc, stt, nodes, B, b * k, base, int(L_t.max()) + b * k, vlog, scratch=sc.sc_t, tree=(b, 0))
     # ---- accept
     toks = torch.empty(B, k + 1, dtype=torch.int32, device=dev)
     res = torch.empty(3, B, dtype=torch.int32, device=dev)  # n_accepted, branch, final token
-    N.call("pse_tree_accept", p_root.data_ptr(), V, None, q_root.data_ptr(), V, None, vlog.data_ptr(), k * V, V,
-           dchain.data_ptr(), R * V, V, chain.data_ptr(), N.ptr(u), U, B, b, k, V, T, toks.data_ptr(),
-           res[0].data_ptr(), res[1].data_ptr(), res[2].data_ptr(), st)
+    N.call("pse_tree_accept", p_root.data_ptr(), V, None, q_root.data_ptr(), V, None, vlog.data_ptr(), b * k * V, V,
+           b * V, dchain.data_ptr(), b * V, V, R * V, chain.data_ptr(), N.ptr(u), U, B, b, k, V, T,
+           toks.data_ptr(), res[0].data_ptr(), res[1].data_ptr(), res[2].data_ptr(), st)
+    # ---- keep the accepted nodes of the kept branch: node (j, m) at L + m*b + j moves to L + m
+    dj = torch.arange(k, device=dev, dtype=torch.int32).view(1, -1) * b + res[1].view(-1, 1)
+    src = dj.contiguous()
+    nacc_d = res[0].contiguous()
+    for c, L in ((dc, L_d), (tc, L_t)):
+        slots = c.slots_tensor(ids)
+        root = torch.from_numpy(L.astype(np.int32)).to(dev)
+        for layer in range(c.n_layers):
+            N.call("pse_kv_compact", c.state, c.layer(layer), slots.data_ptr(), root.data_ptr(), src.data_ptr(),
+                   nacc_d.data_ptr(), B, k, st)
+        new_len = (root + nacc_d).contiguous()
+        N.call("pse_kv_truncate", c.state, slots.data_ptr(), B, new_len.data_ptr(), None, None, st)
     res_h = res.cpu().numpy()
     toks_h = toks.cpu().numpy()
-    nacc, br, fin = res_h[0].astype(np.int64), res_h[1].astype(np.int64), res_h[2]
-    # ---- keep the accepted branch rows: truncate, then release the rest
-    for c, sl, L, forks in ((dc, sd_all, L_d, fork_d), (tc, st_all, L_t, fork_t)):
-        keep = sl[np.arange(B), br].astype(np.int32)
-        new_len = (L + nacc).astype(np.int32)
-        keep_d = torch.from_numpy(keep).to(dev)  # both arrays stay referenced until the launch is queued
-        len_d = torch.from_numpy(new_len).to(dev)
-        N.call("pse_kv_truncate", c.state, keep_d.data_ptr(), B, len_d.data_ptr(), None, None, st)
-        c.note_lengths_slots(keep, new_len.astype(np.int64))
-        c.resolve_forks(ids, forks, br)
+    nacc, fin = res_h[0].astype(np.int64), res_h[2]
+    dc.note_lengths(ids, L_d + nacc)
+    tc.note_lengths(ids, L_t + nacc)
     # ---- the bonus call (engine/speculative.py:166-177): the final token on both models
     fin_d = torch.from_numpy(fin.astype(np.int32)).to(dev)
     out = []

@@ -243,6 +243,118 @@ def test_paged_attention_matches_oracle(case, generic):
     assert np.abs(got - want).max() < tol
 
 
+TREE_ATTN_CASES = [
+    # rows, branches, depth0, width, q_heads, kv_heads, head_dim, block_size, max_root, dtype
+    (4, 2, 0, 8, 12, 12, 64, 16, 700, torch.bfloat16),     # verify of 2 x 4 nodes
+    (4, 3, 2, 3, 12, 12, 64, 16, 700, torch.bfloat16),     # a draft call at depth 2
+    (3, 4, 0, 16, 32, 8, 128, 16, 900, torch.bfloat16),    # GQA 4 x 16 nodes = 64 query rows
+    (2, 4, 0, 20, 12, 12, 64, 32, 3000, torch.bfloat16),   # long root context: split-KV
+    (3, 2, 0, 6, 4, 4, 8, 4, 50, torch.float32),
+    (2, 2, 1, 2, 2, 2, 16, 3, 40, torch.float32),
+    (2, 1, 0, 5, 4, 4, 16, 4, 30, torch.float32),          # one branch: the causal rule
+]
+
+
+@pytest.mark.parametrize("generic", [False, True])
+@pytest.mark.parametrize("case", TREE_ATTN_CASES)
+def test_paged_attention_tree_matches_oracle(case, generic):
+    """pse_paged_attention_tree: each token-tree node sees the root context and
+    its own branch, against the oracle's attention under the same mask."""
+    N = _N()
+    rows, b, d0, width, hq, hk, hd, bs, max_root, dtype = case
+    if generic and dtype == torch.float32:
+        pytest.skip("fp32 pools always run the generic kernel")
+    rng = np.random.default_rng(100 + TREE_ATTN_CASES.index(case))
+    root = rng.integers(1, max_root, size=rows)
+    base = root + d0 * b
+    need = [(int(x) + width + bs - 1) // bs for x in base]
+    nb = sum(need) + 5
+    c = _cache(n_layers=1, n_heads=hk, head_dim=hd, block_size=bs, num_blocks=nb, dtype=dtype,
+               max_requests=rows, max_blocks_per_request=max(need))
+    perm = rng.permutation(nb)
+    tables, o = [], 0
+    for i, n in enumerate(need):
+        tables.append(perm[o:o + n].tolist())
+        o += n
+        c._blocks.block_table[i, :n] = torch.tensor(tables[-1], dtype=torch.int32)
+        c._blocks.nblocks[i] = n
+        c._blocks.seq_len[i] = int(base[i]) + width
+    g = torch.Generator().manual_seed(11)
+    kp = torch.randn(nb, hk, bs, hd, generator=g)
+    vp = torch.randn(nb, hk, bs, hd, generator=g)
+    c.k_pool[0].copy_(kp.to(dtype))
+    c.v_pool[0].copy_(vp.to(dtype))
+    q = torch.randn(rows * width, hq * hd, generator=g).to(dtype)
+    qd = q.cuda()
+    out = torch.empty_like(qd)
+    slots = torch.arange(rows, dtype=torch.int32, device="cuda")
+    base_d = torch.tensor(base, dtype=torch.int32, device="cuda")
+    max_ctx = int(base.max()) + width
+    ws_bytes = N.size_call("pse_paged_attention_workspace", rows, width, hq, hk, hd, max_ctx)
+    ws = torch.zeros(max(ws_bytes, 1), dtype=torch.uint8, device="cuda")
+    N.call("pse_attention_force_generic", 1 if generic else 0)
+    try:
+        N.call("pse_paged_attention_tree", c.state, c.layer(0), qd.data_ptr(), hq * hd, out.data_ptr(), hq * hd,
+               slots.data_ptr(), base_d.data_ptr(), rows, width, hq, 1.0 / math.sqrt(hd), max_ctx, None,
+               ws.data_ptr(), ws.numel(), b, d0, N.stream_ptr())
+        torch.cuda.synchronize()
+    finally:
+        N.call("pse_attention_force_generic", 0)
+    assert int(c._blocks.status.item()) == 0
+    want = oracle_attention(q.float().view(rows, width, hq, hd).numpy(), kp.to(dtype).float().numpy(),
+                            vp.to(dtype).float().numpy(), tables, base, tree=(b, d0))
+    got = out.float().cpu().view(rows, width, hq, hd).numpy()
+    tol = F32_TOL if dtype == torch.float32 else BF16_TOL
+    assert np.abs(got - want).max() < tol
+
+
+def test_kv_compact_moves_the_kept_nodes():
+    """pse_kv_compact: per row, the tokens at root + src[m] land at root + m,
+    the rest of the row untouched (fp32 and bf16 pools)."""
+    N = _N()
+    for dtype in (torch.float32, torch.bfloat16):
+        rows, hk, hd, bs, k = 3, 2, 8, 4, 4
+        c = _cache(n_layers=1, n_heads=hk, head_dim=hd, block_size=bs, num_blocks=40, dtype=dtype,
+                   max_requests=rows, max_blocks_per_request=10)
+        root = np.array([5, 0, 9])
+        b = 3
+        for i in range(rows):
+            n = (int(root[i]) + b * k + bs - 1) // bs
+            c._blocks.block_table[i, :n] = torch.arange(i * 12, i * 12 + n, dtype=torch.int32)
+            c._blocks.nblocks[i] = n
+            c._blocks.seq_len[i] = int(root[i]) + b * k
+        c.k_pool.copy_(torch.randn_like(c.k_pool, dtype=torch.float32).to(dtype))
+        c.v_pool.copy_(torch.randn_like(c.v_pool, dtype=torch.float32).to(dtype))
+        before_k = c.k_pool.clone()
+        before_v = c.v_pool.clone()
+        branch = np.array([2, 0, 1])
+        n_keep = np.array([3, 0, 4])
+        src = (np.arange(k)[None, :] * b + branch[:, None]).astype(np.int32)
+        # device arrays held in names until the launch is queued
+        slots_d = torch.arange(rows, dtype=torch.int32).cuda()
+        root_d = torch.tensor(root, dtype=torch.int32).cuda()
+        src_d = torch.from_numpy(src).cuda()
+        keep_d = torch.tensor(n_keep, dtype=torch.int32).cuda()
+        N.call("pse_kv_compact", c.state, c.layer(0), slots_d.data_ptr(), root_d.data_ptr(), src_d.data_ptr(),
+               keep_d.data_ptr(), rows, k, N.stream_ptr())
+        torch.cuda.synchronize()
+        assert int(c._blocks.status.item()) == 0
+
+        def tok(pool, i, p):
+            blk = int(c._blocks.block_table[i, p // bs])
+            return pool[0, blk, :, p % bs]
+
+        for i in range(rows):
+            for p in range(int(root[i]) + b * k):
+                m = p - int(root[i])
+                if 0 <= m < n_keep[i]:
+                    want_k = tok(before_k, i, int(root[i]) + int(src[i, m]))
+                    want_v = tok(before_v, i, int(root[i]) + int(src[i, m]))
+                else:
+                    want_k, want_v = tok(before_k, i, p), tok(before_v, i, p)
+                assert torch.equal(tok(c.k_pool, i, p), want_k) and torch.equal(tok(c.v_pool, i, p), want_v)
+
+
 # ---------------------------------------------------------------- Philox, sampling, accept
 def test_philox_uniforms_bit_exact():
     N = _N()

@@ -5,10 +5,10 @@ the reference's linear rule, several keep the target's distribution).
 * the accept kernel gives the oracle's tokens, accepted counts and branches
   exactly on random logits (T = 0 and T > 0, 1 to 8 branches, vocabularies up
   to 32000);
-* a whole step (forks, draft chains, verify, accept, the kept branch's K/V,
-  the bonus call) gives the oracle's full-recomputation step draw for draw,
-  and each request's cached K/V afterwards equals the reference model's K/V
-  of its committed sequence;
+* a whole step (draft chains and verify with tree-masked attention, accept,
+  the kept branch's K/V moved into place, the bonus call) gives the oracle's
+  full-recomputation step draw for draw, and each request's cached K/V
+  afterwards equals the reference model's K/V of its committed sequence;
 * greedy tree decoding through the unchanged scheduler loop equals each
   request's solo ``generate_cached``, with the pool whole at the end;
 * one branch is the linear step; T = 1 first tokens follow the target's
@@ -74,8 +74,8 @@ def _run_tree_accept(N, p_root, q_root, p_chain, q_chain, u, chain, b, k, T):
     ud = u.cuda()
     toks = torch.empty(rows, k + 1, dtype=torch.int32, device="cuda")
     res = torch.empty(3, rows, dtype=torch.int32, device="cuda")
-    N.call("pse_tree_accept", pr.data_ptr(), V, None, qr.data_ptr(), V, None, ver.data_ptr(), k * V, V,
-           dch.data_ptr(), rows * b * V, V, ch.data_ptr(), ud.data_ptr(), u.shape[1], rows, b, k, V, T,
+    N.call("pse_tree_accept", pr.data_ptr(), V, None, qr.data_ptr(), V, None, ver.data_ptr(), b * k * V, k * V, V,
+           dch.data_ptr(), b * V, V, rows * b * V, ch.data_ptr(), ud.data_ptr(), u.shape[1], rows, b, k, V, T,
            toks.data_ptr(), res[0].data_ptr(), res[1].data_ptr(), res[2].data_ptr(), N.stream_ptr())
     return toks.cpu().numpy(), res.cpu().numpy()
 
@@ -161,23 +161,29 @@ def test_tree_step_matches_oracle_step_and_cache(b, k, T, bs):
         assert sorted(c.allocator.free_list()) == list(range(400))
 
 
-@pytest.mark.parametrize("b,k,bs,batch", [(2, 3, 4, 3), (3, 4, 16, 5), (2, 2, 1, 2)])
-def test_tree_scheduler_greedy_equals_solo(b, k, bs, batch):
+@pytest.mark.parametrize("b,k,bs,batch,prefix", [(2, 3, 4, 3, False), (3, 4, 16, 5, False), (2, 2, 1, 2, False),
+                                                  (2, 3, 4, 4, True)])
+def test_tree_scheduler_greedy_equals_solo(b, k, bs, batch, prefix):
     import pse
     d, t = _models(b + 31 * k)
     with torch.no_grad():
         for pd, pt in zip(d.parameters(), t.parameters()):
             pd.copy_(pt + 0.05 * torch.randn_like(pt))
     rng = np.random.default_rng(b * k)
-    reqs = [pse.Request(f"r{i}", rng.integers(0, 64, size=int(rng.integers(1, 16))).tolist(),
+    shared = rng.integers(0, 64, size=2 * bs + 1).tolist() if prefix else []
+    reqs = [pse.Request(f"r{i}", shared + rng.integers(0, 64, size=int(rng.integers(1, 16))).tolist(),
                         int(rng.integers(1, 12))) for i in range(9)]
     nb = 500
-    dc, tc = _caches(bs, nb)
+    hd = CFG.d_model // CFG.n_heads
+    dc, tc = (pse.PagedKVCache(CFG.n_layers, CFG.n_heads, hd, bs, nb, prefix_cache=prefix) for _ in range(2))
     res = pse.run_continuous_speculative_batches(d, t, reqs, dc, tc, batch, k=k, tree_branches=b)
     by = {r.request_id: r.output_ids for r in res}
     for q in reqs:
         assert by[q.request_id] == generate_cached(t, torch.tensor([q.prompt_ids]), q.max_new_tokens), q
     for c in (dc, tc):
+        if prefix:
+            assert c.prefix.stats()["hit_tokens"] > 0
+            c.prefix.clear()
         assert sorted(c.allocator.free_list()) == list(range(nb))
 
 
