@@ -237,3 +237,42 @@ def test_tree_first_token_follows_the_target_softmax():
     w, _ = weights(logits[0, -1].numpy(), 1.0)
     law = w.astype(np.float64) / w.astype(np.float64).sum()
     assert chisquare(counts, counts.sum() * law).pvalue > 0.001
+
+
+def test_tree_step_llama_matches_oracle_step():
+    """Llama-style pair (GQA, RoPE at the nodes' own positions): tree steps
+    against the oracle's full recomputation, fp32, T = 0 and T = 1."""
+    import pse
+    from oracle.model import LlamaConfig, TinyLlama
+    torch.manual_seed(21)
+    cfg = LlamaConfig(vocab_size=64, d_model=64, n_layers=2, n_heads=4, n_kv_heads=2, d_ff=96, max_seq_len=256)
+    t = TinyLlama(cfg).eval()
+    d = TinyLlama(cfg).eval()
+    with torch.no_grad():
+        for pd, pt in zip(d.parameters(), t.parameters()):
+            pd.copy_(pt + 0.02 * torch.randn_like(pt))
+    hd = cfg.d_model // cfg.n_heads
+    rng = np.random.default_rng(21)
+    prompts = [rng.integers(0, 64, size=int(rng.integers(2, 12))).tolist() for _ in range(4)]
+    ids = [f"l{i}" for i in range(4)]
+    for T in (0.0, 1.0):
+        dc = pse.PagedKVCache(cfg.n_layers, cfg.n_kv_heads, hd, 4, 300)
+        tc = pse.PagedKVCache(cfg.n_layers, cfg.n_kv_heads, hd, 4, 300)
+        out = pse.prefill_requests(d, t, dc, tc, ids, prompts)
+        dn = {r: out[r][0] for r in ids}
+        tn = {r: out[r][1] for r in ids}
+        seqs = {r: list(p) for r, p in zip(ids, prompts)}
+        b, k = 3, 3
+        for step in range(3):
+            u = rng.random((4, tree_uniform_count(k, b)))
+            res = pse.batched_tree_speculative_step(d, t, ids, dc, tc, dn, tn, k, b, T, uniforms=u)
+            for i, r in enumerate(ids):
+                want, n, _, _ = tree_step_row(d, t, seqs[r], k, b, T, u[i])
+                assert res.accepted_tokens[r] == want, (T, step, r)
+                seqs[r].extend(want)
+            dn, tn = res.draft_next_logits, res.target_next_logits
+        for r in ids:
+            ks, _, _, _ = tc.gather([r])
+            with torch.no_grad():
+                _, past = t(torch.tensor([seqs[r]]))
+            assert torch.allclose(ks[0][0].cpu(), past[0][0][0], atol=1e-4)
