@@ -855,10 +855,12 @@ def micro_tree(args, device):
             pd.copy_(pt + args.tree_noise * pt.float().std() * torch.randn_like(pt))
     outs, lines = {}, {}
     for b in (1, 2, 4):
+        # one pair of caches per form, the workload run twice on it: the timed
+        # run replays the graphs the untimed one captured (one per batch size)
+        dc = cache_for(d, w, n, torch.bfloat16, device, 2 * (k + 2) * b, prompts)
+        tc = cache_for(t, w, n, torch.bfloat16, device, 2 * (k + 2) * b, prompts)
         for run in ("warm", "timed"):
             reqs = [Request(f"{run}{i}", p, max_new) for i, p in enumerate(prompts)]
-            dc = cache_for(d, w, n, torch.bfloat16, device, 2 * (k + 2) * b, prompts)
-            tc = cache_for(t, w, n, torch.bfloat16, device, 2 * (k + 2) * b, prompts)
             steps = [0]
             torch.cuda.synchronize()
             t0 = time.perf_counter()
@@ -877,9 +879,10 @@ def micro_tree(args, device):
                 outs[b] = by
                 lines[b] = {"value": toks / secs, "unit": "tokens/s", "seconds": secs, "steps": steps[0],
                             "tokens_per_row_step": toks / max(1, steps[0]) / n}
-            del dc, tc, res
-            gc.collect()
-            torch.cuda.empty_cache()
+            del res
+        del dc, tc
+        gc.collect()
+        torch.cuda.empty_cache()
     print(json.dumps({"metric": "committed tokens/s (scheduler, token-tree speculation)", "workload":
                       f"gpt2-small pair, {n} requests x {max_new} new, k={k}, greedy, bf16, draft = target + "
                       f"{args.tree_noise:g} sd noise", "linear": lines[1], "branches_2": lines[2],
