@@ -941,9 +941,9 @@ def micro_gemm(args, device):
             ours()
             lib.pse_gemm_pair_tiles(1)
 
-        if args.gemm_only:  # plain launches of the tcgen05 kernel only (a short program for ncu)
+        if args.gemm_only:  # plain launches of one GEMM only (a short program for ncu)
             for _ in range(max(args.steps, 1)):
-                ours()
+                (cublas if args.gemm_impl == "cublas" else ours)()
             torch.cuda.synchronize()
             rows.append({"gemm": name, "M": M, "K": K, "N": Nn, "launches": max(args.steps, 1)})
             continue
@@ -1175,11 +1175,16 @@ def main():
     ap.add_argument("--gemm-only", default=None, choices=sorted(GEMM_SHAPES),
                     help="--micro gemm: launch only this shape's tcgen05 GEMM, --steps times, without graphs or "
                          "timing (a short program for ncu)")
+    ap.add_argument("--gemm-impl", default="tc", choices=["tc", "cublas"],
+                    help="--gemm-only: launch the tcgen05 GEMM (tc) or cuBLAS through torch (cublas)")
     ap.add_argument("--prefill-kernel", default="tc", choices=["tc", "off", "single"],
                     help="wide attention calls (prefill) on the tcgen05 kernels, on the mma.sync kernel, or on the "
                          "one-query-tile tcgen05 kernel at every head_dim")
     ap.add_argument("--attn-pages", default="permuted", choices=["permuted", "contiguous"],
                     help="--micro attn: block tables a random permutation of the pool, or consecutive blocks")
+    ap.add_argument("--tc-gemm", default=None, choices=["off", "gelu", "all"],
+                    help="bf16 projections: cuBLAS (off), the tcgen05 GEMM for the GELU up-projections only (gelu), "
+                         "or the tcgen05 GEMM for every projection (all); default: the engine's setting")
     ap.add_argument("--profile-step", action="store_true",
                     help="after warm-up run one eager step inside the NVTX range 'pse_step' and exit (for ncu)")
     args = ap.parse_args()
@@ -1237,6 +1242,9 @@ def main():
     torch.cuda.set_device(device)
     import pse._build
     pse._build.build()
+    if args.tc_gemm is not None:
+        import pse.engine
+        pse.engine.USE_TC_GEMM = {"off": False, "gelu": "gelu", "all": True}[args.tc_gemm]
     if args.micro == "attn":
         micro_attention(args, device)
         return

@@ -1191,20 +1191,25 @@ __global__ void __launch_bounds__(kStThreads, 1) accept_stream_kernel(AcceptArgs
 // into 8 warp segments of `seg` entries (a multiple of 128); a warp reads its
 // segment as 128-entry rows, lane l taking entries 4l..4l+3 with one 16-byte
 // load, four rows' loads issued before their arithmetic.  Per position:
-//   1. maxima of s = l / T over the target (P) and draft (Q) logits: the only
-//      read from HBM (ld.global.cg, cached in L2 only);
-//   2. fp64 segment sums of w = expf(s - m) for P and Q (re-read from L2);
-//      every thread reads the drafted token's two logits itself (one
-//      broadcast load per warp) for the accept test;
-//   3. after a rejection, fp64 segment sums of the residual (re-read again);
-//   4. inverse CDF: every warp finds the crossing segment from the segment
+//   1. one read from HBM (ld.global.cg, cached in L2 only) of the target (P)
+//      and draft (Q) logits: maxima of s = l / T and the segment sums of
+//      w = expf(s - m), kept against each lane's running maximum and moved to
+//      the row's maximum M in fp64 (online softmax); every thread reads the
+//      drafted token's two logits itself (one broadcast load per warp) for
+//      the accept test, with w = expf(s - M);
+//   2. after a rejection, fp64 segment sums of the residual (re-read from L2)
+//      with w = expf(s - M);
+//   3. inverse CDF: every warp finds the crossing segment from the segment
 //      sums (none: the last segment holding a nonzero entry, scanned with no
 //      threshold); that segment's warp re-reads and scans it, remembering
 //      its last nonzero entry for the no-crossing case.
+// The normalisers differ from sums of the expf(s - M) weights only by
+// rounding (the weights of one row agree with the fp64-exact ones to an ulp
+// either way); draws and accept decisions are those of the fp64 definition
+// except where a uniform lies within that rounding of a boundary.
 // The clusters in flight are capped so that their rows (2 x V x 4 bytes each)
 // stay within kSpL2Budget of L2: every re-read hits L2 (ncu: DRAM reads 1.11x
-// the needed bytes at vocab 128256).  The kernel is issue-bound: ~15
-// instructions per logit per pass (expf, the fp64 conversion and sum).
+// the needed bytes at vocab 128256).
 //
 // Every warp stores its segment's partial into the mailbox of every CTA of
 // the cluster (DSMEM) before one cluster barrier; each warp then reduces the
@@ -1231,6 +1236,39 @@ struct SpMail {
 
 __device__ __forceinline__ float4 neg_inf4() { return make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY); }
 
+// Online softmax sums.  A sum z of exp(s_i - m) is kept against a running
+// maximum m; when a batch raises the maximum to c, z is multiplied by
+// exp(m - c) in fp64 (rare: a handful of times per lane and row for
+// unordered logits).  Four weights are added in fp32 and the group in fp64.
+template <int B>
+__device__ __forceinline__ void online_add(const float4 (&s)[B], float& m, double& z) {
+  float c = m;
+#pragma unroll
+  for (int b = 0; b < B; ++b) c = fmaxf(c, fmaxf(fmaxf(s[b].x, s[b].y), fmaxf(s[b].z, s[b].w)));
+  if (c > m) {
+    if (z > 0.0) z *= exp((double)m - (double)c);
+    m = c;
+  }
+  if (m == -INFINITY) return;  // nothing but pads so far
+#pragma unroll
+  for (int b = 0; b < B; ++b) {
+    const float4 w = make_float4(expf(s[b].x - m), expf(s[b].y - m), expf(s[b].z - m), expf(s[b].w - m));
+    z += (double)((w.x + w.y) + (w.z + w.w));
+  }
+}
+
+// z (kept against m) moved to the maximum M >= m.
+__device__ __forceinline__ double rescaled(double z, float m, float M) {
+  return z > 0.0 && m != M ? z * exp((double)m - (double)M) : z;
+}
+
+// Lanes' (m, z) pairs combined: every lane gets the warp's maximum and sum.
+__device__ __forceinline__ void online_warp(float& m, double& z) {
+  const float M = warp_max(m);
+  z = warp_sum_d(rescaled(z, m, M));
+  m = M;
+}
+
 template <int C>
 __global__ void __launch_bounds__(kSpThreads, 4) accept_split_kernel(AcceptArgs a, int rows, int seg) {
   __shared__ SpMail box[2];
@@ -1253,28 +1291,42 @@ __global__ void __launch_bounds__(kSpThreads, 4) accept_split_kernel(AcceptArgs 
       const bool bonus = j == k;  // every draft accepted: sample target[k]
       const float* P = target_row(a, i, j);
       const float* Q = bonus ? P : draft_row(a, i, j);
-      // ---- 1. maxima of s = l / T
-      float mp = -INFINITY, mq = -INFINITY;
-#pragma unroll 4
-      for (int c = 0; c < n_c; ++c) {
-        const int e = e0 + c * 128;
-        if (e < V) {
-          const float4 sp = scale_s(ld_l2(P + e), T);
-          mp = fmaxf(mp, fmaxf(fmaxf(sp.x, sp.y), fmaxf(sp.z, sp.w)));
-          if (!bonus) {
-            const float4 sq = scale_s(ld_l2(Q + e), T);
-            mq = fmaxf(mq, fmaxf(fmaxf(sq.x, sq.y), fmaxf(sq.z, sq.w)));
-          }
-        }
+      // ---- 1. one pass from HBM: maxima of s = l / T and sums of exp(s - max),
+      //      kept against a running maximum and rescaled when it grows; the
+      //      drafted token's two logits (one broadcast load per warp)
+      const int x = bonus ? -1 : drafted[j];
+      const bool x_ok = x >= 0 && x < V;
+      float lpx = 0.f, lqx = 0.f;
+      if (x_ok) {
+        lpx = __ldcg(P + x);
+        lqx = __ldcg(Q + x);
       }
-      mp = warp_max(mp);
-      mq = warp_max(mq);
+      float mp = -INFINITY, mq = -INFINITY;
+      double sp = 0.0, sq = 0.0;
+      for (int c0 = 0; c0 < n_c; c0 += kSpBatch) {
+        float4 sp4[kSpBatch], sq4[kSpBatch];
+#pragma unroll
+        for (int b = 0; b < kSpBatch; ++b) {
+          const int e = e0 + (c0 + b) * 128;
+          const bool ok = c0 + b < n_c && e < V;  // -inf pads weigh 0
+          sp4[b] = ok ? scale_s(ld_l2(P + e), T) : neg_inf4();
+          sq4[b] = ok && !bonus ? scale_s(ld_l2(Q + e), T) : neg_inf4();
+        }
+        online_add<kSpBatch>(sp4, mp, sp);
+        if (!bonus) online_add<kSpBatch>(sq4, mq, sq);
+      }
+      online_warp(mp, sp);
+      online_warp(mq, sq);
       if (lane < C) {
         const uint32_t b = peer_addr(&box[ph], lane);
         st_peer(b + (uint32_t)offsetof(SpMail, mx[0][0]) + 4u * g, mp);
         st_peer(b + (uint32_t)offsetof(SpMail, mx[1][0]) + 4u * g, mq);
+        st_peer(b + (uint32_t)offsetof(SpMail, sum[0][0]) + 8u * g, sp);
+        st_peer(b + (uint32_t)offsetof(SpMail, sum[1][0]) + 8u * g, sq);
       }
       cluster_sync_all();
+      double segv[kSpG];  // segment sums of the distribution the draw descends
+      double Zp = 0.0, Zq = 0.0;
       {
         const SpMail& m = box[ph];
         float x0 = -INFINITY, y0 = -INFINITY;
@@ -1288,60 +1340,13 @@ __global__ void __launch_bounds__(kSpThreads, 4) accept_split_kernel(AcceptArgs 
         }
         mp = warp_max(x0);
         mq = warp_max(y0);
-      }
-      ph ^= 1;
-      // ---- 2. weights: segment sums; the drafted token's logits
-      const int x = bonus ? -1 : drafted[j];
-      const bool x_ok = x >= 0 && x < V;
-      float lpx = 0.f, lqx = 0.f;
-      if (x_ok) {
-        lpx = __ldcg(P + x);
-        lqx = __ldcg(Q + x);
-      }
-      double sp = 0.0, sq = 0.0;
-      for (int c0 = 0; c0 < n_c; c0 += kSpBatch) {
-        float4 lp4[kSpBatch], lq4[kSpBatch];
-#pragma unroll
-        for (int b = 0; b < kSpBatch; ++b) {
-          const int e = e0 + (c0 + b) * 128;
-          const bool ok = c0 + b < n_c && e < V;  // -inf pads weigh 0
-          lp4[b] = ok ? ld_l2(P + e) : neg_inf4();
-          lq4[b] = ok && !bonus ? ld_l2(Q + e) : neg_inf4();
-        }
-#pragma unroll
-        for (int b = 0; b < kSpBatch; ++b) {
-          const float4 wp = weights4(lp4[b], T, mp);
-          sp += (double)wp.x;
-          sp += (double)wp.y;
-          sp += (double)wp.z;
-          sp += (double)wp.w;
-          if (!bonus) {
-            const float4 wq = weights4(lq4[b], T, mq);
-            sq += (double)wq.x;
-            sq += (double)wq.y;
-            sq += (double)wq.z;
-            sq += (double)wq.w;
-          }
-        }
-      }
-      sp = warp_sum_d(sp);
-      sq = warp_sum_d(sq);
-      if (lane < C) {
-        const uint32_t b = peer_addr(&box[ph], lane);
-        st_peer(b + (uint32_t)offsetof(SpMail, sum[0][0]) + 8u * g, sp);
-        st_peer(b + (uint32_t)offsetof(SpMail, sum[1][0]) + 8u * g, sq);
-      }
-      cluster_sync_all();
-      double segv[kSpG];  // segment sums of the distribution the draw descends
-      double Zp = 0.0, Zq = 0.0;
-      {
-        const SpMail& m = box[ph];
+        // every segment's sum moved to the row's maximum, in fixed order
 #pragma unroll
         for (int jj = 0; jj < kSpG; ++jj) {
           const int sg = kSpG * lane + jj;
-          segv[jj] = sg < n_seg ? m.sum[0][sg] : 0.0;
+          segv[jj] = sg < n_seg ? rescaled(m.sum[0][sg], m.mx[0][sg], mp) : 0.0;
           Zp += segv[jj];
-          Zq += sg < n_seg ? m.sum[1][sg] : 0.0;
+          Zq += sg < n_seg ? rescaled(m.sum[1][sg], m.mx[1][sg], mq) : 0.0;
         }
       }
       ph ^= 1;
@@ -1369,7 +1374,7 @@ __global__ void __launch_bounds__(kSpThreads, 4) accept_split_kernel(AcceptArgs 
         n_acc = j;
         invp = 1.0 / Zp;
         invq = 1.0 / Zq;
-        // ---- 3. residual segment sums
+        // ---- 2. residual segment sums
         double sr = 0.0;
         for (int c0 = 0; c0 < n_c; c0 += kSpBatch) {
           float4 lp4[kSpBatch], lq4[kSpBatch];
@@ -1414,7 +1419,7 @@ __global__ void __launch_bounds__(kSpThreads, 4) accept_split_kernel(AcceptArgs 
           for (int jj = 0; jj < kSpG; ++jj) segv[jj] = segr[jj];
         }
       }
-      // ---- 4. inverse CDF: segment -> 128-entry row -> entry
+      // ---- 3. inverse CDF: segment -> 128-entry row -> entry
       double t = u[2 * k] * (use_resid ? R : Zp);
       double run = 0.0;
       int g_scan = group_cross<kSpG>(segv, t, run);
