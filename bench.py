@@ -136,9 +136,10 @@ def build_pair(workload, dtype, device, seed=0):
     return d.eval(), t.eval()
 
 
-def cache_for(model, workload, n_rows, dtype, device, extra_tokens, prompts=None):
+def cache_for(model, workload, n_rows, dtype, device, extra_tokens, prompts=None, n_blocks=None):
     """A pool for n_rows requests of the workload: every row sized for the
-    longest prompt, or, given the prompts, for each prompt's own length."""
+    longest prompt, or, given the prompts, for each prompt's own length, or
+    ``n_blocks`` blocks."""
     import pse
     cfg = model.cfg
     kv = getattr(cfg, "n_kv_heads", cfg.n_heads)
@@ -149,6 +150,8 @@ def cache_for(model, workload, n_rows, dtype, device, extra_tokens, prompts=None
         nb = n_rows * ((per_row + bs - 1) // bs) + 8
     else:
         nb = sum((len(p) + workload.max_new_tokens + extra_tokens + bs - 1) // bs for p in prompts) + 8
+    if n_blocks:
+        nb = n_blocks
     return pse.PagedKVCache(cfg.n_layers, kv, hd, bs, nb, dtype=dtype, device=device, max_requests=n_rows,
                             max_blocks_per_request=(per_row + bs - 1) // bs)
 
@@ -674,7 +677,7 @@ def micro_prefill(args, device):
                       "identical_tables_and_free_lists": same}), flush=True)
 
 
-def micro_scheduler(args, device, emit=True):
+def micro_scheduler(args, device, emit=True, warm=True):
     """The whole workload through run_continuous_speculative_batches (FIFO
     admission up to the batch size, batched prefill, steps until every request
     has max_new_tokens, as the reference's own benchmark drives it): committed
@@ -688,20 +691,28 @@ def micro_scheduler(args, device, emit=True):
     dtype = torch.bfloat16 if w.dtype == "bfloat16" else torch.float32
     n = args.rows or w.n_requests
     prompts = wl.prompts(w, seed=0, n=n)
+    batch = args.max_batch or w.max_batch_size
     d, t = build_pair(w, dtype, device)
     if args.sched_mode == "self":
         d = t  # draft == target: every draft accepted (the reference benchmark's ceiling configuration)
+    pool_blocks = None
+    if args.pool_gb:
+        # both pools get the block count that puts pool_gb of the target's K/V on the device
+        cfg = t.cfg
+        blk = (cfg.n_layers * getattr(cfg, "n_kv_heads", cfg.n_heads) * (cfg.d_model // cfg.n_heads) * 2
+               * w.block_size * (2 if dtype == torch.bfloat16 else 4))
+        pool_blocks = int(args.pool_gb * 1e9) // blk
     out = {}
-    for run in ("warm", "timed"):
+    for run in (("warm", "timed") if warm else ("timed",)):
         reqs = [Request(f"{run}{i}", p, w.max_new_tokens) for i, p in enumerate(prompts)]
-        dc = cache_for(d, w, n, dtype, device, w.k + 2, prompts)
-        tc = cache_for(t, w, n, dtype, device, w.k + 2, prompts)
+        dc = cache_for(d, w, n, dtype, device, w.k + 2, prompts, n_blocks=pool_blocks)
+        tc = cache_for(t, w, n, dtype, device, w.k + 2, prompts, n_blocks=pool_blocks)
         torch.cuda.synchronize()
         t0 = time.perf_counter()
         if args.sched_mode == "plain":
-            res = pse.run_plain_continuous_batches(t, reqs, tc, w.max_batch_size)
+            res = pse.run_plain_continuous_batches(t, reqs, tc, batch)
         else:
-            res = pse.run_continuous_speculative_batches(d, t, reqs, dc, tc, w.max_batch_size, k=w.k,
+            res = pse.run_continuous_speculative_batches(d, t, reqs, dc, tc, batch, k=w.k,
                                                          temperature=w.temperature,
                                                          defer_bonus=False if args.reference_structure else None,
                                                          device_bookkeeping=not args.sched_host_loop)
@@ -744,9 +755,12 @@ def micro_scheduler(args, device, emit=True):
         cpu = {"value": ctoks / csecs, "unit": "tokens/s", "cores": os.cpu_count() or 1, "kind": "port",
                "sample": f"the whole {w.name} workload ({n} requests), fp32 oracle port"}
     res = {"metric": "committed tokens/s (scheduler, whole workload)", "workload": w.name, "k": w.k,
-           "temperature": w.temperature, "requests": n, "max_batch_size": w.max_batch_size,
+           "temperature": w.temperature, "requests": n, "max_batch_size": batch,
+           "pool": (f"{args.pool_gb:g} GB of target K/V ({pool_blocks} blocks of {w.block_size} tokens per cache)"
+                    if pool_blocks else "sized to the workload's prompts"),
            "step": "reference structure" if args.reference_structure else "default (bonus deferred)",
            "bookkeeping": "host" if args.sched_host_loop else "device",
+           "untimed_warm_run": warm,
            "mode": {"spec": "speculative, independent draft", "self": "speculative, draft = target",
                     "plain": "plain continuous batching, no speculation"}[args.sched_mode],
            "generated_tokens": toks, "seconds": secs, "value": toks / secs, "unit": "tokens/s",
@@ -1069,6 +1083,27 @@ def kernel_configs(args, device):
     return out
 
 
+def llama_whole(args, device):
+    """The Llama-style configuration as specified: all 2048 requests through
+    the scheduler on this GPU (batched prefill and every decode step), the
+    pools sized to ~150 GB of the target's K/V (less if the GPU has less
+    free), at most 1024 requests in flight (2048 prompts' K/V would not fit
+    150 GB).  One run, graph captures inside the timed region."""
+    import copy
+    gc.collect()
+    torch.cuda.empty_cache()
+    free = torch.cuda.mem_get_info(device)[0] / 1e9
+    a = copy.copy(args)
+    a.workload, a.rows, a.sched_mode, a.reference_structure = "llama-1b", None, "spec", False
+    a.sched_host_loop, a.no_cpu_baseline = False, True
+    a.max_batch, a.pool_gb = 1024, float(min(150.0, int(free * 0.94 - 14.0)))
+    r = micro_scheduler(a, device, emit=False, warm=False)
+    gc.collect()
+    torch.cuda.empty_cache()
+    return {k: r[k] for k in ("value", "unit", "seconds", "generated_tokens", "requests", "max_batch_size", "pool",
+                              "step", "bookkeeping", "untimed_warm_run")}
+
+
 def llama_step(args, device, peak):
     """The Llama-style configuration's step on this GPU (512 rows of its
     workload, bf16, k=4, block 32): the same measurement as the headline on a
@@ -1143,6 +1178,11 @@ def main():
     ap.add_argument("--k", type=int, default=None, help="draft length (default: the workload's)")
     ap.add_argument("--sched-mode", default="spec", choices=["spec", "self", "plain"],
                     help="--micro scheduler: independent draft, draft = target, or no speculation")
+    ap.add_argument("--max-batch", type=int, default=None,
+                    help="--micro scheduler: max_batch_size of the scheduler (default: the workload's)")
+    ap.add_argument("--pool-gb", type=float, default=None,
+                    help="--micro scheduler: size each pool to this many GB of the target's K/V (default: every "
+                         "request's own prompt + new tokens)")
     ap.add_argument("--sched-host-loop", action="store_true",
                     help="--micro scheduler: per-row bookkeeping on the host (the reference's loop) instead of "
                          "on the device")
@@ -1158,6 +1198,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-kernel-configs", action="store_true",
                     help="skip the 5a / 5b / 5c kernel configurations after the step (they run at N=1 only)")
+    ap.add_argument("--no-llama-whole", action="store_true",
+                    help="skip the Llama-style whole workload (2048 requests, ~150 GB pools, about a minute) among "
+                         "the kernel configurations")
     ap.add_argument("--micro", choices=["attn", "accept", "churn", "prefill", "scheduler", "gemm", "prefix", "tree"],
                     default=None,
                     help="kernel microbenchmark instead of the step")
@@ -1278,6 +1321,8 @@ def main():
         kernel_cfgs = kernel_configs(args, device)
         if args.workload == "gpt2-small":
             kernel_cfgs["4_llama_1b_step"] = llama_step(args, device, peak)
+            if not args.no_llama_whole:
+                kernel_cfgs["4_llama_1b_whole_workload"] = llama_whole(args, device)
         kernel_cfgs["self_draft_step"] = self_draft_step(args, device)
     check = token_check(args, r["check_rows"], os.cpu_count() or 1) if rank == 0 else None
     cpu = None
