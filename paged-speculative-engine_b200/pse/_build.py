@@ -32,16 +32,29 @@ def needs_build() -> bool:
 
 
 def build(force: bool = False, verbose: bool = False) -> str:
+    """Compile libpse.so if a source is newer than it (or ``force``).  Several
+    processes may call this at once (one per GPU under torchrun): the build
+    runs under an exclusive file lock, the staleness test is repeated once the
+    lock is held, and each build writes its own temporary file before the
+    atomic rename."""
     if not force and not needs_build():
         return LIB
+    import fcntl
     os.makedirs(os.path.dirname(LIB), exist_ok=True)
-    tmp = LIB + ".tmp"
-    cmd = [nvcc(), *ARCH, "-O3", "-lineinfo", "-std=c++17", "-shared", "-Xcompiler", "-fPIC",
-           f"-I{INCLUDE}", "-o", tmp] + [os.path.join(CSRC, s) for s in SOURCES]
-    if verbose:
-        print(" ".join(cmd))
-    subprocess.run(cmd, check=True)
-    os.replace(tmp, LIB)
+    with open(LIB + ".lock", "w") as lock:
+        fcntl.flock(lock, fcntl.LOCK_EX)
+        try:
+            if not force and not needs_build():
+                return LIB  # another process built it while this one waited
+            tmp = f"{LIB}.tmp{os.getpid()}"
+            cmd = [nvcc(), *ARCH, "-O3", "-lineinfo", "-std=c++17", "-shared", "-Xcompiler", "-fPIC",
+                   f"-I{INCLUDE}", "-o", tmp] + [os.path.join(CSRC, s) for s in SOURCES]
+            if verbose:
+                print(" ".join(cmd))
+            subprocess.run(cmd, check=True)
+            os.replace(tmp, LIB)
+        finally:
+            fcntl.flock(lock, fcntl.LOCK_UN)
     return LIB
 
 
