@@ -687,10 +687,17 @@ def micro_scheduler(args, device, emit=True, warm=True):
     import pse
     from pse import workload as wl
     from pse.scheduler import Request
+    from pse.dist import reduce_stats, shard_requests
     w = wl.WORKLOADS[args.workload]
     dtype = torch.bfloat16 if w.dtype == "bfloat16" else torch.float32
-    n = args.rows or w.n_requests
-    prompts = wl.prompts(w, seed=0, n=n)
+    world = torch.distributed.get_world_size() if torch.distributed.is_initialized() else 1
+    rank = torch.distributed.get_rank() if world > 1 else 0
+    n_all = args.rows or w.n_requests
+    # the job is n_all requests; with several ranks each runs its LPT shard (strong scaling)
+    shard = shard_requests([Request(f"r{i}", p, w.max_new_tokens)
+                            for i, p in enumerate(wl.prompts(w, seed=0, n=n_all))], world, rank)
+    prompts = [r.prompt_ids for r in shard]
+    n = len(prompts)
     batch = args.max_batch or w.max_batch_size
     d, t = build_pair(w, dtype, device)
     if args.sched_mode == "self":
@@ -708,7 +715,10 @@ def micro_scheduler(args, device, emit=True, warm=True):
         dc = cache_for(d, w, n, dtype, device, w.k + 2, prompts, n_blocks=pool_blocks)
         tc = cache_for(t, w, n, dtype, device, w.k + 2, prompts, n_blocks=pool_blocks)
         torch.cuda.synchronize()
-        t0 = time.perf_counter()
+        if world > 1:
+            torch.distributed.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
         if args.sched_mode == "plain":
             res = pse.run_plain_continuous_batches(t, reqs, tc, batch)
         else:
@@ -716,18 +726,24 @@ def micro_scheduler(args, device, emit=True, warm=True):
                                                          temperature=w.temperature,
                                                          defer_bonus=False if args.reference_structure else None,
                                                          device_bookkeeping=not args.sched_host_loop)
+        e1.record()
         torch.cuda.synchronize()
-        out[run] = (time.perf_counter() - t0, sum(len(r.output_ids) - len(p) for r, p in
-                                                   zip(sorted(res, key=lambda r: int(r.request_id[len(run):])),
-                                                       prompts)))
+        # device time from the first launch to the last (the host loop's gaps included)
+        out[run] = (e0.elapsed_time(e1) / 1000.0, sum(len(r.output_ids) - len(p) for r, p in
+                                                       zip(sorted(res, key=lambda r: int(r.request_id[len(run):])),
+                                                           prompts)))
         # the caches hold their step runners (and those their graphs): free
         # the warm-up run's pools before the timed run allocates its own
         del dc, tc, res
         gc.collect()
         torch.cuda.empty_cache()
     secs, toks = out["timed"]
+    per_rank = None
+    if world > 1:
+        toks, secs, per = reduce_stats(toks, secs, None, device=device)
+        per_rank = [{"tokens": p[0], "seconds": round(p[1], 3)} for p in per]
     cpu = None
-    if not args.no_cpu_baseline and args.sched_mode == "spec":
+    if not args.no_cpu_baseline and args.sched_mode == "spec" and world == 1:
         # the reference's CPU path (oracle port, fp32) on the same whole workload, all host threads
         from oracle import scheduler as OS
         from oracle.model import ModelConfig as OMC, TinyGPT as OTG, LlamaConfig as OLC, TinyLlama as OTL
@@ -755,7 +771,7 @@ def micro_scheduler(args, device, emit=True, warm=True):
         cpu = {"value": ctoks / csecs, "unit": "tokens/s", "cores": os.cpu_count() or 1, "kind": "port",
                "sample": f"the whole {w.name} workload ({n} requests), fp32 oracle port"}
     res = {"metric": "committed tokens/s (scheduler, whole workload)", "workload": w.name, "k": w.k,
-           "temperature": w.temperature, "requests": n, "max_batch_size": batch,
+           "temperature": w.temperature, "requests": n_all, "n_gpus": world, "max_batch_size": batch,
            "pool": (f"{args.pool_gb:g} GB of target K/V ({pool_blocks} blocks of {w.block_size} tokens per cache)"
                     if pool_blocks else "sized to the workload's prompts"),
            "step": "reference structure" if args.reference_structure else "default (bonus deferred)",
@@ -764,8 +780,9 @@ def micro_scheduler(args, device, emit=True, warm=True):
            "mode": {"spec": "speculative, independent draft", "self": "speculative, draft = target",
                     "plain": "plain continuous batching, no speculation"}[args.sched_mode],
            "generated_tokens": toks, "seconds": secs, "value": toks / secs, "unit": "tokens/s",
-           "cpu_baseline": cpu}
-    if emit:
+           "timing": "CUDA events from the first launch to the last; max over ranks",
+           "per_rank": per_rank, "cpu_baseline": cpu}
+    if emit and rank == 0:
         print(json.dumps(res), flush=True)
     return res
 
@@ -1302,6 +1319,9 @@ def main():
         return
     if args.micro == "scheduler":
         micro_scheduler(args, device)
+        if world > 1:
+            torch.distributed.barrier()
+            torch.distributed.destroy_process_group()
         return
     if args.micro == "prefix":
         micro_prefix(args, device)
