@@ -397,6 +397,36 @@ int pse_sched_commit(const int32_t *tokens, int32_t tok_stride, const int32_t *n
                      int32_t rows, const int64_t *out_off, const int32_t *max_new, int32_t *generated,
                      int32_t *out, int32_t *finished, void *stream);
 
+/* Input of the verify call when every row's final token from the previous
+ * step is still pending (its position reserved, its K/V not yet written):
+ * ids[i * (k + 1)] = last_token[slots[i]] (0 for a slot outside
+ * [0, n_slots)), ids[i * (k + 1) + j] = drafts[i * k + j - 1] for j = 1..k,
+ * first_pos[i] = base[i] - 1.  Stands in for the token list of the
+ * reference's bonus call (engine/speculative.py:166-177) followed by its
+ * width-k verify (engine/speculative.py:115-117), run as one call. */
+int pse_step_verify_ids(const int32_t *last_token, int32_t n_slots, const int32_t *slots, const int32_t *drafts,
+                        const int32_t *base, int32_t rows, int32_t k, int32_t *ids, int32_t *first_pos,
+                        void *stream);
+
+/* Input of the draft's bonus call (engine/speculative.py:166-177), merged
+ * with the last draft round's call into one width-2 call: ids2[2 i] =
+ * drafts[i * k + k - 1] if n_acc[i] == k else final[i], ids2[2 i + 1] =
+ * final[i], pos[i] = base0[i] + min(n_acc[i], k - 1), sel[i] = 2 i + (n_acc[i]
+ * == k) (the hidden row whose logits become the row's draft_next_logits). */
+int pse_step_bonus_ids(const int32_t *n_acc, const int32_t *drafts, const int32_t *final_tok, const int32_t *base0,
+                       int32_t rows, int32_t k, int32_t *ids2, int32_t *pos, int64_t *sel, void *stream);
+
+/* End of a speculative step: final[i] becomes the last token of slot
+ * slots_d[i] in the draft cache and of slots_t[i] in the target cache (slots
+ * outside [0, n_slots) are skipped), and pack receives [tokens (rows x (k+1))
+ * | n_acc (rows) | *status_d | *status_t] for the step's one device-to-host
+ * copy (the accepted tokens of engine/speculative.py:159-164 with the
+ * caches' error words). */
+int pse_step_finish(const int32_t *final_tok, const int32_t *slots_d, const int32_t *slots_t, int32_t rows,
+                    int32_t *last_d, int32_t n_slots_d, int32_t *last_t, int32_t n_slots_t, const int32_t *tokens,
+                    int32_t k, const int32_t *n_acc, const int32_t *status_d, const int32_t *status_t,
+                    int32_t *pack, void *stream);
+
 /* Number of kernels the library registers (load check) and a version tag. */
 int pse_version(void);
 int pse_warmup(void);

@@ -87,6 +87,9 @@ _PROTOS = {
     "pse_paged_attention_noalloc": ([BlockState, KVLayer, c_p, c_i64, c_p, c_i64, c_p, c_p, c_i32, c_i32, c_i32,
                                      c_f32, c_i32, c_p], 1),
     "pse_sched_commit": ([c_p, c_i32, c_p, c_p, c_i32, c_p, c_p, c_p, c_p, c_p, c_p], 1),
+    "pse_step_verify_ids": ([c_p, c_i32, c_p, c_p, c_p, c_i32, c_i32, c_p, c_p, c_p], 1),
+    "pse_step_bonus_ids": ([c_p, c_p, c_p, c_p, c_i32, c_i32, c_p, c_p, c_p, c_p], 1),
+    "pse_step_finish": ([c_p, c_p, c_p, c_i32, c_p, c_i32, c_p, c_i32, c_p, c_i32, c_p, c_p, c_p, c_p, c_p], 1),
 }
 _SIZE_PROTOS = {
     "pse_paged_attention_workspace": [c_i32, c_i32, c_i32, c_i32, c_i32, c_i32],

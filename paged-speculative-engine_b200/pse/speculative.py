@@ -374,10 +374,8 @@ class _StepBuffers:
         self.B = B
         # the draft's tail call (its last round + its bonus, width 2): ids, the
         # row each request's next logits come from, those hidden rows
-        self.nclamp = torch.empty(B, **i32)
         self.ids2 = torch.empty(B, 2, **i32)
         self.sel = torch.empty(B, dtype=torch.int64, device=device)
-        self.even = torch.arange(0, 2 * B, 2, dtype=torch.int64, device=device)
         self.hsel = torch.empty(B, d_draft, dtype=draft_dtype, device=device)
         # the step's per-row host inputs, copied to the device in one transfer:
         # [slots_d | slots_t | req_key | steps | order_d | order_t | ords]
@@ -517,9 +515,9 @@ class StepRunner:
             # [final, d_1..d_k] without allocating; its column 0 gives what the
             # reference's bonus call returned as target_next.
             N.call("pse_kv_reserve", self.tcache.state, b.slots_t.data_ptr(), B, k, b.base[k].data_ptr(), st)
-            torch.sub(b.base[k], 1, out=b.basem1)
-            b.vids[:, 0] = self.tcache.last_token.index_select(0, b.slots_t.long())
-            b.vids[:, 1:] = b.drafts
+            lt = self.tcache.last_token
+            N.call("pse_step_verify_ids", lt.data_ptr(), lt.numel(), b.slots_t.data_ptr(), b.drafts.data_ptr(),
+                   b.base[k].data_ptr(), B, k, b.vids.data_ptr(), b.basem1.data_ptr(), st)
             forward(self.dm_t, self.tcache, b.slots_t, b.vids.view(-1), B, k + 1, b.basem1, max_ctx_t, b.vlog2,
                     scratch=self.sc_t, row_order=b.order_t, reserve=False)
             t0, t0_stride, t0_index = b.vlog2.data_ptr(), (k + 1) * V, None
@@ -550,14 +548,10 @@ class StepRunner:
         # (as the reference's bonus append does), then the call runs at
         # base + min(n, k-1) without allocating.
         N.call("pse_kv_reserve", self.dcache.state, b.slots_d.data_ptr(), B, 1, b.base[k + 1].data_ptr(), st)
-        full = b.n_acc.eq(k)
-        torch.where(full, b.drafts[:, k - 1], b.final, out=b.ids2[:, 0])
-        b.ids2[:, 1].copy_(b.final)
-        torch.clamp(b.n_acc, max=k - 1, out=b.nclamp)
-        torch.add(b.base[0], b.nclamp, out=b.base[k + 3])
+        N.call("pse_step_bonus_ids", b.n_acc.data_ptr(), b.drafts.data_ptr(), b.final.data_ptr(),
+               b.base[0].data_ptr(), B, k, b.ids2.data_ptr(), b.base[k + 3].data_ptr(), b.sel.data_ptr(), st)
         forward(self.dm_d, self.dcache, b.slots_d, b.ids2.view(-1), B, 2, b.base[k + 3], max_ctx_d, None,
                 scratch=self.sc_d, row_order=b.order_d, reserve=False)
-        torch.add(b.even, full, out=b.sel)
         torch.index_select(self.sc_d.h[:2 * B], 0, b.sel, out=b.hsel)
         lm_head(self.dm_d, b.hsel, b.blog)
         N.call("pse_scatter_rows", b.blog.data_ptr(), V, b.slots_d.data_ptr(), B, V, dnext.data_ptr(), V,
@@ -571,13 +565,10 @@ class StepRunner:
             # the reference's bonus append without its forward: the final
             # token's position is reserved in the same order (same blocks)
             N.call("pse_kv_reserve", self.tcache.state, b.slots_t.data_ptr(), B, 1, b.base[k + 2].data_ptr(), st)
-        self.dcache.last_token.index_copy_(0, b.slots_d.long(), b.final)
-        self.tcache.last_token.index_copy_(0, b.slots_t.long(), b.final)
-        nt = B * (k + 1)
-        b.pack[:nt].copy_(b.tokens.view(-1))
-        b.pack[nt:nt + B].copy_(b.n_acc)
-        b.pack[nt + B:nt + B + 1].copy_(self.dcache.status_tensor())
-        b.pack[nt + B + 1:nt + B + 2].copy_(self.tcache.status_tensor())
+        ld, lt = self.dcache.last_token, self.tcache.last_token
+        N.call("pse_step_finish", b.final.data_ptr(), b.slots_d.data_ptr(), b.slots_t.data_ptr(), B, ld.data_ptr(),
+               ld.numel(), lt.data_ptr(), lt.numel(), b.tokens.data_ptr(), k, b.n_acc.data_ptr(),
+               self.dcache.status_tensor().data_ptr(), self.tcache.status_tensor().data_ptr(), b.pack.data_ptr(), st)
 
     # ---------------------------------------------------------------- host side
     def step(self, request_ids, draft_next_logits, target_next_logits, temperature, generator=None,

@@ -192,3 +192,68 @@ def test_device_bookkeeping_rejects_duplicate_ids_like_host_loop():
         with pytest.raises(ValueError):
             pse.run_continuous_speculative_batches(d, t, reqs, dc, tc, 4, k=2, temperature=0.0,
                                                    device_bookkeeping=dev)
+
+
+@pytest.mark.parametrize("rows,k", [(1, 1), (7, 3), (300, 5), (2500, 8)])
+def test_step_glue_kernels_match_their_tensor_statements(rows, k):
+    """The step's integer hand-offs (pse_step_verify_ids, pse_step_bonus_ids,
+    pse_step_finish) equal the tensor operations they replace, bit for bit,
+    including rows that accepted every draft and slots outside the table."""
+    import pse._native as N
+    dev = torch.device("cuda")
+    g = torch.Generator(device="cpu").manual_seed(rows * 10 + k)
+    n_slots = rows + 17
+    slots_d = torch.randperm(n_slots, generator=g)[:rows].to(torch.int32)
+    slots_t = torch.randperm(n_slots, generator=g)[:rows].to(torch.int32)
+    drafts = torch.randint(0, 32000, (rows, k), generator=g, dtype=torch.int32)
+    final = torch.randint(0, 32000, (rows,), generator=g, dtype=torch.int32)
+    n_acc = torch.randint(0, k + 1, (rows,), generator=g, dtype=torch.int32)
+    n_acc[::3] = k  # every draft accepted
+    base = torch.randint(1, 5000, (rows,), generator=g, dtype=torch.int32)
+    last = torch.randint(0, 32000, (n_slots,), generator=g, dtype=torch.int32)
+    tokens = torch.randint(-1, 32000, (rows, k + 1), generator=g, dtype=torch.int32)
+    to = lambda t: t.to(dev)
+    slots_d, slots_t, drafts, final, n_acc, base, last, tokens = map(
+        to, (slots_d, slots_t, drafts, final, n_acc, base, last, tokens))
+    st = N.stream_ptr()
+    # verify ids from pending rows
+    ids = torch.full((rows, k + 1), -9, dtype=torch.int32, device=dev)
+    first = torch.full((rows,), -9, dtype=torch.int32, device=dev)
+    N.call("pse_step_verify_ids", last.data_ptr(), n_slots, slots_t.data_ptr(), drafts.data_ptr(), base.data_ptr(),
+           rows, k, ids.data_ptr(), first.data_ptr(), st)
+    want = torch.cat([last.index_select(0, slots_t.long()).view(-1, 1), drafts], dim=1)
+    assert torch.equal(ids, want) and torch.equal(first, base - 1)
+    # the draft's tail call
+    ids2 = torch.full((rows, 2), -9, dtype=torch.int32, device=dev)
+    pos = torch.full((rows,), -9, dtype=torch.int32, device=dev)
+    sel = torch.full((rows,), -9, dtype=torch.int64, device=dev)
+    N.call("pse_step_bonus_ids", n_acc.data_ptr(), drafts.data_ptr(), final.data_ptr(), base.data_ptr(), rows, k,
+           ids2.data_ptr(), pos.data_ptr(), sel.data_ptr(), st)
+    full = n_acc.eq(k)
+    assert torch.equal(ids2[:, 0], torch.where(full, drafts[:, k - 1], final))
+    assert torch.equal(ids2[:, 1], final)
+    assert torch.equal(pos, base + torch.clamp(n_acc, max=k - 1))
+    assert torch.equal(sel, torch.arange(0, 2 * rows, 2, device=dev) + full)
+    # end of the step
+    last_d, last_t = last.clone(), last.clone().flip(0).contiguous()
+    want_d, want_t = last_d.clone(), last_t.clone()
+    want_d.index_copy_(0, slots_d.long(), final)
+    want_t.index_copy_(0, slots_t.long(), final)
+    sd_word = torch.tensor([5], dtype=torch.int32, device=dev)
+    st_word = torch.tensor([32], dtype=torch.int32, device=dev)
+    pack = torch.full((rows * (k + 2) + 2,), -9, dtype=torch.int32, device=dev)
+    N.call("pse_step_finish", final.data_ptr(), slots_d.data_ptr(), slots_t.data_ptr(), rows, last_d.data_ptr(),
+           n_slots, last_t.data_ptr(), n_slots, tokens.data_ptr(), k, n_acc.data_ptr(), sd_word.data_ptr(),
+           st_word.data_ptr(), pack.data_ptr(), st)
+    torch.cuda.synchronize()
+    assert torch.equal(last_d, want_d) and torch.equal(last_t, want_t)
+    nt = rows * (k + 1)
+    assert torch.equal(pack[:nt], tokens.view(-1)) and torch.equal(pack[nt:nt + rows], n_acc)
+    assert pack[nt + rows].item() == 5 and pack[nt + rows + 1].item() == 32
+    # a slot outside the table is skipped (verify ids read 0 for it)
+    bad = slots_t.clone()
+    bad[0] = n_slots + 3
+    N.call("pse_step_verify_ids", last.data_ptr(), n_slots, bad.data_ptr(), drafts.data_ptr(), base.data_ptr(),
+           rows, k, ids.data_ptr(), first.data_ptr(), st)
+    torch.cuda.synchronize()
+    assert ids[0, 0].item() == 0
