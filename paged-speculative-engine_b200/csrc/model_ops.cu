@@ -67,8 +67,7 @@ __global__ void __launch_bounds__(THREADS) norm_kernel(const float* x, int64_t l
   }
 }
 
-// Residual add fused with the following norm, one warp per row (the row
-// lives in registers; no block-wide synchronisation):
+// Residual add fused with the following norm (the row lives in registers):
 //   if y:  x[r] += y[r] (+ bias)      (engine/model.py:140-141)
 //   out[r] = LayerNorm(x[r]) or RMSNorm(x[r])   (engine/model.py:124-126, 155)
 
