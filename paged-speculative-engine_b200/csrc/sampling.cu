@@ -130,21 +130,24 @@ __device__ int block_argmax(const float* row, int V, Scratch& sh) {
   float bv = -INFINITY;
   int bi = INT_MAX;
   if ((V & 3) == 0 && (reinterpret_cast<uintptr_t>(row) & 15) == 0) {
-    // 16-byte loads, four rows of candidates per thread in index order
+    // 16-byte loads, four of them in flight per thread, candidates taken in
+    // index order
     const float4* r4 = reinterpret_cast<const float4*>(row);
     const int n4 = V >> 2;
+    const int bd = blockDim.x;
     int e = threadIdx.x;
-    for (; e + blockDim.x < n4; e += 2 * blockDim.x) {
-      const float4 a = r4[e], b = r4[e + blockDim.x];
-      argmax_step(a.x, 4 * e, bv, bi);
-      argmax_step(a.y, 4 * e + 1, bv, bi);
-      argmax_step(a.z, 4 * e + 2, bv, bi);
-      argmax_step(a.w, 4 * e + 3, bv, bi);
-      const int f = e + blockDim.x;
-      argmax_step(b.x, 4 * f, bv, bi);
-      argmax_step(b.y, 4 * f + 1, bv, bi);
-      argmax_step(b.z, 4 * f + 2, bv, bi);
-      argmax_step(b.w, 4 * f + 3, bv, bi);
+    for (; e + 3 * bd < n4; e += 4 * bd) {
+      float4 a[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) a[q] = r4[e + q * bd];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int f = 4 * (e + q * bd);
+        argmax_step(a[q].x, f, bv, bi);
+        argmax_step(a[q].y, f + 1, bv, bi);
+        argmax_step(a[q].z, f + 2, bv, bi);
+        argmax_step(a[q].w, f + 3, bv, bi);
+      }
     }
     for (; e < n4; e += blockDim.x) {
       const float4 a = r4[e];
