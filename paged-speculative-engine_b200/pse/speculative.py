@@ -617,21 +617,33 @@ class StepRunner:
             key_np = np.array([_fnv1a(r) for r in request_ids], dtype=np.uint32).view(np.int32)
             steps_np = np.fromiter((steps.get(r, 0) for r in request_ids), np.int32, B)
         views = []
+        prev_steps = []
 
         def while_device_runs():
-            # the next-logits dicts depend only on the slots: build them during the step
+            # the next-logits dicts depend only on the slots, and the per-request
+            # step counts on nothing the step computes: both are done during the step
             views.append(dict(zip(request_ids, map(dviews.__getitem__, sd))))
             views.append(dict(zip(request_ids, map((tviews if defer_bonus is False else pviews).__getitem__, stt))))
+            prev_steps.extend(map(steps.get, request_ids))
+            for r, n in zip(request_ids, prev_steps):
+                steps[r] = (n or 0) + 1
 
-        b, nacc_np = self._run(request_ids, sd_np, st_np, temperature, generator, uniforms, use_graph, defer_bonus,
-                               key_np, steps_np, while_device_runs=while_device_runs)
+        try:
+            b, nacc_np = self._run(request_ids, sd_np, st_np, temperature, generator, uniforms, use_graph,
+                                   defer_bonus, key_np, steps_np, while_device_runs=while_device_runs)
+        except BaseException:
+            # a failed step does not count
+            for r, n in zip(request_ids, prev_steps):
+                if n is None:
+                    steps.pop(r, None)
+                else:
+                    steps[r] = n
+            raise
         toks = b.host_pack_np[:B * (k + 1)].reshape(B, k + 1).tolist()
         nacc = nacc_np.tolist()
         accepted = {r: toks[i][: nacc[i] + 1] for i, r in enumerate(request_ids)}
         n_acc = dict(zip(request_ids, nacc))
         dn, tn = views
-        for r in request_ids:
-            steps[r] = steps.get(r, 0) + 1
         return BatchStepResult(accepted, n_acc, dn, tn)
 
     def step_rows(self, request_ids, sd_np, st_np, ords_np, commit: CommitArena, temperature, generator=None,
