@@ -544,7 +544,7 @@ def micro_attention(args, device, emit=True):
     torch.cuda.synchronize()
     # device time: the launches captured in one CUDA graph (no host dispatch between them)
     graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph):
+    with N.graph_capture(graph):
         for _ in range(args.steps):
             launch()
     graph.replay()
@@ -984,7 +984,7 @@ def micro_gemm(args, device):
                 fn()
             torch.cuda.synchronize()
             graph = torch.cuda.CUDAGraph()  # device time: 50 calls captured, no host dispatch in the timing
-            with torch.cuda.graph(graph):
+            with N.graph_capture(graph):
                 for _ in range(50):
                     fn()
             graph.replay()
@@ -1033,7 +1033,7 @@ def micro_churn(args, device, emit=True):
 
     torch.cuda.synchronize()
     g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g):
+    with N.graph_capture(g):
         st = N.stream_ptr()
         for j in range(steps):
             step(j)

@@ -7,7 +7,9 @@ are ordered with (and capturable alongside) torch's own work.
 """
 from __future__ import annotations
 
+import contextlib
 import ctypes
+import gc
 import os
 import threading
 from collections import Counter
@@ -159,3 +161,22 @@ def dtype_code(dtype: torch.dtype) -> int:
     if dtype == torch.bfloat16:
         return PSE_BF16
     raise ValueError(f"unsupported dtype {dtype} (float32 or bfloat16)")
+
+
+@contextlib.contextmanager
+def graph_capture(graph):
+    """``torch.cuda.graph(graph)`` with Python's cyclic garbage collector held
+    off for the capture.  A collection that runs in the middle of a capture
+    frees whatever dead reference cycles hold: CUDA graphs of runners that are
+    no longer used, pinned host buffers.  Releasing them makes CUDA calls that
+    are not permitted while a stream is capturing, and the capture is then
+    invalidated (cudaErrorStreamCaptureInvalidated).  Those cycles are
+    collected later, outside any capture."""
+    enabled = gc.isenabled()
+    gc.disable()
+    try:
+        with torch.cuda.graph(graph):
+            yield
+    finally:
+        if enabled:
+            gc.enable()

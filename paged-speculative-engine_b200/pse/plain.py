@@ -125,7 +125,7 @@ class DecodeRunner:
             self.graphs[key].replay()
         elif use_graph and key in self.warm:
             g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g):
+            with N.graph_capture(g):
                 self._program(b, max_ctx, commit)
             self.graphs[key] = g
             g.replay()

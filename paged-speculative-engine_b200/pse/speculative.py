@@ -749,7 +749,7 @@ class StepRunner:
             self.graphs[key].replay()
         elif graphs and key in self.warm:
             g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g):
+            with N.graph_capture(g):
                 self._program(b, T, philox, mcd, mct, in_pending, out_defer, commit)
             self.graphs[key] = g
             g.replay()

@@ -222,7 +222,7 @@ class TreeStepRunner:
             self.graphs[key].replay()
         elif graphs and key in self.warm:
             g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g):
+            with N.graph_capture(g):
                 self._program(f, T, philox, mcd, mct)
             self.graphs[key] = g
             g.replay()

@@ -39,7 +39,7 @@ def test_churn_from_a_graph_is_bit_exact(rows, bs, steps, seed):
     acc_d = torch.from_numpy(acc).cuda()
     torch.cuda.synchronize()
     g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g):
+    with N.graph_capture(g):
         st = N.stream_ptr()
         for j in range(steps):
             N.call("pse_kv_reserve", c.state, slots.data_ptr(), rows, 8, base.data_ptr(), st)

@@ -257,3 +257,27 @@ def test_step_glue_kernels_match_their_tensor_statements(rows, k):
            rows, k, ids.data_ptr(), first.data_ptr(), st)
     torch.cuda.synchronize()
     assert ids[0, 0].item() == 0
+
+
+def test_graph_capture_holds_off_the_collector():
+    """The library's captures run with Python's cyclic collector disabled (a
+    collection mid-capture can destroy dead runners' CUDA graphs, which is not
+    permitted while a stream captures) and restore it afterwards, also when the
+    captured program raises."""
+    import gc
+    import pse._native as N
+    x = torch.zeros(4, device="cuda")
+    g = torch.cuda.CUDAGraph()
+    assert gc.isenabled()
+    with N.graph_capture(g):
+        assert not gc.isenabled()
+        x.add_(1)
+    assert gc.isenabled()
+    g.replay()
+    torch.cuda.synchronize()
+    assert x.tolist() == [1.0] * 4
+    g2 = torch.cuda.CUDAGraph()
+    with pytest.raises(RuntimeError):
+        with N.graph_capture(g2):
+            raise RuntimeError("program failed")
+    assert gc.isenabled()
