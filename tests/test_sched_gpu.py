@@ -279,5 +279,6 @@ def test_graph_capture_holds_off_the_collector():
     g2 = torch.cuda.CUDAGraph()
     with pytest.raises(RuntimeError):
         with N.graph_capture(g2):
+            x.add_(1)
             raise RuntimeError("program failed")
     assert gc.isenabled()
