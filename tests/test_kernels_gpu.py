@@ -1,7 +1,7 @@
 """Kernel parity against the CPU oracle through the C ABI (libpse.so).
 
 Integer work (free list, block tables, Philox, token choices) must match bit
-for bit; floating-point outputs within the north-star tolerances (1e-4 abs in
+for bit; floating-point outputs within the stated tolerances (1e-4 abs in
 fp32, 2e-2 abs in bf16).  GPU only."""
 from __future__ import annotations
 
