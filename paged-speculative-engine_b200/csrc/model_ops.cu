@@ -28,6 +28,48 @@ __global__ void embed_kernel(const int32_t* ids, const int32_t* base_len, const 
   }
 }
 
+// bf16 tables with d a multiple of 8: each thread adds 8 consecutive columns
+// (one 16-byte load from each table, two float4 stores), so a row's loads are
+// in flight together; the same fp32 sums as embed_kernel.
+__global__ void embed_bf16x8_kernel(const int32_t* ids, const int32_t* base_len, const int32_t* positions,
+                                    int width, const __nv_bfloat16* tok_emb, const __nv_bfloat16* pos_emb, int d,
+                                    float* x, int vocab, int n_pos) {
+  pdl_wait();
+  pdl_trigger();
+  const int t = blockIdx.x;
+  const int i = t / width, w = t % width;
+  const int64_t tok = ids[t];
+  const int64_t pos = positions ? (int64_t)positions[t] : base_len ? (int64_t)base_len[i] + w : 0;
+  const bool tok_ok = tok >= 0 && tok < vocab;
+  const bool pos_ok = pos_emb != nullptr && pos >= 0 && pos < n_pos;
+  for (int c = threadIdx.x * 8; c < d; c += blockDim.x * 8) {
+    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (tok_ok) {
+      const uint4 a = *reinterpret_cast<const uint4*>(tok_emb + tok * d + c);
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&a);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 f = __bfloat1622float2(h[q]);
+        v[2 * q] = f.x;
+        v[2 * q + 1] = f.y;
+      }
+    }
+    if (pos_ok) {
+      const uint4 a = *reinterpret_cast<const uint4*>(pos_emb + pos * d + c);
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&a);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 f = __bfloat1622float2(h[q]);
+        v[2 * q] += f.x;
+        v[2 * q + 1] += f.y;
+      }
+    }
+    float* xr = x + (int64_t)t * d + c;
+    *reinterpret_cast<float4*>(xr) = make_float4(v[0], v[1], v[2], v[3]);
+    *reinterpret_cast<float4*>(xr + 4) = make_float4(v[4], v[5], v[6], v[7]);
+  }
+}
+
 template <int THREADS>
 __device__ __forceinline__ float block_sum_f(float v, float* sh) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -363,12 +405,24 @@ constexpr int64_t kIdx32 = 1ll << 30;
 
 using namespace pse;
 
+static bool embed_vec_ok(const void* tok_emb, const void* pos_emb, const float* x, int d, int dtype) {
+  const uintptr_t bits = reinterpret_cast<uintptr_t>(tok_emb) | reinterpret_cast<uintptr_t>(pos_emb) |
+                         reinterpret_cast<uintptr_t>(x);
+  return dtype == PSE_BF16 && d % 8 == 0 && (bits & 15) == 0;
+}
+
 extern "C" int pse_embed(const int32_t* ids, const int32_t* base_len, int32_t rows, int32_t width,
                          const void* tok_emb, const void* pos_emb, int32_t d, int32_t emb_dtype, int32_t vocab,
                          int32_t n_pos, float* x, void* stream) {
   if (rows < 0 || width < 0 || d <= 0 || vocab <= 0) return PSE_EINVAL;
   if (rows == 0 || width == 0) return PSE_OK;
   if (!ids || !tok_emb || !x || (pos_emb && !base_len)) return PSE_EINVAL;
+  if (embed_vec_ok(tok_emb, pos_emb, x, d, emb_dtype)) {
+    cudaError_t e = launch_pdl(embed_bf16x8_kernel, dim3((unsigned)(rows * width)), dim3(128), 0,
+                               (cudaStream_t)stream, ids, base_len, (const int32_t*)nullptr, width,
+                               (const __nv_bfloat16*)tok_emb, (const __nv_bfloat16*)pos_emb, d, x, vocab, n_pos);
+    return e == cudaSuccess ? PSE_OK : (int)e;
+  }
   cudaError_t e = launch_pdl(embed_kernel, dim3((unsigned)(rows * width)), dim3(128), 0, (cudaStream_t)stream, ids,
                              base_len, (const int32_t*)nullptr, width, tok_emb, pos_emb, d, emb_dtype, x, vocab, n_pos);
   if (e != cudaSuccess) return (int)e;
@@ -381,6 +435,12 @@ extern "C" int pse_embed_pos(const int32_t* ids, const int32_t* positions, int32
   if (rows < 0 || width < 0 || d <= 0 || vocab <= 0) return PSE_EINVAL;
   if (rows == 0 || width == 0) return PSE_OK;
   if (!ids || !tok_emb || !x || (pos_emb && !positions)) return PSE_EINVAL;
+  if (embed_vec_ok(tok_emb, pos_emb, x, d, emb_dtype)) {
+    cudaError_t e = launch_pdl(embed_bf16x8_kernel, dim3((unsigned)(rows * width)), dim3(128), 0,
+                               (cudaStream_t)stream, ids, (const int32_t*)nullptr, positions, width,
+                               (const __nv_bfloat16*)tok_emb, (const __nv_bfloat16*)pos_emb, d, x, vocab, n_pos);
+    return e == cudaSuccess ? PSE_OK : (int)e;
+  }
   cudaError_t e = launch_pdl(embed_kernel, dim3((unsigned)(rows * width)), dim3(128), 0, (cudaStream_t)stream, ids,
                              (const int32_t*)nullptr, positions, width, tok_emb, pos_emb, d, emb_dtype, x, vocab,
                              n_pos);

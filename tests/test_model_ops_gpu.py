@@ -66,3 +66,39 @@ def test_add_norm_matches_torch(d, dtype, variant):
     assert (got - want).abs().max().item() < tol
     if pad:
         assert torch.isnan(out[:, d:].float()).all()  # nothing written past the row
+
+
+@pytest.mark.parametrize("d,pos,dtype", [(768, True, torch.bfloat16), (2048, False, torch.bfloat16),
+                                         (100, True, torch.bfloat16), (384, True, torch.float32)])
+def test_embed_matches_torch(d, pos, dtype):
+    """``pse_embed`` / ``pse_embed_pos`` (engine/model.py:175-181: token plus
+    learned position embedding) equal the fp32 sum of the table rows exactly:
+    the bf16 vector path (d a multiple of 8), the scalar path (other d, fp32
+    tables); ids and positions out of range read as zero rows."""
+    N = _N()
+    g = torch.Generator(device="cuda").manual_seed(d)
+    vocab, n_pos, rows, width = 1000, 300, 37, 3
+    tok = torch.randn(vocab, d, device="cuda", generator=g).to(dtype)
+    pe = torch.randn(n_pos, d, device="cuda", generator=g).to(dtype) if pos else None
+    ids = torch.randint(0, vocab, (rows * width,), device="cuda", generator=g, dtype=torch.int32)
+    ids[5] = vocab + 7  # out of range: no token row
+    base = torch.randint(0, n_pos - width, (rows,), device="cuda", generator=g, dtype=torch.int32)
+    base[3] = n_pos  # every position of row 3 out of range: no position row
+    x = torch.full((rows * width, d), float("nan"), device="cuda")
+    dt = N.dtype_code(dtype)
+    N.call("pse_embed", ids.data_ptr(), base.data_ptr(), rows, width, tok.data_ptr(),
+           None if pe is None else pe.data_ptr(), d, dt, vocab, n_pos, x.data_ptr(), N.stream_ptr())
+    positions = (base.view(-1, 1).long() + torch.arange(width, device="cuda").view(1, -1)).reshape(-1)
+    want = torch.where((ids.long() < vocab).view(-1, 1), tok.float()[ids.long().clamp(max=vocab - 1)],
+                       torch.zeros((), device="cuda"))
+    if pe is not None:
+        ok = (positions < n_pos).view(-1, 1)
+        want = want + torch.where(ok, pe.float()[positions.clamp(max=n_pos - 1)], torch.zeros((), device="cuda"))
+    torch.cuda.synchronize()
+    assert torch.equal(x, want)
+    x2 = torch.full_like(x, float("nan"))
+    pos32 = positions.to(torch.int32)
+    N.call("pse_embed_pos", ids.data_ptr(), pos32.data_ptr(), rows, width, tok.data_ptr(),
+           None if pe is None else pe.data_ptr(), d, dt, vocab, n_pos, x2.data_ptr(), N.stream_ptr())
+    torch.cuda.synchronize()
+    assert torch.equal(x2, want)
